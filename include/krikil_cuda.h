@@ -1,0 +1,235 @@
+/*
+ * krikil_cuda.h -- C ABI of the B200 (sm_100a) implementation of krikil-rs's
+ * per-layer inference path for the Pebble-25M hybrid Mamba2 + attention model.
+ *
+ * The reference is a Rust library whose public surface is src/lib.rs:1-6; its
+ * model API (src/model.rs) is what a Rust `build.rs` + `extern "C"` binding of
+ * this header replaces.  Each entry point below names the reference interface
+ * it stands in for.  All computation is fp32, on the GPU; there is no CPU
+ * fallback -- if the device or the kernels are unusable, calls fail with
+ * KRK_CUDA and krk_last_error() says why.
+ *
+ * Conventions
+ *  - Every function returns a krk_status; 0 is success.  On failure the
+ *    calling thread's krk_last_error() holds a message (the reference's
+ *    anyhow error text where one exists).  Nothing throws across the ABI.
+ *  - Handles are opaque.  A model is immutable after load and may be shared by
+ *    states on the same device; a state is owned by one thread at a time
+ *    ("thread-compatible": calls on one state must not overlap).
+ *  - Host buffers belong to the caller and are only read/written during the
+ *    call.  Per-kernel entry points (krk_k_*) take DEVICE pointers and a CUDA
+ *    stream (cudaStream_t passed as void*, NULL = legacy default stream) and
+ *    are asynchronous.
+ *  - A state holds `batch` independent sequences (the reference has exactly
+ *    one, i.e. batch = 1).
+ */
+#ifndef KRIKIL_CUDA_H
+#define KRIKIL_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KRK_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define KRK_API __attribute__((visibility("default")))
+#else
+#define KRK_API
+#endif
+
+/* Model dimensions (src/model.rs:12-30). */
+#define KRK_HIDDEN 608
+#define KRK_VOCAB 2048
+#define KRK_INTERMEDIATE 2432
+#define KRK_LAYERS 8
+#define KRK_ATTN_HEADS 8
+#define KRK_ATTN_HEAD_DIM 76
+#define KRK_MAMBA_D_STATE 128
+#define KRK_MAMBA_D_CONV 4
+#define KRK_MAMBA_D_INNER 1216
+#define KRK_MAMBA_HEAD_DIM 64
+#define KRK_MAMBA_HEADS 19
+#define KRK_MAMBA_D_IN_PROJ 2707
+#define KRK_MAMBA_D_XBC 1472
+#define KRK_EOS_TOKEN 0
+
+typedef enum krk_status {
+    KRK_OK = 0,
+    KRK_BAD_TOKEN = 1,        /* token id >= vocab (src/model.rs:333-335, :588-590) */
+    KRK_CONTEXT_OVERFLOW = 2, /* position would exceed the context limit (src/model.rs:321-327, :591-593) */
+    KRK_EMPTY = 3,            /* empty prompt (src/model.rs:317-319) */
+    KRK_IO = 4,               /* file missing / unreadable / malformed safetensors (src/model.rs:235-239) */
+    KRK_NOT_FOUND = 5,        /* tensor missing from the checkpoint (src/model.rs:243-244) */
+    KRK_INVALID = 6,          /* bad argument (null handle, size or alignment) */
+    KRK_CUDA = 7,             /* CUDA runtime error or no usable device */
+    KRK_CHECK_FAILED = 8      /* internal consistency check failed */
+} krk_status;
+
+typedef struct krk_model krk_model;
+typedef struct krk_state krk_state;
+
+/* Message of the last failure on this thread ("" if none). */
+KRK_API const char* krk_last_error(void);
+KRK_API const char* krk_status_string(int status);
+KRK_API int krk_abi_version(void);
+
+/* ------------------------------------------------------------------ model */
+
+/* PebbleModel::load_safetensors (src/model.rs:233-313).  Reads the tensors the
+ * reference reads, by the same names (wte.weight, lnf.weight,
+ * blocks.{i}.ln.weight, blocks.{i}.mixer.{in_proj.weight, conv1d.weight,
+ * conv1d.bias, dt_bias, A_log, D, norm.weight, out_proj.weight} for Mamba
+ * layers i%4<3, blocks.{i}.{ln1,wqkv,wo,ln2,fc1,fc2}.weight otherwise),
+ * precomputes A = -exp(A_log) (src/model.rs:273-274) and uploads everything to
+ * `device`.  Like the reference it does not check shapes, only that each
+ * tensor is little-endian F32 with exactly the element count the model uses.
+ * File and format errors are reported before the device is touched. */
+KRK_API int krk_model_load(const char* path, int device, krk_model** out);
+KRK_API int krk_model_free(krk_model* model);
+KRK_API int krk_model_device(const krk_model* model, int* device);
+/* The CUDA stream (cudaStream_t) the model's states run on. */
+KRK_API int krk_model_stream(const krk_model* model, void** stream);
+
+/* ------------------------------------------------------------------ state */
+
+/* PebbleState::new(&config, max_ctx) (src/model.rs:204-219), for `batch`
+ * independent sequences: per sequence 6 Mamba layers of conv [1472][4] and SSD
+ * [19][64][128] state, 2 attention layers of K/V caches [max_ctx][608], all in
+ * device memory and zeroed. */
+KRK_API int krk_state_create(const krk_model* model, int batch, int max_ctx, krk_state** out);
+KRK_API int krk_state_free(krk_state* state);
+/* PebbleState::reset (src/model.rs:221-229) for the sequences whose mask byte
+ * is non-zero (mask NULL = all): position 0, Mamba state zeroed, attention
+ * length 0. */
+KRK_API int krk_state_reset(krk_state* state, const uint8_t* mask);
+KRK_API int krk_state_batch(const krk_state* state, int* batch);
+KRK_API int krk_state_context_limit(const krk_state* state, int* max_ctx);
+/* current_pos of each sequence (src/model.rs:200), pos_out[batch]. */
+KRK_API int krk_state_positions(const krk_state* state, int64_t* pos_out);
+
+/* PebbleModel::forward_prefill (src/model.rs:316-368), batched: sequence b
+ * consumes tokens[off_b .. off_b + lens[b]) (prompts packed back to back,
+ * off_b = lens[0] + ... + lens[b-1]) starting at its current position.
+ * logits_out (host, [batch][2048], may be NULL) receives each sequence's
+ * last-token logits.  Checks, in the reference's order, before any state is
+ * touched: every lens[b] >= 1 (KRK_EMPTY), pos_b + lens[b] <= max_ctx
+ * (KRK_CONTEXT_OVERFLOW), every token < 2048 (KRK_BAD_TOKEN). */
+KRK_API int krk_prefill(const krk_model* model, krk_state* state, const uint32_t* tokens, const int32_t* lens,
+                        float* logits_out);
+
+/* PebbleModel::forward_step (src/model.rs:586-624), batched: sequence b
+ * consumes tokens[b] at its current position.  logits_out (host,
+ * [batch][2048], may be NULL).  Checks before any state change: every token <
+ * 2048 (KRK_BAD_TOKEN), then every position < max_ctx (KRK_CONTEXT_OVERFLOW). */
+KRK_API int krk_step(const krk_model* model, krk_state* state, const uint32_t* tokens, float* logits_out);
+
+/* The greedy path of GenerationEngine::generate_with_callback
+ * (src/generate.rs:55-133) with Sampler::sample at temperature 0
+ * (src/sampler.rs:43-80), run for all sequences at once with the sampling on
+ * the device: reset, prefill the packed prompts, then per step choose each
+ * sequence's token (repetition penalty over prompt + generated tokens when
+ * repetition_penalty != 1, first maximum wins) and feed it back.  A sequence
+ * stops after max_new_tokens tokens, when its position reaches max_ctx, or --
+ * if stop_at_eos -- when it picks KRK_EOS_TOKEN (not emitted).  With
+ * stop_at_eos = 0 every sequence emits min(max_new_tokens, max_ctx - len + 1)
+ * tokens.  tokens_out (host, [batch][max_new_tokens]) and n_out (host,
+ * [batch]) receive the generated ids and their counts. */
+KRK_API int krk_generate_greedy(const krk_model* model, krk_state* state, const uint32_t* prompts,
+                                const int32_t* lens, int max_new_tokens, float repetition_penalty, int stop_at_eos,
+                                uint32_t* tokens_out, int32_t* n_out);
+
+/* Test hook: copies one sequence's layer state to host memory.
+ *   what 0: conv state [1472][4] (Mamba layers)   what 1: SSD state [19][64][128]
+ *   what 2: K cache [max_ctx][608] (attention)     what 3: V cache [max_ctx][608]
+ * n = number of floats available at out (must be >= the size above). */
+KRK_API int krk_state_export(const krk_state* state, int seq, int layer, int what, float* out, int64_t n);
+
+/* Kernels this library launched in this process (graph replays count each
+ * kernel node). */
+KRK_API int krk_launch_count(uint64_t* count);
+
+/* ------------------------------------------------------ per-kernel entry points
+ * Device pointers, fp32, asynchronous on `stream`.  Each names the reference
+ * code it computes. */
+
+/* src/math.rs:41-54 on rows: y[r] = rms_norm(x[r], w, eps), [rows][dim],
+ * dim % 128 == 0, dim <= 1024. */
+KRK_API int krk_k_rmsnorm_rows(const float* x, const float* w, float eps, int64_t rows, int dim, float* y,
+                               void* stream);
+
+/* src/math.rs:41-54 on feature-major activations (column m of x[k*ldx + m],
+ * k < K <= 1216, m < M): out[k*ldo+m] = x*scale(m)*w[k], the sum of squares
+ * accumulated in the reference's sequential order. */
+KRK_API int krk_k_rmsnorm_fm(const float* x, int ldx, const float* w, float eps, int K, int M, float* out, int ldo,
+                             void* stream);
+
+/* Gate + gated RMSNorm + residual (src/model.rs:688-693, src/math.rs:56-68,
+ * residual add src/model.rs:699-701): y = rms_norm(x * silu(z), w, eps) + res
+ * over [rows][dim], dim % 128 == 0, dim <= 1024. */
+KRK_API int krk_k_gated_rmsnorm_residual(const float* x, const float* z, const float* res, const float* w, float eps,
+                                         int64_t rows, int dim, float* y, void* stream);
+
+/* Projection C = A . W^T (src/math.rs:130-153 gemv and :188-211 gemm_transb)
+ * with the reference dot's exact rounding.  At: A feature-major [K][lda];
+ * Wt: W K-major [K][ldw]; C batch-major [M][ldc] (out_fm = 0) or
+ * feature-major [N][ldc] (out_fm = 1).  epilogue 0: store, 1: C += result
+ * (residual), 2: store gelu(result) (src/math.rs:17-39).  M % 64 == 0,
+ * N % 32 == 0, K % 32 == 0, leading dims % 4 == 0, pointers 16-byte aligned. */
+KRK_API int krk_k_gemm(const float* At, int lda, const float* Wt, int ldw, float* C, int ldc, int M, int N, int K,
+                       int epilogue, int out_fm, void* stream);
+
+/* Embedding gather (src/model.rs:330-338, :598) into feature-major
+ * out[k*ldo + m] = wte[tok[m]*K + k]. */
+KRK_API int krk_k_embed(const uint32_t* tok, const float* wte, int vocab, int K, int M, float* out, int ldo,
+                        void* stream);
+
+/* Pointwise silu (op 0, src/math.rs:3-6), softplus (op 1, :8-15),
+ * gelu (op 2, :17-39). */
+KRK_API int krk_k_pointwise(int op, const float* x, float* y, int64_t n, void* stream);
+
+/* Causal depthwise conv1d (kernel 4) + SiLU on x, then the Mamba2 SSD single-
+ * step update (src/model.rs:643-685) for batch B, H heads of P = 64 channels,
+ * N = 128 states, B/C given directly:
+ *   x [B][H*P] raw conv input, bm/cm [B][N], dt [B][H] (raw; softplus(dt +
+ *   dt_bias) inside), conv_state [B][H*P][3] (previous 3 inputs, updated),
+ *   conv_w [H*P][4], conv_b [H*P], ssm [B][H][P][N] (updated), dt_bias/a_neg/
+ *   dsk [H] (a_neg = A = -exp(A_log)), y [B][H*P] = sum_n s*C + D*x. */
+KRK_API int krk_k_conv_ssd_step(const float* x, const float* bm, const float* cm, const float* dt,
+                                float* conv_state, const float* conv_w, const float* conv_b, float* ssm,
+                                const float* dt_bias, const float* a_neg, const float* dsk, float* y, int B, int H,
+                                int P, int N, void* stream);
+
+/* The same conv + SSD recurrence over T tokens per sequence (the prefill form,
+ * src/model.rs:392-454): x [B][T][H*P], bm/cm [B][T][N], dt [B][T][H],
+ * y [B][T][H*P]; the SSD state is carried in registers across the sequence
+ * and the inputs are staged through shared memory chunk by chunk. */
+KRK_API int krk_k_conv_ssd_scan(const float* x, const float* bm, const float* cm, const float* dt,
+                                float* conv_state, const float* conv_w, const float* conv_b, float* ssm,
+                                const float* dt_bias, const float* a_neg, const float* dsk, float* y, int B, int T,
+                                int H, int P, int N, void* stream);
+
+/* Decode RoPE (src/math.rs:234-260) + KV-cache append (src/model.rs:730-733)
+ * + single-query softmax attention (src/model.rs:736-760) on a [B][H][ctx][dh]
+ * cache: q,k,v [B][H][dh] (dh = 64 or 76), pos [B] (int32, < ctx), kc/vc
+ * updated at slot pos[b], out [B][H][dh].  Keys are processed in splits of
+ * `split` (multiple of 64; 0 picks 256); when a sequence needs more than one
+ * split, `work` must hold krk_attn_work_floats() floats of device scratch. */
+KRK_API size_t krk_attn_work_floats(int B, int H, int dh, int ctx, int split);
+KRK_API int krk_k_rope_kv_attn_decode(const float* q, const float* k, const float* v, float* kc, float* vc,
+                                      const int32_t* pos, float* out, float* work, int B, int H, int dh, int ctx,
+                                      int split, float theta, void* stream);
+
+/* Greedy pick (src/sampler.rs:50-80) per row of logits [B][ld]: repetition
+ * penalty on tokens whose bit is set in seen [B][vocab/32] (seen may be NULL;
+ * penalty 1 disables it), then the first maximum; tok [B]. */
+KRK_API int krk_k_greedy(const float* logits, int64_t ld, int vocab, int B, uint32_t* seen, float penalty,
+                         uint32_t* tok, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* KRIKIL_CUDA_H */

@@ -1,0 +1,930 @@
+// Host runtime behind include/krikil_cuda.h: weights, per-sequence state in
+// HBM, batched prefill / decode orchestration, and the C ABI.
+//
+// Layouts in device memory (fp32):
+//  weights   projections stored K-major (W^T, [in][out], out padded to 32):
+//            in_proj [608][2720], out_proj [1216][608], wqkv [608][1824],
+//            wo [608][608], fc1 [608][2432], fc2 [2432][608], LM head = wte^T
+//            [608][2048]; wte [2048][608] row-major for the embedding gather.
+//  state     per Mamba layer conv [B][1472][4] and SSD [B][19][64][128]; per
+//            attention layer K and V caches [B][ctx][608] (row t = the 8 heads'
+//            76-dim vectors, as src/model.rs:141-142).
+//  decode    activations between projections are feature-major ([features]
+//            [Mp], Mp = B rounded up to 64) so each projection's A operand is a
+//            dense K-major tile; projection outputs that feed per-sequence
+//            kernels (in_proj, wqkv, logits) are batch-major.
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <algorithm>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "../../include/krikil_cuda.h"
+#include "kernels.h"
+#include "safetensors.h"
+
+namespace {
+
+constexpr int HID = KRK_HIDDEN, VOC = KRK_VOCAB, INTER = KRK_INTERMEDIATE, NL = KRK_LAYERS;
+constexpr int NH = KRK_ATTN_HEADS, HD = KRK_ATTN_HEAD_DIM;
+constexpr int DS = KRK_MAMBA_D_STATE, DI = KRK_MAMBA_D_INNER, MP = KRK_MAMBA_HEAD_DIM, MH = KRK_MAMBA_HEADS;
+constexpr int DIP = KRK_MAMBA_D_IN_PROJ, DXBC = KRK_MAMBA_D_XBC;
+constexpr int DIP_PAD = 2720;  // in_proj output width padded to the 32-column tile
+constexpr int QKV = 3 * HID;
+constexpr float RMS_EPS = 1e-6f, MNORM_EPS = 1e-5f, THETA = 10000.0f;
+constexpr int SEEN_WORDS = VOC / 32;
+constexpr int64_t PREFILL_GROUP_TOKENS = 16384;
+
+// Column offsets inside one in_proj output row: z | x | B | C | dt (src/model.rs:638-640, :656-658).
+constexpr int OFF_Z = 0, OFF_X = DI, OFF_B = DI + DI, OFF_C = DI + DI + DS, OFF_DT = DI + DXBC;
+
+inline bool is_mamba(int l) { return l % 4 < 3; }  // src/model.rs:207, :261
+inline int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
+
+thread_local std::string g_err;
+
+int fail(int status, const std::string& msg) {
+    g_err = msg;
+    return status;
+}
+
+struct KrkError {
+    int status;
+    std::string msg;
+};
+
+inline void ck(cudaError_t e, const char* what) {
+    if (e != cudaSuccess) throw KrkError{KRK_CUDA, std::string(what) + ": " + cudaGetErrorString(e)};
+}
+
+// Restores the caller's current device on scope exit.
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        cudaGetDevice(&prev);
+        if (prev != dev) ck(cudaSetDevice(dev), "cudaSetDevice");
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        cudaGetDevice(&cur);
+        if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+// A device arena: one cudaMalloc, bump-allocated 256-byte aligned slices.
+struct Arena {
+    char* base = nullptr;
+    size_t cap = 0, used = 0;
+    void reserve(size_t bytes) {
+        release();
+        if (bytes == 0) return;
+        ck(cudaMalloc(&base, bytes), "cudaMalloc");
+        cap = bytes;
+        used = 0;
+    }
+    template <typename T>
+    T* take(size_t count) {
+        size_t off = round_up((int64_t)used, 256);
+        size_t bytes = count * sizeof(T);
+        if (off + bytes > cap) throw KrkError{KRK_CHECK_FAILED, "internal arena overflow"};
+        used = off + bytes;
+        return reinterpret_cast<T*>(base + off);
+    }
+    void release() {
+        if (base) cudaFree(base);
+        base = nullptr;
+        cap = used = 0;
+    }
+    ~Arena() { release(); }
+};
+
+// Byte budget of a list of slices (mirrors Arena::take's alignment).
+struct Budget {
+    size_t bytes = 0;
+    template <typename T>
+    void add(size_t count) { bytes = round_up((int64_t)bytes, 256) + count * sizeof(T); }
+};
+
+struct LayerW {
+    // Mamba (src/model.rs:86-96)
+    float *ln = nullptr, *in_t = nullptr, *conv_w = nullptr, *conv_b = nullptr, *dt_bias = nullptr,
+          *a_neg = nullptr, *dsk = nullptr, *norm_w = nullptr, *out_t = nullptr;
+    // Attention (src/model.rs:98-105)
+    float *ln1 = nullptr, *qkv_t = nullptr, *wo_t = nullptr, *ln2 = nullptr, *fc1_t = nullptr, *fc2_t = nullptr;
+};
+
+}  // namespace
+
+struct krk_model {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    Arena arena;
+    float *wte = nullptr, *wte_t = nullptr, *lnf = nullptr;
+    LayerW L[NL];
+};
+
+namespace {
+
+struct PrefillWs {
+    int64_t cap_tokens = 0;
+    int cap_seqs = 0;
+    Arena arena;
+    float *x_t, *hn_t, *zx, *xbc, *y_t, *yn_t, *qkv, *ao_t, *mlp_t;
+    uint32_t* tok;
+    int32_t *row_seq, *cu, *start, *last, *dst;
+};
+
+}  // namespace
+
+struct krk_state {
+    const krk_model* m = nullptr;
+    int B = 0, ctx = 0;
+    int64_t Mp = 0;
+    Arena arena;
+    float *conv[NL] = {}, *ssm[NL] = {}, *kc[NL] = {}, *vc[NL] = {};
+    int32_t* pos_d = nullptr;
+    uint8_t* active_d = nullptr;
+    uint32_t* seen_d = nullptr;
+    uint32_t* tok_d = nullptr;
+    int32_t* limit_d = nullptr;
+    int32_t* step_d = nullptr;
+    float *h_t, *hn_t, *zx, *y_t, *yn_t, *qkv, *ao_t, *mlp_t, *logits, *attn_work;
+    int attn_split = 2048;
+    std::vector<int64_t> pos_h;
+    PrefillWs pre;
+    Arena hist_arena;
+    int64_t hist_cap = 0;
+    uint32_t* hist_d = nullptr;
+};
+
+namespace {
+
+// ------------------------------------------------------------------ loading
+struct HostTensor {
+    const float* p;
+    size_t n;
+};
+
+HostTensor get_tensor(const krk::SafeTensorsFile& f, const std::string& name, size_t expect) {
+    const krk::TensorInfo* t = f.info(name);
+    if (!t) throw KrkError{KRK_NOT_FOUND, "Tensor '" + name + "' not found in model"};
+    if (t->dtype != "F32") throw KrkError{KRK_IO, "Tensor '" + name + "' has dtype " + t->dtype + ", expected F32"};
+    size_t n = (size_t)((t->end - t->begin) / 4);
+    if (n != expect)
+        throw KrkError{KRK_IO, "Tensor '" + name + "' holds " + std::to_string(n) + " floats, expected " +
+                                   std::to_string(expect)};
+    return {reinterpret_cast<const float*>(f.data(*t)), n};  // x86 host: little-endian, unaligned loads are fine
+}
+
+// rows x cols (row-major) -> [cols][ld] (transposed, columns padded with zeros)
+std::vector<float> transpose_pad(const float* w, int rows, int cols, int ld) {
+    std::vector<float> out((size_t)cols * ld, 0.0f);
+    for (int r = 0; r < rows; ++r) {
+        const float* src = w + (size_t)r * cols;
+        for (int c = 0; c < cols; ++c) {
+            float v;
+            memcpy(&v, src + c, 4);
+            out[(size_t)c * ld + r] = v;
+        }
+    }
+    return out;
+}
+
+std::vector<float> copy_vec(const HostTensor& t) {
+    std::vector<float> v(t.n);
+    memcpy(v.data(), t.p, t.n * 4);
+    return v;
+}
+
+struct HostWeights {
+    struct Upload {
+        float** dst;
+        std::vector<float> data;
+    };
+    std::vector<Upload> ups;
+};
+
+// Reads and checks every tensor (src/model.rs:256-294) and prepares the device
+// layouts on the host; touches no device.
+void read_weights(krk_model* m, const std::string& path, HostWeights& hw) {
+    krk::SafeTensorsFile f;
+    std::string err;
+    if (!f.open(path, err)) throw KrkError{KRK_IO, err};
+    auto add = [&](float** dst, std::vector<float>&& v) { hw.ups.push_back({dst, std::move(v)}); };
+
+    HostTensor wte = get_tensor(f, "wte.weight", (size_t)VOC * HID);
+    HostTensor lnf = get_tensor(f, "lnf.weight", HID);
+    add(&m->wte, copy_vec(wte));
+    add(&m->wte_t, transpose_pad(wte.p, VOC, HID, VOC));
+    add(&m->lnf, copy_vec(lnf));
+    for (int i = 0; i < NL; ++i) {
+        const std::string p = "blocks." + std::to_string(i) + ".";
+        LayerW& L = m->L[i];
+        if (is_mamba(i)) {
+            add(&L.ln, copy_vec(get_tensor(f, p + "ln.weight", HID)));
+            HostTensor inp = get_tensor(f, p + "mixer.in_proj.weight", (size_t)DIP * HID);
+            add(&L.in_t, transpose_pad(inp.p, DIP, HID, DIP_PAD));
+            add(&L.conv_w, copy_vec(get_tensor(f, p + "mixer.conv1d.weight", (size_t)DXBC * 4)));
+            add(&L.conv_b, copy_vec(get_tensor(f, p + "mixer.conv1d.bias", DXBC)));
+            add(&L.dt_bias, copy_vec(get_tensor(f, p + "mixer.dt_bias", MH)));
+            std::vector<float> alog = copy_vec(get_tensor(f, p + "mixer.A_log", MH));
+            for (float& v : alog) v = -expf(v);  // A = -exp(A_log) (src/model.rs:273-274)
+            add(&L.a_neg, std::move(alog));
+            add(&L.dsk, copy_vec(get_tensor(f, p + "mixer.D", MH)));
+            add(&L.norm_w, copy_vec(get_tensor(f, p + "mixer.norm.weight", DI)));
+            HostTensor outp = get_tensor(f, p + "mixer.out_proj.weight", (size_t)HID * DI);
+            add(&L.out_t, transpose_pad(outp.p, HID, DI, HID));
+        } else {
+            add(&L.ln1, copy_vec(get_tensor(f, p + "ln1.weight", HID)));
+            HostTensor wqkv = get_tensor(f, p + "wqkv.weight", (size_t)QKV * HID);
+            add(&L.qkv_t, transpose_pad(wqkv.p, QKV, HID, QKV));
+            HostTensor wo = get_tensor(f, p + "wo.weight", (size_t)HID * HID);
+            add(&L.wo_t, transpose_pad(wo.p, HID, HID, HID));
+            add(&L.ln2, copy_vec(get_tensor(f, p + "ln2.weight", HID)));
+            HostTensor fc1 = get_tensor(f, p + "fc1.weight", (size_t)INTER * HID);
+            add(&L.fc1_t, transpose_pad(fc1.p, INTER, HID, INTER));
+            HostTensor fc2 = get_tensor(f, p + "fc2.weight", (size_t)HID * INTER);
+            add(&L.fc2_t, transpose_pad(fc2.p, HID, INTER, HID));
+        }
+    }
+}
+
+void upload_weights(krk_model* m, HostWeights& hw) {
+    Budget bud;
+    for (auto& u : hw.ups) bud.add<float>(u.data.size());
+    m->arena.reserve(bud.bytes);
+    for (auto& u : hw.ups) {
+        *u.dst = m->arena.take<float>(u.data.size());
+        ck(cudaMemcpy(*u.dst, u.data.data(), u.data.size() * 4, cudaMemcpyHostToDevice), "weight upload");
+    }
+}
+
+// ------------------------------------------------------------------ state
+void create_state(krk_state* s, const krk_model* m, int B, int ctx) {
+    s->m = m;
+    s->B = B;
+    s->ctx = ctx;
+    s->Mp = round_up(B, 64);
+    const int64_t Mp = s->Mp;
+    s->attn_split = (int64_t)B * NH >= 2 * 148 ? 2048 : 256;
+    const size_t work = krk::attn_decode_work_floats(B, NH, HD, ctx, s->attn_split);
+    Budget b;
+    for (int l = 0; l < NL; ++l) {
+        if (is_mamba(l)) {
+            b.add<float>((size_t)B * DXBC * 4);
+            b.add<float>((size_t)B * MH * MP * DS);
+        } else {
+            b.add<float>((size_t)B * ctx * HID);
+            b.add<float>((size_t)B * ctx * HID);
+        }
+    }
+    b.add<int32_t>(B); b.add<uint8_t>(B); b.add<uint32_t>((size_t)B * SEEN_WORDS); b.add<uint32_t>(Mp);
+    b.add<int32_t>(B); b.add<int32_t>(1);
+    b.add<float>(HID * Mp); b.add<float>(HID * Mp); b.add<float>(Mp * DIP_PAD); b.add<float>(DI * Mp);
+    b.add<float>(DI * Mp); b.add<float>(Mp * QKV); b.add<float>(HID * Mp); b.add<float>(INTER * Mp);
+    b.add<float>(Mp * VOC); b.add<float>(work);
+    s->arena.reserve(b.bytes);
+    for (int l = 0; l < NL; ++l) {
+        if (is_mamba(l)) {
+            s->conv[l] = s->arena.take<float>((size_t)B * DXBC * 4);
+            s->ssm[l] = s->arena.take<float>((size_t)B * MH * MP * DS);
+        } else {
+            s->kc[l] = s->arena.take<float>((size_t)B * ctx * HID);
+            s->vc[l] = s->arena.take<float>((size_t)B * ctx * HID);
+        }
+    }
+    s->pos_d = s->arena.take<int32_t>(B);
+    s->active_d = s->arena.take<uint8_t>(B);
+    s->seen_d = s->arena.take<uint32_t>((size_t)B * SEEN_WORDS);
+    s->tok_d = s->arena.take<uint32_t>(Mp);
+    s->limit_d = s->arena.take<int32_t>(B);
+    s->step_d = s->arena.take<int32_t>(1);
+    s->h_t = s->arena.take<float>(HID * Mp);
+    s->hn_t = s->arena.take<float>(HID * Mp);
+    s->zx = s->arena.take<float>(Mp * DIP_PAD);
+    s->y_t = s->arena.take<float>(DI * Mp);
+    s->yn_t = s->arena.take<float>(DI * Mp);
+    s->qkv = s->arena.take<float>(Mp * QKV);
+    s->ao_t = s->arena.take<float>(HID * Mp);
+    s->mlp_t = s->arena.take<float>(INTER * Mp);
+    s->logits = s->arena.take<float>(Mp * VOC);
+    s->attn_work = s->arena.take<float>(work);
+    ck(cudaMemsetAsync(s->arena.base, 0, s->arena.cap, m->stream), "state memset");
+    ck(cudaStreamSynchronize(m->stream), "state init");
+    s->pos_h.assign(B, 0);
+}
+
+void ensure_prefill_ws(krk_state* s, int64_t tokens, int seqs) {
+    PrefillWs& w = s->pre;
+    if (tokens <= w.cap_tokens && seqs <= w.cap_seqs) return;
+    const int64_t T = round_up(std::max<int64_t>(tokens, w.cap_tokens), 64);
+    const int S = std::max(seqs, w.cap_seqs);
+    Budget b;
+    b.add<float>(HID * T); b.add<float>(HID * T); b.add<float>(T * DIP_PAD); b.add<float>(T * DXBC);
+    b.add<float>(DI * T); b.add<float>(DI * T); b.add<float>(T * QKV); b.add<float>(HID * T);
+    b.add<float>(INTER * T);
+    b.add<uint32_t>(T); b.add<int32_t>(T); b.add<int32_t>(S + 1); b.add<int32_t>(S); b.add<int32_t>(S);
+    b.add<int32_t>(S);
+    ck(cudaStreamSynchronize(s->m->stream), "prefill ws sync");
+    w.arena.reserve(b.bytes);
+    w.x_t = w.arena.take<float>(HID * T);
+    w.hn_t = w.arena.take<float>(HID * T);
+    w.zx = w.arena.take<float>(T * DIP_PAD);
+    w.xbc = w.arena.take<float>(T * DXBC);
+    w.y_t = w.arena.take<float>(DI * T);
+    w.yn_t = w.arena.take<float>(DI * T);
+    w.qkv = w.arena.take<float>(T * QKV);
+    w.ao_t = w.arena.take<float>(HID * T);
+    w.mlp_t = w.arena.take<float>(INTER * T);
+    w.tok = w.arena.take<uint32_t>(T);
+    w.row_seq = w.arena.take<int32_t>(T);
+    w.cu = w.arena.take<int32_t>(S + 1);
+    w.start = w.arena.take<int32_t>(S);
+    w.last = w.arena.take<int32_t>(S);
+    w.dst = w.arena.take<int32_t>(S);
+    ck(cudaMemsetAsync(w.arena.base, 0, w.arena.cap, s->m->stream), "prefill ws memset");
+    w.cap_tokens = T;
+    w.cap_seqs = S;
+}
+
+inline void kk(cudaError_t e, const char* what) { ck(e, what); }
+
+// Zeroes the padding columns [valid, ld) of a feature-major [rows][ld] buffer.
+void zero_pad_cols(float* buf, int64_t ld, int64_t valid, int rows, cudaStream_t st) {
+    if (valid >= ld) return;
+    kk(cudaMemset2DAsync(buf + valid, ld * 4, 0, (ld - valid) * 4, rows, st), "memset2d");
+}
+
+// ------------------------------------------------------------------ forward
+// Final norm + tied LM head on the decode buffers (src/model.rs:620-621).
+void lm_head(krk_state* s) {
+    const krk_model* m = s->m;
+    cudaStream_t st = m->stream;
+    const int Mp = (int)s->Mp;
+    kk(krk::rmsnorm_fm(s->h_t, Mp, m->lnf, RMS_EPS, HID, s->B, s->hn_t, Mp, st), "lnf");
+    kk(krk::gemm(s->hn_t, Mp, m->wte_t, VOC, s->logits, VOC, Mp, VOC, HID, krk::EPI_STORE, false, st), "lm head");
+}
+
+// One decode step for all sequences: tokens in tok_d, positions in pos_d
+// (src/model.rs:586-624).  Does not advance positions.
+void decode_forward(krk_state* s, const uint8_t* active) {
+    const krk_model* m = s->m;
+    cudaStream_t st = m->stream;
+    const int B = s->B, Mp = (int)s->Mp;
+    kk(krk::embed_fm(s->tok_d, m->wte, VOC, HID, B, s->h_t, Mp, st), "embed");
+    for (int l = 0; l < NL; ++l) {
+        const LayerW& L = m->L[l];
+        if (is_mamba(l)) {  // src/model.rs:626-702
+            kk(krk::rmsnorm_fm(s->h_t, Mp, L.ln, RMS_EPS, HID, B, s->hn_t, Mp, st), "ln");
+            kk(krk::gemm(s->hn_t, Mp, L.in_t, DIP_PAD, s->zx, DIP_PAD, Mp, DIP_PAD, HID, krk::EPI_STORE, false, st),
+               "in_proj");
+            kk(krk::conv_step4(s->zx + OFF_X, DIP_PAD, s->conv[l], L.conv_w, L.conv_b, B, DXBC, active, st), "conv");
+            krk::SsdStepArgs a{};
+            a.x = s->zx + OFF_X; a.x_sb = DIP_PAD;
+            a.bm = s->zx + OFF_B; a.cm = s->zx + OFF_C; a.bc_sb = DIP_PAD;
+            a.dt = s->zx + OFF_DT; a.dt_sb = DIP_PAD;
+            a.z = s->zx + OFF_Z; a.z_sb = DIP_PAD;
+            a.ssm = s->ssm[l];
+            a.dt_bias = L.dt_bias; a.a_neg = L.a_neg; a.dsk = L.dsk;
+            a.y = s->y_t; a.y_sb = 1; a.y_sc = Mp;
+            a.active = active;
+            a.B = B; a.H = MH; a.P = MP; a.N = DS;
+            kk(krk::ssd_step(a, false, st), "ssd step");
+            kk(krk::rmsnorm_fm(s->y_t, Mp, L.norm_w, MNORM_EPS, DI, B, s->yn_t, Mp, st), "gated norm");
+            kk(krk::gemm(s->yn_t, Mp, L.out_t, HID, s->h_t, Mp, Mp, HID, DI, krk::EPI_RESIDUAL, true, st), "out_proj");
+        } else {  // src/model.rs:704-783
+            kk(krk::rmsnorm_fm(s->h_t, Mp, L.ln1, RMS_EPS, HID, B, s->hn_t, Mp, st), "ln1");
+            kk(krk::gemm(s->hn_t, Mp, L.qkv_t, QKV, s->qkv, QKV, Mp, QKV, HID, krk::EPI_STORE, false, st), "wqkv");
+            krk::AttnDecodeArgs a{};
+            a.q = s->qkv; a.k = s->qkv + HID; a.v = s->qkv + 2 * HID; a.in_sb = QKV; a.in_sh = HD;
+            a.kc = s->kc[l]; a.vc = s->vc[l]; a.c_sb = (int64_t)s->ctx * HID; a.c_sh = HD; a.c_st = HID;
+            a.pos = s->pos_d; a.active = active;
+            a.out = s->ao_t; a.o_sb = 1; a.o_sh = (int64_t)HD * Mp; a.o_sd = Mp;
+            a.work = s->attn_work;
+            a.B = B; a.H = NH; a.dh = HD; a.ctx = s->ctx; a.split = s->attn_split; a.theta = THETA;
+            kk(krk::attn_decode(a, st), "attention");
+            kk(krk::gemm(s->ao_t, Mp, L.wo_t, HID, s->h_t, Mp, Mp, HID, HID, krk::EPI_RESIDUAL, true, st), "wo");
+            kk(krk::rmsnorm_fm(s->h_t, Mp, L.ln2, RMS_EPS, HID, B, s->hn_t, Mp, st), "ln2");
+            kk(krk::gemm(s->hn_t, Mp, L.fc1_t, INTER, s->mlp_t, Mp, Mp, INTER, HID, krk::EPI_GELU, true, st), "fc1");
+            kk(krk::gemm(s->mlp_t, Mp, L.fc2_t, HID, s->h_t, Mp, Mp, HID, INTER, krk::EPI_RESIDUAL, true, st), "fc2");
+        }
+    }
+    lm_head(s);
+}
+
+// Prefill of sequences [g0, g0+S) whose packed tokens are already in pre.tok etc.
+void prefill_group(krk_state* s, int g0, int S, int64_t rows) {
+    const krk_model* m = s->m;
+    cudaStream_t st = m->stream;
+    PrefillWs& w = s->pre;
+    const int T = (int)round_up(rows, 64);
+    const int R = (int)rows;
+    zero_pad_cols(w.x_t, T, R, HID, st);
+    zero_pad_cols(w.hn_t, T, R, HID, st);
+    zero_pad_cols(w.y_t, T, R, DI, st);
+    zero_pad_cols(w.yn_t, T, R, DI, st);
+    zero_pad_cols(w.ao_t, T, R, HID, st);
+    kk(krk::embed_fm(w.tok, m->wte, VOC, HID, R, w.x_t, T, st), "embed");
+    for (int l = 0; l < NL; ++l) {
+        const LayerW& L = m->L[l];
+        if (is_mamba(l)) {  // src/model.rs:370-464
+            kk(krk::rmsnorm_fm(w.x_t, T, L.ln, RMS_EPS, HID, R, w.hn_t, T, st), "ln");
+            kk(krk::gemm(w.hn_t, T, L.in_t, DIP_PAD, w.zx, DIP_PAD, T, DIP_PAD, HID, krk::EPI_STORE, false, st),
+               "in_proj");
+            kk(krk::conv_prefill4(w.zx + OFF_X, DIP_PAD, w.xbc, DXBC, s->conv[l] + (size_t)g0 * DXBC * 4, L.conv_w,
+                                  L.conv_b, w.cu, S, DXBC, st),
+               "conv");
+            krk::SsdScanArgs a{};
+            a.x = w.xbc; a.x_rs = DXBC;
+            a.bm = w.xbc + DI; a.cm = w.xbc + DI + DS; a.bc_rs = DXBC;
+            a.dt = w.zx + OFF_DT; a.dt_rs = DIP_PAD;
+            a.z = w.zx + OFF_Z; a.z_rs = DIP_PAD;
+            a.ssm = s->ssm[l] + (size_t)g0 * MH * MP * DS;
+            a.dt_bias = L.dt_bias; a.a_neg = L.a_neg; a.dsk = L.dsk;
+            a.y = w.y_t; a.y_rs = 1; a.y_cs = T;
+            a.cu_seqlens = w.cu;
+            a.S = S; a.H = MH; a.P = MP; a.N = DS;
+            kk(krk::ssd_scan(a, false, st), "ssd scan");
+            kk(krk::rmsnorm_fm(w.y_t, T, L.norm_w, MNORM_EPS, DI, R, w.yn_t, T, st), "gated norm");
+            kk(krk::gemm(w.yn_t, T, L.out_t, HID, w.x_t, T, T, HID, DI, krk::EPI_RESIDUAL, true, st), "out_proj");
+        } else {  // src/model.rs:466-583
+            kk(krk::rmsnorm_fm(w.x_t, T, L.ln1, RMS_EPS, HID, R, w.hn_t, T, st), "ln1");
+            kk(krk::gemm(w.hn_t, T, L.qkv_t, QKV, w.qkv, QKV, T, QKV, HID, krk::EPI_STORE, false, st), "wqkv");
+            float* kc = s->kc[l] + (size_t)g0 * s->ctx * HID;
+            float* vc = s->vc[l] + (size_t)g0 * s->ctx * HID;
+            const int64_t c_sb = (int64_t)s->ctx * HID;
+            kk(krk::rope_kv_prefill(w.qkv, QKV, kc, vc, c_sb, HD, HID, w.cu, w.start, S, NH, HD, R, THETA, st),
+               "rope/kv");
+            kk(krk::attn_prefill(w.qkv, QKV, kc, vc, c_sb, HD, HID, w.cu, w.start, w.row_seq, S, NH, HD, R, s->ctx,
+                                 w.ao_t, 1, T, st),
+               "attention");
+            kk(krk::gemm(w.ao_t, T, L.wo_t, HID, w.x_t, T, T, HID, HID, krk::EPI_RESIDUAL, true, st), "wo");
+            kk(krk::rmsnorm_fm(w.x_t, T, L.ln2, RMS_EPS, HID, R, w.hn_t, T, st), "ln2");
+            kk(krk::gemm(w.hn_t, T, L.fc1_t, INTER, w.mlp_t, T, T, INTER, HID, krk::EPI_GELU, true, st), "fc1");
+            kk(krk::gemm(w.mlp_t, T, L.fc2_t, HID, w.x_t, T, T, HID, INTER, krk::EPI_RESIDUAL, true, st), "fc2");
+        }
+    }
+    // last token of each sequence -> decode residual buffer column g0 + s
+    kk(krk::gather_cols(w.x_t, T, w.last, s->h_t, (int)s->Mp, w.dst, HID, S, st), "gather last");
+}
+
+// Validates and runs a batched prefill; on return the decode buffers hold the
+// logits of each sequence's last token.  mark: record prompt tokens in the
+// repetition-penalty bitmaps.
+int run_prefill(krk_state* s, const uint32_t* tokens, const int32_t* lens, bool mark) {
+    const int B = s->B;
+    if (!lens) return fail(KRK_INVALID, "null lens");
+    int64_t total = 0;
+    for (int b = 0; b < B; ++b) {
+        if (lens[b] <= 0) return fail(KRK_EMPTY, "Cannot prefill empty sequence");
+        total += lens[b];
+    }
+    if (!tokens) return fail(KRK_INVALID, "null tokens");
+    for (int b = 0; b < B; ++b)
+        if (s->pos_h[b] + lens[b] > s->ctx)
+            return fail(KRK_CONTEXT_OVERFLOW, "Sequence length " + std::to_string(s->pos_h[b] + lens[b]) +
+                                                  " exceeds context limit " + std::to_string(s->ctx));
+    for (int64_t i = 0; i < total; ++i)
+        if (tokens[i] >= (uint32_t)VOC)
+            return fail(KRK_BAD_TOKEN,
+                        "Token ID " + std::to_string(tokens[i]) + " exceeds vocab size " + std::to_string(VOC));
+    cudaStream_t st = s->m->stream;
+    int64_t off = 0;
+    int g0 = 0;
+    while (g0 < B) {
+        int g1 = g0;
+        int64_t rows = 0;
+        while (g1 < B && (g1 == g0 || rows + lens[g1] <= PREFILL_GROUP_TOKENS)) rows += lens[g1++];
+        const int S = g1 - g0;
+        ensure_prefill_ws(s, rows, S);
+        PrefillWs& w = s->pre;
+        std::vector<int32_t> cu(S + 1), start(S), last(S), dst(S), row_seq(rows);
+        cu[0] = 0;
+        for (int i = 0; i < S; ++i) {
+            cu[i + 1] = cu[i] + lens[g0 + i];
+            start[i] = (int32_t)s->pos_h[g0 + i];
+            last[i] = cu[i + 1] - 1;
+            dst[i] = g0 + i;
+            for (int r = cu[i]; r < cu[i + 1]; ++r) row_seq[r] = i;
+        }
+        kk(cudaMemcpyAsync(w.tok, tokens + off, rows * 4, cudaMemcpyHostToDevice, st), "h2d tokens");
+        kk(cudaMemcpyAsync(w.cu, cu.data(), (S + 1) * 4, cudaMemcpyHostToDevice, st), "h2d cu");
+        kk(cudaMemcpyAsync(w.start, start.data(), S * 4, cudaMemcpyHostToDevice, st), "h2d start");
+        kk(cudaMemcpyAsync(w.last, last.data(), S * 4, cudaMemcpyHostToDevice, st), "h2d last");
+        kk(cudaMemcpyAsync(w.dst, dst.data(), S * 4, cudaMemcpyHostToDevice, st), "h2d dst");
+        kk(cudaMemcpyAsync(w.row_seq, row_seq.data(), rows * 4, cudaMemcpyHostToDevice, st), "h2d row_seq");
+        prefill_group(s, g0, S, rows);
+        if (mark)
+            kk(krk::mark_seen(w.tok, w.row_seq, (int)rows, s->seen_d + (size_t)g0 * SEEN_WORDS, SEEN_WORDS, st),
+               "mark seen");
+        kk(cudaStreamSynchronize(st), "prefill group");  // the host vectors above go out of scope
+        off += rows;
+        g0 = g1;
+    }
+    lm_head(s);
+    for (int b = 0; b < B; ++b) s->pos_h[b] += lens[b];
+    std::vector<int32_t> p32(s->pos_h.begin(), s->pos_h.end());
+    kk(cudaMemcpyAsync(s->pos_d, p32.data(), B * 4, cudaMemcpyHostToDevice, st), "h2d pos");
+    kk(cudaStreamSynchronize(st), "prefill");
+    return KRK_OK;
+}
+
+int copy_logits(krk_state* s, float* logits_out) {
+    if (!logits_out) return KRK_OK;
+    kk(cudaMemcpy2DAsync(logits_out, VOC * 4, s->logits, VOC * 4, VOC * 4, s->B, cudaMemcpyDeviceToHost,
+                         s->m->stream),
+       "d2h logits");
+    kk(cudaStreamSynchronize(s->m->stream), "d2h logits");
+    return KRK_OK;
+}
+
+template <typename F>
+int guarded(F&& f) {
+    try {
+        g_err.clear();
+        return f();
+    } catch (const KrkError& e) {
+        return fail(e.status, e.msg);
+    } catch (const std::bad_alloc&) {
+        return fail(KRK_CHECK_FAILED, "host out of memory");
+    } catch (const std::exception& e) {
+        return fail(KRK_CHECK_FAILED, e.what());
+    }
+}
+
+int cuda_status(cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return KRK_OK;
+    return fail(e == cudaErrorInvalidValue ? KRK_INVALID : KRK_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+int reset_state(krk_state* s, const uint8_t* mask) {
+    DeviceGuard g(s->m->device);
+    cudaStream_t st = s->m->stream;
+    for (int b = 0; b < s->B; ++b) {
+        if (mask && !mask[b]) continue;
+        s->pos_h[b] = 0;
+        for (int l = 0; l < NL; ++l) {
+            if (!is_mamba(l)) continue;  // attention reset only rewinds the length
+            kk(cudaMemsetAsync(s->conv[l] + (size_t)b * DXBC * 4, 0, (size_t)DXBC * 4 * 4, st), "reset conv");
+            kk(cudaMemsetAsync(s->ssm[l] + (size_t)b * MH * MP * DS, 0, (size_t)MH * MP * DS * 4, st), "reset ssm");
+        }
+        kk(cudaMemsetAsync(s->seen_d + (size_t)b * SEEN_WORDS, 0, SEEN_WORDS * 4, st), "reset seen");
+    }
+    std::vector<int32_t> p32(s->pos_h.begin(), s->pos_h.end());
+    kk(cudaMemcpyAsync(s->pos_d, p32.data(), s->B * 4, cudaMemcpyHostToDevice, st), "h2d pos");
+    kk(cudaStreamSynchronize(st), "reset");
+    return KRK_OK;
+}
+
+}  // namespace
+
+// =================================================================== C ABI
+extern "C" {
+
+const char* krk_last_error(void) { return g_err.c_str(); }
+
+const char* krk_status_string(int status) {
+    switch (status) {
+        case KRK_OK: return "ok";
+        case KRK_BAD_TOKEN: return "token id exceeds vocab size";
+        case KRK_CONTEXT_OVERFLOW: return "context limit exceeded";
+        case KRK_EMPTY: return "empty sequence";
+        case KRK_IO: return "i/o or format error";
+        case KRK_NOT_FOUND: return "tensor not found";
+        case KRK_INVALID: return "invalid argument";
+        case KRK_CUDA: return "cuda error";
+        case KRK_CHECK_FAILED: return "internal check failed";
+        default: return "unknown status";
+    }
+}
+
+int krk_abi_version(void) { return KRK_ABI_VERSION; }
+
+int krk_model_load(const char* path, int device, krk_model** out) {
+    return guarded([&]() -> int {
+        if (!path || !out) return fail(KRK_INVALID, "null path or output handle");
+        *out = nullptr;
+        std::unique_ptr<krk_model> m(new krk_model());
+        HostWeights hw;
+        read_weights(m.get(), path, hw);  // file and format errors come first, as in the reference
+        int ndev = 0;
+        cudaError_t e = cudaGetDeviceCount(&ndev);
+        if (e != cudaSuccess || ndev == 0)
+            return fail(KRK_CUDA, std::string("no CUDA device: ") + cudaGetErrorString(e));
+        if (device < 0 || device >= ndev) return fail(KRK_INVALID, "device index out of range");
+        DeviceGuard g(device);
+        m->device = device;
+        ck(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking), "stream create");
+        try {
+            upload_weights(m.get(), hw);
+        } catch (...) {
+            m->arena.release();
+            cudaStreamDestroy(m->stream);
+            throw;
+        }
+        *out = m.release();
+        return KRK_OK;
+    });
+}
+
+int krk_model_free(krk_model* m) {
+    if (!m) return KRK_OK;
+    return guarded([&]() -> int {
+        DeviceGuard g(m->device);
+        cudaStreamSynchronize(m->stream);
+        m->arena.release();
+        cudaStreamDestroy(m->stream);
+        delete m;
+        return KRK_OK;
+    });
+}
+
+int krk_model_device(const krk_model* m, int* device) {
+    if (!m || !device) return fail(KRK_INVALID, "null argument");
+    *device = m->device;
+    return KRK_OK;
+}
+
+int krk_model_stream(const krk_model* m, void** stream) {
+    if (!m || !stream) return fail(KRK_INVALID, "null argument");
+    *stream = (void*)m->stream;
+    return KRK_OK;
+}
+
+int krk_state_create(const krk_model* m, int batch, int max_ctx, krk_state** out) {
+    return guarded([&]() -> int {
+        if (!m || !out) return fail(KRK_INVALID, "null model or output handle");
+        if (batch <= 0 || max_ctx <= 0) return fail(KRK_INVALID, "batch and max_ctx must be positive");
+        *out = nullptr;
+        DeviceGuard g(m->device);
+        std::unique_ptr<krk_state> s(new krk_state());
+        create_state(s.get(), m, batch, max_ctx);
+        *out = s.release();
+        return KRK_OK;
+    });
+}
+
+int krk_state_free(krk_state* s) {
+    if (!s) return KRK_OK;
+    return guarded([&]() -> int {
+        DeviceGuard g(s->m->device);
+        cudaStreamSynchronize(s->m->stream);
+        s->pre.arena.release();
+        s->hist_arena.release();
+        s->arena.release();
+        delete s;
+        return KRK_OK;
+    });
+}
+
+int krk_state_reset(krk_state* s, const uint8_t* mask) {
+    return guarded([&]() -> int {
+        if (!s) return fail(KRK_INVALID, "null state");
+        return reset_state(s, mask);
+    });
+}
+
+int krk_state_batch(const krk_state* s, int* batch) {
+    if (!s || !batch) return fail(KRK_INVALID, "null argument");
+    *batch = s->B;
+    return KRK_OK;
+}
+
+int krk_state_context_limit(const krk_state* s, int* max_ctx) {
+    if (!s || !max_ctx) return fail(KRK_INVALID, "null argument");
+    *max_ctx = s->ctx;
+    return KRK_OK;
+}
+
+int krk_state_positions(const krk_state* s, int64_t* pos_out) {
+    if (!s || !pos_out) return fail(KRK_INVALID, "null argument");
+    for (int b = 0; b < s->B; ++b) pos_out[b] = s->pos_h[b];
+    return KRK_OK;
+}
+
+int krk_prefill(const krk_model* m, krk_state* s, const uint32_t* tokens, const int32_t* lens, float* logits_out) {
+    return guarded([&]() -> int {
+        if (!m || !s || s->m != m) return fail(KRK_INVALID, "null handle or state of another model");
+        DeviceGuard g(m->device);
+        int rc = run_prefill(s, tokens, lens, false);
+        if (rc) return rc;
+        return copy_logits(s, logits_out);
+    });
+}
+
+int krk_step(const krk_model* m, krk_state* s, const uint32_t* tokens, float* logits_out) {
+    return guarded([&]() -> int {
+        if (!m || !s || s->m != m) return fail(KRK_INVALID, "null handle or state of another model");
+        if (!tokens) return fail(KRK_INVALID, "null tokens");
+        for (int b = 0; b < s->B; ++b)
+            if (tokens[b] >= (uint32_t)VOC)
+                return fail(KRK_BAD_TOKEN,
+                            "Token ID " + std::to_string(tokens[b]) + " exceeds vocab size " + std::to_string(VOC));
+        for (int b = 0; b < s->B; ++b)
+            if (s->pos_h[b] >= s->ctx)
+                return fail(KRK_CONTEXT_OVERFLOW, "Context limit " + std::to_string(s->ctx) + " reached");
+        DeviceGuard g(m->device);
+        cudaStream_t st = m->stream;
+        kk(cudaMemcpyAsync(s->tok_d, tokens, s->B * 4, cudaMemcpyHostToDevice, st), "h2d tokens");
+        decode_forward(s, nullptr);
+        kk(krk::advance_pos(s->pos_d, nullptr, s->B, st), "advance");
+        for (int b = 0; b < s->B; ++b) s->pos_h[b] += 1;
+        if (logits_out) return copy_logits(s, logits_out);
+        kk(cudaStreamSynchronize(st), "step");
+        return KRK_OK;
+    });
+}
+
+int krk_generate_greedy(const krk_model* m, krk_state* s, const uint32_t* prompts, const int32_t* lens,
+                        int max_new_tokens, float repetition_penalty, int stop_at_eos, uint32_t* tokens_out,
+                        int32_t* n_out) {
+    return guarded([&]() -> int {
+        if (!m || !s || s->m != m) return fail(KRK_INVALID, "null handle or state of another model");
+        if (max_new_tokens <= 0 || !tokens_out || !n_out) return fail(KRK_INVALID, "bad output arguments");
+        DeviceGuard g(m->device);
+        cudaStream_t st = m->stream;
+        const int B = s->B;
+        // state.reset() (src/generate.rs:65)
+        int rc = reset_state(s, nullptr);
+        if (rc) return rc;
+        rc = run_prefill(s, prompts, lens, true);
+        if (rc) return rc;
+        // Tokens each sequence can emit: the loop pushes a token, then stops if
+        // current_pos >= context_limit (src/generate.rs:87-110).
+        std::vector<int32_t> limit(B);
+        int max_steps = 0;
+        for (int b = 0; b < B; ++b) {
+            limit[b] = (int32_t)std::min<int64_t>(max_new_tokens, (int64_t)s->ctx - lens[b] + 1);
+            max_steps = std::max(max_steps, limit[b]);
+        }
+        if ((int64_t)max_steps * B > s->hist_cap) {
+            s->hist_arena.reserve((size_t)max_steps * B * 4 + 256);
+            s->hist_d = s->hist_arena.take<uint32_t>((size_t)max_steps * B);
+            s->hist_cap = (int64_t)max_steps * B;
+        }
+        kk(cudaMemcpyAsync(s->limit_d, limit.data(), B * 4, cudaMemcpyHostToDevice, st), "h2d limit");
+        kk(cudaMemsetAsync(s->active_d, 1, B, st), "active");
+        kk(cudaMemsetAsync(s->step_d, 0, 4, st), "step");
+        kk(cudaMemsetAsync(s->hist_d, 0xff, (size_t)max_steps * B * 4, st), "hist");
+        krk::GreedyArgs ga{};
+        ga.logits = s->logits; ga.ld = VOC; ga.vocab = VOC; ga.B = B;
+        ga.seen = s->seen_d; ga.penalty = repetition_penalty;
+        ga.tok = s->tok_d; ga.active = s->active_d; ga.hist = s->hist_d; ga.step = s->step_d;
+        ga.limit = s->limit_d; ga.stop_eos = stop_at_eos; ga.eos = KRK_EOS_TOKEN;
+        ga.pos = nullptr;
+        // first token from the prefill logits (src/generate.rs:81-82)
+        kk(krk::greedy(ga, st), "greedy");
+        ga.pos = s->pos_d;
+        for (int i = 1; i < max_steps; ++i) {
+            decode_forward(s, s->active_d);
+            kk(krk::greedy(ga, st), "greedy");
+        }
+        std::vector<uint32_t> hist((size_t)max_steps * B);
+        std::vector<int32_t> pos(B);
+        kk(cudaMemcpyAsync(hist.data(), s->hist_d, hist.size() * 4, cudaMemcpyDeviceToHost, st), "d2h tokens");
+        kk(cudaMemcpyAsync(pos.data(), s->pos_d, B * 4, cudaMemcpyDeviceToHost, st), "d2h pos");
+        kk(cudaStreamSynchronize(st), "generate");
+        for (int b = 0; b < B; ++b) {
+            int n = 0;
+            for (int i = 0; i < limit[b]; ++i) {
+                uint32_t t = hist[(size_t)i * B + b];
+                if (t == 0xffffffffu || (stop_at_eos && t == (uint32_t)KRK_EOS_TOKEN)) break;
+                tokens_out[(size_t)b * max_new_tokens + n++] = t;
+            }
+            n_out[b] = n;
+            s->pos_h[b] = pos[b];
+        }
+        return KRK_OK;
+    });
+}
+
+int krk_state_export(const krk_state* s, int seq, int layer, int what, float* out, int64_t n) {
+    return guarded([&]() -> int {
+        if (!s || !out || seq < 0 || seq >= s->B || layer < 0 || layer >= NL)
+            return fail(KRK_INVALID, "bad export arguments");
+        const float* src = nullptr;
+        int64_t cnt = 0;
+        if (is_mamba(layer) && what == 0) {
+            src = s->conv[layer] + (size_t)seq * DXBC * 4;
+            cnt = (int64_t)DXBC * 4;
+        } else if (is_mamba(layer) && what == 1) {
+            src = s->ssm[layer] + (size_t)seq * MH * MP * DS;
+            cnt = (int64_t)MH * MP * DS;
+        } else if (!is_mamba(layer) && what == 2) {
+            src = s->kc[layer] + (size_t)seq * s->ctx * HID;
+            cnt = (int64_t)s->ctx * HID;
+        } else if (!is_mamba(layer) && what == 3) {
+            src = s->vc[layer] + (size_t)seq * s->ctx * HID;
+            cnt = (int64_t)s->ctx * HID;
+        } else {
+            return fail(KRK_INVALID, "layer has no such state");
+        }
+        if (n < cnt) return fail(KRK_INVALID, "output buffer too small");
+        DeviceGuard g(s->m->device);
+        kk(cudaMemcpyAsync(out, src, cnt * 4, cudaMemcpyDeviceToHost, s->m->stream), "d2h state");
+        kk(cudaStreamSynchronize(s->m->stream), "export");
+        return KRK_OK;
+    });
+}
+
+int krk_launch_count(uint64_t* count) {
+    if (!count) return fail(KRK_INVALID, "null argument");
+    *count = krk::launch_count();
+    return KRK_OK;
+}
+
+// ------------------------------------------------------ per-kernel entry points
+int krk_k_rmsnorm_rows(const float* x, const float* w, float eps, int64_t rows, int dim, float* y, void* stream) {
+    return cuda_status(krk::rmsnorm_rows(x, w, eps, rows, dim, y, (cudaStream_t)stream), "rmsnorm_rows");
+}
+
+int krk_k_rmsnorm_fm(const float* x, int ldx, const float* w, float eps, int K, int M, float* out, int ldo,
+                     void* stream) {
+    return cuda_status(krk::rmsnorm_fm(x, ldx, w, eps, K, M, out, ldo, (cudaStream_t)stream), "rmsnorm_fm");
+}
+
+int krk_k_gated_rmsnorm_residual(const float* x, const float* z, const float* res, const float* w, float eps,
+                                 int64_t rows, int dim, float* y, void* stream) {
+    return cuda_status(krk::gated_rmsnorm_residual(x, z, res, w, eps, rows, dim, y, (cudaStream_t)stream),
+                       "gated_rmsnorm_residual");
+}
+
+int krk_k_gemm(const float* At, int lda, const float* Wt, int ldw, float* C, int ldc, int M, int N, int K,
+               int epilogue, int out_fm, void* stream) {
+    if (epilogue < 0 || epilogue > 2) return fail(KRK_INVALID, "epilogue must be 0, 1 or 2");
+    return cuda_status(krk::gemm(At, lda, Wt, ldw, C, ldc, M, N, K, epilogue, out_fm != 0, (cudaStream_t)stream),
+                       "gemm");
+}
+
+int krk_k_embed(const uint32_t* tok, const float* wte, int vocab, int K, int M, float* out, int ldo, void* stream) {
+    return cuda_status(krk::embed_fm(tok, wte, vocab, K, M, out, ldo, (cudaStream_t)stream), "embed");
+}
+
+int krk_k_pointwise(int op, const float* x, float* y, int64_t n, void* stream) {
+    return cuda_status(krk::pointwise(op, x, y, n, (cudaStream_t)stream), "pointwise");
+}
+
+int krk_k_conv_ssd_step(const float* x, const float* bm, const float* cm, const float* dt, float* conv_state,
+                        const float* conv_w, const float* conv_b, float* ssm, const float* dt_bias,
+                        const float* a_neg, const float* dsk, float* y, int B, int H, int P, int N, void* stream) {
+    if (P != 64 || N != 128) return fail(KRK_INVALID, "conv_ssd_step supports head dim 64 and d_state 128");
+    krk::SsdStepArgs a{};
+    a.x = x; a.x_sb = (int64_t)H * P;
+    a.bm = bm; a.cm = cm; a.bc_sb = N;
+    a.dt = dt; a.dt_sb = H;
+    a.conv_state = conv_state; a.conv_w = conv_w; a.conv_b = conv_b;
+    a.ssm = ssm; a.dt_bias = dt_bias; a.a_neg = a_neg; a.dsk = dsk;
+    a.y = y; a.y_sb = (int64_t)H * P; a.y_sc = 1;
+    a.B = B; a.H = H; a.P = P; a.N = N;
+    return cuda_status(krk::ssd_step(a, true, (cudaStream_t)stream), "conv_ssd_step");
+}
+
+int krk_k_conv_ssd_scan(const float* x, const float* bm, const float* cm, const float* dt, float* conv_state,
+                        const float* conv_w, const float* conv_b, float* ssm, const float* dt_bias,
+                        const float* a_neg, const float* dsk, float* y, int B, int T, int H, int P, int N,
+                        void* stream) {
+    if (P != 64 || N != 128) return fail(KRK_INVALID, "conv_ssd_scan supports head dim 64 and d_state 128");
+    if (T <= 0) return fail(KRK_INVALID, "T must be positive");
+    krk::SsdScanArgs a{};
+    a.x = x; a.x_rs = (int64_t)H * P;
+    a.bm = bm; a.cm = cm; a.bc_rs = N;
+    a.dt = dt; a.dt_rs = H;
+    a.conv_state = conv_state; a.conv_w = conv_w; a.conv_b = conv_b;
+    a.ssm = ssm; a.dt_bias = dt_bias; a.a_neg = a_neg; a.dsk = dsk;
+    a.y = y; a.y_rs = (int64_t)H * P; a.y_cs = 1;
+    a.cu_seqlens = nullptr; a.uniform_len = T;
+    a.S = B; a.H = H; a.P = P; a.N = N;
+    return cuda_status(krk::ssd_scan(a, true, (cudaStream_t)stream), "conv_ssd_scan");
+}
+
+size_t krk_attn_work_floats(int B, int H, int dh, int ctx, int split) {
+    if (split <= 0) split = 256;
+    if (B <= 0 || H <= 0 || dh <= 0 || ctx <= 0) return 0;
+    return krk::attn_decode_work_floats(B, H, dh, ctx, split);
+}
+
+int krk_k_rope_kv_attn_decode(const float* q, const float* k, const float* v, float* kc, float* vc,
+                              const int32_t* pos, float* out, float* work, int B, int H, int dh, int ctx,
+                              int split, float theta, void* stream) {
+    krk::AttnDecodeArgs a{};
+    a.q = q; a.k = k; a.v = v; a.in_sb = (int64_t)H * dh; a.in_sh = dh;
+    a.kc = kc; a.vc = vc; a.c_sb = (int64_t)H * ctx * dh; a.c_sh = (int64_t)ctx * dh; a.c_st = dh;
+    a.pos = pos; a.active = nullptr;
+    a.out = out; a.o_sb = (int64_t)H * dh; a.o_sh = dh; a.o_sd = 1;
+    a.work = work;
+    a.B = B; a.H = H; a.dh = dh; a.ctx = ctx; a.split = split <= 0 ? 256 : split; a.theta = theta;
+    return cuda_status(krk::attn_decode(a, (cudaStream_t)stream), "rope_kv_attn_decode");
+}
+
+int krk_k_greedy(const float* logits, int64_t ld, int vocab, int B, uint32_t* seen, float penalty, uint32_t* tok,
+                 void* stream) {
+    krk::GreedyArgs a{};
+    a.logits = logits; a.ld = ld; a.vocab = vocab; a.B = B; a.seen = seen; a.penalty = penalty; a.tok = tok;
+    return cuda_status(krk::greedy(a, (cudaStream_t)stream), "greedy");
+}
+
+}  // extern "C"

@@ -1,0 +1,56 @@
+// Shared device helpers for the krikil B200 kernels (fp32 throughout).
+//
+// Every kernel in this library is compiled with --fmad=false, so a*b+c is a
+// rounded multiply followed by a rounded add, exactly as the reference's Rust
+// code evaluates it; fused multiply-adds appear only where written as fmaf().
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#define KRK_DEV __device__ __forceinline__
+
+namespace krk {
+
+// src/math.rs:3-6
+KRK_DEV float silu(float x) { return x / (1.0f + expf(-x)); }
+
+// src/math.rs:8-15
+KRK_DEV float softplus(float x) { return x > 20.0f ? x : logf(1.0f + expf(x)); }
+
+// src/math.rs:23-39: erf by Abramowitz & Stegun formula 7.1.26 (the published
+// five-term polynomial in t = 1/(1+p|x|) times exp(-x^2)).
+KRK_DEV float as_erf(float x) {
+    const float a1 = 0.254829592f, a2 = -0.284496736f, a3 = 1.421413741f;
+    const float a4 = -1.453152027f, a5 = 1.061405429f, p = 0.3275911f;
+    float sign = x < 0.0f ? -1.0f : 1.0f;
+    float ax = fabsf(x);
+    float t = 1.0f / (1.0f + p * ax);
+    float poly = ((((a5 * t + a4) * t) + a3) * t + a2) * t + a1;
+    return sign * (1.0f - poly * t * expf(-ax * ax));
+}
+
+// src/math.rs:17-21 (FRAC_1_SQRT_2 as an f32 constant)
+KRK_DEV float gelu(float x) { return 0.5f * x * (1.0f + as_erf(x * 0.70710678118654752f)); }
+
+KRK_DEV float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+KRK_DEV float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// 16-byte global->shared asynchronous copy (bypasses L1).
+KRK_DEV void cp_async16(void* smem, const void* gmem) {
+    unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem));
+}
+KRK_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+KRK_DEV void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
+
+}  // namespace krk

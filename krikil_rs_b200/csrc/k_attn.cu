@@ -1,0 +1,392 @@
+// Attention kernels: RoPE + KV-cache append + single-query softmax attention
+// for decode (split over the cache like flash-decoding), and RoPE/append plus
+// causal attention for prefill (fp32).
+#include "common.cuh"
+#include "kernels.h"
+
+namespace krk {
+namespace {
+
+// src/math.rs:70-124: the reference dot product (8 FMA lanes, fixed fold,
+// unfused scalar tail).  a and b are 16-byte aligned shared or global rows.
+KRK_DEV float dot_ref(const float* a, const float* b, int len) {
+    float l0 = 0.f, l1 = 0.f, l2 = 0.f, l3 = 0.f, l4 = 0.f, l5 = 0.f, l6 = 0.f, l7 = 0.f;
+    const int chunks = len >> 3;
+    for (int c = 0; c < chunks; ++c) {
+        const float4 a0 = *reinterpret_cast<const float4*>(a + 8 * c);
+        const float4 a1 = *reinterpret_cast<const float4*>(a + 8 * c + 4);
+        const float4 b0 = *reinterpret_cast<const float4*>(b + 8 * c);
+        const float4 b1 = *reinterpret_cast<const float4*>(b + 8 * c + 4);
+        l0 = fmaf(a0.x, b0.x, l0); l1 = fmaf(a0.y, b0.y, l1);
+        l2 = fmaf(a0.z, b0.z, l2); l3 = fmaf(a0.w, b0.w, l3);
+        l4 = fmaf(a1.x, b1.x, l4); l5 = fmaf(a1.y, b1.y, l5);
+        l6 = fmaf(a1.z, b1.z, l6); l7 = fmaf(a1.w, b1.w, l7);
+    }
+    float r = ((l0 + l4) + (l2 + l6)) + ((l1 + l5) + (l3 + l7));
+    for (int i = chunks * 8; i < len; ++i) r = r + a[i] * b[i];
+    return r;
+}
+
+// src/math.rs:243-257: rotate-half on the pair (i, i + dh/2) at position pos.
+KRK_DEV void rope_pair(float& x0, float& x1, float c, float s) {
+    const float a = x0, b = x1;
+    x0 = a * c - b * s;
+    x1 = a * s + b * c;
+}
+KRK_DEV void rope_cs(int i, int dh, int pos, float theta, float& c, float& s) {
+    const float invf = 1.0f / powf(theta, ((float)i * 2.0f) / (float)dh);
+    const float ang = (float)pos * invf;
+    c = cosf(ang);
+    s = sinf(ang);
+}
+
+constexpr int AD_THREADS = 128;
+constexpr int AD_TILE = 128;
+constexpr int AD_RED = 512;
+
+template <int DH>
+struct AdLayout {
+    static constexpr int DH4 = DH / 4;
+    static constexpr int KLD = (DH4 & 1) ? DH : DH + 4;  // odd float4 stride: conflict-free row reads
+    static constexpr int G = AD_THREADS / DH4;           // key groups in the PV phase
+};
+
+template <int DH>
+size_t ad_smem_bytes(int split) {
+    return sizeof(float) * (3 * DH + AD_RED + split + AD_TILE * AdLayout<DH>::KLD + 64);
+}
+
+KRK_DEV float block_reduce(float v, float* scratch, bool is_max) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    v = is_max ? warp_max(v) : warp_sum(v);
+    __syncthreads();
+    if (lane == 0) scratch[warp] = v;
+    __syncthreads();
+    float r = scratch[0];
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) r = is_max ? fmaxf(r, scratch[w]) : r + scratch[w];
+    return r;
+}
+
+template <int DH>
+__global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(AttnDecodeArgs a, int max_splits) {
+    using L = AdLayout<DH>;
+    constexpr int HALF = DH / 2;
+    extern __shared__ __align__(16) float sm[];
+    float* qs = sm;
+    float* kn = qs + DH;
+    float* vn = kn + DH;
+    float* red = vn + DH;
+    float* sc = red + AD_RED;
+    float* tile = sc + a.split;
+    float* scratch = tile + AD_TILE * L::KLD;
+
+    const int b = blockIdx.x, h = blockIdx.y, sp = blockIdx.z, tid = threadIdx.x;
+    if (a.active && !a.active[b]) return;
+    const int pos = a.pos[b];
+    if (pos < 0 || pos >= a.ctx) return;  // the host rejects these before launch
+    const int nkeys = pos + 1;
+    const int j0 = sp * a.split;
+    if (j0 >= nkeys) return;
+    const int j1 = min(nkeys, j0 + a.split);
+    const int nsplit = (nkeys + a.split - 1) / a.split;
+
+    const size_t in_off = (size_t)b * a.in_sb + (size_t)h * a.in_sh;
+    if (tid < DH) {
+        qs[tid] = a.q[in_off + tid];
+        kn[tid] = a.k[in_off + tid];
+        vn[tid] = a.v[in_off + tid];
+    }
+    __syncthreads();
+    if (tid < HALF) {  // src/model.rs:721-728
+        float c, s;
+        rope_cs(tid, DH, pos, a.theta, c, s);
+        rope_pair(qs[tid], qs[tid + HALF], c, s);
+        rope_pair(kn[tid], kn[tid + HALF], c, s);
+    }
+    __syncthreads();
+    const size_t cbase = (size_t)b * a.c_sb + (size_t)h * a.c_sh;
+    if (j1 == nkeys && tid < DH) {  // KV append (src/model.rs:730-733), done by the split holding slot pos
+        a.kc[cbase + (size_t)pos * a.c_st + tid] = kn[tid];
+        a.vc[cbase + (size_t)pos * a.c_st + tid] = vn[tid];
+    }
+
+    // scores (src/model.rs:742-748): dot(q_h, k_j) * (1/sqrt(dh))
+    const float scale = 1.0f / sqrtf((float)DH);
+    float mx = -INFINITY;
+    for (int t0 = j0; t0 < j1; t0 += AD_TILE) {
+        const int nk = min(AD_TILE, j1 - t0);
+        for (int i = tid; i < nk * L::DH4; i += AD_THREADS) {
+            const int r = i / L::DH4, c4 = i % L::DH4;
+            float* dst = tile + r * L::KLD + c4 * 4;
+            const int j = t0 + r;
+            if (j == pos) *reinterpret_cast<float4*>(dst) = *reinterpret_cast<const float4*>(kn + c4 * 4);
+            else cp_async16(dst, a.kc + cbase + (size_t)j * a.c_st + c4 * 4);
+        }
+        cp_async_commit();
+        cp_async_wait<0>();
+        __syncthreads();
+        if (tid < nk) {
+            const float sv = dot_ref(qs, tile + tid * L::KLD, DH) * scale;
+            sc[t0 - j0 + tid] = sv;
+            mx = fmaxf(mx, sv);
+        }
+        __syncthreads();
+    }
+    // softmax over this split (src/math.rs:213-232)
+    const float m = block_reduce(mx, scratch, true);
+    const int n = j1 - j0;
+    float lsum = 0.0f;
+    for (int j = tid; j < n; j += AD_THREADS) {
+        const float e = expf(sc[j] - m);
+        sc[j] = e;
+        lsum += e;
+    }
+    const float l = block_reduce(lsum, scratch, false);
+    if (nsplit == 1) {
+        const float inv = 1.0f / l;
+        for (int j = tid; j < n; j += AD_THREADS) sc[j] = sc[j] * inv;
+    }
+    __syncthreads();
+
+    // out += w_j * v_j (src/model.rs:752-759)
+    const int g = tid / L::DH4, d4 = tid % L::DH4;
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int t0 = j0; t0 < j1; t0 += AD_TILE) {
+        const int nk = min(AD_TILE, j1 - t0);
+        for (int i = tid; i < nk * L::DH4; i += AD_THREADS) {
+            const int r = i / L::DH4, c4 = i % L::DH4;
+            float* dst = tile + r * L::KLD + c4 * 4;
+            const int j = t0 + r;
+            if (j == pos) *reinterpret_cast<float4*>(dst) = *reinterpret_cast<const float4*>(vn + c4 * 4);
+            else cp_async16(dst, a.vc + cbase + (size_t)j * a.c_st + c4 * 4);
+        }
+        cp_async_commit();
+        cp_async_wait<0>();
+        __syncthreads();
+        if (g < L::G) {
+            for (int r = g; r < nk; r += L::G) {
+                const float w = sc[t0 - j0 + r];
+                const float4 vv = *reinterpret_cast<const float4*>(tile + r * L::KLD + d4 * 4);
+                o.x = o.x + w * vv.x;
+                o.y = o.y + w * vv.y;
+                o.z = o.z + w * vv.z;
+                o.w = o.w + w * vv.w;
+            }
+        }
+        __syncthreads();
+    }
+    if (g < L::G) *reinterpret_cast<float4*>(red + g * DH + d4 * 4) = o;
+    __syncthreads();
+    if (tid < DH) {
+        float acc = red[tid];
+        for (int gg = 1; gg < L::G; ++gg) acc = acc + red[gg * DH + tid];
+        if (nsplit == 1) {
+            a.out[(size_t)b * a.o_sb + (size_t)h * a.o_sh + (size_t)tid * a.o_sd] = acc;
+        } else {
+            float* wp = a.work + (((size_t)b * a.H + h) * max_splits + sp) * (DH + 2);
+            wp[tid] = acc;
+            if (tid == 0) {
+                wp[DH] = m;
+                wp[DH + 1] = l;
+            }
+        }
+    }
+}
+
+// Merges the per-split (max, sum, unnormalised out) partials of one (b, h).
+__global__ void attn_combine_kernel(AttnDecodeArgs a, int max_splits) {
+    const int b = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
+    if (a.active && !a.active[b]) return;
+    const int pos = a.pos[b];
+    if (pos < 0 || pos >= a.ctx) return;
+    const int nsplit = (pos + a.split) / a.split;
+    if (nsplit <= 1 || d >= a.dh) return;
+    const float* wp = a.work + ((size_t)b * a.H + h) * max_splits * (a.dh + 2);
+    float m = -INFINITY;
+    for (int c = 0; c < nsplit; ++c) m = fmaxf(m, wp[c * (a.dh + 2) + a.dh]);
+    float l = 0.0f, o = 0.0f;
+    for (int c = 0; c < nsplit; ++c) {
+        const float* p = wp + c * (a.dh + 2);
+        const float e = expf(p[a.dh] - m);
+        l = l + p[a.dh + 1] * e;
+        o = o + p[d] * e;
+    }
+    a.out[(size_t)b * a.o_sb + (size_t)h * a.o_sh + (size_t)d * a.o_sd] = o * (1.0f / l);
+}
+
+// ---------------------------------------------------------------------------
+// Prefill: RoPE on q (in place) and k, append k and v to the cache
+// (src/model.rs:489-511).  One thread per (row, head, pair i < dh/2).
+// ---------------------------------------------------------------------------
+__global__ void rope_kv_prefill_kernel(float* __restrict__ qkv, int64_t q_rs, float* __restrict__ kc,
+                                       float* __restrict__ vc, int64_t c_sb, int64_t c_sh, int64_t c_st,
+                                       const int32_t* __restrict__ cu, const int32_t* __restrict__ start, int S,
+                                       int H, int dh, int total_rows, float theta) {
+    const int half = dh / 2;
+    const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (gid >= (int64_t)total_rows * H * half) return;
+    const int i = (int)(gid % half);
+    const int h = (int)((gid / half) % H);
+    const int row = (int)(gid / ((int64_t)half * H));
+    int lo = 0, hi = S;  // sequence of this row: cu[s] <= row < cu[s+1]
+    while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (cu[mid] <= row) lo = mid; else hi = mid;
+    }
+    const int sq = lo;
+    const int pos = start[sq] + (row - cu[sq]);
+    float c, s;
+    rope_cs(i, dh, pos, theta, c, s);
+    float* qr = qkv + (size_t)row * q_rs + (size_t)h * dh;
+    float* kr = qkv + (size_t)row * q_rs + (size_t)H * dh + (size_t)h * dh;
+    const float* vr = qkv + (size_t)row * q_rs + (size_t)2 * H * dh + (size_t)h * dh;
+    rope_pair(qr[i], qr[i + half], c, s);
+    float k0 = kr[i], k1 = kr[i + half];
+    rope_pair(k0, k1, c, s);
+    const size_t cb = (size_t)sq * c_sb + (size_t)h * c_sh + (size_t)pos * c_st;
+    kc[cb + i] = k0;
+    kc[cb + i + half] = k1;
+    vc[cb + i] = vr[i];
+    vc[cb + i + half] = vr[i + half];
+}
+
+// Causal attention for packed prefill rows (src/model.rs:519-548): one warp per
+// (row, head).  Scores are full reference dots (lane per key); after the max
+// and the sum of exponentials, each lane owns output dims d = lane + 32i and
+// accumulates w_j * v_j[d] over j in order.
+template <int DH>
+__global__ void attn_prefill_kernel(const float* __restrict__ qkv, int64_t q_rs, const float* __restrict__ kc,
+                                    const float* __restrict__ vc, int64_t c_sb, int64_t c_sh, int64_t c_st,
+                                    const int32_t* __restrict__ cu, const int32_t* __restrict__ start,
+                                    const int32_t* __restrict__ row_seq, int H, int total_rows, int ctx,
+                                    float* __restrict__ out, int64_t o_rs, int64_t o_cs) {
+    constexpr int ND = (DH + 31) / 32;
+    extern __shared__ __align__(16) float sm[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    float* qsh = sm + warp * DH;
+    float* sc = sm + nw * DH + (size_t)warp * ctx;
+    const int row = blockIdx.x * nw + warp, h = blockIdx.y;
+    if (row >= total_rows) return;
+    const int sq = row_seq[row];
+    const int qpos = start[sq] + (row - cu[sq]);
+    const int nk = qpos + 1;
+    const float* qr = qkv + (size_t)row * q_rs + (size_t)h * DH;
+    for (int d = lane; d < DH; d += 32) qsh[d] = qr[d];
+    __syncwarp();
+    const float scale = 1.0f / sqrtf((float)DH);
+    const size_t cb = (size_t)sq * c_sb + (size_t)h * c_sh;
+    float mx = -INFINITY;
+    for (int j = lane; j < nk; j += 32) {
+        const float sv = dot_ref(qsh, kc + cb + (size_t)j * c_st, DH) * scale;
+        sc[j] = sv;
+        mx = fmaxf(mx, sv);
+    }
+    mx = warp_max(mx);
+    float ls = 0.0f;
+    for (int j = lane; j < nk; j += 32) {
+        const float e = expf(sc[j] - mx);
+        sc[j] = e;
+        ls += e;
+    }
+    ls = warp_sum(ls);
+    const float inv = 1.0f / ls;
+    __syncwarp();
+    float o[ND];
+#pragma unroll
+    for (int i = 0; i < ND; ++i) o[i] = 0.0f;
+    for (int j = 0; j < nk; ++j) {
+        const float w = sc[j] * inv;
+        const float* vr = vc + cb + (size_t)j * c_st;
+#pragma unroll
+        for (int i = 0; i < ND; ++i) {
+            const int d = lane + 32 * i;
+            if (d < DH) o[i] = o[i] + w * vr[d];
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < ND; ++i) {
+        const int d = lane + 32 * i;
+        if (d < DH) out[(size_t)row * o_rs + (size_t)(h * DH + d) * o_cs] = o[i];
+    }
+}
+
+}  // namespace
+
+size_t attn_decode_work_floats(int B, int H, int dh, int ctx, int split) {
+    const int ms = (ctx + split - 1) / split;
+    return (size_t)B * H * ms * (dh + 2);
+}
+
+cudaError_t attn_decode(const AttnDecodeArgs& a, cudaStream_t s) {
+    if (a.B <= 0 || a.H <= 0 || a.ctx <= 0 || a.split <= 0 || a.split % 64 || (a.dh != 64 && a.dh != 76) ||
+        (a.c_sb & 3) || (a.c_sh & 3) || (a.c_st & 3) || (((uintptr_t)a.kc | (uintptr_t)a.vc) & 15))
+        return cudaErrorInvalidValue;
+    const int max_splits = (a.ctx + a.split - 1) / a.split;
+    if (max_splits > 1 && !a.work) return cudaErrorInvalidValue;
+    dim3 grid(a.B, a.H, max_splits);
+    cudaError_t e;
+    if (a.dh == 76) {
+        static DeviceOnce once;
+        const size_t smem = ad_smem_bytes<76>(a.split);
+        if (smem > 227 * 1024) return cudaErrorInvalidValue;
+        if ((e = once.set_smem((const void*)attn_decode_kernel<76>, 227 * 1024)) != cudaSuccess) return e;
+        attn_decode_kernel<76><<<grid, AD_THREADS, smem, s>>>(a, max_splits);
+    } else {
+        static DeviceOnce once;
+        const size_t smem = ad_smem_bytes<64>(a.split);
+        if (smem > 227 * 1024) return cudaErrorInvalidValue;
+        if ((e = once.set_smem((const void*)attn_decode_kernel<64>, 227 * 1024)) != cudaSuccess) return e;
+        attn_decode_kernel<64><<<grid, AD_THREADS, smem, s>>>(a, max_splits);
+    }
+    add_launches(1);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    if (max_splits > 1) {
+        attn_combine_kernel<<<dim3(a.B, a.H), 128, 0, s>>>(a, max_splits);
+        add_launches(1);
+        e = cudaGetLastError();
+    }
+    return e;
+}
+
+cudaError_t rope_kv_prefill(float* qkv, int64_t q_rs, float* kc, float* vc, int64_t c_sb, int64_t c_sh,
+                            int64_t c_st, const int32_t* cu_seqlens, const int32_t* start, int S, int H, int dh,
+                            int total_rows, float theta, cudaStream_t s) {
+    if (S <= 0 || H <= 0 || dh <= 0 || (dh & 1) || total_rows <= 0) return cudaErrorInvalidValue;
+    const int64_t n = (int64_t)total_rows * H * (dh / 2);
+    rope_kv_prefill_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(qkv, q_rs, kc, vc, c_sb, c_sh, c_st,
+                                                                       cu_seqlens, start, S, H, dh, total_rows,
+                                                                       theta);
+    add_launches(1);
+    return cudaGetLastError();
+}
+
+cudaError_t attn_prefill(const float* qkv, int64_t q_rs, const float* kc, const float* vc, int64_t c_sb,
+                         int64_t c_sh, int64_t c_st, const int32_t* cu_seqlens, const int32_t* start,
+                         const int32_t* row_seq, int S, int H, int dh, int total_rows, int ctx, float* out,
+                         int64_t o_rs, int64_t o_cs, cudaStream_t s) {
+    (void)S;
+    if (H <= 0 || total_rows <= 0 || ctx <= 0 || (dh != 64 && dh != 76) || (q_rs & 3) || (c_st & 3) ||
+        (c_sh & 3) || (c_sb & 3) || (((uintptr_t)qkv | (uintptr_t)kc | (uintptr_t)vc) & 15))
+        return cudaErrorInvalidValue;
+    int nw = 8;
+    while (nw > 1 && (size_t)nw * (dh + ctx) * sizeof(float) > 200 * 1024) nw >>= 1;
+    const size_t smem = (size_t)nw * (dh + ctx) * sizeof(float);
+    if (smem > 227 * 1024) return cudaErrorInvalidValue;
+    dim3 grid((total_rows + nw - 1) / nw, H);
+    cudaError_t e;
+    if (dh == 76) {
+        static DeviceOnce once;
+        if ((e = once.set_smem((const void*)attn_prefill_kernel<76>, 227 * 1024)) != cudaSuccess) return e;
+        attn_prefill_kernel<76><<<grid, nw * 32, smem, s>>>(qkv, q_rs, kc, vc, c_sb, c_sh, c_st, cu_seqlens,
+                                                            start, row_seq, H, total_rows, ctx, out, o_rs, o_cs);
+    } else {
+        static DeviceOnce once;
+        if ((e = once.set_smem((const void*)attn_prefill_kernel<64>, 227 * 1024)) != cudaSuccess) return e;
+        attn_prefill_kernel<64><<<grid, nw * 32, smem, s>>>(qkv, q_rs, kc, vc, c_sb, c_sh, c_st, cu_seqlens,
+                                                            start, row_seq, H, total_rows, ctx, out, o_rs, o_cs);
+    }
+    add_launches(1);
+    return cudaGetLastError();
+}
+
+}  // namespace krk

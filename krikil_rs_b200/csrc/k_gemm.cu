@@ -1,0 +1,190 @@
+// fp32 projections C = A . W^T on the SIMT FP32 pipes, reproducing the
+// reference's dot-product rounding exactly.
+//
+// The reference computes every projection output as dot(W[r], x) with the AVX2
+// kernel of src/math.rs:89-124: eight lanes, lane j accumulating
+// a[j+8i]*b[j+8i] with a fused multiply-add in increasing i, folded as
+// ((l0+l4)+(l2+l6)) + ((l1+l5)+(l3+l7)).  (All K here are multiples of 8, so
+// its scalar tail is empty.)  This kernel maps those eight lanes onto the eight
+// warps of a CTA: warp w owns the k = w (mod 8) slice of every K-block and keeps
+// a full 64x32 output tile of partial sums in registers (8x8 per thread); the
+// eight warp tiles are folded in the reference's order through shared memory in
+// the epilogue.  The result is bit-identical to the reference gemv for any M.
+//
+// Operands: A feature-major (At[k][m], contiguous along m) and W K-major
+// (Wt[k][n], contiguous along n), so that every 32-row K-block of both is a
+// dense tile that cp.async moves straight into shared memory (3-stage pipeline)
+// and the inner loop reads 8 m and 8 n values with four 16-byte shared loads.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace krk {
+namespace {
+
+constexpr int BM = 64, BN = 32, BK = 32, NSTAGE = 3, NT = 256;
+constexpr int A_TILE = BK * BM;
+constexpr int W_TILE = BK * BN;
+constexpr int STAGE = A_TILE + W_TILE;
+constexpr int RLD_BM = BN + 4;  // partials red[w][m][n] for batch-major output
+constexpr int RLD_FM = BM + 4;  // partials red[w][n][m] for feature-major output
+constexpr int RED_FLOATS = 8 * BM * RLD_BM;
+constexpr int SMEM_FLOATS = RED_FLOATS > NSTAGE * STAGE ? RED_FLOATS : NSTAGE * STAGE;
+constexpr size_t SMEM_BYTES = SMEM_FLOATS * sizeof(float);
+
+KRK_DEV float4 f4add(float4 a, float4 b) { return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w); }
+
+// ((l0+l4)+(l2+l6)) + ((l1+l5)+(l3+l7)): the fold of src/math.rs:110-117.
+KRK_DEV float4 fold8(const float4* l) {
+    float4 s04 = f4add(l[0], l[4]), s15 = f4add(l[1], l[5]), s26 = f4add(l[2], l[6]), s37 = f4add(l[3], l[7]);
+    return f4add(f4add(s04, s26), f4add(s15, s37));
+}
+
+template <int EPI, bool OUT_FM>
+__global__ void __launch_bounds__(NT, 2)
+    gemm_lane8_kernel(const float* __restrict__ At, int lda, const float* __restrict__ Wt, int ldw,
+                      float* __restrict__ C, int ldc, int K) {
+    extern __shared__ __align__(16) float sm[];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int lm = lane >> 2, ln = lane & 3;
+    const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
+    const int nkb = K / BK;
+
+    auto load_stage = [&](int kb, int st) {
+        float* As = sm + st * STAGE;
+        float* Ws = As + A_TILE;
+        const int k0 = kb * BK;
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            int idx = tid + j * NT;
+            int r = idx >> 4, c4 = idx & 15;
+            cp_async16(As + r * BM + c4 * 4, At + (size_t)(k0 + r) * lda + m0 + c4 * 4);
+        }
+        int r = tid >> 3, c4 = tid & 7;
+        cp_async16(Ws + r * BN + c4 * 4, Wt + (size_t)(k0 + r) * ldw + n0 + c4 * 4);
+    };
+
+    // Thread (lm, ln) owns m in {lm*4+i, 32+lm*4+i} and n in {ln*4+j, 16+ln*4+j}
+    // (i, j < 4), so each 16-byte shared load of a warp hits distinct banks.
+    float acc[8][8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
+
+#pragma unroll
+    for (int s = 0; s < NSTAGE - 1; ++s) {
+        if (s < nkb) load_stage(s, s);
+        cp_async_commit();
+    }
+    for (int kb = 0; kb < nkb; ++kb) {
+        cp_async_wait<NSTAGE - 2>();
+        __syncthreads();
+        const int pf = kb + NSTAGE - 1;
+        if (pf < nkb) load_stage(pf, pf % NSTAGE);
+        cp_async_commit();
+        const float* As = sm + (kb % NSTAGE) * STAGE;
+        const float* Ws = As + A_TILE;
+#pragma unroll
+        for (int i = 0; i < BK / 8; ++i) {
+            const int k = warp + 8 * i;  // this warp's lane of the reference dot
+            float4 a0 = *reinterpret_cast<const float4*>(As + k * BM + lm * 4);
+            float4 a1 = *reinterpret_cast<const float4*>(As + k * BM + 32 + lm * 4);
+            float4 w0 = *reinterpret_cast<const float4*>(Ws + k * BN + ln * 4);
+            float4 w1 = *reinterpret_cast<const float4*>(Ws + k * BN + 16 + ln * 4);
+            const float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+            const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+            for (int r = 0; r < 8; ++r)
+#pragma unroll
+                for (int c = 0; c < 8; ++c) acc[r][c] = fmaf(a[r], w[c], acc[r][c]);
+        }
+    }
+    cp_async_wait<0>();
+    __syncthreads();
+
+    // Spill the eight lane-partial tiles, laid out along the output's
+    // contiguous dimension.
+    float* red = sm;
+    if (!OUT_FM) {
+        float* base = red + warp * (BM * RLD_BM);
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+            const int m = (r < 4) ? lm * 4 + r : 32 + lm * 4 + (r - 4);
+            float* d = base + m * RLD_BM;
+            *reinterpret_cast<float4*>(d + ln * 4) = make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
+            *reinterpret_cast<float4*>(d + 16 + ln * 4) = make_float4(acc[r][4], acc[r][5], acc[r][6], acc[r][7]);
+        }
+    } else {
+        float* base = red + warp * (BN * RLD_FM);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            const int n = (c < 4) ? ln * 4 + c : 16 + ln * 4 + (c - 4);
+            float* d = base + n * RLD_FM;
+            *reinterpret_cast<float4*>(d + lm * 4) = make_float4(acc[0][c], acc[1][c], acc[2][c], acc[3][c]);
+            *reinterpret_cast<float4*>(d + 32 + lm * 4) = make_float4(acc[4][c], acc[5][c], acc[6][c], acc[7][c]);
+        }
+    }
+    __syncthreads();
+
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+        const int idx = tid + j * NT;
+        const float* part;
+        int wstride;
+        float* out;
+        if (!OUT_FM) {
+            const int m = idx >> 3, n4 = idx & 7;
+            part = red + m * RLD_BM + n4 * 4;
+            wstride = BM * RLD_BM;
+            out = C + (size_t)(m0 + m) * ldc + n0 + n4 * 4;
+        } else {
+            const int n = idx >> 4, m4 = idx & 15;
+            part = red + n * RLD_FM + m4 * 4;
+            wstride = BN * RLD_FM;
+            out = C + (size_t)(n0 + n) * ldc + m0 + m4 * 4;
+        }
+        float4 l[8];
+#pragma unroll
+        for (int w = 0; w < 8; ++w) l[w] = *reinterpret_cast<const float4*>(part + w * wstride);
+        float4 v = fold8(l);
+        if (EPI == EPI_RESIDUAL) {
+            float4 o = *reinterpret_cast<const float4*>(out);  // x += out (src/model.rs:699-701)
+            v = f4add(o, v);
+        } else if (EPI == EPI_GELU) {
+            v = make_float4(gelu(v.x), gelu(v.y), gelu(v.z), gelu(v.w));
+        }
+        *reinterpret_cast<float4*>(out) = v;
+    }
+}
+
+template <int EPI, bool OUT_FM>
+cudaError_t launch(const float* At, int lda, const float* Wt, int ldw, float* C, int ldc, int M, int N, int K,
+                   cudaStream_t s) {
+    static DeviceOnce once;
+    cudaError_t e = once.set_smem((const void*)gemm_lane8_kernel<EPI, OUT_FM>, SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    dim3 grid(M / BM, N / BN);
+    gemm_lane8_kernel<EPI, OUT_FM><<<grid, NT, SMEM_BYTES, s>>>(At, lda, Wt, ldw, C, ldc, K);
+    add_launches(1);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t gemm(const float* At, int lda, const float* Wt, int ldw, float* C, int ldc, int M, int N, int K,
+                 int epilogue, bool out_fm, cudaStream_t s) {
+    if (M <= 0 || N <= 0 || K <= 0 || M % BM || N % BN || K % BK || lda % 4 || ldw % 4 || ldc % 4 || lda < M ||
+        ldw < N || ldc < (out_fm ? M : N) || ((uintptr_t)At | (uintptr_t)Wt | (uintptr_t)C) % 16)
+        return cudaErrorInvalidValue;
+    switch (epilogue * 2 + (out_fm ? 1 : 0)) {
+        case EPI_STORE * 2 + 0: return launch<EPI_STORE, false>(At, lda, Wt, ldw, C, ldc, M, N, K, s);
+        case EPI_STORE * 2 + 1: return launch<EPI_STORE, true>(At, lda, Wt, ldw, C, ldc, M, N, K, s);
+        case EPI_RESIDUAL * 2 + 0: return launch<EPI_RESIDUAL, false>(At, lda, Wt, ldw, C, ldc, M, N, K, s);
+        case EPI_RESIDUAL * 2 + 1: return launch<EPI_RESIDUAL, true>(At, lda, Wt, ldw, C, ldc, M, N, K, s);
+        case EPI_GELU * 2 + 0: return launch<EPI_GELU, false>(At, lda, Wt, ldw, C, ldc, M, N, K, s);
+        case EPI_GELU * 2 + 1: return launch<EPI_GELU, true>(At, lda, Wt, ldw, C, ldc, M, N, K, s);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace krk

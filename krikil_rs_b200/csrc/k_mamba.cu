@@ -1,0 +1,339 @@
+// Mamba2 kernels: causal depthwise conv1d + SiLU, and the SSD state update as a
+// single decode step and as a prefill scan over packed sequences (fp32).
+//
+// SSD recurrence (src/model.rs:661-685, per token, head h, row p, state n):
+//   dt  = softplus(dt_raw[h] + dt_bias[h]);  dA = exp(dt * A[h])
+//   s[p][n] = s[p][n]*dA + B[n]*(x[p]*dt);  y[p] = sum_n s[p][n]*C[n] + D[h]*x[p]
+// followed by the gate y *= silu(z) (src/model.rs:688-690).
+#include "common.cuh"
+#include "kernels.h"
+
+namespace krk {
+namespace {
+
+constexpr int SSD_P = 64;   // Mamba head dim (src/model.rs:25)
+constexpr int SSD_N = 128;  // d_state (src/model.rs:22)
+
+// ---------------------------------------------------------------------------
+// Decode: one CTA per (sequence b, head h), 4 warps.  The head's 64x128 state
+// block (32 KB) is streamed once: each warp walks 16 rows p, a row being 32
+// lanes x float4 (one coalesced 512-byte load and store).  The state update
+// uses the reference's unfused rounding, so the new state is bit-identical to
+// the reference given the same x, B, dt; y[p] is a per-lane sequential sum of
+// four products followed by a warp tree.  CONV: the head's 64 x channels go
+// through the 4-tap causal conv + SiLU first, on a 3-slot state [B][H*P][3].
+// ---------------------------------------------------------------------------
+template <bool CONV>
+__global__ void __launch_bounds__(128) ssd_step_kernel(SsdStepArgs a) {
+    const int b = blockIdx.x, h = blockIdx.y;
+    if (a.active && !a.active[b]) return;
+    __shared__ float xs[SSD_P], gs[SSD_P];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int c0 = h * SSD_P;
+    if (tid < SSD_P) {
+        const int c = c0 + tid;
+        float xv;
+        if (CONV) {
+            float* cs = a.conv_state + ((size_t)b * a.H * SSD_P + c) * 3;
+            const float s0 = cs[0], s1 = cs[1], s2 = cs[2];
+            const float xr = a.x[(size_t)b * a.x_sb + c];
+            const float* w = a.conv_w + (size_t)c * 4;
+            const float val = s0 * w[0] + s1 * w[1] + s2 * w[2] + xr * w[3] + a.conv_b[c];
+            cs[0] = s1;
+            cs[1] = s2;
+            cs[2] = xr;
+            xv = silu(val);
+        } else {
+            xv = a.x[(size_t)b * a.x_sb + c];
+        }
+        xs[tid] = xv;
+        gs[tid] = a.z ? silu(a.z[(size_t)b * a.z_sb + c]) : 1.0f;
+    }
+    const float dtv = softplus(a.dt[(size_t)b * a.dt_sb + h] + a.dt_bias[h]);
+    const float dA = expf(dtv * a.a_neg[h]);
+    const float dsk = a.dsk[h];
+    const float4 B4 = *reinterpret_cast<const float4*>(a.bm + (size_t)b * a.bc_sb + lane * 4);
+    const float4 C4 = *reinterpret_cast<const float4*>(a.cm + (size_t)b * a.bc_sb + lane * 4);
+    __syncthreads();
+
+    float* st = a.ssm + ((size_t)b * a.H + h) * (SSD_P * SSD_N) + lane * 4;
+    const bool gate = a.z != nullptr;
+#pragma unroll
+    for (int r0 = 0; r0 < 16; r0 += 8) {
+        const int pbase = warp * 16 + r0;
+        float4 s[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) s[i] = __ldcs(reinterpret_cast<const float4*>(st + (pbase + i) * SSD_N));
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int p = pbase + i;
+            const float xp = xs[p];
+            const float xdt = xp * dtv;
+            float4 ns;
+            ns.x = s[i].x * dA + B4.x * xdt;
+            ns.y = s[i].y * dA + B4.y * xdt;
+            ns.z = s[i].z * dA + B4.z * xdt;
+            ns.w = s[i].w * dA + B4.w * xdt;
+            __stcs(reinterpret_cast<float4*>(st + p * SSD_N), ns);
+            float part = ns.x * C4.x;
+            part = part + ns.y * C4.y;
+            part = part + ns.z * C4.z;
+            part = part + ns.w * C4.w;
+            part = warp_sum(part);
+            if (lane == 0) {
+                float yv = part + dsk * xp;
+                if (gate) yv = yv * gs[p];
+                a.y[(size_t)b * a.y_sb + (size_t)(c0 + p) * a.y_sc] = yv;
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Decode conv on the model's shift-register state [B][C][4] (src/model.rs:643-654).
+// ---------------------------------------------------------------------------
+__global__ void conv_step4_kernel(float* __restrict__ xbc, int64_t x_sb, float* __restrict__ state,
+                                  const float* __restrict__ w, const float* __restrict__ bias, int B, int C,
+                                  const uint8_t* __restrict__ active) {
+    const int c = blockIdx.x * blockDim.x + threadIdx.x, b = blockIdx.y;
+    if (c >= C || (active && !active[b])) return;
+    float4* sp = reinterpret_cast<float4*>(state + ((size_t)b * C + c) * 4);
+    const float4 s = *sp;
+    float* xp = xbc + (size_t)b * x_sb + c;
+    const float x = *xp;
+    const float4 wv = *reinterpret_cast<const float4*>(w + (size_t)c * 4);
+    // after the shift the window is [s.y, s.z, s.w, x]
+    const float val = s.y * wv.x + s.z * wv.y + s.w * wv.z + x * wv.w + bias[c];
+    *sp = make_float4(s.y, s.z, s.w, x);
+    *xp = silu(val);
+}
+
+// ---------------------------------------------------------------------------
+// Prefill conv: one thread per (sequence, channel) walks the sequence's rows in
+// order with the 4-slot window in registers (src/model.rs:399-410).
+// ---------------------------------------------------------------------------
+__global__ void conv_prefill4_kernel(const float* __restrict__ xin, int64_t x_rs, float* __restrict__ xout,
+                                     int64_t o_rs, float* __restrict__ state, const float* __restrict__ w,
+                                     const float* __restrict__ bias, const int32_t* __restrict__ cu, int C) {
+    const int c = blockIdx.x * blockDim.x + threadIdx.x, sq = blockIdx.y;
+    if (c >= C) return;
+    const int r0 = cu[sq], r1 = cu[sq + 1];
+    float4* sp = reinterpret_cast<float4*>(state + ((size_t)sq * C + c) * 4);
+    float4 s = *sp;
+    const float4 wv = *reinterpret_cast<const float4*>(w + (size_t)c * 4);
+    const float bb = bias[c];
+    int r = r0;
+    for (; r + 4 <= r1; r += 4) {
+        float xv[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) xv[i] = xin[(size_t)(r + i) * x_rs + c];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            s = make_float4(s.y, s.z, s.w, xv[i]);
+            const float val = s.x * wv.x + s.y * wv.y + s.z * wv.z + s.w * wv.w + bb;
+            xout[(size_t)(r + i) * o_rs + c] = silu(val);
+        }
+    }
+    for (; r < r1; ++r) {
+        s = make_float4(s.y, s.z, s.w, xin[(size_t)r * x_rs + c]);
+        const float val = s.x * wv.x + s.y * wv.y + s.z * wv.z + s.w * wv.w + bb;
+        xout[(size_t)r * o_rs + c] = silu(val);
+    }
+    *sp = s;
+}
+
+// ---------------------------------------------------------------------------
+// Prefill scan: one CTA per (sequence, head), 256 threads; thread (p, q) keeps
+// state row p, columns n = 16j + 4q + e (j < 8, e < 4) in registers for the
+// whole sequence.  Tokens are staged CH at a time in shared memory (x, gate,
+// B, C, dt, dA); y of the chunk is buffered and written coalesced.  The state
+// update uses one FMA per element (s = fma(s, dA, B*xdt)) and y four partial
+// FMA chains, so results agree with the sequential reference within rounding.
+// CONV: conv + SiLU of the head's 64 x channels on a 3-slot state is applied
+// while staging, by threads 0..63, each owning one channel's window.
+// ---------------------------------------------------------------------------
+constexpr int SCAN_CH = 32;
+constexpr int SCAN_YLD = SCAN_CH + 1;
+constexpr size_t SCAN_SMEM =
+    sizeof(float) * (SCAN_CH * SSD_P * 2 + SCAN_CH * SSD_N * 2 + SCAN_CH * 2 + SSD_P * SCAN_YLD);
+
+template <bool CONV, bool GATE>
+__global__ void __launch_bounds__(256) ssd_scan_kernel(SsdScanArgs a) {
+    extern __shared__ __align__(16) float sm[];
+    float* sB = sm;                       // [CH][N]
+    float* sC = sB + SCAN_CH * SSD_N;     // [CH][N]
+    float* sx = sC + SCAN_CH * SSD_N;     // [CH][P]
+    float* sg = sx + SCAN_CH * SSD_P;     // [CH][P]
+    float* sdt = sg + SCAN_CH * SSD_P;    // [CH]
+    float* sda = sdt + SCAN_CH;           // [CH]
+    float* sy = sda + SCAN_CH;            // [P][CH+1]
+
+    const int sq = blockIdx.x, h = blockIdx.y;
+    const int tid = threadIdx.x, p = tid >> 2, q = tid & 3;
+    const int r0 = a.cu_seqlens ? a.cu_seqlens[sq] : sq * a.uniform_len;
+    const int r1 = a.cu_seqlens ? a.cu_seqlens[sq + 1] : (sq + 1) * a.uniform_len;
+    const float dtb = a.dt_bias[h], an = a.a_neg[h], dsk = a.dsk[h];
+    const int c0 = h * SSD_P;
+
+    float* st = a.ssm + (((size_t)sq * a.H + h) * SSD_P + p) * SSD_N + 4 * q;
+    float s[32];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        float4 v = *reinterpret_cast<const float4*>(st + 16 * j);
+        s[4 * j] = v.x; s[4 * j + 1] = v.y; s[4 * j + 2] = v.z; s[4 * j + 3] = v.w;
+    }
+    float cw0 = 0.f, cw1 = 0.f, cw2 = 0.f, cw3 = 0.f, cb = 0.f, w0 = 0.f, w1 = 0.f, w2 = 0.f;
+    float* cst = nullptr;
+    if (CONV && tid < SSD_P) {
+        const int c = c0 + tid;
+        cst = a.conv_state + ((size_t)sq * a.H * SSD_P + c) * 3;
+        w0 = cst[0]; w1 = cst[1]; w2 = cst[2];
+        cw0 = a.conv_w[c * 4]; cw1 = a.conv_w[c * 4 + 1]; cw2 = a.conv_w[c * 4 + 2]; cw3 = a.conv_w[c * 4 + 3];
+        cb = a.conv_b[c];
+    }
+
+    for (int base = r0; base < r1; base += SCAN_CH) {
+        const int nt = min(SCAN_CH, r1 - base);
+        __syncthreads();
+        for (int i = tid; i < nt * (SSD_N / 4); i += 256) {
+            const int t = i / (SSD_N / 4), c4 = i % (SSD_N / 4);
+            const size_t row = (size_t)(base + t);
+            *reinterpret_cast<float4*>(sB + t * SSD_N + c4 * 4) =
+                __ldg(reinterpret_cast<const float4*>(a.bm + row * a.bc_rs + c4 * 4));
+            *reinterpret_cast<float4*>(sC + t * SSD_N + c4 * 4) =
+                __ldg(reinterpret_cast<const float4*>(a.cm + row * a.bc_rs + c4 * 4));
+        }
+        for (int i = tid; i < nt * (SSD_P / 4); i += 256) {
+            const int t = i / (SSD_P / 4), c4 = i % (SSD_P / 4);
+            const size_t row = (size_t)(base + t);
+            *reinterpret_cast<float4*>(sx + t * SSD_P + c4 * 4) =
+                __ldg(reinterpret_cast<const float4*>(a.x + row * a.x_rs + c0 + c4 * 4));
+            if (GATE) {
+                float4 zv = __ldg(reinterpret_cast<const float4*>(a.z + row * a.z_rs + c0 + c4 * 4));
+                *reinterpret_cast<float4*>(sg + t * SSD_P + c4 * 4) =
+                    make_float4(silu(zv.x), silu(zv.y), silu(zv.z), silu(zv.w));
+            }
+        }
+        if (tid < nt) {
+            const float dtv = softplus(a.dt[(size_t)(base + tid) * a.dt_rs + h] + dtb);
+            sdt[tid] = dtv;
+            sda[tid] = expf(dtv * an);
+        }
+        __syncthreads();
+        if (CONV) {
+            if (tid < SSD_P) {
+                for (int t = 0; t < nt; ++t) {
+                    const float xr = sx[t * SSD_P + tid];
+                    const float val = w0 * cw0 + w1 * cw1 + w2 * cw2 + xr * cw3 + cb;
+                    w0 = w1; w1 = w2; w2 = xr;
+                    sx[t * SSD_P + tid] = silu(val);
+                }
+            }
+            __syncthreads();
+        }
+        for (int t = 0; t < nt; ++t) {
+            const float dA = sda[t];
+            const float xv = sx[t * SSD_P + p];
+            const float xdt = xv * sdt[t];
+            const float* Bt = sB + t * SSD_N + 4 * q;
+            const float* Ct = sC + t * SSD_N + 4 * q;
+            float y0 = 0.f, y1 = 0.f, y2 = 0.f, y3 = 0.f;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const float4 bv = *reinterpret_cast<const float4*>(Bt + 16 * j);
+                const float4 cv = *reinterpret_cast<const float4*>(Ct + 16 * j);
+                s[4 * j] = fmaf(s[4 * j], dA, bv.x * xdt);
+                s[4 * j + 1] = fmaf(s[4 * j + 1], dA, bv.y * xdt);
+                s[4 * j + 2] = fmaf(s[4 * j + 2], dA, bv.z * xdt);
+                s[4 * j + 3] = fmaf(s[4 * j + 3], dA, bv.w * xdt);
+                y0 = fmaf(s[4 * j], cv.x, y0);
+                y1 = fmaf(s[4 * j + 1], cv.y, y1);
+                y2 = fmaf(s[4 * j + 2], cv.z, y2);
+                y3 = fmaf(s[4 * j + 3], cv.w, y3);
+            }
+            float y = (y0 + y1) + (y2 + y3);
+            y += __shfl_xor_sync(0xffffffffu, y, 1);
+            y += __shfl_xor_sync(0xffffffffu, y, 2);
+            if (q == 0) {
+                float yv = y + dsk * xv;
+                if (GATE) yv = yv * sg[t * SSD_P + p];
+                sy[p * SCAN_YLD + t] = yv;
+            }
+        }
+        __syncthreads();
+        if (a.y_rs == 1) {  // feature-major output: each channel's rows are contiguous
+            for (int i = tid; i < SSD_P * nt; i += 256) {
+                const int pp = i / nt, t = i % nt;
+                a.y[(size_t)(base + t) + (size_t)(c0 + pp) * a.y_cs] = sy[pp * SCAN_YLD + t];
+            }
+        } else {
+            for (int i = tid; i < nt * SSD_P; i += 256) {
+                const int t = i / SSD_P, pp = i % SSD_P;
+                a.y[(size_t)(base + t) * a.y_rs + (size_t)(c0 + pp) * a.y_cs] = sy[pp * SCAN_YLD + t];
+            }
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+        *reinterpret_cast<float4*>(st + 16 * j) = make_float4(s[4 * j], s[4 * j + 1], s[4 * j + 2], s[4 * j + 3]);
+    if (CONV && tid < SSD_P) {
+        cst[0] = w0; cst[1] = w1; cst[2] = w2;
+    }
+}
+
+}  // namespace
+
+cudaError_t ssd_step(const SsdStepArgs& a, bool conv, cudaStream_t s) {
+    if (a.P != SSD_P || a.N != SSD_N || a.B <= 0 || a.H <= 0 || (a.bc_sb & 3) ||
+        (((uintptr_t)a.bm | (uintptr_t)a.cm | (uintptr_t)a.ssm) & 15))
+        return cudaErrorInvalidValue;
+    dim3 grid(a.B, a.H);
+    if (conv) ssd_step_kernel<true><<<grid, 128, 0, s>>>(a);
+    else ssd_step_kernel<false><<<grid, 128, 0, s>>>(a);
+    add_launches(1);
+    return cudaGetLastError();
+}
+
+cudaError_t conv_step4(float* xbc, int64_t x_sb, float* state, const float* w, const float* bias, int B, int C,
+                       const uint8_t* active, cudaStream_t s) {
+    if (B <= 0 || C <= 0 || (((uintptr_t)state | (uintptr_t)w) & 15)) return cudaErrorInvalidValue;
+    dim3 grid((C + 127) / 128, B);
+    conv_step4_kernel<<<grid, 128, 0, s>>>(xbc, x_sb, state, w, bias, B, C, active);
+    add_launches(1);
+    return cudaGetLastError();
+}
+
+cudaError_t conv_prefill4(const float* xin, int64_t x_rs, float* xout, int64_t o_rs, float* state, const float* w,
+                          const float* bias, const int32_t* cu_seqlens, int S, int C, cudaStream_t s) {
+    if (S <= 0 || C <= 0 || (((uintptr_t)state | (uintptr_t)w) & 15)) return cudaErrorInvalidValue;
+    dim3 grid((C + 127) / 128, S);
+    conv_prefill4_kernel<<<grid, 128, 0, s>>>(xin, x_rs, xout, o_rs, state, w, bias, cu_seqlens, C);
+    add_launches(1);
+    return cudaGetLastError();
+}
+
+cudaError_t ssd_scan(const SsdScanArgs& a, bool conv, cudaStream_t s) {
+    if (a.P != SSD_P || a.N != SSD_N || a.S <= 0 || a.H <= 0 || (a.bc_rs & 3) || (a.x_rs & 3) ||
+        (a.z && (a.z_rs & 3)) || (!a.cu_seqlens && a.uniform_len <= 0) ||
+        (((uintptr_t)a.bm | (uintptr_t)a.cm | (uintptr_t)a.ssm | (uintptr_t)a.x | (uintptr_t)a.z) & 15))
+        return cudaErrorInvalidValue;
+    dim3 grid(a.S, a.H);
+    cudaError_t e;
+#define KRK_SCAN(CV, GT)                                                                              \
+    {                                                                                                 \
+        static DeviceOnce once;                                                                       \
+        e = once.set_smem((const void*)ssd_scan_kernel<CV, GT>, SCAN_SMEM);                           \
+        if (e != cudaSuccess) return e;                                                               \
+        ssd_scan_kernel<CV, GT><<<grid, 256, SCAN_SMEM, s>>>(a);                                      \
+    }
+    if (conv) {
+        if (a.z) KRK_SCAN(true, true) else KRK_SCAN(true, false)
+    } else {
+        if (a.z) KRK_SCAN(false, true) else KRK_SCAN(false, false)
+    }
+#undef KRK_SCAN
+    add_launches(1);
+    return cudaGetLastError();
+}
+
+}  // namespace krk

@@ -1,0 +1,142 @@
+// Host-side launchers of the krikil B200 kernels (internal C++ interface; the
+// public boundary is the C ABI in include/krikil_cuda.h).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace krk {
+
+// Number of kernels this library has launched in this process (graph replays
+// count every kernel node of the graph).
+uint64_t launch_count();
+void add_launches(uint64_t n);
+
+// Raises a kernel's dynamic shared-memory limit once per device.
+struct DeviceOnce {
+    unsigned long long mask = 0;
+    cudaError_t set_smem(const void* func, size_t bytes);
+};
+
+// ---------------------------------------------------------------- projections
+// C = A . W^T in fp32 with the reference's dot-product order (see k_gemm.cu).
+//   At: A stored feature-major, At[k*lda + m]  (M columns, K rows)
+//   Wt: W stored K-major,       Wt[k*ldw + n]
+//   out_fm=false: C[m*ldc + n];  out_fm=true: C[n*ldc + m]
+// M % 64 == 0, N % 32 == 0, K % 32 == 0; leading dims % 4 == 0; 16-B aligned.
+enum GemmEpilogue { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_GELU = 2 };
+cudaError_t gemm(const float* At, int lda, const float* Wt, int ldw, float* C, int ldc, int M, int N, int K,
+                 int epilogue, bool out_fm, cudaStream_t s);
+
+// ---------------------------------------------------------------- norms
+// out[k*ldo+m] = x[k*ldx+m] * scale(m) * w[k], scale from the sequential sum of
+// squares over k (src/math.rs:41-54) -- feature-major activations.
+cudaError_t rmsnorm_fm(const float* x, int ldx, const float* w, float eps, int K, int M, float* out, int ldo,
+                       cudaStream_t s);
+// Row-major RMSNorm over [rows, dim].
+cudaError_t rmsnorm_rows(const float* x, const float* w, float eps, int64_t rows, int dim, float* y, cudaStream_t s);
+// y = rmsnorm(x * silu(z)) * w + res over [rows, dim] (dim % 128 == 0, dim <= 1024).
+cudaError_t gated_rmsnorm_residual(const float* x, const float* z, const float* res, const float* w, float eps,
+                                   int64_t rows, int dim, float* y, cudaStream_t s);
+// Embedding gather into feature-major out[k*ldo + m] = wte[tok[m]*K + k]
+// (ids >= vocab, which the host rejects beforehand, gather zeros).
+cudaError_t embed_fm(const uint32_t* tok, const float* wte, int vocab, int K, int M, float* out, int ldo,
+                     cudaStream_t s);
+// Elementwise silu / softplus / gelu (op 0/1/2) for unit tests.
+cudaError_t pointwise(int op, const float* x, float* y, int64_t n, cudaStream_t s);
+
+// ---------------------------------------------------------------- Mamba2
+struct SsdStepArgs {
+    const float* x; int64_t x_sb;            // x(b,c) = x[b*x_sb + c], c < H*P (raw if conv, else activated)
+    const float* bm; const float* cm; int64_t bc_sb;  // B(b,n), C(b,n)
+    const float* dt; int64_t dt_sb;          // dt_raw(b,h)
+    const float* z; int64_t z_sb;            // gate input z(b,c) or nullptr
+    float* conv_state;                       // conv on x channels only: [B][H*P][3]
+    const float* conv_w; const float* conv_b;  // [H*P][4], [H*P]
+    float* ssm;                              // [B][H][P][N]
+    const float* dt_bias; const float* a_neg; const float* dsk;  // [H]
+    float* y; int64_t y_sb; int64_t y_sc;    // y(b,c) = y[b*y_sb + c*y_sc]
+    const uint8_t* active;                   // [B] or nullptr: inactive sequences are left untouched
+    int B, H, P, N;
+};
+cudaError_t ssd_step(const SsdStepArgs& a, bool conv, cudaStream_t s);
+
+// Decode conv on the model's 4-slot shift-register state (src/model.rs:643-654):
+// xbc(b,c) (in place, raw -> silu(conv)), state [B][C][4].
+cudaError_t conv_step4(float* xbc, int64_t x_sb, float* state, const float* w, const float* bias, int B, int C,
+                       const uint8_t* active, cudaStream_t s);
+
+// Prefill conv over packed sequences (rows cu[s]..cu[s+1]), 4-slot state [S][C][4].
+cudaError_t conv_prefill4(const float* xin, int64_t x_rs, float* xout, int64_t o_rs, float* state, const float* w,
+                          const float* bias, const int32_t* cu_seqlens, int S, int C, cudaStream_t s);
+
+struct SsdScanArgs {
+    const float* x; int64_t x_rs;            // x(row,c)
+    const float* bm; const float* cm; int64_t bc_rs;
+    const float* dt; int64_t dt_rs;
+    const float* z; int64_t z_rs;            // nullable
+    float* conv_state; const float* conv_w; const float* conv_b;  // conv on x channels: [S][H*P][3]
+    float* ssm;                              // [S][H][P][N]
+    const float* dt_bias; const float* a_neg; const float* dsk;
+    float* y; int64_t y_rs; int64_t y_cs;    // y(row,c) = y[row*y_rs + c*y_cs]
+    const int32_t* cu_seqlens;               // [S+1]; nullptr: sequence s is rows [s*uniform_len, (s+1)*uniform_len)
+    int uniform_len;
+    int S, H, P, N;
+};
+cudaError_t ssd_scan(const SsdScanArgs& a, bool conv, cudaStream_t s);
+
+// ---------------------------------------------------------------- attention
+// Decode: per sequence b and head h, RoPE on q and the new k at position pos[b],
+// append k,v at slot pos[b], softmax(q.K^T/sqrt(dh)).V over slots 0..pos[b].
+// Cache element (b,h,t,d) at cache[b*c_sb + h*c_sh + t*c_st + d].
+struct AttnDecodeArgs {
+    const float* q; const float* k; const float* v; int64_t in_sb; int64_t in_sh;  // (b,h,d) at b*in_sb + h*in_sh + d
+    float* kc; float* vc; int64_t c_sb; int64_t c_sh; int64_t c_st;
+    const int32_t* pos;                      // [B]
+    const uint8_t* active;                   // [B] or nullptr
+    float* out; int64_t o_sb; int64_t o_sh; int64_t o_sd;  // out(b,h,d)
+    float* work;                             // split partials: [B*H*max_splits*(dh+2)] floats
+    int B, H, dh, ctx, split;                // keys per split (multiple of 64)
+    float theta;
+};
+size_t attn_decode_work_floats(int B, int H, int dh, int ctx, int split);
+cudaError_t attn_decode(const AttnDecodeArgs& a, cudaStream_t s);
+
+// Prefill: RoPE q in place and k into the cache, v into the cache, for packed rows.
+// qkv(row) = qkv[row*q_rs + ...] with q | k | v of H*dh each; cache layout as above
+// with c_sb the per-sequence stride; start[s] = first position of sequence s.
+cudaError_t rope_kv_prefill(float* qkv, int64_t q_rs, float* kc, float* vc, int64_t c_sb, int64_t c_sh,
+                            int64_t c_st, const int32_t* cu_seqlens, const int32_t* start, int S, int H, int dh,
+                            int total_rows, float theta, cudaStream_t s);
+// Causal attention of packed query rows over their sequence's cache.
+cudaError_t attn_prefill(const float* qkv, int64_t q_rs, const float* kc, const float* vc, int64_t c_sb,
+                         int64_t c_sh, int64_t c_st, const int32_t* cu_seqlens, const int32_t* start,
+                         const int32_t* row_seq, int S, int H, int dh, int total_rows, int ctx, float* out,
+                         int64_t o_rs, int64_t o_cs, cudaStream_t s);
+
+// ---------------------------------------------------------------- sampling
+// Greedy choice per sequence (src/sampler.rs:50-80): repetition penalty on the
+// tokens whose bit is set in seen[b][vocab/32] (when penalty != 1), then the
+// first maximum.  Writes tok[b] and sets its seen bit.  Optional bookkeeping of
+// batched generation (any pointer may be null):
+//   hist[*step * B + b] = tok[b];  pos[b] += 1;
+//   limit/eos: active[b] = 0 once step+1 >= limit[b] or (stop_eos and tok == eos);
+//   step: the caller's step counter, incremented after use.
+struct GreedyArgs {
+    const float* logits; int64_t ld; int vocab; int B;
+    uint32_t* seen; float penalty;
+    uint32_t* tok;
+    uint8_t* active;
+    uint32_t* hist; int32_t* step; int32_t* pos; const int32_t* limit;
+    int stop_eos; uint32_t eos;
+};
+cudaError_t greedy(const GreedyArgs& a, cudaStream_t s);
+// Sets the seen bit of each packed row's token for its sequence.
+cudaError_t mark_seen(const uint32_t* tok, const int32_t* row_seq, int rows, uint32_t* seen, int words,
+                      cudaStream_t s);
+// pos[b] += 1 for active sequences.
+cudaError_t advance_pos(int32_t* pos, const uint8_t* active, int B, cudaStream_t s);
+// dst[k*ldd + dcol[j]] = src[k*lds + scol[j]] for j < n, k < K (feature-major column gather).
+cudaError_t gather_cols(const float* src, int lds, const int32_t* scol, float* dst, int ldd, const int32_t* dcol,
+                        int K, int n, cudaStream_t s);
+
+}  // namespace krk

@@ -1,0 +1,165 @@
+"""The CPU oracle against the reference's own known-answer tests and against an
+independent float64 model (no GPU)."""
+import json
+import os
+
+import numpy as np
+import pytest
+
+import oracle as O
+from tests.np_pebble import NpPebble
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+
+
+# ---- src/math.rs:266-297 ---------------------------------------------------
+def test_dot_product_known_answer():
+    a = np.array([1, 2, 3, 4, 5, 6, 7, 8, 9], np.float32)
+    b = np.array([2, 1, 0, -1, 3, 2, 1, 0, -2], np.float32)
+    assert abs(O.dot(a, b) - float((a * b).sum())) < 1e-5
+
+
+def test_rms_norm_known_answer():
+    out = O.rms_norm([1.0, 2.0, 3.0, 4.0], [1.0] * 4, 1e-6)
+    rstd = 1.0 / np.sqrt(np.float32(30.0 / 4.0) + np.float32(1e-6))
+    assert abs(out[0] - 1.0 * rstd) < 1e-5
+    assert abs(out[3] - 4.0 * rstd) < 1e-5
+
+
+def test_gelu_known_answer():
+    assert abs(O.gelu(0.0)) < 1e-5
+    assert abs(O.gelu(1.0) - 0.8413447) < 1e-4
+    assert abs(O.gelu(-1.0) - (-0.1586553)) < 1e-4
+
+
+# ---- src/sampler.rs:160-182 --------------------------------------------------
+def test_greedy_sampling_known_answer():
+    assert O.sample_greedy([1.0, 5.0, 3.0, 2.0], []) == 1
+
+
+def test_repetition_penalty_known_answer():
+    assert O.sample_greedy([1.0, 5.0, 3.0, 2.0], [1], penalty=3.0) == 2
+
+
+def test_greedy_first_max_and_nan():
+    assert O.sample_greedy([3.0, 7.0, 7.0, 1.0], []) == 1
+    assert O.sample_greedy([np.nan, 2.0, np.nan], []) == 1
+    assert O.sample_greedy([np.nan, np.nan], []) == 0
+    assert O.sample_greedy([-np.inf, -np.inf], []) == 0
+    # negative logits are multiplied by the penalty
+    assert O.sample_greedy([-1.0, -1.5], [0], penalty=2.0) == 1
+
+
+# ---- dot order: src/math.rs:89-124 -------------------------------------------
+def test_dot_close_to_float64():
+    rng = np.random.default_rng(3)
+    for n in (8, 9, 76, 608, 1216, 2432, 13):
+        a = rng.standard_normal(n).astype(np.float32)
+        b = rng.standard_normal(n).astype(np.float32)
+        ref = float(np.dot(a.astype(np.float64), b.astype(np.float64)))
+        assert abs(O.dot(a, b) - ref) < 1e-5 * max(1.0, float(np.abs(a * b).sum()))
+
+
+def test_gemv_rows_threading_invariant():
+    rng = np.random.default_rng(4)
+    w = rng.standard_normal((300, 608)).astype(np.float32)
+    x = rng.standard_normal(608).astype(np.float32)
+    out = O.gemv(w, x)
+    for r in (0, 63, 64, 299):
+        assert out[r] == O.dot(w[r], x)  # bitwise: each row is one dot
+
+
+# ---- full model vs independent float64 numpy ---------------------------------
+@pytest.mark.parametrize("perturb", [False, True])
+def test_oracle_model_matches_float64(perturb, synth_weights, synth_weights_perturbed):
+    w = synth_weights_perturbed if perturb else synth_weights
+    m = O.OracleModel(w)
+    st = O.OracleState(64)
+    ref = NpPebble(w, 64)
+    toks = [5, 1999, 17, 300, 42, 7]
+    lo = O.forward_prefill(m, st, toks)
+    lr = ref.prefill(toks)
+    np.testing.assert_allclose(lo, lr, atol=2e-5, rtol=1e-4)
+    for t in (11, 2047, 0):
+        np.testing.assert_allclose(O.forward_step(m, st, t), ref.step(t), atol=2e-5, rtol=1e-4)
+    assert st.current_pos == len(toks) + 3
+    np.testing.assert_allclose(st.ssm[0], ref.ssm[0], atol=1e-5, rtol=1e-4)
+    np.testing.assert_allclose(st.conv[4], ref.conv[4], atol=1e-6, rtol=1e-5)
+    np.testing.assert_allclose(st.kc[7][:9], ref.k[7][:9], atol=1e-5, rtol=1e-4)
+
+
+def test_prefill_then_prefill_equals_one_prefill(synth_weights):
+    """Prefill at a nonzero start (src/model.rs:495, :506) continues the sequence."""
+    m = O.OracleModel(synth_weights)
+    s1, s2 = O.OracleState(32), O.OracleState(32)
+    toks = [9, 8, 7, 6, 5, 4, 3]
+    a = O.forward_prefill(m, s1, toks)
+    O.forward_prefill(m, s2, toks[:3])
+    b = O.forward_prefill(m, s2, toks[3:])
+    np.testing.assert_allclose(a, b, atol=1e-5, rtol=1e-5)
+    assert s2.current_pos == 7 and s2.cur_len(3) == 7
+
+
+def test_oracle_errors(synth_weights):
+    m = O.OracleModel(synth_weights)
+    st = O.OracleState(4)
+    with pytest.raises(O.OracleError) as e:
+        O.forward_prefill(m, st, [])
+    assert e.value.code == O.EMPTY
+    with pytest.raises(O.OracleError) as e:
+        O.forward_prefill(m, st, [1, 2048])
+    assert e.value.code == O.BAD_TOKEN
+    assert st.current_pos == 0
+    with pytest.raises(O.OracleError) as e:
+        O.forward_prefill(m, st, [1, 2, 3, 4, 5])
+    assert e.value.code == O.CONTEXT_OVERFLOW
+    O.forward_prefill(m, st, [1, 2, 3, 4])
+    with pytest.raises(O.OracleError) as e:
+        O.forward_step(m, st, 1)
+    assert e.value.code == O.CONTEXT_OVERFLOW
+    with pytest.raises(O.OracleError) as e:
+        O.forward_step(m, st, 5000)
+    assert e.value.code == O.BAD_TOKEN
+    st.reset()
+    assert st.current_pos == 0 and not st.ssm[0].any()
+
+
+def test_generate_greedy_loop_semantics(synth_weights):
+    """src/generate.rs:86-110: count, context limit and determinism."""
+    m = O.OracleModel(synth_weights)
+    st = O.OracleState(16)
+    out, _ = O.generate_greedy(m, st, [3, 1, 4, 1, 5], 20, eos=None)
+    assert len(out) == 16 - 5 + 1  # stops once current_pos reaches the limit
+    st2 = O.OracleState(16)
+    out2, _ = O.generate_greedy(m, st2, [3, 1, 4, 1, 5], 20, eos=None)
+    assert out == out2
+
+
+# ---- golden fixtures of the reference ----------------------------------------
+def test_golden_fixtures_consistent():
+    with open(os.path.join(GOLDEN, "reference_prefill_logits.json")) as f:
+        pre = json.load(f)
+    with open(os.path.join(GOLDEN, "reference_step_logits.json")) as f:
+        stp = json.load(f)
+    assert len(pre["logits"]) == 2048 and len(stp["logits"]) == 2048
+    assert stp["tokens"] == pre["tokens"] + [stp["step_token"]]
+    assert int(np.argmax(pre["logits"])) == stp["step_token"] == 199  # greedy continuation
+    assert int(np.argmax(stp["logits"])) == 490
+
+
+@pytest.mark.skipif(not os.environ.get("KRIKIL_PEBBLE_WEIGHTS"), reason="real Pebble-25M checkpoint not available")
+def test_oracle_matches_reference_golden_logits():
+    """src/model.rs:791-932 with the real weights: max-abs < 1e-4, same argmax."""
+    from krikil_rs_b200 import synth
+    w = synth.load_safetensors(os.environ["KRIKIL_PEBBLE_WEIGHTS"])
+    m = O.OracleModel(w)
+    with open(os.path.join(GOLDEN, "reference_prefill_logits.json")) as f:
+        pre = json.load(f)
+    with open(os.path.join(GOLDEN, "reference_step_logits.json")) as f:
+        stp = json.load(f)
+    st = O.OracleState(2048)
+    lg = O.forward_prefill(m, st, pre["tokens"])
+    assert np.abs(lg - np.array(pre["logits"], np.float32)).max() < 1e-4
+    assert int(np.argmax(lg)) == int(np.argmax(pre["logits"]))
+    lg2 = O.forward_step(m, st, stp["step_token"])
+    assert np.abs(lg2 - np.array(stp["logits"], np.float32)).max() < 1e-4
