@@ -1,0 +1,403 @@
+#!/usr/bin/env python
+"""Benchmark: batched greedy decode of the Pebble-25M architecture on B200.
+
+Workload (one "step"): krk_generate_greedy over `--seqs` independent sequences
+per GPU -- prompts of 128 token ids ~U[0,2048) (numpy seed 1), 256 new tokens
+each with EOS ignored, context 2048 -- on random-init seed-0 weights (the real
+checkpoint is not distributed).  Throughput = generated tokens / time, summed
+over all ranks.  With N GPUs each rank runs its own disjoint slice of
+N*seqs sequences (no collectives on the data path; weak scaling).
+
+  value  device time of the generate calls (inputs already on the device)
+  e2e    the same calls timed end to end on the device clock, including the
+         pinned-host -> device prompt copy and the device -> host token read
+  kernels  per-kernel HBM throughput of the fused layer kernels at their
+         benchmark shapes (gated norm [16384,512], RoPE+KV+attention
+         [64,8,2048,64], conv+SSD step [256,16,64,128], conv+SSD scan T=2048)
+
+`--impl reference` times the CPU restatement of the reference path (the Rust
+crate cannot be built on these machines) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+HID, VOC, INTER, DIP, DI, QKV = 608, 2048, 2432, 2707, 1216, 1824
+MAMBA_LAYERS, ATTN_LAYERS = 6, 2
+SSD_STATE_FLOATS = 19 * 64 * 128
+METRIC = "decode tokens/s (batched greedy, Pebble-25M architecture, fp32)"
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--seqs", type=int, default=1024, help="sequences per GPU")
+    ap.add_argument("--prompt-len", type=int, default=128)
+    ap.add_argument("--new-tokens", type=int, default=256)
+    ap.add_argument("--ctx", type=int, default=2048)
+    ap.add_argument("--no-kernels", action="store_true", help="skip the per-kernel table")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
+    return ap.parse_args()
+
+
+# ----------------------------------------------------------------- peaks / clocks
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, dev: int):
+        self.dev, self.proc, self.lines = dev, None, []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.dev), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            p = [x.strip() for x in ln.split(",")]
+            if len(p) < 7:
+                continue
+            try:
+                sm.append(float(p[0]))
+                mx = float(p[1])
+            except ValueError:
+                continue
+            for n, v in zip(names, p[3:7]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------------- algorithmic work
+def gemm_flops_per_generate(b, prompt, steps):
+    per_tok = 2 * HID * (MAMBA_LAYERS * (DIP + HID * 2) + ATTN_LAYERS * (QKV + HID + 2 * INTER))
+    # in_proj + out_proj (608x1216 == 1216x608) per Mamba layer; wqkv, wo, fc1, fc2 per attention layer
+    lm = 2 * HID * VOC
+    return b * (prompt + steps) * per_tok + b * (steps + 1) * lm
+
+
+def ssd_step_bytes_per_launch(b):
+    # state read + write, x/z/B/C/dt reads, y write (fp32)
+    return b * 4 * (2 * SSD_STATE_FLOATS + DI + DI + 128 + 128 + 19 + DI)
+
+
+def attn_decode_bytes(b, prompt, steps):
+    # every decode step of both attention layers reads K and V rows 0..pos and
+    # writes the new k, v row; q read and out write are 2 more rows
+    rows = sum(p + 1 for p in range(prompt, prompt + steps))
+    return ATTN_LAYERS * b * 4 * HID * (2 * rows + 4 * steps)
+
+
+# ----------------------------------------------------------------- CPU baseline
+def cpu_baseline(args, budget_s: float):
+    """The oracle (CPU restatement of the reference path) on this host's cores:
+    whole sequences (prompt + new tokens, batch 1 as the reference runs) until
+    the time budget is used."""
+    import oracle as O
+    from krikil_rs_b200 import synth
+    threads = os.cpu_count() or 1
+    O.lib.orc_set_num_threads(threads)
+    model = O.OracleModel(synth.make_weights(0))
+    prompts = synth.decode_prompts(max(args.seqs, 64), args.prompt_len, seed=1)
+    new = args.new_tokens
+    t0 = time.perf_counter()
+    toks, nseq = 0, 0
+    while nseq == 0 or (time.perf_counter() - t0 < budget_s and nseq < len(prompts)):
+        out, _ = O.generate_greedy(model, O.OracleState(args.ctx), prompts[nseq].tolist(), new, eos=None)
+        toks += len(out)
+        nseq += 1
+    dt = time.perf_counter() - t0
+    return {"value": toks / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{nseq} sequence(s) x ({args.prompt_len}-token prompt + {new} greedy tokens), batch 1, "
+                      f"oracle C restatement (-O3 AVX2/FMA, OpenMP {threads} threads), {dt:.1f} s"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count() or 1))
+    budget = max(3.0, min(20.0, args.cpu_seconds))
+    for _ in range(args.warmup):
+        cpu_baseline(args, 0.0)
+    vals = [cpu_baseline(args, budget) for _ in range(args.steps)]
+    v = statistics.median(x["value"] for x in vals)
+    cb = dict(vals[0])
+    cb["value"] = v
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded prompts, random-init weights)",
+            "config": workload_config(args),
+            "cpu_baseline": cb,
+            "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "note": "the reference Rust crate cannot be built here (no cargo); its path is timed through the "
+                    "oracle's C restatement on the host cores"}
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(args):
+    return {"workload": "batched greedy decode of Pebble-25M (config.json dims), random-init seed 0",
+            "seqs_per_gpu": args.seqs, "prompt_len": args.prompt_len, "new_tokens": args.new_tokens,
+            "ctx": args.ctx, "eos": "ignored", "prompts": "U[0,2048) numpy seed 1",
+            "l2": "inputs larger than L2 (SSD state 3.8 GB + KV cache per GPU)"}
+
+
+# ----------------------------------------------------------------- per-kernel table
+def kernel_table(torch, peak):
+    from krikil_rs_b200 import kernels as K, synth
+    dev = torch.device("cuda")
+    res = {}
+
+    def timeit(fn, iters=10, warm=3):
+        for _ in range(warm):
+            fn()
+        torch.cuda.synchronize()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
+        for a, b in evs:
+            a.record()
+            fn()
+            b.record()
+        torch.cuda.synchronize()
+        return statistics.median(a.elapsed_time(b) for a, b in evs)
+
+    def put(name, nbytes, ms, extra=None):
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        res[name] = {"ms": round(ms, 4), "bytes": int(nbytes), "gbs": round(gbs, 1), "frac": round(gbs / peak, 3)}
+        if extra:
+            res[name].update(extra)
+
+    x, z, r, w = (torch.from_numpy(a).to(dev) for a in synth.fused_norm_inputs())
+    y = torch.empty_like(x)
+    put("gated_rmsnorm_residual[16384,512]", 4 * x.numel() * 4 + w.numel() * 4,
+        timeit(lambda: K.gated_rmsnorm_residual(x, z, r, w, 1e-5, y)))
+    del x, z, r, y
+
+    q, k, v, pos, kc, vc = synth.attn_decode_inputs()
+    q, k, v, kc, vc = (torch.from_numpy(a).to(dev) for a in (q, k, v, kc, vc))
+    posd = torch.from_numpy(pos).to(dev)
+    work = torch.empty(K.attn_work_floats(64, 8, 64, 2048, 256), device=dev)
+    out = torch.empty_like(q)
+    nb = int(sum((int(p) + 1) * 8 * 64 * 4 * 2 for p in pos) + 64 * 8 * 64 * 4 * 6)
+    put("rope_kv_attn_decode[64,8,2048,64]", nb,
+        timeit(lambda: K.rope_kv_attn_decode(q, k, v, kc, vc, posd, split=256, work=work, out=out)))
+    del kc, vc
+
+    xs, bm, cm, dt, cs, ssm = synth.conv_ssd_inputs(256, 1)
+    cw, cb, dtb, an, dsk = (torch.from_numpy(a).to(dev) for a in synth.conv_ssd_params())
+    xs, bm, cm, dt = (torch.from_numpy(np.ascontiguousarray(a[:, 0])).to(dev) for a in (xs, bm, cm, dt))
+    cs, ssm = torch.from_numpy(cs).to(dev), torch.from_numpy(ssm).to(dev)
+    ys = torch.empty((256, 1024), device=dev)
+    nb = 2 * ssm.numel() * 4 + 2 * cs.numel() * 4 + (xs.numel() + bm.numel() + cm.numel() + dt.numel()) * 4 + \
+        ys.numel() * 4
+    put("conv_ssd_step[256,16,64,128]", nb,
+        timeit(lambda: K.conv_ssd_step(xs, bm, cm, dt, cs, cw, cb, ssm, dtb, an, dsk, ys)))
+
+    T = 2048
+    xs, bm, cm, dt, cs0, ssm0 = synth.conv_ssd_inputs(256, T, seed=5, state_scale=0.0)
+    xs, bm, cm, dt = (torch.from_numpy(a).to(dev) for a in (xs, bm, cm, dt))
+    cs, ssm = torch.from_numpy(cs0).to(dev), torch.from_numpy(ssm0).to(dev)
+    yt = torch.empty((256, T, 1024), device=dev)
+    nb = (xs.numel() + yt.numel() + bm.numel() + cm.numel() + dt.numel()) * 4 + 2 * ssm.numel() * 4
+    ms = timeit(lambda: K.conv_ssd_scan(xs, bm, cm, dt, cs, cw, cb, ssm, dtb, an, dsk, yt), iters=3, warm=1)
+    flops = 256 * T * 16 * 64 * 128 * 5  # per state element per token: 2 mul + 1 add (update), mul + add (y)
+    fp32_peak = 148 * 128 * 2 * 1.965e9  # nominal FP32 SIMT FLOP/s (no measured figure exists)
+    put("conv_ssd_scan[256,2048,16,64,128]", nb, ms,
+        {"tflops": round(flops / (ms * 1e-3) / 1e12, 2), "fp32_frac_nominal": round(flops / (ms * 1e-3) / fp32_peak, 3)})
+    del xs, bm, cm, dt, yt
+    torch.cuda.empty_cache()
+    return res
+
+
+# ----------------------------------------------------------------- our arm
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+    torch.cuda.set_device(local)
+
+    from krikil_rs_b200 import PebbleModel, PebbleState, launch_count, synth
+    from krikil_rs_b200._lib import check, lib
+
+    peak, peak_kind = measured_peaks()
+    path = synth.weights_file(0)
+    model = PebbleModel.load_safetensors(path, device=local)
+    seqs, plen, new = args.seqs, args.prompt_len, args.new_tokens
+    prompts = synth.decode_prompts(world * seqs, plen, seed=1)[rank * seqs:(rank + 1) * seqs]
+    state = PebbleState(model, args.ctx, batch=seqs)
+
+    # pinned host buffers for the end-to-end calls
+    toks_h = torch.from_numpy(np.ascontiguousarray(prompts.reshape(-1).view(np.int32))).pin_memory()
+    lens_h = torch.full((seqs,), plen, dtype=torch.int32).pin_memory()
+    out_h = torch.zeros((seqs, new), dtype=torch.int32).pin_memory()
+    n_h = torch.zeros((seqs,), dtype=torch.int32).pin_memory()
+
+    def generate():
+        check(lib.krk_generate_greedy(model._h, state._h, toks_h.data_ptr(), lens_h.data_ptr(), new, 1.0, 0,
+                                      out_h.data_ptr(), n_h.data_ptr()))
+
+    for _ in range(args.warmup):
+        generate()
+    stream = torch.cuda.ExternalStream(model.stream)
+    state.profile(True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    l0 = launch_count()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    gen_tokens = 0
+    for _ in range(args.steps):
+        generate()
+        gen_tokens += int(n_h.sum())
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    launches = launch_count() - l0
+    clk = clocks.stop()
+    e2e_ms = ev0.elapsed_time(ev1)
+    prof = state.profile_read()
+    state.profile(False)
+    dev_ms = prof["device_total"][0]
+    if world > 1:
+        t = torch.tensor([e2e_ms, dev_ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms, dev_ms = float(t[0]), float(t[1])
+        g = torch.tensor([gen_tokens], dtype=torch.int64, device="cuda")
+        dist.all_reduce(g)
+        total_tokens = int(g[0])
+        dist.barrier()
+    else:
+        total_tokens = gen_tokens
+    expect = world * seqs * min(new, args.ctx - plen + 1) * args.steps
+    assert total_tokens == expect, (total_tokens, expect)
+
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return
+
+    steps_per_gen = min(new, args.ctx - plen)
+    # dominant HBM kernel: the decode SSD update
+    ssd_ms, ssd_n = prof["ssd_step"]
+    ssd_bytes = ssd_step_bytes_per_launch(seqs) * ssd_n
+    ssd_gbs = ssd_bytes / (ssd_ms * 1e-3) / 1e9
+    gemm_ms, gemm_n = prof["gemm"]
+    gemm_flops = gemm_flops_per_generate(seqs, plen, steps_per_gen) * args.steps
+    attn_ms, attn_n = prof["attn_decode"]
+    attn_bytes = attn_decode_bytes(seqs, plen, steps_per_gen) * args.steps
+    share = {k: round(v[0] / dev_ms, 4) for k, v in prof.items() if k != "device_total"}
+    fp32_tflops_nominal = 148 * 128 * 2 * 1.965e9 / 1e12  # 148 SMs x 128 FP32 lanes x FMA x 1965 MHz
+    gemm_tflops = gemm_flops / (gemm_ms * 1e-3) / 1e12 if gemm_ms else 0.0
+
+    line = {
+        "metric": METRIC,
+        "value": total_tokens / (dev_ms * 1e-3),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": dev_ms / args.steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded prompts, random-init weights)",
+        "config": dict(workload_config(args), parallelism=f"replicas x{world} (no collectives)"),
+        "e2e": {"value": total_tokens / (e2e_ms * 1e-3), "unit": "tokens/s",
+                "h2d_bytes_per_step": int(toks_h.numel() * 4 + lens_h.numel() * 4),
+                "d2h_bytes_per_step": int(out_h.numel() * 4 + n_h.numel() * 4 + seqs * 4),
+                "ms_per_step": e2e_ms / args.steps},
+        "roofline": {"kernel": "ssd_step (decode SSD update + gate)", "bound": "hbm",
+                     "achieved": round(ssd_gbs, 1), "peak": peak, "unit": "GB/s", "frac": round(ssd_gbs / peak, 3),
+                     "traffic": None, "peak_kind": peak_kind,
+                     "algorithmic_bytes_per_launch": ssd_step_bytes_per_launch(seqs),
+                     "launches": ssd_n, "avg_launch_us": round(ssd_ms * 1e3 / max(ssd_n, 1), 2)},
+        "roofline_gemm": {"kernel": "gemm_lane8 (fp32 SIMT projections)", "bound": "fp32",
+                          "achieved": round(gemm_tflops, 2), "unit": "TFLOP/s",
+                          "peak_nominal": round(fp32_tflops_nominal, 1),
+                          "frac_nominal": round(gemm_tflops / fp32_tflops_nominal, 3),
+                          "launches": gemm_n},
+        "roofline_attn": {"kernel": "attn_decode", "bound": "hbm",
+                          "achieved": round(attn_bytes / (attn_ms * 1e-3) / 1e9, 1) if attn_ms else None,
+                          "unit": "GB/s", "launches": attn_n},
+        "time_share": share,
+        "gpu_launches": launches,
+        "clocks": clk,
+    }
+    if not args.no_kernels:
+        line["kernels"] = kernel_table(torch, peak)
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(args, args.cpu_seconds)
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse_args()
+    if args.warmup < 3:
+        print("warning: fewer than 3 warm-up steps", file=sys.stderr)
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

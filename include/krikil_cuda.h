@@ -152,6 +152,28 @@ KRK_API int krk_state_export(const krk_state* state, int seq, int layer, int wha
  * kernel node). */
 KRK_API int krk_launch_count(uint64_t* count);
 
+/* Measurement hook (no reference counterpart; the reference only times whole
+ * calls, src/generate.rs:76-78, :116-122): with profiling on, every later
+ * prefill / step / generate call on this state brackets each kernel launch
+ * with CUDA events on the model stream and accumulates the device time per
+ * kernel class; KRK_PROF_DEVICE_TOTAL is the device time of whole calls, from
+ * after the inputs reach the device to before the outputs leave it.
+ * krk_state_profile resets the totals. */
+enum {
+    KRK_PROF_DEVICE_TOTAL = 0,
+    KRK_PROF_GEMM = 1,         /* projections */
+    KRK_PROF_SSD_STEP = 2,     /* decode SSD update + gate */
+    KRK_PROF_ATTN_DECODE = 3,  /* RoPE + KV append + decode attention (+ split combine) */
+    KRK_PROF_NORM = 4,         /* RMSNorm / gated RMSNorm */
+    KRK_PROF_CONV = 5,         /* causal conv1d + SiLU */
+    KRK_PROF_SSD_SCAN = 6,     /* prefill SSD scan */
+    KRK_PROF_ATTN_PREFILL = 7, /* prefill causal attention */
+    KRK_PROF_OTHER = 8,        /* embedding, RoPE prefill, sampling, bookkeeping */
+    KRK_PROF_CLASSES = 9
+};
+KRK_API int krk_state_profile(krk_state* state, int enable);
+KRK_API int krk_state_profile_read(const krk_state* state, int cls, double* total_ms, int64_t* launches);
+
 /* ------------------------------------------------------ per-kernel entry points
  * Device pointers, fp32, asynchronous on `stream`.  Each names the reference
  * code it computes. */

@@ -42,6 +42,8 @@ _SIGS = {
     "krk_generate_greedy": (_i32, [_vp, _vp, _vp, _vp, _i32, _f32, _i32, _vp, _vp]),
     "krk_state_export": (_i32, [_vp, _i32, _i32, _i32, _vp, _i64]),
     "krk_launch_count": (_i32, [C.POINTER(C.c_uint64)]),
+    "krk_state_profile": (_i32, [_vp, _i32]),
+    "krk_state_profile_read": (_i32, [_vp, _i32, C.POINTER(C.c_double), C.POINTER(_i64)]),
     "krk_k_rmsnorm_rows": (_i32, [_fp, _fp, _f32, _i64, _i32, _fp, _vp]),
     "krk_k_rmsnorm_fm": (_i32, [_fp, _i32, _fp, _f32, _i32, _i32, _fp, _i32, _vp]),
     "krk_k_gated_rmsnorm_residual": (_i32, [_fp, _fp, _fp, _fp, _f32, _i64, _i32, _fp, _vp]),
@@ -63,6 +65,10 @@ for _name, (_res, _args) in _SIGS.items():
 EXPORTED = tuple(_SIGS)
 
 OK, BAD_TOKEN, CONTEXT_OVERFLOW, EMPTY, IO, NOT_FOUND, INVALID, CUDA, CHECK_FAILED = range(9)
+
+# krk_state_profile_read classes
+PROF_CLASSES = ("device_total", "gemm", "ssd_step", "attn_decode", "norm", "conv", "ssd_scan", "attn_prefill",
+                "other")
 
 
 class KrikilError(RuntimeError):

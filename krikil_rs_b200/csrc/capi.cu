@@ -129,6 +129,45 @@ struct krk_model {
 
 namespace {
 
+// Per-kernel-class CUDA-event timing of a state's calls (krk_state_profile).
+struct Prof {
+    bool on = false;
+    bool total_open = false;
+    cudaEvent_t total_start = nullptr;
+    std::vector<cudaEvent_t> pool;
+    struct Pending {
+        int cls;
+        cudaEvent_t a, b;
+    };
+    std::vector<Pending> pending;
+    double ms[KRK_PROF_CLASSES] = {};
+    int64_t n[KRK_PROF_CLASSES] = {};
+    cudaEvent_t get() {
+        if (pool.empty()) {
+            cudaEvent_t e;
+            ck(cudaEventCreate(&e), "event create");
+            return e;
+        }
+        cudaEvent_t e = pool.back();
+        pool.pop_back();
+        return e;
+    }
+    void clear_events() {
+        for (auto& p : pending) {
+            pool.push_back(p.a);
+            pool.push_back(p.b);
+        }
+        pending.clear();
+        if (total_start) pool.push_back(total_start);
+        total_start = nullptr;
+        total_open = false;
+    }
+    ~Prof() {
+        clear_events();
+        for (auto e : pool) cudaEventDestroy(e);
+    }
+};
+
 struct PrefillWs {
     int64_t cap_tokens = 0;
     int cap_seqs = 0;
@@ -150,12 +189,14 @@ struct krk_state {
     uint8_t* active_d = nullptr;
     uint32_t* seen_d = nullptr;
     uint32_t* tok_d = nullptr;
-    int32_t* limit_d = nullptr;
+    int32_t* tlimit_d = nullptr;
+    int32_t* slimit_d = nullptr;
     int32_t* step_d = nullptr;
     float *h_t, *hn_t, *zx, *y_t, *yn_t, *qkv, *ao_t, *mlp_t, *logits, *attn_work;
     int attn_split = 2048;
     std::vector<int64_t> pos_h;
     PrefillWs pre;
+    Prof prof;
     Arena hist_arena;
     int64_t hist_cap = 0;
     uint32_t* hist_d = nullptr;
@@ -283,7 +324,7 @@ void create_state(krk_state* s, const krk_model* m, int B, int ctx) {
         }
     }
     b.add<int32_t>(B); b.add<uint8_t>(B); b.add<uint32_t>((size_t)B * SEEN_WORDS); b.add<uint32_t>(Mp);
-    b.add<int32_t>(B); b.add<int32_t>(1);
+    b.add<int32_t>(B); b.add<int32_t>(B); b.add<int32_t>(1);
     b.add<float>(HID * Mp); b.add<float>(HID * Mp); b.add<float>(Mp * DIP_PAD); b.add<float>(DI * Mp);
     b.add<float>(DI * Mp); b.add<float>(Mp * QKV); b.add<float>(HID * Mp); b.add<float>(INTER * Mp);
     b.add<float>(Mp * VOC); b.add<float>(work);
@@ -301,7 +342,8 @@ void create_state(krk_state* s, const krk_model* m, int B, int ctx) {
     s->active_d = s->arena.take<uint8_t>(B);
     s->seen_d = s->arena.take<uint32_t>((size_t)B * SEEN_WORDS);
     s->tok_d = s->arena.take<uint32_t>(Mp);
-    s->limit_d = s->arena.take<int32_t>(B);
+    s->tlimit_d = s->arena.take<int32_t>(B);
+    s->slimit_d = s->arena.take<int32_t>(B);
     s->step_d = s->arena.take<int32_t>(1);
     s->h_t = s->arena.take<float>(HID * Mp);
     s->hn_t = s->arena.take<float>(HID * Mp);
@@ -359,14 +401,59 @@ void zero_pad_cols(float* buf, int64_t ld, int64_t valid, int rows, cudaStream_t
     kk(cudaMemset2DAsync(buf + valid, ld * 4, 0, (ld - valid) * 4, rows, st), "memset2d");
 }
 
+// Records CUDA events around f() on the model stream when profiling is on.
+template <typename F>
+void timed(krk_state* s, int cls, F&& f) {
+    if (!s->prof.on) {
+        f();
+        return;
+    }
+    cudaStream_t st = s->m->stream;
+    cudaEvent_t a = s->prof.get(), b = s->prof.get();
+    kk(cudaEventRecord(a, st), "event");
+    f();
+    kk(cudaEventRecord(b, st), "event");
+    s->prof.pending.push_back({cls, a, b});
+}
+
+// Device-time bracket of a whole call: opened after the call's inputs reached
+// the device, closed before its outputs leave it.
+void total_begin(krk_state* s) {
+    if (!s->prof.on || s->prof.total_open) return;
+    s->prof.total_start = s->prof.get();
+    kk(cudaEventRecord(s->prof.total_start, s->m->stream), "event");
+    s->prof.total_open = true;
+}
+void total_end(krk_state* s) {
+    if (!s->prof.on || !s->prof.total_open) return;
+    cudaEvent_t b = s->prof.get();
+    kk(cudaEventRecord(b, s->m->stream), "event");
+    s->prof.pending.push_back({KRK_PROF_DEVICE_TOTAL, s->prof.total_start, b});
+    s->prof.total_start = nullptr;
+    s->prof.total_open = false;
+}
+// Called after the stream is synchronised: folds pending event pairs into totals.
+void prof_collect(krk_state* s) {
+    if (!s->prof.on) return;
+    for (auto& p : s->prof.pending) {
+        float ms = 0.0f;
+        kk(cudaEventElapsedTime(&ms, p.a, p.b), "event elapsed");
+        s->prof.ms[p.cls] += ms;
+        s->prof.n[p.cls] += 1;
+    }
+    s->prof.clear_events();
+}
+
 // ------------------------------------------------------------------ forward
 // Final norm + tied LM head on the decode buffers (src/model.rs:620-621).
 void lm_head(krk_state* s) {
     const krk_model* m = s->m;
     cudaStream_t st = m->stream;
     const int Mp = (int)s->Mp;
-    kk(krk::rmsnorm_fm(s->h_t, Mp, m->lnf, RMS_EPS, HID, s->B, s->hn_t, Mp, st), "lnf");
-    kk(krk::gemm(s->hn_t, Mp, m->wte_t, VOC, s->logits, VOC, Mp, VOC, HID, krk::EPI_STORE, false, st), "lm head");
+    timed(s, KRK_PROF_NORM, [&] { kk(krk::rmsnorm_fm(s->h_t, Mp, m->lnf, RMS_EPS, HID, s->B, s->hn_t, Mp, st), "lnf"); });
+    timed(s, KRK_PROF_GEMM, [&] {
+        kk(krk::gemm(s->hn_t, Mp, m->wte_t, VOC, s->logits, VOC, Mp, VOC, HID, krk::EPI_STORE, false, st), "lm head");
+    });
 }
 
 // One decode step for all sequences: tokens in tok_d, positions in pos_d
@@ -375,14 +462,14 @@ void decode_forward(krk_state* s, const uint8_t* active) {
     const krk_model* m = s->m;
     cudaStream_t st = m->stream;
     const int B = s->B, Mp = (int)s->Mp;
-    kk(krk::embed_fm(s->tok_d, m->wte, VOC, HID, B, s->h_t, Mp, st), "embed");
+    timed(s, KRK_PROF_OTHER, [&] { kk(krk::embed_fm(s->tok_d, m->wte, VOC, HID, B, s->h_t, Mp, st), "embed"); });
     for (int l = 0; l < NL; ++l) {
         const LayerW& L = m->L[l];
         if (is_mamba(l)) {  // src/model.rs:626-702
-            kk(krk::rmsnorm_fm(s->h_t, Mp, L.ln, RMS_EPS, HID, B, s->hn_t, Mp, st), "ln");
-            kk(krk::gemm(s->hn_t, Mp, L.in_t, DIP_PAD, s->zx, DIP_PAD, Mp, DIP_PAD, HID, krk::EPI_STORE, false, st),
-               "in_proj");
-            kk(krk::conv_step4(s->zx + OFF_X, DIP_PAD, s->conv[l], L.conv_w, L.conv_b, B, DXBC, active, st), "conv");
+            timed(s, KRK_PROF_NORM, [&] { kk(krk::rmsnorm_fm(s->h_t, Mp, L.ln, RMS_EPS, HID, B, s->hn_t, Mp, st), "ln"); });
+            timed(s, KRK_PROF_GEMM, [&] { kk(krk::gemm(s->hn_t, Mp, L.in_t, DIP_PAD, s->zx, DIP_PAD, Mp, DIP_PAD, HID, krk::EPI_STORE, false, st),
+               "in_proj"); });
+            timed(s, KRK_PROF_CONV, [&] { kk(krk::conv_step4(s->zx + OFF_X, DIP_PAD, s->conv[l], L.conv_w, L.conv_b, B, DXBC, active, st), "conv"); });
             krk::SsdStepArgs a{};
             a.x = s->zx + OFF_X; a.x_sb = DIP_PAD;
             a.bm = s->zx + OFF_B; a.cm = s->zx + OFF_C; a.bc_sb = DIP_PAD;
@@ -393,12 +480,12 @@ void decode_forward(krk_state* s, const uint8_t* active) {
             a.y = s->y_t; a.y_sb = 1; a.y_sc = Mp;
             a.active = active;
             a.B = B; a.H = MH; a.P = MP; a.N = DS;
-            kk(krk::ssd_step(a, false, st), "ssd step");
-            kk(krk::rmsnorm_fm(s->y_t, Mp, L.norm_w, MNORM_EPS, DI, B, s->yn_t, Mp, st), "gated norm");
-            kk(krk::gemm(s->yn_t, Mp, L.out_t, HID, s->h_t, Mp, Mp, HID, DI, krk::EPI_RESIDUAL, true, st), "out_proj");
+            timed(s, KRK_PROF_SSD_STEP, [&] { kk(krk::ssd_step(a, false, st), "ssd step"); });
+            timed(s, KRK_PROF_NORM, [&] { kk(krk::rmsnorm_fm(s->y_t, Mp, L.norm_w, MNORM_EPS, DI, B, s->yn_t, Mp, st), "gated norm"); });
+            timed(s, KRK_PROF_GEMM, [&] { kk(krk::gemm(s->yn_t, Mp, L.out_t, HID, s->h_t, Mp, Mp, HID, DI, krk::EPI_RESIDUAL, true, st), "out_proj"); });
         } else {  // src/model.rs:704-783
-            kk(krk::rmsnorm_fm(s->h_t, Mp, L.ln1, RMS_EPS, HID, B, s->hn_t, Mp, st), "ln1");
-            kk(krk::gemm(s->hn_t, Mp, L.qkv_t, QKV, s->qkv, QKV, Mp, QKV, HID, krk::EPI_STORE, false, st), "wqkv");
+            timed(s, KRK_PROF_NORM, [&] { kk(krk::rmsnorm_fm(s->h_t, Mp, L.ln1, RMS_EPS, HID, B, s->hn_t, Mp, st), "ln1"); });
+            timed(s, KRK_PROF_GEMM, [&] { kk(krk::gemm(s->hn_t, Mp, L.qkv_t, QKV, s->qkv, QKV, Mp, QKV, HID, krk::EPI_STORE, false, st), "wqkv"); });
             krk::AttnDecodeArgs a{};
             a.q = s->qkv; a.k = s->qkv + HID; a.v = s->qkv + 2 * HID; a.in_sb = QKV; a.in_sh = HD;
             a.kc = s->kc[l]; a.vc = s->vc[l]; a.c_sb = (int64_t)s->ctx * HID; a.c_sh = HD; a.c_st = HID;
@@ -406,11 +493,11 @@ void decode_forward(krk_state* s, const uint8_t* active) {
             a.out = s->ao_t; a.o_sb = 1; a.o_sh = (int64_t)HD * Mp; a.o_sd = Mp;
             a.work = s->attn_work;
             a.B = B; a.H = NH; a.dh = HD; a.ctx = s->ctx; a.split = s->attn_split; a.theta = THETA;
-            kk(krk::attn_decode(a, st), "attention");
-            kk(krk::gemm(s->ao_t, Mp, L.wo_t, HID, s->h_t, Mp, Mp, HID, HID, krk::EPI_RESIDUAL, true, st), "wo");
-            kk(krk::rmsnorm_fm(s->h_t, Mp, L.ln2, RMS_EPS, HID, B, s->hn_t, Mp, st), "ln2");
-            kk(krk::gemm(s->hn_t, Mp, L.fc1_t, INTER, s->mlp_t, Mp, Mp, INTER, HID, krk::EPI_GELU, true, st), "fc1");
-            kk(krk::gemm(s->mlp_t, Mp, L.fc2_t, HID, s->h_t, Mp, Mp, HID, INTER, krk::EPI_RESIDUAL, true, st), "fc2");
+            timed(s, KRK_PROF_ATTN_DECODE, [&] { kk(krk::attn_decode(a, st), "attention"); });
+            timed(s, KRK_PROF_GEMM, [&] { kk(krk::gemm(s->ao_t, Mp, L.wo_t, HID, s->h_t, Mp, Mp, HID, HID, krk::EPI_RESIDUAL, true, st), "wo"); });
+            timed(s, KRK_PROF_NORM, [&] { kk(krk::rmsnorm_fm(s->h_t, Mp, L.ln2, RMS_EPS, HID, B, s->hn_t, Mp, st), "ln2"); });
+            timed(s, KRK_PROF_GEMM, [&] { kk(krk::gemm(s->hn_t, Mp, L.fc1_t, INTER, s->mlp_t, Mp, Mp, INTER, HID, krk::EPI_GELU, true, st), "fc1"); });
+            timed(s, KRK_PROF_GEMM, [&] { kk(krk::gemm(s->mlp_t, Mp, L.fc2_t, HID, s->h_t, Mp, Mp, HID, INTER, krk::EPI_RESIDUAL, true, st), "fc2"); });
         }
     }
     lm_head(s);
@@ -428,16 +515,16 @@ void prefill_group(krk_state* s, int g0, int S, int64_t rows) {
     zero_pad_cols(w.y_t, T, R, DI, st);
     zero_pad_cols(w.yn_t, T, R, DI, st);
     zero_pad_cols(w.ao_t, T, R, HID, st);
-    kk(krk::embed_fm(w.tok, m->wte, VOC, HID, R, w.x_t, T, st), "embed");
+    timed(s, KRK_PROF_OTHER, [&] { kk(krk::embed_fm(w.tok, m->wte, VOC, HID, R, w.x_t, T, st), "embed"); });
     for (int l = 0; l < NL; ++l) {
         const LayerW& L = m->L[l];
         if (is_mamba(l)) {  // src/model.rs:370-464
-            kk(krk::rmsnorm_fm(w.x_t, T, L.ln, RMS_EPS, HID, R, w.hn_t, T, st), "ln");
-            kk(krk::gemm(w.hn_t, T, L.in_t, DIP_PAD, w.zx, DIP_PAD, T, DIP_PAD, HID, krk::EPI_STORE, false, st),
-               "in_proj");
-            kk(krk::conv_prefill4(w.zx + OFF_X, DIP_PAD, w.xbc, DXBC, s->conv[l] + (size_t)g0 * DXBC * 4, L.conv_w,
+            timed(s, KRK_PROF_NORM, [&] { kk(krk::rmsnorm_fm(w.x_t, T, L.ln, RMS_EPS, HID, R, w.hn_t, T, st), "ln"); });
+            timed(s, KRK_PROF_GEMM, [&] { kk(krk::gemm(w.hn_t, T, L.in_t, DIP_PAD, w.zx, DIP_PAD, T, DIP_PAD, HID, krk::EPI_STORE, false, st),
+               "in_proj"); });
+            timed(s, KRK_PROF_CONV, [&] { kk(krk::conv_prefill4(w.zx + OFF_X, DIP_PAD, w.xbc, DXBC, s->conv[l] + (size_t)g0 * DXBC * 4, L.conv_w,
                                   L.conv_b, w.cu, S, DXBC, st),
-               "conv");
+               "conv"); });
             krk::SsdScanArgs a{};
             a.x = w.xbc; a.x_rs = DXBC;
             a.bm = w.xbc + DI; a.cm = w.xbc + DI + DS; a.bc_rs = DXBC;
@@ -448,28 +535,28 @@ void prefill_group(krk_state* s, int g0, int S, int64_t rows) {
             a.y = w.y_t; a.y_rs = 1; a.y_cs = T;
             a.cu_seqlens = w.cu;
             a.S = S; a.H = MH; a.P = MP; a.N = DS;
-            kk(krk::ssd_scan(a, false, st), "ssd scan");
-            kk(krk::rmsnorm_fm(w.y_t, T, L.norm_w, MNORM_EPS, DI, R, w.yn_t, T, st), "gated norm");
-            kk(krk::gemm(w.yn_t, T, L.out_t, HID, w.x_t, T, T, HID, DI, krk::EPI_RESIDUAL, true, st), "out_proj");
+            timed(s, KRK_PROF_SSD_SCAN, [&] { kk(krk::ssd_scan(a, false, st), "ssd scan"); });
+            timed(s, KRK_PROF_NORM, [&] { kk(krk::rmsnorm_fm(w.y_t, T, L.norm_w, MNORM_EPS, DI, R, w.yn_t, T, st), "gated norm"); });
+            timed(s, KRK_PROF_GEMM, [&] { kk(krk::gemm(w.yn_t, T, L.out_t, HID, w.x_t, T, T, HID, DI, krk::EPI_RESIDUAL, true, st), "out_proj"); });
         } else {  // src/model.rs:466-583
-            kk(krk::rmsnorm_fm(w.x_t, T, L.ln1, RMS_EPS, HID, R, w.hn_t, T, st), "ln1");
-            kk(krk::gemm(w.hn_t, T, L.qkv_t, QKV, w.qkv, QKV, T, QKV, HID, krk::EPI_STORE, false, st), "wqkv");
+            timed(s, KRK_PROF_NORM, [&] { kk(krk::rmsnorm_fm(w.x_t, T, L.ln1, RMS_EPS, HID, R, w.hn_t, T, st), "ln1"); });
+            timed(s, KRK_PROF_GEMM, [&] { kk(krk::gemm(w.hn_t, T, L.qkv_t, QKV, w.qkv, QKV, T, QKV, HID, krk::EPI_STORE, false, st), "wqkv"); });
             float* kc = s->kc[l] + (size_t)g0 * s->ctx * HID;
             float* vc = s->vc[l] + (size_t)g0 * s->ctx * HID;
             const int64_t c_sb = (int64_t)s->ctx * HID;
-            kk(krk::rope_kv_prefill(w.qkv, QKV, kc, vc, c_sb, HD, HID, w.cu, w.start, S, NH, HD, R, THETA, st),
-               "rope/kv");
-            kk(krk::attn_prefill(w.qkv, QKV, kc, vc, c_sb, HD, HID, w.cu, w.start, w.row_seq, S, NH, HD, R, s->ctx,
+            timed(s, KRK_PROF_OTHER, [&] { kk(krk::rope_kv_prefill(w.qkv, QKV, kc, vc, c_sb, HD, HID, w.cu, w.start, S, NH, HD, R, THETA, st),
+               "rope/kv"); });
+            timed(s, KRK_PROF_ATTN_PREFILL, [&] { kk(krk::attn_prefill(w.qkv, QKV, kc, vc, c_sb, HD, HID, w.cu, w.start, w.row_seq, S, NH, HD, R, s->ctx,
                                  w.ao_t, 1, T, st),
-               "attention");
-            kk(krk::gemm(w.ao_t, T, L.wo_t, HID, w.x_t, T, T, HID, HID, krk::EPI_RESIDUAL, true, st), "wo");
-            kk(krk::rmsnorm_fm(w.x_t, T, L.ln2, RMS_EPS, HID, R, w.hn_t, T, st), "ln2");
-            kk(krk::gemm(w.hn_t, T, L.fc1_t, INTER, w.mlp_t, T, T, INTER, HID, krk::EPI_GELU, true, st), "fc1");
-            kk(krk::gemm(w.mlp_t, T, L.fc2_t, HID, w.x_t, T, T, HID, INTER, krk::EPI_RESIDUAL, true, st), "fc2");
+               "attention"); });
+            timed(s, KRK_PROF_GEMM, [&] { kk(krk::gemm(w.ao_t, T, L.wo_t, HID, w.x_t, T, T, HID, HID, krk::EPI_RESIDUAL, true, st), "wo"); });
+            timed(s, KRK_PROF_NORM, [&] { kk(krk::rmsnorm_fm(w.x_t, T, L.ln2, RMS_EPS, HID, R, w.hn_t, T, st), "ln2"); });
+            timed(s, KRK_PROF_GEMM, [&] { kk(krk::gemm(w.hn_t, T, L.fc1_t, INTER, w.mlp_t, T, T, INTER, HID, krk::EPI_GELU, true, st), "fc1"); });
+            timed(s, KRK_PROF_GEMM, [&] { kk(krk::gemm(w.mlp_t, T, L.fc2_t, HID, w.x_t, T, T, HID, INTER, krk::EPI_RESIDUAL, true, st), "fc2"); });
         }
     }
     // last token of each sequence -> decode residual buffer column g0 + s
-    kk(krk::gather_cols(w.x_t, T, w.last, s->h_t, (int)s->Mp, w.dst, HID, S, st), "gather last");
+    timed(s, KRK_PROF_OTHER, [&] { kk(krk::gather_cols(w.x_t, T, w.last, s->h_t, (int)s->Mp, w.dst, HID, S, st), "gather last"); });
 }
 
 // Validates and runs a batched prefill; on return the decode buffers hold the
@@ -517,10 +604,11 @@ int run_prefill(krk_state* s, const uint32_t* tokens, const int32_t* lens, bool 
         kk(cudaMemcpyAsync(w.last, last.data(), S * 4, cudaMemcpyHostToDevice, st), "h2d last");
         kk(cudaMemcpyAsync(w.dst, dst.data(), S * 4, cudaMemcpyHostToDevice, st), "h2d dst");
         kk(cudaMemcpyAsync(w.row_seq, row_seq.data(), rows * 4, cudaMemcpyHostToDevice, st), "h2d row_seq");
+        total_begin(s);
         prefill_group(s, g0, S, rows);
         if (mark)
-            kk(krk::mark_seen(w.tok, w.row_seq, (int)rows, s->seen_d + (size_t)g0 * SEEN_WORDS, SEEN_WORDS, st),
-               "mark seen");
+            timed(s, KRK_PROF_OTHER, [&] { kk(krk::mark_seen(w.tok, w.row_seq, (int)rows, s->seen_d + (size_t)g0 * SEEN_WORDS, SEEN_WORDS, st),
+               "mark seen"); });
         kk(cudaStreamSynchronize(st), "prefill group");  // the host vectors above go out of scope
         off += rows;
         g0 = g1;
@@ -543,7 +631,7 @@ int copy_logits(krk_state* s, float* logits_out) {
 }
 
 template <typename F>
-int guarded(F&& f) {
+int guarded(F&& f) {  // runs f, turning exceptions into a status + message
     try {
         g_err.clear();
         return f();
@@ -712,7 +800,11 @@ int krk_prefill(const krk_model* m, krk_state* s, const uint32_t* tokens, const 
         DeviceGuard g(m->device);
         int rc = run_prefill(s, tokens, lens, false);
         if (rc) return rc;
-        return copy_logits(s, logits_out);
+        total_end(s);
+        rc = copy_logits(s, logits_out);
+        kk(cudaStreamSynchronize(m->stream), "prefill");
+        prof_collect(s);
+        return rc;
     });
 }
 
@@ -730,12 +822,16 @@ int krk_step(const krk_model* m, krk_state* s, const uint32_t* tokens, float* lo
         DeviceGuard g(m->device);
         cudaStream_t st = m->stream;
         kk(cudaMemcpyAsync(s->tok_d, tokens, s->B * 4, cudaMemcpyHostToDevice, st), "h2d tokens");
+        total_begin(s);
         decode_forward(s, nullptr);
-        kk(krk::advance_pos(s->pos_d, nullptr, s->B, st), "advance");
+        timed(s, KRK_PROF_OTHER, [&] { kk(krk::advance_pos(s->pos_d, nullptr, s->B, st), "advance"); });
         for (int b = 0; b < s->B; ++b) s->pos_h[b] += 1;
-        if (logits_out) return copy_logits(s, logits_out);
+        total_end(s);
+        int rc = KRK_OK;
+        if (logits_out) rc = copy_logits(s, logits_out);
         kk(cudaStreamSynchronize(st), "step");
-        return KRK_OK;
+        prof_collect(s);
+        return rc;
     });
 }
 
@@ -753,44 +849,52 @@ int krk_generate_greedy(const krk_model* m, krk_state* s, const uint32_t* prompt
         if (rc) return rc;
         rc = run_prefill(s, prompts, lens, true);
         if (rc) return rc;
-        // Tokens each sequence can emit: the loop pushes a token, then stops if
-        // current_pos >= context_limit (src/generate.rs:87-110).
-        std::vector<int32_t> limit(B);
-        int max_steps = 0;
+        // src/generate.rs:86-114 per sequence: a pick is pushed unless it is EOS;
+        // after a push the loop stops if current_pos >= context_limit, else it
+        // runs forward_step -- also after the max_new_tokens-th push.  So a
+        // sequence pushes at most tlimit = min(max_new, ctx - len + 1) tokens
+        // and runs at most slimit = min(max_new, ctx - len) decode steps.
+        std::vector<int32_t> tlimit(B), slimit(B);
+        int max_picks = 0, max_steps = 0;
         for (int b = 0; b < B; ++b) {
-            limit[b] = (int32_t)std::min<int64_t>(max_new_tokens, (int64_t)s->ctx - lens[b] + 1);
-            max_steps = std::max(max_steps, limit[b]);
+            tlimit[b] = (int32_t)std::min<int64_t>(max_new_tokens, (int64_t)s->ctx - lens[b] + 1);
+            slimit[b] = (int32_t)std::min<int64_t>(max_new_tokens, (int64_t)s->ctx - lens[b]);
+            max_picks = std::max(max_picks, tlimit[b]);
+            max_steps = std::max(max_steps, slimit[b]);
         }
-        if ((int64_t)max_steps * B > s->hist_cap) {
-            s->hist_arena.reserve((size_t)max_steps * B * 4 + 256);
-            s->hist_d = s->hist_arena.take<uint32_t>((size_t)max_steps * B);
-            s->hist_cap = (int64_t)max_steps * B;
+        if ((int64_t)max_picks * B > s->hist_cap) {
+            s->hist_arena.reserve((size_t)max_picks * B * 4 + 256);
+            s->hist_d = s->hist_arena.take<uint32_t>((size_t)max_picks * B);
+            s->hist_cap = (int64_t)max_picks * B;
         }
-        kk(cudaMemcpyAsync(s->limit_d, limit.data(), B * 4, cudaMemcpyHostToDevice, st), "h2d limit");
+        kk(cudaMemcpyAsync(s->tlimit_d, tlimit.data(), B * 4, cudaMemcpyHostToDevice, st), "h2d limit");
+        kk(cudaMemcpyAsync(s->slimit_d, slimit.data(), B * 4, cudaMemcpyHostToDevice, st), "h2d limit");
         kk(cudaMemsetAsync(s->active_d, 1, B, st), "active");
         kk(cudaMemsetAsync(s->step_d, 0, 4, st), "step");
-        kk(cudaMemsetAsync(s->hist_d, 0xff, (size_t)max_steps * B * 4, st), "hist");
+        kk(cudaMemsetAsync(s->hist_d, 0xff, (size_t)max_picks * B * 4, st), "hist");
         krk::GreedyArgs ga{};
         ga.logits = s->logits; ga.ld = VOC; ga.vocab = VOC; ga.B = B;
         ga.seen = s->seen_d; ga.penalty = repetition_penalty;
         ga.tok = s->tok_d; ga.active = s->active_d; ga.hist = s->hist_d; ga.step = s->step_d;
-        ga.limit = s->limit_d; ga.stop_eos = stop_at_eos; ga.eos = KRK_EOS_TOKEN;
+        ga.tlimit = s->tlimit_d; ga.slimit = s->slimit_d; ga.stop_eos = stop_at_eos; ga.eos = KRK_EOS_TOKEN;
         ga.pos = nullptr;
-        // first token from the prefill logits (src/generate.rs:81-82)
-        kk(krk::greedy(ga, st), "greedy");
+        // first pick from the prefill logits (src/generate.rs:81-82)
+        timed(s, KRK_PROF_OTHER, [&] { kk(krk::greedy(ga, st), "greedy"); });
         ga.pos = s->pos_d;
-        for (int i = 1; i < max_steps; ++i) {
+        for (int i = 0; i < max_steps; ++i) {
             decode_forward(s, s->active_d);
-            kk(krk::greedy(ga, st), "greedy");
+            timed(s, KRK_PROF_OTHER, [&] { kk(krk::greedy(ga, st), "greedy"); });
         }
-        std::vector<uint32_t> hist((size_t)max_steps * B);
+        total_end(s);
+        std::vector<uint32_t> hist((size_t)max_picks * B);
         std::vector<int32_t> pos(B);
         kk(cudaMemcpyAsync(hist.data(), s->hist_d, hist.size() * 4, cudaMemcpyDeviceToHost, st), "d2h tokens");
         kk(cudaMemcpyAsync(pos.data(), s->pos_d, B * 4, cudaMemcpyDeviceToHost, st), "d2h pos");
         kk(cudaStreamSynchronize(st), "generate");
+        prof_collect(s);
         for (int b = 0; b < B; ++b) {
             int n = 0;
-            for (int i = 0; i < limit[b]; ++i) {
+            for (int i = 0; i < tlimit[b]; ++i) {
                 uint32_t t = hist[(size_t)i * B + b];
                 if (t == 0xffffffffu || (stop_at_eos && t == (uint32_t)KRK_EOS_TOKEN)) break;
                 tokens_out[(size_t)b * max_new_tokens + n++] = t;
@@ -829,6 +933,29 @@ int krk_state_export(const krk_state* s, int seq, int layer, int what, float* ou
         kk(cudaStreamSynchronize(s->m->stream), "export");
         return KRK_OK;
     });
+}
+
+int krk_state_profile(krk_state* s, int enable) {
+    return guarded([&]() -> int {
+        if (!s) return fail(KRK_INVALID, "null state");
+        DeviceGuard g(s->m->device);
+        kk(cudaStreamSynchronize(s->m->stream), "profile");
+        s->prof.clear_events();
+        s->prof.on = enable != 0;
+        for (int i = 0; i < KRK_PROF_CLASSES; ++i) {
+            s->prof.ms[i] = 0.0;
+            s->prof.n[i] = 0;
+        }
+        return KRK_OK;
+    });
+}
+
+int krk_state_profile_read(const krk_state* s, int cls, double* total_ms, int64_t* launches) {
+    if (!s || cls < 0 || cls >= KRK_PROF_CLASSES || !total_ms || !launches)
+        return fail(KRK_INVALID, "bad profile arguments");
+    *total_ms = s->prof.ms[cls];
+    *launches = s->prof.n[cls];
+    return KRK_OK;
 }
 
 int krk_launch_count(uint64_t* count) {

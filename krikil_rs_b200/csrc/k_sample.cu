@@ -41,14 +41,16 @@ __global__ void __launch_bounds__(256) greedy_kernel(GreedyArgs a) {
             if (bv_s[w] > best || (bv_s[w] == best && bi_s[w] < bi)) { best = bv_s[w]; bi = bi_s[w]; }
         const uint32_t t = bi >= a.vocab ? 0u : (uint32_t)bi;
         if (was_active) {
-            a.tok[b] = t;
-            if (a.seen) atomicOr(a.seen + (size_t)b * (a.vocab / 32) + (t >> 5), 1u << (t & 31));
-            const int step = step_s;
-            if (a.hist) a.hist[(size_t)step * a.B + b] = t;
             if (a.pos) a.pos[b] += 1;
-            if (a.active) {
-                const bool stop = (a.limit && step + 1 >= a.limit[b]) || (a.stop_eos && t == a.eos);
-                if (stop) a.active[b] = 0;
+            const int step = step_s;
+            if (a.tlimit && step >= a.tlimit[b]) {
+                if (a.active) a.active[b] = 0;  // sampled after the last counted token: unused
+            } else {
+                a.tok[b] = t;
+                if (a.seen) atomicOr(a.seen + (size_t)b * (a.vocab / 32) + (t >> 5), 1u << (t & 31));
+                if (a.hist) a.hist[(size_t)step * a.B + b] = t;
+                const bool stop = (a.stop_eos && t == a.eos) || (a.slimit && step + 1 > a.slimit[b]);
+                if (stop && a.active) a.active[b] = 0;
             }
         }
     }

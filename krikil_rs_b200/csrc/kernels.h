@@ -116,17 +116,20 @@ cudaError_t attn_prefill(const float* qkv, int64_t q_rs, const float* kc, const 
 // ---------------------------------------------------------------- sampling
 // Greedy choice per sequence (src/sampler.rs:50-80): repetition penalty on the
 // tokens whose bit is set in seen[b][vocab/32] (when penalty != 1), then the
-// first maximum.  Writes tok[b] and sets its seen bit.  Optional bookkeeping of
-// batched generation (any pointer may be null):
-//   hist[*step * B + b] = tok[b];  pos[b] += 1;
-//   limit/eos: active[b] = 0 once step+1 >= limit[b] or (stop_eos and tok == eos);
-//   step: the caller's step counter, incremented after use.
+// first maximum.  Writes tok[b] and sets its seen bit.  Bookkeeping of batched
+// generation, mirroring src/generate.rs:86-114 (any pointer may be null):
+//   pos[b] += 1          the logits came from a decode step of sequence b
+//   step                 index of this pick (the caller's counter, bumped after)
+//   tlimit[b]            picks at step >= tlimit[b] are discarded
+//   hist[step*B + b]     the recorded pick
+//   active[b] = 0        after an EOS pick (stop_eos), a discarded pick, or a
+//                        pick with step + 1 > slimit[b] (no further decode step)
 struct GreedyArgs {
     const float* logits; int64_t ld; int vocab; int B;
     uint32_t* seen; float penalty;
     uint32_t* tok;
     uint8_t* active;
-    uint32_t* hist; int32_t* step; int32_t* pos; const int32_t* limit;
+    uint32_t* hist; int32_t* step; int32_t* pos; const int32_t* tlimit; const int32_t* slimit;
     int stop_eos; uint32_t eos;
 };
 cudaError_t greedy(const GreedyArgs& a, cudaStream_t s);

@@ -165,6 +165,19 @@ class PebbleState:
         check(lib.krk_state_export(self._h, seq, layer, what, _ptr(out), out.size))
         return out
 
+    def profile(self, enable: bool = True) -> None:
+        """Turn per-kernel-class CUDA-event timing of later calls on/off (resets totals)."""
+        check(lib.krk_state_profile(self._h, int(bool(enable))))
+
+    def profile_read(self) -> dict:
+        """{class: (device ms, launches)} accumulated since profile()."""
+        out = {}
+        for i, name in enumerate(_lib.PROF_CLASSES):
+            ms, n = C.c_double(), C.c_int64()
+            check(lib.krk_state_profile_read(self._h, i, C.byref(ms), C.byref(n)))
+            out[name] = (ms.value, n.value)
+        return out
+
     def close(self) -> None:
         if self._h:
             lib.krk_state_free(self._h)

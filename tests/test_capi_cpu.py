@@ -1,0 +1,103 @@
+"""The C-ABI library on a machine without a GPU: it loads, exports every entry
+point include/krikil_cuda.h declares, and reports file/format errors (which
+the loader checks before touching a device) with the reference's messages."""
+import ctypes as C
+import os
+import re
+import struct
+
+import numpy as np
+import pytest
+
+from krikil_rs_b200 import _lib, synth
+from krikil_rs_b200._lib import KrikilError, lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _declared():
+    with open(os.path.join(ROOT, "include", "krikil_cuda.h")) as f:
+        src = f.read()
+    return sorted(set(re.findall(r"KRK_API\s+[\w\s\*]+?\b(krk_\w+)\s*\(", src)))
+
+
+def test_header_declares_entry_points():
+    names = _declared()
+    assert "krk_model_load" in names and "krk_k_gemm" in names and len(names) >= 29
+
+
+def test_library_exports_every_declared_symbol():
+    for name in _declared():
+        assert hasattr(lib, name), name
+    assert set(_lib.EXPORTED) >= set(_declared())
+
+
+def test_abi_version_and_status_strings():
+    assert lib.krk_abi_version() == 1
+    assert lib.krk_status_string(_lib.BAD_TOKEN) == b"token id exceeds vocab size"
+
+
+def _load(path):
+    h = C.c_void_p()
+    return lib.krk_model_load(path.encode(), 0, C.byref(h)), lib.krk_last_error().decode()
+
+
+def test_load_missing_file(tmp_path):
+    rc, msg = _load(str(tmp_path / "nope.safetensors"))
+    assert rc == _lib.IO and "Failed to open model file" in msg
+
+
+def test_load_truncated_and_malformed(tmp_path):
+    p = tmp_path / "t.safetensors"
+    p.write_bytes(b"\x01\x02")
+    assert _load(str(p))[0] == _lib.IO
+    p.write_bytes(struct.pack("<Q", 1000) + b"{}")
+    rc, msg = _load(str(p))
+    assert rc == _lib.IO and "header length exceeds file" in msg
+    hdr = b'{"wte.weight": {"dtype": "F32", "shape": [2], "data_offsets": [0, 64]}}'
+    p.write_bytes(struct.pack("<Q", len(hdr)) + hdr + b"\0" * 8)
+    rc, msg = _load(str(p))
+    assert rc == _lib.IO and "exceed" in msg
+
+
+def test_load_missing_tensor(tmp_path):
+    w = {"wte.weight": np.zeros((2048, 608), np.float32)}
+    p = str(tmp_path / "m.safetensors")
+    synth.save_safetensors(p, w)
+    rc, msg = _load(p)
+    assert rc == _lib.NOT_FOUND and msg == "Tensor 'lnf.weight' not found in model"
+
+
+def test_load_wrong_size_and_dtype(tmp_path):
+    w = synth.make_weights(0)
+    w["blocks.3.wo.weight"] = w["blocks.3.wo.weight"][:100]
+    p = str(tmp_path / "m.safetensors")
+    synth.save_safetensors(p, w)
+    rc, msg = _load(p)
+    assert rc == _lib.IO and "blocks.3.wo.weight" in msg
+    # shapes are not checked (like the reference), only element counts:
+    w = synth.make_weights(0)
+    w["blocks.0.mixer.conv1d.weight"] = w["blocks.0.mixer.conv1d.weight"].reshape(1472, 4)
+    synth.save_safetensors(p, w)
+    rc, msg = _load(p)
+    assert rc in (_lib.OK, _lib.CUDA)  # CUDA when this machine has no GPU
+
+
+def test_python_mirror_raises_krikil_error(tmp_path):
+    from krikil_rs_b200 import PebbleModel
+    with pytest.raises(KrikilError) as e:
+        PebbleModel.load_safetensors(str(tmp_path / "missing"))
+    assert e.value.status == _lib.IO
+
+
+def test_synth_safetensors_roundtrip(tmp_path):
+    w = synth.make_weights(0)
+    assert len(w) == 2 + 6 * 9 + 2 * 6
+    p = str(tmp_path / "w.safetensors")
+    synth.save_safetensors(p, w)
+    r = synth.load_safetensors(p)
+    for k in w:
+        np.testing.assert_array_equal(w[k], r[k])
+    w2 = synth.make_weights(0)
+    assert all(np.array_equal(w[k], w2[k]) for k in w)
+    assert (w["blocks.0.mixer.A_log"] >= 0).all() and (w["blocks.0.mixer.A_log"] <= np.log(16)).all()

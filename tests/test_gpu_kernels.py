@@ -1,0 +1,252 @@
+"""Per-kernel parity of the CUDA library (through its C ABI) against the CPU
+oracle, on seeded inputs.  Tolerances are written per test; projections and the
+feature-major RMSNorm are bit-exact by construction."""
+import numpy as np
+import pytest
+
+import oracle as O
+from krikil_rs_b200 import synth
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+if not torch.cuda.is_available():  # pragma: no cover
+    pytest.skip("no CUDA device", allow_module_level=True)
+
+from krikil_rs_b200 import kernels as K  # noqa: E402
+
+DEV = torch.device("cuda:0")
+
+
+def cu(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(DEV)
+
+
+def np_(t):
+    torch.cuda.synchronize()
+    return t.cpu().numpy()
+
+
+# ------------------------------------------------------------- projections
+@pytest.mark.parametrize("m,n,k", [(64, 32, 32), (128, 2720, 608), (64, 608, 1216), (192, 608, 2432),
+                                   (64, 2048, 608), (256, 1824, 608)])
+@pytest.mark.parametrize("out_fm", [False, True])
+def test_gemm_bit_exact_vs_reference_dot(m, n, k, out_fm):
+    rng = np.random.default_rng(m * 7 + n + k)
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    w = (0.02 * rng.standard_normal((n, k))).astype(np.float32)
+    ref = O.gemm_transb(a, w)  # each element = the reference dot (src/math.rs:89-124)
+    c = K.gemm(cu(a.T.copy()), cu(w.T.copy()), 0, out_fm)
+    got = np_(c).T if out_fm else np_(c)
+    np.testing.assert_array_equal(got, ref)
+
+
+def test_gemm_residual_and_gelu_epilogues():
+    rng = np.random.default_rng(1)
+    m, n, k = 128, 608, 2432
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    w = (0.02 * rng.standard_normal((n, k))).astype(np.float32)
+    res = rng.standard_normal((n, m)).astype(np.float32)
+    ref = O.gemm_transb(a, w)
+    c = cu(res.copy())
+    K.gemm(cu(a.T.copy()), cu(w.T.copy()), 1, True, c)
+    np.testing.assert_array_equal(np_(c), res + ref.T)
+    g = np_(K.gemm(cu(a.T.copy()), cu(w.T.copy()), 2, True))
+    gref = np.vectorize(O.gelu, otypes=[np.float32])(ref.T)
+    np.testing.assert_allclose(g, gref, atol=1e-6, rtol=1e-5)
+
+
+def test_gemm_rejects_bad_shapes():
+    from krikil_rs_b200._lib import KrikilError
+    with pytest.raises(KrikilError):
+        K.gemm(torch.zeros(32, 60, device=DEV), torch.zeros(32, 32, device=DEV))
+
+
+# ------------------------------------------------------------- norms
+@pytest.mark.parametrize("kdim,m,ld", [(608, 64, 64), (1216, 37, 64), (608, 1, 64), (608, 1024, 1024)])
+def test_rmsnorm_feature_major_bit_exact(kdim, m, ld):
+    rng = np.random.default_rng(kdim + m)
+    x = rng.standard_normal((ld, kdim)).astype(np.float32)
+    w = (1 + 0.1 * rng.standard_normal(kdim)).astype(np.float32)
+    eps = 1e-6 if kdim == 608 else 1e-5
+    out = np_(K.rmsnorm_fm(cu(x.T.copy()), cu(w), eps, m))
+    for col in range(m):
+        np.testing.assert_array_equal(out[:, col], O.rms_norm(x[col], w, eps))
+
+
+def test_rmsnorm_rows():
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal((1000, 512)).astype(np.float32)
+    w = (1 + 0.1 * rng.standard_normal(512)).astype(np.float32)
+    np.testing.assert_allclose(np_(K.rmsnorm_rows(cu(x), cu(w), 1e-6)), O.rms_norm_rows(x, w, 1e-6),
+                               atol=1e-5, rtol=1e-5)
+
+
+def test_gated_rmsnorm_residual_full_size():
+    """Config: x,z,res ~N(0,1) [16384,512], w ~N(1,0.1), eps 1e-5."""
+    x, z, res, w = synth.fused_norm_inputs()
+    got = np_(K.gated_rmsnorm_residual(cu(x), cu(z), cu(res), cu(w), 1e-5))
+    ref = O.gated_rmsnorm_residual(x, z, res, w, 1e-5)
+    np.testing.assert_allclose(got, ref, atol=1e-4, rtol=1e-5)
+    assert np.abs(got - ref).max() < 1e-5
+
+
+@pytest.mark.parametrize("dim", [128, 256, 1024])
+def test_gated_rmsnorm_residual_dims(dim):
+    x, z, res, w = synth.fused_norm_inputs(rows=33, dim=dim, seed=dim)
+    got = np_(K.gated_rmsnorm_residual(cu(x), cu(z), cu(res), cu(w), 1e-5))
+    np.testing.assert_allclose(got, O.gated_rmsnorm_residual(x, z, res, w, 1e-5), atol=1e-5, rtol=1e-5)
+
+
+# ------------------------------------------------------------- pointwise / embed
+@pytest.mark.parametrize("op,fn", [(0, O.silu), (1, O.softplus), (2, O.gelu)])
+def test_pointwise(op, fn):
+    x = np.concatenate([np.linspace(-30, 30, 5001), [0.0, -0.0, 20.0, 20.000002, -87.0, 88.0]]).astype(np.float32)
+    got = np_(K.pointwise(op, cu(x)))
+    ref = np.array([fn(float(v)) for v in x], np.float32)
+    np.testing.assert_allclose(got, ref, atol=1e-6, rtol=2e-6)
+
+
+def test_embed_exact():
+    rng = np.random.default_rng(2)
+    wte = rng.standard_normal((2048, 608)).astype(np.float32)
+    tok = np.array([0, 2047, 5, 5, 1000], np.uint32)
+    out = np_(K.embed(cu(tok.view(np.int32)), cu(wte), ld=64))
+    np.testing.assert_array_equal(out[:, :5].T, wte[tok])
+    assert not out[:, 5:].any()
+
+
+# ------------------------------------------------------------- Mamba2
+def _ssd_case(bsz, t, nh=16, seed=0, state_scale=1.0):
+    x, bm, cm, dt, cs, ssm = synth.conv_ssd_inputs(bsz, t, nh=nh, seed=seed, state_scale=state_scale)
+    params = synth.conv_ssd_params(nh=nh, seed=seed)
+    return x, bm, cm, dt, cs, ssm, params
+
+
+def test_conv_ssd_step_full_size():
+    """Config: batch 256, 16 heads x 64, d_state 128, conv state [256,1024,3]."""
+    x, bm, cm, dt, cs, ssm, (cw, cb, dtb, an, dsk) = _ssd_case(256, 1)
+    g_cs, g_ssm = cu(cs), cu(ssm)
+    y = K.conv_ssd_step(cu(x[:, 0]), cu(bm[:, 0]), cu(cm[:, 0]), cu(dt[:, 0]), g_cs, cu(cw), cu(cb), g_ssm,
+                        cu(dtb), cu(an), cu(dsk))
+    o_cs, o_ssm = cs.copy(), ssm.copy()
+    yr = O.conv_ssd_step(x[:, 0].copy(), bm[:, 0].copy(), cm[:, 0].copy(), dt[:, 0].copy(), o_cs, cw, cb, dtb,
+                         an, dsk, o_ssm)
+    np.testing.assert_array_equal(np_(g_cs), o_cs)  # conv state is a pure shift
+    np.testing.assert_allclose(np_(g_ssm), o_ssm, atol=1e-4, rtol=1e-5)
+    np.testing.assert_allclose(np_(y), yr, atol=1e-4, rtol=1e-5)
+
+
+def test_conv_ssd_step_repeated_steps():
+    x, bm, cm, dt, cs, ssm, (cw, cb, dtb, an, dsk) = _ssd_case(8, 6, seed=3)
+    g_cs, g_ssm = cu(cs), cu(ssm)
+    o_cs, o_ssm = cs.copy(), ssm.copy()
+    for t in range(6):
+        y = K.conv_ssd_step(cu(x[:, t]), cu(bm[:, t]), cu(cm[:, t]), cu(dt[:, t]), g_cs, cu(cw), cu(cb), g_ssm,
+                            cu(dtb), cu(an), cu(dsk))
+        yr = O.conv_ssd_step(x[:, t].copy(), bm[:, t].copy(), cm[:, t].copy(), dt[:, t].copy(), o_cs, cw, cb,
+                             dtb, an, dsk, o_ssm)
+        np.testing.assert_allclose(np_(y), yr, atol=1e-4, rtol=1e-5)
+    np.testing.assert_allclose(np_(g_ssm), o_ssm, atol=1e-4, rtol=1e-5)
+
+
+@pytest.mark.parametrize("bsz,t", [(3, 1), (2, 31), (2, 33), (4, 100)])
+def test_conv_ssd_scan_vs_oracle(bsz, t):
+    x, bm, cm, dt, cs, ssm, (cw, cb, dtb, an, dsk) = _ssd_case(bsz, t, seed=t)
+    g_cs, g_ssm = cu(cs), cu(ssm)
+    y = K.conv_ssd_scan(cu(x), cu(bm), cu(cm), cu(dt), g_cs, cu(cw), cu(cb), g_ssm, cu(dtb), cu(an), cu(dsk))
+    o_cs, o_ssm = cs.copy(), ssm.copy()
+    yr = O.conv_ssd_scan(x, bm, cm, dt, o_cs, cw, cb, dtb, an, dsk, o_ssm)
+    np.testing.assert_array_equal(np_(g_cs), o_cs)
+    np.testing.assert_allclose(np_(g_ssm), o_ssm, atol=1e-4, rtol=1e-5)
+    np.testing.assert_allclose(np_(y), yr, atol=1e-4, rtol=1e-5)
+
+
+def test_conv_ssd_scan_equals_repeated_steps():
+    """The prefill scan and T single steps implement the same recurrence."""
+    x, bm, cm, dt, cs, ssm, (cw, cb, dtb, an, dsk) = _ssd_case(4, 40, seed=9)
+    s_cs, s_ssm = cu(cs), cu(ssm)
+    ys = K.conv_ssd_scan(cu(x), cu(bm), cu(cm), cu(dt), s_cs, cu(cw), cu(cb), s_ssm, cu(dtb), cu(an), cu(dsk))
+    t_cs, t_ssm = cu(cs), cu(ssm)
+    yt = [np_(K.conv_ssd_step(cu(x[:, i]), cu(bm[:, i]), cu(cm[:, i]), cu(dt[:, i]), t_cs, cu(cw), cu(cb), t_ssm,
+                              cu(dtb), cu(an), cu(dsk))) for i in range(40)]
+    np.testing.assert_allclose(np_(ys), np.stack(yt, 1), atol=1e-4, rtol=1e-5)
+    np.testing.assert_allclose(np_(s_ssm), np_(t_ssm), atol=1e-4, rtol=1e-5)
+
+
+def test_conv_ssd_scan_split_invariance_full_size():
+    """Config shapes (B=256, T=2048): one 2048-token scan equals two 1024-token
+    scans carrying the state (bitwise: chunk boundaries coincide), and sampled
+    sequences match the oracle's sequential recurrence."""
+    bsz, t = 256, 2048
+    x, bm, cm, dt, cs, ssm, (cw, cb, dtb, an, dsk) = _ssd_case(bsz, t, seed=11, state_scale=0.0)
+    gx, gb, gc, gd = cu(x), cu(bm), cu(cm), cu(dt)
+    a_cs, a_ssm = cu(cs), cu(ssm)
+    ya = K.conv_ssd_scan(gx, gb, gc, gd, a_cs, cu(cw), cu(cb), a_ssm, cu(dtb), cu(an), cu(dsk))
+    b_cs, b_ssm = cu(cs), cu(ssm)
+    h = t // 2
+    y1 = K.conv_ssd_scan(gx[:, :h].contiguous(), gb[:, :h].contiguous(), gc[:, :h].contiguous(),
+                         gd[:, :h].contiguous(), b_cs, cu(cw), cu(cb), b_ssm, cu(dtb), cu(an), cu(dsk))
+    y2 = K.conv_ssd_scan(gx[:, h:].contiguous(), gb[:, h:].contiguous(), gc[:, h:].contiguous(),
+                         gd[:, h:].contiguous(), b_cs, cu(cw), cu(cb), b_ssm, cu(dtb), cu(an), cu(dsk))
+    assert torch.equal(ya, torch.cat([y1, y2], 1))
+    assert torch.equal(a_ssm, b_ssm) and torch.equal(a_cs, b_cs)
+    ya_h, ssm_h = np_(ya), np_(a_ssm)
+    for b in (0, 255):
+        o_cs, o_ssm = cs[b:b + 1].copy(), ssm[b:b + 1].copy()
+        yr = O.conv_ssd_scan(x[b:b + 1], bm[b:b + 1], cm[b:b + 1], dt[b:b + 1], o_cs, cw, cb, dtb, an, dsk, o_ssm)
+        np.testing.assert_allclose(ya_h[b:b + 1], yr, atol=1e-4, rtol=1e-5)
+        np.testing.assert_allclose(ssm_h[b:b + 1], o_ssm, atol=1e-4, rtol=1e-5)
+
+
+# ------------------------------------------------------------- attention
+@pytest.mark.parametrize("split", [256, 2048])
+def test_rope_kv_attn_decode_full_size(split):
+    """Config: q,k,v [64,8,1,64], positions ~U[0,2048), cache [64,8,2048,64]."""
+    q, k, v, pos, kc, vc = synth.attn_decode_inputs()
+    g_kc, g_vc = cu(kc), cu(vc)
+    out = K.rope_kv_attn_decode(cu(q), cu(k), cu(v), g_kc, g_vc, cu(pos), split=split)
+    o_kc, o_vc = kc.copy(), vc.copy()
+    ref = O.rope_kv_attn_decode(q, k, v, o_kc, o_vc, pos)
+    np.testing.assert_allclose(np_(out), ref, atol=1e-4, rtol=1e-5)
+    gk, gv = np_(g_kc), np_(g_vc)
+    for b in range(64):
+        np.testing.assert_allclose(gk[b, :, pos[b]], o_kc[b, :, pos[b]], atol=1e-6, rtol=1e-6)
+        np.testing.assert_array_equal(gv[b, :, pos[b]], o_vc[b, :, pos[b]])
+        np.testing.assert_array_equal(gk[b, :, : pos[b]], kc[b, :, : pos[b]])  # history untouched
+
+
+@pytest.mark.parametrize("dh,ctx,posv", [(76, 16, [0, 15, 7]), (64, 300, [0, 63, 64, 299]), (76, 700, [699, 1, 256])])
+def test_rope_kv_attn_decode_edges(dh, ctx, posv):
+    """First slot, last slot, split boundaries, head dim 76 (19 float4s)."""
+    rng = np.random.default_rng(dh + ctx)
+    bsz, nh = len(posv), 8
+    q = rng.standard_normal((bsz, nh, dh)).astype(np.float32)
+    k = rng.standard_normal((bsz, nh, dh)).astype(np.float32)
+    v = rng.standard_normal((bsz, nh, dh)).astype(np.float32)
+    kc = rng.standard_normal((bsz, nh, ctx, dh)).astype(np.float32)
+    vc = rng.standard_normal((bsz, nh, ctx, dh)).astype(np.float32)
+    pos = np.array(posv, np.int32)
+    out = K.rope_kv_attn_decode(cu(q), cu(k), cu(v), cu(kc), cu(vc), cu(pos), split=64)
+    ref = O.rope_kv_attn_decode(q, k, v, kc.copy(), vc.copy(), pos)
+    np.testing.assert_allclose(np_(out), ref, atol=1e-4, rtol=1e-5)
+
+
+# ------------------------------------------------------------- sampling
+def test_greedy_matches_sampler():
+    rng = np.random.default_rng(6)
+    lg = rng.standard_normal((5, 2048)).astype(np.float32)
+    lg[1, 100] = lg[1, 700] = 50.0  # tie: the lower index wins
+    lg[2, :] = np.nan
+    lg[2, 3] = 1.0
+    lg[3, :] = -np.inf
+    tok = np_(K.greedy(cu(lg)))
+    assert [int(t) for t in tok] == [O.sample_greedy(lg[i], []) for i in range(5)]
+    assert tok[1] == 100 and tok[3] == 0
+    seen = np.zeros((5, 64), np.uint32)
+    ctx = [[int(np.argmax(lg[0]))], [100, 5], [], [1], list(range(0, 2048, 3))]
+    for b, c in enumerate(ctx):
+        for t in c:
+            seen[b, t // 32] |= np.uint32(1 << (t % 32))
+    tok = np_(K.greedy(cu(lg), cu(seen.view(np.int32)), 1.2))
+    assert [int(t) for t in tok] == [O.sample_greedy(lg[i], ctx[i], 1.2) for i in range(5)]
