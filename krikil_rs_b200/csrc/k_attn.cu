@@ -33,11 +33,16 @@ KRK_DEV void rope_pair(float& x0, float& x1, float c, float s) {
     x0 = a * c - b * s;
     x1 = a * s + b * c;
 }
+// The f32 operations are the reference's; powf, cosf and sinf are evaluated in
+// double precision and rounded once to f32 (a correctly rounded result, which
+// is what the host libm returns for all but rare arguments), because the angle
+// pos * invf reaches ~2047 rad and f32 library errors of a few ulps would show.
 KRK_DEV void rope_cs(int i, int dh, int pos, float theta, float& c, float& s) {
-    const float invf = 1.0f / powf(theta, ((float)i * 2.0f) / (float)dh);
+    const float e = ((float)i * 2.0f) / (float)dh;
+    const float invf = 1.0f / (float)pow((double)theta, (double)e);
     const float ang = (float)pos * invf;
-    c = cosf(ang);
-    s = sinf(ang);
+    c = (float)cos((double)ang);
+    s = (float)sin((double)ang);
 }
 
 constexpr int AD_THREADS = 128;

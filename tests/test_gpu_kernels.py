@@ -211,7 +211,7 @@ def test_rope_kv_attn_decode_full_size(split):
     np.testing.assert_allclose(np_(out), ref, atol=1e-4, rtol=1e-5)
     gk, gv = np_(g_kc), np_(g_vc)
     for b in range(64):
-        np.testing.assert_allclose(gk[b, :, pos[b]], o_kc[b, :, pos[b]], atol=1e-6, rtol=1e-6)
+        np.testing.assert_allclose(gk[b, :, pos[b]], o_kc[b, :, pos[b]], atol=1e-5, rtol=1e-5)
         np.testing.assert_array_equal(gv[b, :, pos[b]], o_vc[b, :, pos[b]])
         np.testing.assert_array_equal(gk[b, :, : pos[b]], kc[b, :, : pos[b]])  # history untouched
 
