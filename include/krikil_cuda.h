@@ -245,6 +245,26 @@ KRK_API int krk_k_rope_kv_attn_decode(const float* q, const float* k, const floa
                                       const int32_t* pos, float* out, float* work, int B, int H, int dh, int ctx,
                                       int split, float theta, void* stream);
 
+/* Allocation-free variant of krk_k_rope_kv_attn_decode (no counterpart in the
+ * reference, which has no device memory).  For callers that cannot allocate or
+ * pass device scratch -- a host that binds only this header and has no CUDA
+ * allocator of its own, or a process whose device memory belongs to another
+ * allocator or a fixed budget: the split partials go to a fixed array inside
+ * the library's device image, KRK_ATTN_NOALLOC_MAX_FLOATS floats (4 MiB) held by
+ * every GPU that loads the library until the process exits.  Same arguments and
+ * results as krk_k_rope_kv_attn_decode without `work`; when the cache needs
+ * more than one split and krk_attn_work_floats() exceeds the maximum, the call
+ * fails with KRK_INVALID before launching anything.  It calls no allocator.  The
+ * first call on a device looks up the array's device address (once per device,
+ * with that device current), so make it before any stream capture.  All calls on
+ * a GPU share the array: calls that overlap on the GPU race and must be
+ * serialised by the caller.  No part of the array needs clearing between calls
+ * (each call writes every partial it reads). */
+#define KRK_ATTN_NOALLOC_MAX_FLOATS (1 << 20)
+KRK_API int krk_k_rope_kv_attn_decode_noalloc(const float* q, const float* k, const float* v, float* kc, float* vc,
+                                              const int32_t* pos, float* out, int B, int H, int dh, int ctx,
+                                              int split, float theta, void* stream);
+
 /* Greedy pick (src/sampler.rs:50-80) per row of logits [B][ld]: repetition
  * penalty on tokens whose bit is set in seen [B][vocab/32] (seen may be NULL;
  * penalty 1 disables it), then the first maximum; tok [B]. */

@@ -55,6 +55,7 @@ _SIGS = {
     "krk_attn_work_floats": (C.c_size_t, [_i32, _i32, _i32, _i32, _i32]),
     "krk_k_rope_kv_attn_decode": (_i32, [_fp] * 8 + [_i32] * 5 + [_f32, _vp]),
     "krk_k_greedy": (_i32, [_fp, _i64, _i32, _i32, _vp, _f32, _vp, _vp]),
+    "krk_k_rope_kv_attn_decode_noalloc": (_i32, [_fp] * 7 + [_i32] * 5 + [_f32, _vp]),
 }
 
 for _name, (_res, _args) in _SIGS.items():

@@ -670,6 +670,11 @@ int reset_state(krk_state* s, const uint8_t* mask) {
 
 }  // namespace
 
+namespace krk {
+// Sets the calling thread's krk_last_error() message (for other translation units).
+int report_error(int status, const std::string& msg) { return fail(status, msg); }
+}  // namespace krk
+
 // =================================================================== C ABI
 extern "C" {
 
