@@ -55,6 +55,8 @@ def parse_args():
     ap.add_argument("--no-kernels", action="store_true", help="skip the per-kernel table")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
+    ap.add_argument("--kernels-only", action="store_true", help="only the per-kernel table")
+    ap.add_argument("--scan-t", type=int, default=2048, help="tokens of the conv+SSD scan case")
     return ap.parse_args()
 
 
@@ -193,7 +195,7 @@ def workload_config(args):
 
 
 # ----------------------------------------------------------------- per-kernel table
-def kernel_table(torch, peak):
+def kernel_table(torch, peak, scan_t=2048):
     from krikil_rs_b200 import kernels as K, synth
     dev = torch.device("cuda")
     res = {}
@@ -242,7 +244,7 @@ def kernel_table(torch, peak):
     put("conv_ssd_step[256,16,64,128]", nb,
         timeit(lambda: K.conv_ssd_step(xs, bm, cm, dt, cs, cw, cb, ssm, dtb, an, dsk, ys)))
 
-    T = 2048
+    T = scan_t
     xs, bm, cm, dt, cs0, ssm0 = synth.conv_ssd_inputs(256, T, seed=5, state_scale=0.0)
     xs, bm, cm, dt = (torch.from_numpy(a).to(dev) for a in (xs, bm, cm, dt))
     cs, ssm = torch.from_numpy(cs0).to(dev), torch.from_numpy(ssm0).to(dev)
@@ -251,7 +253,7 @@ def kernel_table(torch, peak):
     ms = timeit(lambda: K.conv_ssd_scan(xs, bm, cm, dt, cs, cw, cb, ssm, dtb, an, dsk, yt), iters=3, warm=1)
     flops = 256 * T * 16 * 64 * 128 * 5  # per state element per token: 2 mul + 1 add (update), mul + add (y)
     fp32_peak = 148 * 128 * 2 * 1.965e9  # nominal FP32 SIMT FLOP/s (no measured figure exists)
-    put("conv_ssd_scan[256,2048,16,64,128]", nb, ms,
+    put(f"conv_ssd_scan[256,{T},16,64,128]", nb, ms,
         {"tflops": round(flops / (ms * 1e-3) / 1e12, 2), "fp32_frac_nominal": round(flops / (ms * 1e-3) / fp32_peak, 3)})
     del xs, bm, cm, dt, yt
     torch.cuda.empty_cache()
@@ -381,7 +383,7 @@ def run_ours(args):
         "clocks": clk,
     }
     if not args.no_kernels:
-        line["kernels"] = kernel_table(torch, peak)
+        line["kernels"] = kernel_table(torch, peak, args.scan_t)
     if not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(args, args.cpu_seconds)
     print(json.dumps(line), flush=True)
@@ -395,6 +397,10 @@ def main():
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
     if args.impl == "reference":
         run_reference(args)
+    elif args.kernels_only:
+        import torch
+        peak, kind = measured_peaks()
+        print(json.dumps({"kernels": kernel_table(torch, peak, args.scan_t), "peak_gbs": peak, "peak_kind": kind}))
     else:
         run_ours(args)
 
