@@ -199,10 +199,16 @@ KRK_API int krk_k_gated_rmsnorm_residual(const float* x, const float* z, const f
  * with the reference dot's exact rounding.  At: A feature-major [K][lda];
  * Wt: W K-major [K][ldw]; C batch-major [M][ldc] (out_fm = 0) or
  * feature-major [N][ldc] (out_fm = 1).  epilogue 0: store, 1: C += result
- * (residual), 2: store gelu(result) (src/math.rs:17-39).  M % 64 == 0,
+ * (residual), 2: store gelu(result) (src/math.rs:17-39).  M % 32 == 0,
  * N % 32 == 0, K % 32 == 0, leading dims % 4 == 0, pointers 16-byte aligned. */
 KRK_API int krk_k_gemm(const float* At, int lda, const float* Wt, int ldw, float* C, int ldc, int M, int N, int K,
                        int epilogue, int out_fm, void* stream);
+
+/* krk_k_gemm with an explicit CTA tile height: 64 or 32 output rows per CTA
+ * (M must be a multiple of it), 0 = the automatic choice krk_k_gemm makes.
+ * Every choice gives bit-identical results. */
+KRK_API int krk_k_gemm_tiled(const float* At, int lda, const float* Wt, int ldw, float* C, int ldc, int M, int N,
+                             int K, int epilogue, int out_fm, int tile_rows, void* stream);
 
 /* Embedding gather (src/model.rs:330-338, :598) into feature-major
  * out[k*ldo + m] = wte[tok[m]*K + k]. */

@@ -193,6 +193,7 @@ struct krk_state {
     int32_t* slimit_d = nullptr;
     int32_t* step_d = nullptr;
     float *h_t, *hn_t, *zx, *y_t, *yn_t, *qkv, *ao_t, *mlp_t, *logits, *attn_work;
+    float2* rope = nullptr;  // (cos, sin) per [position][pair], from the host libm as src/math.rs:243-247
     int attn_split = 2048;
     std::vector<int64_t> pos_h;
     PrefillWs pre;
@@ -327,7 +328,7 @@ void create_state(krk_state* s, const krk_model* m, int B, int ctx) {
     b.add<int32_t>(B); b.add<int32_t>(B); b.add<int32_t>(1);
     b.add<float>(HID * Mp); b.add<float>(HID * Mp); b.add<float>(Mp * DIP_PAD); b.add<float>(DI * Mp);
     b.add<float>(DI * Mp); b.add<float>(Mp * QKV); b.add<float>(HID * Mp); b.add<float>(INTER * Mp);
-    b.add<float>(Mp * VOC); b.add<float>(work);
+    b.add<float>(Mp * VOC); b.add<float>(work); b.add<float2>((size_t)ctx * (HD / 2));
     s->arena.reserve(b.bytes);
     for (int l = 0; l < NL; ++l) {
         if (is_mamba(l)) {
@@ -355,7 +356,19 @@ void create_state(krk_state* s, const krk_model* m, int B, int ctx) {
     s->mlp_t = s->arena.take<float>(INTER * Mp);
     s->logits = s->arena.take<float>(Mp * VOC);
     s->attn_work = s->arena.take<float>(work);
+    s->rope = s->arena.take<float2>((size_t)ctx * (HD / 2));
     ck(cudaMemsetAsync(s->arena.base, 0, s->arena.cap, m->stream), "state memset");
+    // RoPE coefficients exactly as src/math.rs:243-247 computes them, with the
+    // host's f32 powf / cosf / sinf (the functions the reference calls).
+    std::vector<float2> rope((size_t)ctx * (HD / 2));
+    for (int p = 0; p < ctx; ++p)
+        for (int i = 0; i < HD / 2; ++i) {
+            const float invf = 1.0f / powf(THETA, ((float)i * 2.0f) / (float)HD);
+            const float ang = (float)p * invf;
+            rope[(size_t)p * (HD / 2) + i] = make_float2(cosf(ang), sinf(ang));
+        }
+    ck(cudaMemcpyAsync(s->rope, rope.data(), rope.size() * sizeof(float2), cudaMemcpyHostToDevice, m->stream),
+       "rope table");
     ck(cudaStreamSynchronize(m->stream), "state init");
     s->pos_h.assign(B, 0);
 }
@@ -493,6 +506,7 @@ void decode_forward(krk_state* s, const uint8_t* active) {
             a.out = s->ao_t; a.o_sb = 1; a.o_sh = (int64_t)HD * Mp; a.o_sd = Mp;
             a.work = s->attn_work;
             a.B = B; a.H = NH; a.dh = HD; a.ctx = s->ctx; a.split = s->attn_split; a.theta = THETA;
+            a.rope = s->rope;
             timed(s, KRK_PROF_ATTN_DECODE, [&] { kk(krk::attn_decode(a, st), "attention"); });
             timed(s, KRK_PROF_GEMM, [&] { kk(krk::gemm(s->ao_t, Mp, L.wo_t, HID, s->h_t, Mp, Mp, HID, HID, krk::EPI_RESIDUAL, true, st), "wo"); });
             timed(s, KRK_PROF_NORM, [&] { kk(krk::rmsnorm_fm(s->h_t, Mp, L.ln2, RMS_EPS, HID, B, s->hn_t, Mp, st), "ln2"); });
@@ -544,7 +558,7 @@ void prefill_group(krk_state* s, int g0, int S, int64_t rows) {
             float* kc = s->kc[l] + (size_t)g0 * s->ctx * HID;
             float* vc = s->vc[l] + (size_t)g0 * s->ctx * HID;
             const int64_t c_sb = (int64_t)s->ctx * HID;
-            timed(s, KRK_PROF_OTHER, [&] { kk(krk::rope_kv_prefill(w.qkv, QKV, kc, vc, c_sb, HD, HID, w.cu, w.start, S, NH, HD, R, THETA, st),
+            timed(s, KRK_PROF_OTHER, [&] { kk(krk::rope_kv_prefill(w.qkv, QKV, kc, vc, c_sb, HD, HID, w.cu, w.start, S, NH, HD, R, THETA, s->rope, st),
                "rope/kv"); });
             timed(s, KRK_PROF_ATTN_PREFILL, [&] { kk(krk::attn_prefill(w.qkv, QKV, kc, vc, c_sb, HD, HID, w.cu, w.start, w.row_seq, S, NH, HD, R, s->ctx,
                                  w.ao_t, 1, T, st),
@@ -652,6 +666,18 @@ int cuda_status(cudaError_t e, const char* what) {
 int reset_state(krk_state* s, const uint8_t* mask) {
     DeviceGuard g(s->m->device);
     cudaStream_t st = s->m->stream;
+    if (!mask) {  // every sequence: one memset per array
+        for (int l = 0; l < NL; ++l) {
+            if (!is_mamba(l)) continue;
+            kk(cudaMemsetAsync(s->conv[l], 0, (size_t)s->B * DXBC * 4 * 4, st), "reset conv");
+            kk(cudaMemsetAsync(s->ssm[l], 0, (size_t)s->B * MH * MP * DS * 4, st), "reset ssm");
+        }
+        kk(cudaMemsetAsync(s->seen_d, 0, (size_t)s->B * SEEN_WORDS * 4, st), "reset seen");
+        kk(cudaMemsetAsync(s->pos_d, 0, (size_t)s->B * 4, st), "reset pos");
+        std::fill(s->pos_h.begin(), s->pos_h.end(), 0);
+        kk(cudaStreamSynchronize(st), "reset");
+        return KRK_OK;
+    }
     for (int b = 0; b < s->B; ++b) {
         if (mask && !mask[b]) continue;
         s->pos_h[b] = 0;
@@ -992,6 +1018,14 @@ int krk_k_gemm(const float* At, int lda, const float* Wt, int ldw, float* C, int
                        "gemm");
 }
 
+int krk_k_gemm_tiled(const float* At, int lda, const float* Wt, int ldw, float* C, int ldc, int M, int N, int K,
+                     int epilogue, int out_fm, int tile_rows, void* stream) {
+    if (epilogue < 0 || epilogue > 2) return fail(KRK_INVALID, "epilogue must be 0, 1 or 2");
+    return cuda_status(
+        krk::gemm_tiled(At, lda, Wt, ldw, C, ldc, M, N, K, epilogue, out_fm != 0, tile_rows, (cudaStream_t)stream),
+        "gemm");
+}
+
 int krk_k_embed(const uint32_t* tok, const float* wte, int vocab, int K, int M, float* out, int ldo, void* stream) {
     return cuda_status(krk::embed_fm(tok, wte, vocab, K, M, out, ldo, (cudaStream_t)stream), "embed");
 }
@@ -1049,6 +1083,7 @@ int krk_k_rope_kv_attn_decode(const float* q, const float* k, const float* v, fl
     a.out = out; a.o_sb = (int64_t)H * dh; a.o_sh = dh; a.o_sd = 1;
     a.work = work;
     a.B = B; a.H = H; a.dh = dh; a.ctx = ctx; a.split = split <= 0 ? 256 : split; a.theta = theta;
+    a.rope = nullptr;
     return cuda_status(krk::attn_decode(a, (cudaStream_t)stream), "rope_kv_attn_decode");
 }
 

@@ -104,7 +104,13 @@ __global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(AttnDecodeArgs 
     __syncthreads();
     if (tid < HALF) {  // src/model.rs:721-728
         float c, s;
-        rope_cs(tid, DH, pos, a.theta, c, s);
+        if (a.rope) {
+            const float2 cs = a.rope[(size_t)pos * HALF + tid];
+            c = cs.x;
+            s = cs.y;
+        } else {
+            rope_cs(tid, DH, pos, a.theta, c, s);
+        }
         rope_pair(qs[tid], qs[tid + HALF], c, s);
         rope_pair(kn[tid], kn[tid + HALF], c, s);
     }
@@ -226,7 +232,7 @@ __global__ void attn_combine_kernel(AttnDecodeArgs a, int max_splits) {
 __global__ void rope_kv_prefill_kernel(float* __restrict__ qkv, int64_t q_rs, float* __restrict__ kc,
                                        float* __restrict__ vc, int64_t c_sb, int64_t c_sh, int64_t c_st,
                                        const int32_t* __restrict__ cu, const int32_t* __restrict__ start, int S,
-                                       int H, int dh, int total_rows, float theta) {
+                                       int H, int dh, int total_rows, float theta, const float2* __restrict__ rope) {
     const int half = dh / 2;
     const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (gid >= (int64_t)total_rows * H * half) return;
@@ -241,7 +247,13 @@ __global__ void rope_kv_prefill_kernel(float* __restrict__ qkv, int64_t q_rs, fl
     const int sq = lo;
     const int pos = start[sq] + (row - cu[sq]);
     float c, s;
-    rope_cs(i, dh, pos, theta, c, s);
+    if (rope) {
+        const float2 cs = rope[(size_t)pos * half + i];
+        c = cs.x;
+        s = cs.y;
+    } else {
+        rope_cs(i, dh, pos, theta, c, s);
+    }
     float* qr = qkv + (size_t)row * q_rs + (size_t)h * dh;
     float* kr = qkv + (size_t)row * q_rs + (size_t)H * dh + (size_t)h * dh;
     const float* vr = qkv + (size_t)row * q_rs + (size_t)2 * H * dh + (size_t)h * dh;
@@ -355,12 +367,12 @@ cudaError_t attn_decode(const AttnDecodeArgs& a, cudaStream_t s) {
 
 cudaError_t rope_kv_prefill(float* qkv, int64_t q_rs, float* kc, float* vc, int64_t c_sb, int64_t c_sh,
                             int64_t c_st, const int32_t* cu_seqlens, const int32_t* start, int S, int H, int dh,
-                            int total_rows, float theta, cudaStream_t s) {
+                            int total_rows, float theta, const float2* rope, cudaStream_t s) {
     if (S <= 0 || H <= 0 || dh <= 0 || (dh & 1) || total_rows <= 0) return cudaErrorInvalidValue;
     const int64_t n = (int64_t)total_rows * H * (dh / 2);
     rope_kv_prefill_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(qkv, q_rs, kc, vc, c_sb, c_sh, c_st,
                                                                        cu_seqlens, start, S, H, dh, total_rows,
-                                                                       theta);
+                                                                       theta, rope);
     add_launches(1);
     return cudaGetLastError();
 }

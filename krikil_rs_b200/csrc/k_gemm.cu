@@ -21,15 +21,23 @@
 namespace krk {
 namespace {
 
-constexpr int BM = 64, BN = 32, BK = 32, NSTAGE = 3, NT = 256;
-constexpr int A_TILE = BK * BM;
+constexpr int BN = 32, BK = 32, NSTAGE = 3, NT = 256;
 constexpr int W_TILE = BK * BN;
-constexpr int STAGE = A_TILE + W_TILE;
 constexpr int RLD_BM = BN + 4;  // partials red[w][m][n] for batch-major output
-constexpr int RLD_FM = BM + 4;  // partials red[w][n][m] for feature-major output
-constexpr int RED_FLOATS = 8 * BM * RLD_BM;
-constexpr int SMEM_FLOATS = RED_FLOATS > NSTAGE * STAGE ? RED_FLOATS : NSTAGE * STAGE;
-constexpr size_t SMEM_BYTES = SMEM_FLOATS * sizeof(float);
+
+template <int BM>
+struct Tile {
+    static constexpr int TM = BM / 8;                 // rows per thread (8 lanes of rows per warp)
+    static constexpr int A_TILE = BK * BM;
+    static constexpr int STAGE = A_TILE + W_TILE;
+    static constexpr int RLD_FM = BM + 4;             // partials red[w][n][m] for feature-major output
+    static constexpr int RED = 8 * BM * RLD_BM > 8 * BN * RLD_FM ? 8 * BM * RLD_BM : 8 * BN * RLD_FM;
+    static constexpr int SMEM_FLOATS = RED > NSTAGE * STAGE ? RED : NSTAGE * STAGE;
+    static constexpr size_t SMEM_BYTES = SMEM_FLOATS * sizeof(float);
+    static constexpr int A_F4 = A_TILE / 4 / NT;      // float4 copies per thread per K-block
+    static constexpr int OUT_F4 = BM * BN / 4 / NT;   // output float4s per thread
+    static constexpr int MIN_CTAS = BM == 64 ? 2 : 3;
+};
 
 KRK_DEV float4 f4add(float4 a, float4 b) { return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w); }
 
@@ -39,10 +47,20 @@ KRK_DEV float4 fold8(const float4* l) {
     return f4add(f4add(s04, s26), f4add(s15, s37));
 }
 
-template <int EPI, bool OUT_FM>
-__global__ void __launch_bounds__(NT, 2)
+// Thread (lm, ln) of a warp owns rows m(r) and columns n(c), r < TM, c < 8:
+//   BM = 64: m in {lm*4 + i, 32 + lm*4 + i};  BM = 32: m = lm*4 + i
+//   n in {ln*4 + j, 16 + ln*4 + j}
+// so each 16-byte shared load of a warp hits distinct banks.
+template <int BM>
+KRK_DEV int row_of(int lm, int r) { return (r < 4) ? lm * 4 + r : 32 + lm * 4 + (r - 4); }
+KRK_DEV int col_of(int ln, int c) { return (c < 4) ? ln * 4 + c : 16 + ln * 4 + (c - 4); }
+
+template <int BM, int EPI, bool OUT_FM>
+__global__ void __launch_bounds__(NT, Tile<BM>::MIN_CTAS)
     gemm_lane8_kernel(const float* __restrict__ At, int lda, const float* __restrict__ Wt, int ldw,
                       float* __restrict__ C, int ldc, int K) {
+    using T = Tile<BM>;
+    constexpr int TM = T::TM;
     extern __shared__ __align__(16) float sm[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int lm = lane >> 2, ln = lane & 3;
@@ -50,24 +68,22 @@ __global__ void __launch_bounds__(NT, 2)
     const int nkb = K / BK;
 
     auto load_stage = [&](int kb, int st) {
-        float* As = sm + st * STAGE;
-        float* Ws = As + A_TILE;
+        float* As = sm + st * T::STAGE;
+        float* Ws = As + T::A_TILE;
         const int k0 = kb * BK;
 #pragma unroll
-        for (int j = 0; j < 2; ++j) {
+        for (int j = 0; j < T::A_F4; ++j) {
             int idx = tid + j * NT;
-            int r = idx >> 4, c4 = idx & 15;
+            int r = idx / (BM / 4), c4 = idx % (BM / 4);
             cp_async16(As + r * BM + c4 * 4, At + (size_t)(k0 + r) * lda + m0 + c4 * 4);
         }
         int r = tid >> 3, c4 = tid & 7;
         cp_async16(Ws + r * BN + c4 * 4, Wt + (size_t)(k0 + r) * ldw + n0 + c4 * 4);
     };
 
-    // Thread (lm, ln) owns m in {lm*4+i, 32+lm*4+i} and n in {ln*4+j, 16+ln*4+j}
-    // (i, j < 4), so each 16-byte shared load of a warp hits distinct banks.
-    float acc[8][8];
+    float acc[TM][8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i)
+    for (int i = 0; i < TM; ++i)
 #pragma unroll
         for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
 
@@ -82,19 +98,26 @@ __global__ void __launch_bounds__(NT, 2)
         const int pf = kb + NSTAGE - 1;
         if (pf < nkb) load_stage(pf, pf % NSTAGE);
         cp_async_commit();
-        const float* As = sm + (kb % NSTAGE) * STAGE;
-        const float* Ws = As + A_TILE;
+        const float* As = sm + (kb % NSTAGE) * T::STAGE;
+        const float* Ws = As + T::A_TILE;
 #pragma unroll
         for (int i = 0; i < BK / 8; ++i) {
             const int k = warp + 8 * i;  // this warp's lane of the reference dot
-            float4 a0 = *reinterpret_cast<const float4*>(As + k * BM + lm * 4);
-            float4 a1 = *reinterpret_cast<const float4*>(As + k * BM + 32 + lm * 4);
-            float4 w0 = *reinterpret_cast<const float4*>(Ws + k * BN + ln * 4);
-            float4 w1 = *reinterpret_cast<const float4*>(Ws + k * BN + 16 + ln * 4);
-            const float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+            float a[TM];
+            {
+                const float4 a0 = *reinterpret_cast<const float4*>(As + k * BM + lm * 4);
+                a[0] = a0.x; a[1] = a0.y; a[2] = a0.z; a[3] = a0.w;
+                if (TM == 8) {
+                    const float4 a1 = *reinterpret_cast<const float4*>(As + k * BM + 32 + lm * 4);
+                    a[TM == 8 ? 4 : 0] = a1.x; a[TM == 8 ? 5 : 1] = a1.y;
+                    a[TM == 8 ? 6 : 2] = a1.z; a[TM == 8 ? 7 : 3] = a1.w;
+                }
+            }
+            const float4 w0 = *reinterpret_cast<const float4*>(Ws + k * BN + ln * 4);
+            const float4 w1 = *reinterpret_cast<const float4*>(Ws + k * BN + 16 + ln * 4);
             const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
-            for (int r = 0; r < 8; ++r)
+            for (int r = 0; r < TM; ++r)
 #pragma unroll
                 for (int c = 0; c < 8; ++c) acc[r][c] = fmaf(a[r], w[c], acc[r][c]);
         }
@@ -108,26 +131,26 @@ __global__ void __launch_bounds__(NT, 2)
     if (!OUT_FM) {
         float* base = red + warp * (BM * RLD_BM);
 #pragma unroll
-        for (int r = 0; r < 8; ++r) {
-            const int m = (r < 4) ? lm * 4 + r : 32 + lm * 4 + (r - 4);
-            float* d = base + m * RLD_BM;
+        for (int r = 0; r < TM; ++r) {
+            float* d = base + row_of<BM>(lm, r) * RLD_BM;
             *reinterpret_cast<float4*>(d + ln * 4) = make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
             *reinterpret_cast<float4*>(d + 16 + ln * 4) = make_float4(acc[r][4], acc[r][5], acc[r][6], acc[r][7]);
         }
     } else {
-        float* base = red + warp * (BN * RLD_FM);
+        float* base = red + warp * (BN * T::RLD_FM);
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
-            const int n = (c < 4) ? ln * 4 + c : 16 + ln * 4 + (c - 4);
-            float* d = base + n * RLD_FM;
+            float* d = base + col_of(ln, c) * T::RLD_FM;
             *reinterpret_cast<float4*>(d + lm * 4) = make_float4(acc[0][c], acc[1][c], acc[2][c], acc[3][c]);
-            *reinterpret_cast<float4*>(d + 32 + lm * 4) = make_float4(acc[4][c], acc[5][c], acc[6][c], acc[7][c]);
+            if (TM == 8)
+                *reinterpret_cast<float4*>(d + 32 + lm * 4) = make_float4(
+                    acc[TM == 8 ? 4 : 0][c], acc[TM == 8 ? 5 : 1][c], acc[TM == 8 ? 6 : 2][c], acc[TM == 8 ? 7 : 3][c]);
         }
     }
     __syncthreads();
 
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
+    for (int j = 0; j < T::OUT_F4; ++j) {
         const int idx = tid + j * NT;
         const float* part;
         int wstride;
@@ -138,9 +161,9 @@ __global__ void __launch_bounds__(NT, 2)
             wstride = BM * RLD_BM;
             out = C + (size_t)(m0 + m) * ldc + n0 + n4 * 4;
         } else {
-            const int n = idx >> 4, m4 = idx & 15;
-            part = red + n * RLD_FM + m4 * 4;
-            wstride = BN * RLD_FM;
+            const int n = idx / (BM / 4), m4 = idx % (BM / 4);
+            part = red + n * T::RLD_FM + m4 * 4;
+            wstride = BN * T::RLD_FM;
             out = C + (size_t)(n0 + n) * ldc + m0 + m4 * 4;
         }
         float4 l[8];
@@ -157,34 +180,69 @@ __global__ void __launch_bounds__(NT, 2)
     }
 }
 
-template <int EPI, bool OUT_FM>
+template <int BM, int EPI, bool OUT_FM>
 cudaError_t launch(const float* At, int lda, const float* Wt, int ldw, float* C, int ldc, int M, int N, int K,
                    cudaStream_t s) {
     static DeviceOnce once;
-    cudaError_t e = once.set_smem((const void*)gemm_lane8_kernel<EPI, OUT_FM>, SMEM_BYTES);
+    cudaError_t e = once.set_smem((const void*)gemm_lane8_kernel<BM, EPI, OUT_FM>, Tile<BM>::SMEM_BYTES);
     if (e != cudaSuccess) return e;
     dim3 grid(M / BM, N / BN);
-    gemm_lane8_kernel<EPI, OUT_FM><<<grid, NT, SMEM_BYTES, s>>>(At, lda, Wt, ldw, C, ldc, K);
+    gemm_lane8_kernel<BM, EPI, OUT_FM><<<grid, NT, Tile<BM>::SMEM_BYTES, s>>>(At, lda, Wt, ldw, C, ldc, K);
     add_launches(1);
     return cudaGetLastError();
 }
 
+template <int BM>
+cudaError_t dispatch(const float* At, int lda, const float* Wt, int ldw, float* C, int ldc, int M, int N, int K,
+                     int epilogue, bool out_fm, cudaStream_t s) {
+    switch (epilogue * 2 + (out_fm ? 1 : 0)) {
+        case EPI_STORE * 2 + 0: return launch<BM, EPI_STORE, false>(At, lda, Wt, ldw, C, ldc, M, N, K, s);
+        case EPI_STORE * 2 + 1: return launch<BM, EPI_STORE, true>(At, lda, Wt, ldw, C, ldc, M, N, K, s);
+        case EPI_RESIDUAL * 2 + 0: return launch<BM, EPI_RESIDUAL, false>(At, lda, Wt, ldw, C, ldc, M, N, K, s);
+        case EPI_RESIDUAL * 2 + 1: return launch<BM, EPI_RESIDUAL, true>(At, lda, Wt, ldw, C, ldc, M, N, K, s);
+        case EPI_GELU * 2 + 0: return launch<BM, EPI_GELU, false>(At, lda, Wt, ldw, C, ldc, M, N, K, s);
+        case EPI_GELU * 2 + 1: return launch<BM, EPI_GELU, true>(At, lda, Wt, ldw, C, ldc, M, N, K, s);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+int sm_count() {
+    static int n = 0;
+    if (!n) {
+        int dev = 0, v = 148;
+        cudaGetDevice(&dev);
+        if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) v = 148;
+        n = v;
+    }
+    return n;
+}
+
 }  // namespace
+
+// Tile choice: 32-row tiles (3 CTAs per SM, ~10% lower FMA rate than the
+// 64-row tile at full occupancy, measured on B200) only when 64-row tiles would
+// fill fewer than 1.5 waves of 2 CTAs per SM -- e.g. the 608-column projections
+// at batch 1024 (304 tiles on 296 slots).  Both give bit-identical results.
+int gemm_tile_rows(int M, int N) {
+    if (M % 64) return 32;
+    const int64_t t64 = (int64_t)(M / 64) * (N / BN);
+    return 2 * t64 < 3 * (int64_t)sm_count() * 2 ? 32 : 64;
+}
+
+cudaError_t gemm_tiled(const float* At, int lda, const float* Wt, int ldw, float* C, int ldc, int M, int N, int K,
+                       int epilogue, bool out_fm, int tile_rows, cudaStream_t s) {
+    if (tile_rows == 0) tile_rows = gemm_tile_rows(M, N);
+    if (M <= 0 || N <= 0 || K <= 0 || (tile_rows != 32 && tile_rows != 64) || M % tile_rows || N % BN || K % BK ||
+        lda % 4 || ldw % 4 || ldc % 4 || lda < M || ldw < N || ldc < (out_fm ? M : N) ||
+        ((uintptr_t)At | (uintptr_t)Wt | (uintptr_t)C) % 16)
+        return cudaErrorInvalidValue;
+    if (tile_rows == 32) return dispatch<32>(At, lda, Wt, ldw, C, ldc, M, N, K, epilogue, out_fm, s);
+    return dispatch<64>(At, lda, Wt, ldw, C, ldc, M, N, K, epilogue, out_fm, s);
+}
 
 cudaError_t gemm(const float* At, int lda, const float* Wt, int ldw, float* C, int ldc, int M, int N, int K,
                  int epilogue, bool out_fm, cudaStream_t s) {
-    if (M <= 0 || N <= 0 || K <= 0 || M % BM || N % BN || K % BK || lda % 4 || ldw % 4 || ldc % 4 || lda < M ||
-        ldw < N || ldc < (out_fm ? M : N) || ((uintptr_t)At | (uintptr_t)Wt | (uintptr_t)C) % 16)
-        return cudaErrorInvalidValue;
-    switch (epilogue * 2 + (out_fm ? 1 : 0)) {
-        case EPI_STORE * 2 + 0: return launch<EPI_STORE, false>(At, lda, Wt, ldw, C, ldc, M, N, K, s);
-        case EPI_STORE * 2 + 1: return launch<EPI_STORE, true>(At, lda, Wt, ldw, C, ldc, M, N, K, s);
-        case EPI_RESIDUAL * 2 + 0: return launch<EPI_RESIDUAL, false>(At, lda, Wt, ldw, C, ldc, M, N, K, s);
-        case EPI_RESIDUAL * 2 + 1: return launch<EPI_RESIDUAL, true>(At, lda, Wt, ldw, C, ldc, M, N, K, s);
-        case EPI_GELU * 2 + 0: return launch<EPI_GELU, false>(At, lda, Wt, ldw, C, ldc, M, N, K, s);
-        case EPI_GELU * 2 + 1: return launch<EPI_GELU, true>(At, lda, Wt, ldw, C, ldc, M, N, K, s);
-        default: return cudaErrorInvalidValue;
-    }
+    return gemm_tiled(At, lda, Wt, ldw, C, ldc, M, N, K, epilogue, out_fm, 0, s);
 }
 
 }  // namespace krk

@@ -168,7 +168,7 @@ __global__ void __launch_bounds__(256) ssd_scan_kernel(SsdScanArgs a) {
     float* sda = sdt + SCAN_CH;           // [CH]
     float* sy = sda + SCAN_CH;            // [P][CH+1]
 
-    const int sq = blockIdx.x, h = blockIdx.y;
+    const int h = blockIdx.x, sq = blockIdx.y;  // heads of a sequence adjacent: B, C shared in L2
     const int tid = threadIdx.x, p = tid >> 2, q = tid & 3;
     const int r0 = a.cu_seqlens ? a.cu_seqlens[sq] : sq * a.uniform_len;
     const int r1 = a.cu_seqlens ? a.cu_seqlens[sq + 1] : (sq + 1) * a.uniform_len;
@@ -317,7 +317,8 @@ cudaError_t ssd_scan(const SsdScanArgs& a, bool conv, cudaStream_t s) {
         (a.z && (a.z_rs & 3)) || (!a.cu_seqlens && a.uniform_len <= 0) ||
         (((uintptr_t)a.bm | (uintptr_t)a.cm | (uintptr_t)a.ssm | (uintptr_t)a.x | (uintptr_t)a.z) & 15))
         return cudaErrorInvalidValue;
-    dim3 grid(a.S, a.H);
+    if (a.S > 65535) return cudaErrorInvalidValue;
+    dim3 grid(a.H, a.S);
     cudaError_t e;
 #define KRK_SCAN(CV, GT)                                                                              \
     {                                                                                                 \

@@ -27,53 +27,56 @@ namespace {
 // ---------------------------------------------------------------------------
 // Feature-major RMSNorm: out[k][m] = x[k][m] * scale(m) * w[k].
 //
-// One CTA owns 32 columns (sequences).  The [K][32] column block is staged
-// into shared memory with cp.async by all 8 warps at once (a single memory
-// round trip), then warp 0 forms every column's sum of squares in exactly the
-// reference's order -- lane m adds x[k][m]^2 for k = 0..K-1 one after the
-// other (src/math.rs:45-48) -- and all warps write the normalised block
-// (x * scale) * w (src/math.rs:51-53).  K <= 1216.
+// One CTA owns 8 columns (sequences).  The [K][8] column block is staged into
+// shared memory with cp.async by all threads at once (a single memory round
+// trip), then thread m forms column m's sum of squares in exactly the
+// reference's order -- x[k][m]^2 added for k = 0..K-1 one after the other
+// (src/math.rs:45-48), a latency-bound chain, hence few columns per CTA and
+// many CTAs -- and all threads write the normalised block (x * scale) * w
+// (src/math.rs:51-53).  K <= 1216.
 // ---------------------------------------------------------------------------
-constexpr int NORM_COLS = 32;
+constexpr int NORM_COLS = 8;
 constexpr int NORM_MAXK = 1216;
 
 __global__ void __launch_bounds__(256) rmsnorm_fm_kernel(const float* __restrict__ x, int ldx,
                                                          const float* __restrict__ w, float eps, int K, int M,
                                                          float* __restrict__ out, int ldo) {
-    extern __shared__ __align__(16) float blk[];  // [K][32]
+    extern __shared__ __align__(16) float blk[];  // [K][NORM_COLS]
     __shared__ float scale_s[NORM_COLS];
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int tid = threadIdx.x;
     const int m0 = blockIdx.x * NORM_COLS;
     const int ncols = min(NORM_COLS, M - m0);
     const bool full = (ncols == NORM_COLS) && ((ldx & 3) == 0) && ((((uintptr_t)x) & 15) == 0);
     if (full) {
-        for (int i = tid; i < K * 8; i += 256) {
-            int k = i >> 3, c4 = i & 7;
+        for (int i = tid; i < K * (NORM_COLS / 4); i += 256) {
+            int k = i / (NORM_COLS / 4), c4 = i % (NORM_COLS / 4);
             cp_async16(blk + k * NORM_COLS + c4 * 4, x + (size_t)k * ldx + m0 + c4 * 4);
         }
         cp_async_commit();
         cp_async_wait<0>();
     } else {
         for (int i = tid; i < K * NORM_COLS; i += 256) {
-            int k = i >> 5, c = i & 31;
+            int k = i / NORM_COLS, c = i % NORM_COLS;
             blk[i] = c < ncols ? x[(size_t)k * ldx + m0 + c] : 0.0f;
         }
     }
     __syncthreads();
-    if (warp == 0) {
+    if (tid < NORM_COLS) {
         float ss = 0.0f;
 #pragma unroll 8
         for (int k = 0; k < K; ++k) {
-            float v = blk[k * NORM_COLS + lane];
+            float v = blk[k * NORM_COLS + tid];
             ss += v * v;
         }
         float mean = ss / (float)K;
-        scale_s[lane] = 1.0f / sqrtf(mean + eps);
+        scale_s[tid] = 1.0f / sqrtf(mean + eps);
     }
     __syncthreads();
-    if (lane < ncols) {
-        const float sc = scale_s[lane];
-        for (int k = warp; k < K; k += 8) out[(size_t)k * ldo + m0 + lane] = blk[k * NORM_COLS + lane] * sc * w[k];
+    const int c = tid % NORM_COLS;
+    if (c < ncols) {
+        const float sc = scale_s[c];
+        for (int k = tid / NORM_COLS; k < K; k += 256 / NORM_COLS)
+            out[(size_t)k * ldo + m0 + c] = blk[k * NORM_COLS + c] * sc * w[k];
     }
 }
 

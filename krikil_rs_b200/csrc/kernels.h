@@ -22,10 +22,15 @@ struct DeviceOnce {
 //   At: A stored feature-major, At[k*lda + m]  (M columns, K rows)
 //   Wt: W stored K-major,       Wt[k*ldw + n]
 //   out_fm=false: C[m*ldc + n];  out_fm=true: C[n*ldc + m]
-// M % 64 == 0, N % 32 == 0, K % 32 == 0; leading dims % 4 == 0; 16-B aligned.
+// M % 32 == 0, N % 32 == 0, K % 32 == 0; leading dims % 4 == 0; 16-B aligned.
 enum GemmEpilogue { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_GELU = 2 };
 cudaError_t gemm(const float* At, int lda, const float* Wt, int ldw, float* C, int ldc, int M, int N, int K,
                  int epilogue, bool out_fm, cudaStream_t s);
+// Rows per CTA tile (64 or 32) gemm() uses for an M x N output.
+int gemm_tile_rows(int M, int N);
+// gemm() with an explicit CTA tile height (32 or 64; 0 = gemm_tile_rows).
+cudaError_t gemm_tiled(const float* At, int lda, const float* Wt, int ldw, float* C, int ldc, int M, int N, int K,
+                       int epilogue, bool out_fm, int tile_rows, cudaStream_t s);
 
 // ---------------------------------------------------------------- norms
 // out[k*ldo+m] = x[k*ldx+m] * scale(m) * w[k], scale from the sequential sum of
@@ -97,6 +102,7 @@ struct AttnDecodeArgs {
     float* work;                             // split partials: [B*H*max_splits*(dh+2)] floats
     int B, H, dh, ctx, split;                // keys per split (multiple of 64)
     float theta;
+    const float2* rope;                      // optional (cos, sin) table [ctx][dh/2]; null: computed in-kernel
 };
 size_t attn_decode_work_floats(int B, int H, int dh, int ctx, int split);
 cudaError_t attn_decode(const AttnDecodeArgs& a, cudaStream_t s);
@@ -106,7 +112,7 @@ cudaError_t attn_decode(const AttnDecodeArgs& a, cudaStream_t s);
 // with c_sb the per-sequence stride; start[s] = first position of sequence s.
 cudaError_t rope_kv_prefill(float* qkv, int64_t q_rs, float* kc, float* vc, int64_t c_sb, int64_t c_sh,
                             int64_t c_st, const int32_t* cu_seqlens, const int32_t* start, int S, int H, int dh,
-                            int total_rows, float theta, cudaStream_t s);
+                            int total_rows, float theta, const float2* rope, cudaStream_t s);
 // Causal attention of packed query rows over their sequence's cache.
 cudaError_t attn_prefill(const float* qkv, int64_t q_rs, const float* kc, const float* vc, int64_t c_sb,
                          int64_t c_sh, int64_t c_st, const int32_t* cu_seqlens, const int32_t* start,

@@ -50,16 +50,16 @@ def gated_rmsnorm_residual(x, z, res, w, eps: float, y=None) -> torch.Tensor:
 
 
 def gemm(a_t: torch.Tensor, w_t: torch.Tensor, epilogue: int = 0, out_fm: bool = False,
-         c: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """C = A . W^T with a_t = A^T [K, M] and w_t = W^T [K, N]."""
+         c: Optional[torch.Tensor] = None, tile_rows: int = 0) -> torch.Tensor:
+    """C = A . W^T with a_t = A^T [K, M] and w_t = W^T [K, N]; tile_rows 0/32/64."""
     _f32(a_t, w_t, c)
     k, m = a_t.shape
     k2, n = w_t.shape
     assert k == k2
     if c is None:
         c = torch.empty((n, m) if out_fm else (m, n), device=a_t.device, dtype=torch.float32)
-    check(lib.krk_k_gemm(a_t.data_ptr(), m, w_t.data_ptr(), n, c.data_ptr(), c.shape[1], m, n, k, epilogue,
-                         int(out_fm), _stream()))
+    check(lib.krk_k_gemm_tiled(a_t.data_ptr(), m, w_t.data_ptr(), n, c.data_ptr(), c.shape[1], m, n, k, epilogue,
+                               int(out_fm), tile_rows, _stream()))
     return c
 
 

@@ -31,17 +31,19 @@ def np_(t):
 @pytest.mark.parametrize("m,n,k", [(64, 32, 32), (128, 2720, 608), (64, 608, 1216), (192, 608, 2432),
                                    (64, 2048, 608), (256, 1824, 608)])
 @pytest.mark.parametrize("out_fm", [False, True])
-def test_gemm_bit_exact_vs_reference_dot(m, n, k, out_fm):
+@pytest.mark.parametrize("tile", [0, 32, 64])
+def test_gemm_bit_exact_vs_reference_dot(m, n, k, out_fm, tile):
     rng = np.random.default_rng(m * 7 + n + k)
     a = rng.standard_normal((m, k)).astype(np.float32)
     w = (0.02 * rng.standard_normal((n, k))).astype(np.float32)
     ref = O.gemm_transb(a, w)  # each element = the reference dot (src/math.rs:89-124)
-    c = K.gemm(cu(a.T.copy()), cu(w.T.copy()), 0, out_fm)
+    c = K.gemm(cu(a.T.copy()), cu(w.T.copy()), 0, out_fm, tile_rows=tile)
     got = np_(c).T if out_fm else np_(c)
     np.testing.assert_array_equal(got, ref)
 
 
-def test_gemm_residual_and_gelu_epilogues():
+@pytest.mark.parametrize("tile", [32, 64])
+def test_gemm_residual_and_gelu_epilogues(tile):
     rng = np.random.default_rng(1)
     m, n, k = 128, 608, 2432
     a = rng.standard_normal((m, k)).astype(np.float32)
@@ -49,9 +51,12 @@ def test_gemm_residual_and_gelu_epilogues():
     res = rng.standard_normal((n, m)).astype(np.float32)
     ref = O.gemm_transb(a, w)
     c = cu(res.copy())
-    K.gemm(cu(a.T.copy()), cu(w.T.copy()), 1, True, c)
+    K.gemm(cu(a.T.copy()), cu(w.T.copy()), 1, True, c, tile_rows=tile)
     np.testing.assert_array_equal(np_(c), res + ref.T)
-    g = np_(K.gemm(cu(a.T.copy()), cu(w.T.copy()), 2, True))
+    cb = cu(res.T.copy())
+    K.gemm(cu(a.T.copy()), cu(w.T.copy()), 1, False, cb, tile_rows=tile)
+    np.testing.assert_array_equal(np_(cb), res.T + ref)
+    g = np_(K.gemm(cu(a.T.copy()), cu(w.T.copy()), 2, True, tile_rows=tile))
     gref = np.vectorize(O.gelu, otypes=[np.float32])(ref.T)
     np.testing.assert_allclose(g, gref, atol=1e-6, rtol=1e-5)
 
