@@ -227,11 +227,13 @@ def kernel_table(torch, peak, scan_t=2048):
     q, k, v, pos, kc, vc = synth.attn_decode_inputs()
     q, k, v, kc, vc = (torch.from_numpy(a).to(dev) for a in (q, k, v, kc, vc))
     posd = torch.from_numpy(pos).to(dev)
-    work = torch.empty(K.attn_work_floats(64, 8, 64, 2048, 256), device=dev)
+    work = torch.empty(K.attn_work_floats(64, 8, 64, 2048, 64), device=dev)
     out = torch.empty_like(q)
     nb = int(sum((int(p) + 1) * 8 * 64 * 4 * 2 for p in pos) + 64 * 8 * 64 * 4 * 6)
-    put("rope_kv_attn_decode[64,8,2048,64]", nb,
-        timeit(lambda: K.rope_kv_attn_decode(q, k, v, kc, vc, posd, split=256, work=work, out=out)))
+    ms = {sp: timeit(lambda: K.rope_kv_attn_decode(q, k, v, kc, vc, posd, split=sp, work=work, out=out))
+          for sp in (64, 256)}
+    put("rope_kv_attn_decode[64,8,2048,64]", nb, ms[64],
+        {"split": 64, "ms_split256": round(ms[256], 4)})
     del kc, vc
 
     xs, bm, cm, dt, cs, ssm = synth.conv_ssd_inputs(256, 1)

@@ -312,7 +312,7 @@ void create_state(krk_state* s, const krk_model* m, int B, int ctx) {
     s->ctx = ctx;
     s->Mp = round_up(B, 64);
     const int64_t Mp = s->Mp;
-    s->attn_split = (int64_t)B * NH >= 2 * 148 ? 2048 : 256;
+    s->attn_split = 64;  // one 64-key block per CTA (attn_decode_tile_kernel)
     const size_t work = krk::attn_decode_work_floats(B, NH, HD, ctx, s->attn_split);
     Budget b;
     for (int l = 0; l < NL; ++l) {
@@ -471,7 +471,9 @@ void lm_head(krk_state* s) {
 
 // One decode step for all sequences: tokens in tok_d, positions in pos_d
 // (src/model.rs:586-624).  Does not advance positions.
-void decode_forward(krk_state* s, const uint8_t* active) {
+// max_keys: an upper bound on pos + 1 over the batch (the attention grid covers
+// no key block beyond it).
+void decode_forward(krk_state* s, const uint8_t* active, int max_keys) {
     const krk_model* m = s->m;
     cudaStream_t st = m->stream;
     const int B = s->B, Mp = (int)s->Mp;
@@ -507,6 +509,7 @@ void decode_forward(krk_state* s, const uint8_t* active) {
             a.work = s->attn_work;
             a.B = B; a.H = NH; a.dh = HD; a.ctx = s->ctx; a.split = s->attn_split; a.theta = THETA;
             a.rope = s->rope;
+            a.max_keys = max_keys;
             timed(s, KRK_PROF_ATTN_DECODE, [&] { kk(krk::attn_decode(a, st), "attention"); });
             timed(s, KRK_PROF_GEMM, [&] { kk(krk::gemm(s->ao_t, Mp, L.wo_t, HID, s->h_t, Mp, Mp, HID, HID, krk::EPI_RESIDUAL, true, st), "wo"); });
             timed(s, KRK_PROF_NORM, [&] { kk(krk::rmsnorm_fm(s->h_t, Mp, L.ln2, RMS_EPS, HID, B, s->hn_t, Mp, st), "ln2"); });
@@ -854,7 +857,7 @@ int krk_step(const krk_model* m, krk_state* s, const uint32_t* tokens, float* lo
         cudaStream_t st = m->stream;
         kk(cudaMemcpyAsync(s->tok_d, tokens, s->B * 4, cudaMemcpyHostToDevice, st), "h2d tokens");
         total_begin(s);
-        decode_forward(s, nullptr);
+        decode_forward(s, nullptr, (int)*std::max_element(s->pos_h.begin(), s->pos_h.end()) + 1);
         timed(s, KRK_PROF_OTHER, [&] { kk(krk::advance_pos(s->pos_d, nullptr, s->B, st), "advance"); });
         for (int b = 0; b < s->B; ++b) s->pos_h[b] += 1;
         total_end(s);
@@ -912,8 +915,10 @@ int krk_generate_greedy(const krk_model* m, krk_state* s, const uint32_t* prompt
         // first pick from the prefill logits (src/generate.rs:81-82)
         timed(s, KRK_PROF_OTHER, [&] { kk(krk::greedy(ga, st), "greedy"); });
         ga.pos = s->pos_d;
+        // step i runs every active sequence at position pos_h[b] + i at most
+        const int64_t pos0 = *std::max_element(s->pos_h.begin(), s->pos_h.end());
         for (int i = 0; i < max_steps; ++i) {
-            decode_forward(s, s->active_d);
+            decode_forward(s, s->active_d, (int)(pos0 + i + 1));
             timed(s, KRK_PROF_OTHER, [&] { kk(krk::greedy(ga, st), "greedy"); });
         }
         total_end(s);

@@ -46,7 +46,7 @@ KRK_DEV void rope_cs(int i, int dh, int pos, float theta, float& c, float& s) {
 }
 
 constexpr int AD_THREADS = 128;
-constexpr int AD_TILE = 128;
+constexpr int AD_TILE = 64;
 constexpr int AD_RED = 512;
 
 template <int DH>
@@ -204,6 +204,133 @@ __global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(AttnDecodeArgs 
     }
 }
 
+// One 64-key block per CTA (split == AD_TILE): the K and V rows of the block
+// are requested together at entry, so the V copy is in flight while the scores
+// are computed and each CTA waits on memory once; the many small CTAs (5-6 per
+// SM) keep HBM busy between them.  Same arithmetic as attn_decode_kernel.
+template <int DH>
+size_t adt_smem_bytes() {
+    return sizeof(float) * (3 * DH + 2 * AD_TILE + 2 * AD_TILE * AdLayout<DH>::KLD);
+}
+
+template <int DH>
+__global__ void __launch_bounds__(AD_THREADS) attn_decode_tile_kernel(AttnDecodeArgs a, int max_splits) {
+    using L = AdLayout<DH>;
+    constexpr int HALF = DH / 2;
+    static_assert(L::G * DH <= AD_TILE * L::KLD, "PV partials must fit in the K tile");
+    extern __shared__ __align__(16) float sm[];
+    float* kt = sm;                       // [AD_TILE][KLD]; PV partials after the scores
+    float* vt = kt + AD_TILE * L::KLD;    // [AD_TILE][KLD]
+    float* qs = vt + AD_TILE * L::KLD;
+    float* kn = qs + DH;
+    float* vn = kn + DH;
+    float* sc = vn + DH;                  // [AD_TILE]
+    float* scratch = sc + AD_TILE;        // [AD_TILE]
+
+    const int b = blockIdx.x, h = blockIdx.y, sp = blockIdx.z, tid = threadIdx.x;
+    if (a.active && !a.active[b]) return;
+    const int pos = a.pos[b];
+    if (pos < 0 || pos >= a.ctx) return;  // the host rejects these before launch
+    const int nkeys = pos + 1;
+    const int j0 = sp * AD_TILE;
+    if (j0 >= nkeys) return;
+    const int nk = min(AD_TILE, nkeys - j0);
+    const int nsplit = (nkeys + AD_TILE - 1) / AD_TILE;
+    const size_t cbase = (size_t)b * a.c_sb + (size_t)h * a.c_sh;
+
+    // Cached rows j0..j0+nk-1 except the new one (slot pos), K then V.
+    for (int i = tid; i < nk * L::DH4; i += AD_THREADS) {
+        const int r = i / L::DH4, c4 = i % L::DH4;
+        if (j0 + r != pos) cp_async16(kt + r * L::KLD + c4 * 4, a.kc + cbase + (size_t)(j0 + r) * a.c_st + c4 * 4);
+    }
+    cp_async_commit();
+    for (int i = tid; i < nk * L::DH4; i += AD_THREADS) {
+        const int r = i / L::DH4, c4 = i % L::DH4;
+        if (j0 + r != pos) cp_async16(vt + r * L::KLD + c4 * 4, a.vc + cbase + (size_t)(j0 + r) * a.c_st + c4 * 4);
+    }
+    cp_async_commit();
+
+    const size_t in_off = (size_t)b * a.in_sb + (size_t)h * a.in_sh;
+    if (tid < DH) {
+        qs[tid] = a.q[in_off + tid];
+        kn[tid] = a.k[in_off + tid];
+        vn[tid] = a.v[in_off + tid];
+    }
+    __syncthreads();
+    if (tid < HALF) {  // src/model.rs:721-728
+        float c, s;
+        if (a.rope) {
+            const float2 cs = a.rope[(size_t)pos * HALF + tid];
+            c = cs.x;
+            s = cs.y;
+        } else {
+            rope_cs(tid, DH, pos, a.theta, c, s);
+        }
+        rope_pair(qs[tid], qs[tid + HALF], c, s);
+        rope_pair(kn[tid], kn[tid + HALF], c, s);
+    }
+    __syncthreads();
+    if (j0 + nk == nkeys && tid < DH) {  // KV append (src/model.rs:730-733) by the block holding slot pos
+        const int r = pos - j0;
+        kt[r * L::KLD + tid] = kn[tid];
+        vt[r * L::KLD + tid] = vn[tid];
+        a.kc[cbase + (size_t)pos * a.c_st + tid] = kn[tid];
+        a.vc[cbase + (size_t)pos * a.c_st + tid] = vn[tid];
+    }
+    cp_async_wait<1>();  // K rows of this thread landed
+    __syncthreads();
+
+    // scores (src/model.rs:742-748): dot(q_h, k_j) * (1/sqrt(dh))
+    const float scale = 1.0f / sqrtf((float)DH);
+    float mx = -INFINITY;
+    if (tid < nk) {
+        const float sv = dot_ref(qs, kt + tid * L::KLD, DH) * scale;
+        sc[tid] = sv;
+        mx = sv;
+    }
+    // softmax over this block (src/math.rs:213-232)
+    const float m = block_reduce(mx, scratch, true);
+    float e = 0.0f;
+    if (tid < nk) {
+        e = expf(sc[tid] - m);
+        sc[tid] = e;
+    }
+    const float l = block_reduce(e, scratch + 32, false);
+    if (nsplit == 1 && tid < nk) sc[tid] = sc[tid] * (1.0f / l);
+    cp_async_wait<0>();
+    __syncthreads();
+
+    // out += w_j * v_j (src/model.rs:752-759)
+    const int g = tid / L::DH4, d4 = tid % L::DH4;
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (g < L::G) {
+        for (int r = g; r < nk; r += L::G) {
+            const float w = sc[r];
+            const float4 vv = *reinterpret_cast<const float4*>(vt + r * L::KLD + d4 * 4);
+            o.x = o.x + w * vv.x;
+            o.y = o.y + w * vv.y;
+            o.z = o.z + w * vv.z;
+            o.w = o.w + w * vv.w;
+        }
+        *reinterpret_cast<float4*>(kt + g * DH + d4 * 4) = o;
+    }
+    __syncthreads();
+    if (tid < DH) {
+        float acc = kt[tid];
+        for (int gg = 1; gg < L::G; ++gg) acc = acc + kt[gg * DH + tid];
+        if (nsplit == 1) {
+            a.out[(size_t)b * a.o_sb + (size_t)h * a.o_sh + (size_t)tid * a.o_sd] = acc;
+        } else {
+            float* wp = a.work + (((size_t)b * a.H + h) * max_splits + sp) * (DH + 2);
+            wp[tid] = acc;
+            if (tid == 0) {
+                wp[DH] = m;
+                wp[DH + 1] = l;
+            }
+        }
+    }
+}
+
 // Merges the per-split (max, sum, unnormalised out) partials of one (b, h).
 __global__ void attn_combine_kernel(AttnDecodeArgs a, int max_splits) {
     const int b = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
@@ -340,9 +467,18 @@ cudaError_t attn_decode(const AttnDecodeArgs& a, cudaStream_t s) {
         return cudaErrorInvalidValue;
     const int max_splits = (a.ctx + a.split - 1) / a.split;
     if (max_splits > 1 && !a.work) return cudaErrorInvalidValue;
-    dim3 grid(a.B, a.H, max_splits);
+    // blocks past the longest sequence would exit at once: leave them out
+    const int keys = a.max_keys > 0 && a.max_keys < a.ctx ? a.max_keys : a.ctx;
+    dim3 grid(a.B, a.H, (keys + a.split - 1) / a.split);
     cudaError_t e;
-    if (a.dh == 76) {
+    if (a.split == AD_TILE) {
+        const void* fn = a.dh == 76 ? (const void*)attn_decode_tile_kernel<76> : (const void*)attn_decode_tile_kernel<64>;
+        const size_t smem = a.dh == 76 ? adt_smem_bytes<76>() : adt_smem_bytes<64>();
+        static DeviceOnce once76, once64;
+        if ((e = (a.dh == 76 ? once76 : once64).set_smem(fn, smem)) != cudaSuccess) return e;
+        if (a.dh == 76) attn_decode_tile_kernel<76><<<grid, AD_THREADS, smem, s>>>(a, max_splits);
+        else attn_decode_tile_kernel<64><<<grid, AD_THREADS, smem, s>>>(a, max_splits);
+    } else if (a.dh == 76) {
         static DeviceOnce once;
         const size_t smem = ad_smem_bytes<76>(a.split);
         if (smem > 227 * 1024) return cudaErrorInvalidValue;

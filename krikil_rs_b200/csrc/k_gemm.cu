@@ -12,29 +12,31 @@
 // the epilogue.  The result is bit-identical to the reference gemv for any M.
 //
 // Operands: A feature-major (At[k][m], contiguous along m) and W K-major
-// (Wt[k][n], contiguous along n), so that every 32-row K-block of both is a
-// dense tile that cp.async moves straight into shared memory (3-stage pipeline)
-// and the inner loop reads 8 m and 8 n values with four 16-byte shared loads.
+// (Wt[k][n], contiguous along n), so that the rows of both are dense runs that
+// cp.async moves straight into shared memory, and the inner loop reads 8 m and
+// 8 n values with four 16-byte shared loads.  Since warp w only ever reads the
+// rows k = w (mod 8), each warp stages its own four rows of every K-block in a
+// private 4-deep ring: the main loop synchronises the warp, never the CTA.
 #include "common.cuh"
 #include "kernels.h"
 
 namespace krk {
 namespace {
 
-constexpr int BN = 32, BK = 32, NSTAGE = 3, NT = 256;
-constexpr int W_TILE = BK * BN;
+constexpr int BN = 32, BK = 32, NT = 256, WSTAGE = 4;
+constexpr int WROWS = BK / 8;  // K-block rows owned by one warp
 constexpr int RLD_BM = BN + 4;  // partials red[w][m][n] for batch-major output
 
 template <int BM>
 struct Tile {
     static constexpr int TM = BM / 8;                 // rows per thread (8 lanes of rows per warp)
-    static constexpr int A_TILE = BK * BM;
-    static constexpr int STAGE = A_TILE + W_TILE;
+    static constexpr int WST = WROWS * (BM + BN);     // one warp's stage: 4 rows of A, then 4 of W
+    static constexpr int PIPE = 8 * WSTAGE * WST;
     static constexpr int RLD_FM = BM + 4;             // partials red[w][n][m] for feature-major output
     static constexpr int RED = 8 * BM * RLD_BM > 8 * BN * RLD_FM ? 8 * BM * RLD_BM : 8 * BN * RLD_FM;
-    static constexpr int SMEM_FLOATS = RED > NSTAGE * STAGE ? RED : NSTAGE * STAGE;
+    static constexpr int SMEM_FLOATS = RED > PIPE ? RED : PIPE;
     static constexpr size_t SMEM_BYTES = SMEM_FLOATS * sizeof(float);
-    static constexpr int A_F4 = A_TILE / 4 / NT;      // float4 copies per thread per K-block
+    static constexpr int A_F4 = BM / 32;              // float4 copies of A per lane per K-block
     static constexpr int OUT_F4 = BM * BN / 4 / NT;   // output float4s per thread
     static constexpr int MIN_CTAS = BM == 64 ? 2 : 3;
 };
@@ -67,18 +69,20 @@ __global__ void __launch_bounds__(NT, Tile<BM>::MIN_CTAS)
     const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
     const int nkb = K / BK;
 
+    float* ring = sm + warp * (WSTAGE * T::WST);
+    // This warp's rows k0 + warp + 8i (i < 4) of the K-block into ring slot st.
     auto load_stage = [&](int kb, int st) {
-        float* As = sm + st * T::STAGE;
-        float* Ws = As + T::A_TILE;
-        const int k0 = kb * BK;
+        float* As = ring + st * T::WST;
+        float* Ws = As + WROWS * BM;
+        const int k0 = kb * BK + warp;
 #pragma unroll
         for (int j = 0; j < T::A_F4; ++j) {
-            int idx = tid + j * NT;
-            int r = idx / (BM / 4), c4 = idx % (BM / 4);
-            cp_async16(As + r * BM + c4 * 4, At + (size_t)(k0 + r) * lda + m0 + c4 * 4);
+            const int idx = lane + 32 * j;
+            const int r = idx / (BM / 4), c4 = idx % (BM / 4);
+            cp_async16(As + r * BM + c4 * 4, At + (size_t)(k0 + 8 * r) * lda + m0 + c4 * 4);
         }
-        int r = tid >> 3, c4 = tid & 7;
-        cp_async16(Ws + r * BN + c4 * 4, Wt + (size_t)(k0 + r) * ldw + n0 + c4 * 4);
+        const int r = lane >> 3, c4 = lane & 7;
+        cp_async16(Ws + r * BN + c4 * 4, Wt + (size_t)(k0 + 8 * r) * ldw + n0 + c4 * 4);
     };
 
     float acc[TM][8];
@@ -88,33 +92,34 @@ __global__ void __launch_bounds__(NT, Tile<BM>::MIN_CTAS)
         for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
 
 #pragma unroll
-    for (int s = 0; s < NSTAGE - 1; ++s) {
+    for (int s = 0; s < WSTAGE - 1; ++s) {
         if (s < nkb) load_stage(s, s);
         cp_async_commit();
     }
     for (int kb = 0; kb < nkb; ++kb) {
-        cp_async_wait<NSTAGE - 2>();
-        __syncthreads();
-        const int pf = kb + NSTAGE - 1;
-        if (pf < nkb) load_stage(pf, pf % NSTAGE);
+        cp_async_wait<WSTAGE - 2>();
+        // All lanes' copies of slot kb are visible, and every lane is done
+        // reading the slot refilled next (consumed in iteration kb - 1).
+        __syncwarp();
+        const int pf = kb + WSTAGE - 1;
+        if (pf < nkb) load_stage(pf, pf % WSTAGE);
         cp_async_commit();
-        const float* As = sm + (kb % NSTAGE) * T::STAGE;
-        const float* Ws = As + T::A_TILE;
+        const float* As = ring + (kb % WSTAGE) * T::WST;
+        const float* Ws = As + WROWS * BM;
 #pragma unroll
-        for (int i = 0; i < BK / 8; ++i) {
-            const int k = warp + 8 * i;  // this warp's lane of the reference dot
+        for (int i = 0; i < WROWS; ++i) {  // k = kb*32 + warp + 8i: this warp's lane of the reference dot
             float a[TM];
             {
-                const float4 a0 = *reinterpret_cast<const float4*>(As + k * BM + lm * 4);
+                const float4 a0 = *reinterpret_cast<const float4*>(As + i * BM + lm * 4);
                 a[0] = a0.x; a[1] = a0.y; a[2] = a0.z; a[3] = a0.w;
                 if (TM == 8) {
-                    const float4 a1 = *reinterpret_cast<const float4*>(As + k * BM + 32 + lm * 4);
+                    const float4 a1 = *reinterpret_cast<const float4*>(As + i * BM + 32 + lm * 4);
                     a[TM == 8 ? 4 : 0] = a1.x; a[TM == 8 ? 5 : 1] = a1.y;
                     a[TM == 8 ? 6 : 2] = a1.z; a[TM == 8 ? 7 : 3] = a1.w;
                 }
             }
-            const float4 w0 = *reinterpret_cast<const float4*>(Ws + k * BN + ln * 4);
-            const float4 w1 = *reinterpret_cast<const float4*>(Ws + k * BN + 16 + ln * 4);
+            const float4 w0 = *reinterpret_cast<const float4*>(Ws + i * BN + ln * 4);
+            const float4 w1 = *reinterpret_cast<const float4*>(Ws + i * BN + 16 + ln * 4);
             const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
             for (int r = 0; r < TM; ++r)

@@ -103,6 +103,7 @@ struct AttnDecodeArgs {
     int B, H, dh, ctx, split;                // keys per split (multiple of 64)
     float theta;
     const float2* rope;                      // optional (cos, sin) table [ctx][dh/2]; null: computed in-kernel
+    int max_keys;                            // > 0: no sequence has pos + 1 above this; 0: unknown (ctx)
 };
 size_t attn_decode_work_floats(int B, int H, int dh, int ctx, int split);
 cudaError_t attn_decode(const AttnDecodeArgs& a, cudaStream_t s);

@@ -205,7 +205,7 @@ def test_conv_ssd_scan_split_invariance_full_size():
 
 
 # ------------------------------------------------------------- attention
-@pytest.mark.parametrize("split", [256, 2048])
+@pytest.mark.parametrize("split", [64, 256, 2048])
 def test_rope_kv_attn_decode_full_size(split):
     """Config: q,k,v [64,8,1,64], positions ~U[0,2048), cache [64,8,2048,64]."""
     q, k, v, pos, kc, vc = synth.attn_decode_inputs()
