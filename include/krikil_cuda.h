@@ -155,7 +155,7 @@ KRK_API int krk_launch_count(uint64_t* count);
 /* Measurement hook (no reference counterpart; the reference only times whole
  * calls, src/generate.rs:76-78, :116-122): with profiling on, every later
  * prefill / step / generate call on this state brackets each kernel launch
- * with CUDA events on the model stream and accumulates the device time per
+ * with CUDA events on its stream and accumulates the device time per
  * kernel class; KRK_PROF_DEVICE_TOTAL is the device time of whole calls, from
  * after the inputs reach the device to before the outputs leave it.
  * krk_state_profile resets the totals. */
@@ -173,6 +173,12 @@ enum {
 };
 KRK_API int krk_state_profile(krk_state* state, int enable);
 KRK_API int krk_state_profile_read(const krk_state* state, int cls, double* total_ms, int64_t* launches);
+/* Decode sequences processed by the timed launches of a class (the sum over
+ * its decode launches of the sequences each covered; prefill launches add 0).
+ * A decode batch of 256+ sequences runs as two halves on two streams, each
+ * launch timed on its own stream, so per-class times are kernel times that may
+ * overlap and can add up to more than KRK_PROF_DEVICE_TOTAL. */
+KRK_API int krk_state_profile_units(const krk_state* state, int cls, int64_t* units);
 
 /* ------------------------------------------------------ per-kernel entry points
  * Device pointers, fp32, asynchronous on `stream`.  Each names the reference

@@ -122,6 +122,7 @@ struct LayerW {
 struct krk_model {
     int device = 0;
     cudaStream_t stream = nullptr;
+    cudaStream_t stream2 = nullptr;  // second half of a split decode batch
     Arena arena;
     float *wte = nullptr, *wte_t = nullptr, *lnf = nullptr;
     LayerW L[NL];
@@ -138,10 +139,12 @@ struct Prof {
     struct Pending {
         int cls;
         cudaEvent_t a, b;
+        int64_t units;
     };
     std::vector<Pending> pending;
     double ms[KRK_PROF_CLASSES] = {};
     int64_t n[KRK_PROF_CLASSES] = {};
+    int64_t units[KRK_PROF_CLASSES] = {};
     cudaEvent_t get() {
         if (pool.empty()) {
             cudaEvent_t e;
@@ -201,6 +204,7 @@ struct krk_state {
     Arena hist_arena;
     int64_t hist_cap = 0;
     uint32_t* hist_d = nullptr;
+    cudaEvent_t ev_fork = nullptr, ev_join = nullptr;  // ordering of the two decode streams
 };
 
 namespace {
@@ -371,6 +375,8 @@ void create_state(krk_state* s, const krk_model* m, int B, int ctx) {
        "rope table");
     ck(cudaStreamSynchronize(m->stream), "state init");
     s->pos_h.assign(B, 0);
+    ck(cudaEventCreateWithFlags(&s->ev_fork, cudaEventDisableTiming), "event create");
+    ck(cudaEventCreateWithFlags(&s->ev_join, cudaEventDisableTiming), "event create");
 }
 
 void ensure_prefill_ws(krk_state* s, int64_t tokens, int seqs) {
@@ -414,19 +420,23 @@ void zero_pad_cols(float* buf, int64_t ld, int64_t valid, int rows, cudaStream_t
     kk(cudaMemset2DAsync(buf + valid, ld * 4, 0, (ld - valid) * 4, rows, st), "memset2d");
 }
 
-// Records CUDA events around f() on the model stream when profiling is on.
+// Records CUDA events around f() on stream st when profiling is on; units is
+// the number of decode sequences the launch processes (0 elsewhere).
 template <typename F>
-void timed(krk_state* s, int cls, F&& f) {
+void timed_on(krk_state* s, cudaStream_t st, int cls, int64_t units, F&& f) {
     if (!s->prof.on) {
         f();
         return;
     }
-    cudaStream_t st = s->m->stream;
     cudaEvent_t a = s->prof.get(), b = s->prof.get();
     kk(cudaEventRecord(a, st), "event");
     f();
     kk(cudaEventRecord(b, st), "event");
-    s->prof.pending.push_back({cls, a, b});
+    s->prof.pending.push_back({cls, a, b, units});
+}
+template <typename F>
+void timed(krk_state* s, int cls, F&& f) {
+    timed_on(s, s->m->stream, cls, 0, f);
 }
 
 // Device-time bracket of a whole call: opened after the call's inputs reached
@@ -441,7 +451,7 @@ void total_end(krk_state* s) {
     if (!s->prof.on || !s->prof.total_open) return;
     cudaEvent_t b = s->prof.get();
     kk(cudaEventRecord(b, s->m->stream), "event");
-    s->prof.pending.push_back({KRK_PROF_DEVICE_TOTAL, s->prof.total_start, b});
+    s->prof.pending.push_back({KRK_PROF_DEVICE_TOTAL, s->prof.total_start, b, 0});
     s->prof.total_start = nullptr;
     s->prof.total_open = false;
 }
@@ -453,71 +463,141 @@ void prof_collect(krk_state* s) {
         kk(cudaEventElapsedTime(&ms, p.a, p.b), "event elapsed");
         s->prof.ms[p.cls] += ms;
         s->prof.n[p.cls] += 1;
+        s->prof.units[p.cls] += p.units;
     }
     s->prof.clear_events();
 }
 
 // ------------------------------------------------------------------ forward
-// Final norm + tied LM head on the decode buffers (src/model.rs:620-621).
-void lm_head(krk_state* s) {
+// A slice of the decode batch: sequences [b0, b0 + nb), which are columns
+// [b0, b0 + M) of the feature-major activations (M = nb rounded up to 64, or
+// the padded remainder), run on stream st.
+struct Part {
+    int b0, nb, M;
+    cudaStream_t st;
+    int tile_rows;  // GEMM CTA tile height (0: chosen for the kernel running alone)
+};
+
+template <typename F>
+void timed(krk_state* s, const Part& p, int cls, F&& f) {
+    timed_on(s, p.st, cls, p.nb, f);
+}
+
+// Final norm + tied LM head (src/model.rs:620-621).
+void lm_head(krk_state* s, const Part& p) {
     const krk_model* m = s->m;
-    cudaStream_t st = m->stream;
     const int Mp = (int)s->Mp;
-    timed(s, KRK_PROF_NORM, [&] { kk(krk::rmsnorm_fm(s->h_t, Mp, m->lnf, RMS_EPS, HID, s->B, s->hn_t, Mp, st), "lnf"); });
-    timed(s, KRK_PROF_GEMM, [&] {
-        kk(krk::gemm(s->hn_t, Mp, m->wte_t, VOC, s->logits, VOC, Mp, VOC, HID, krk::EPI_STORE, false, st), "lm head");
+    timed(s, p, KRK_PROF_NORM, [&] {
+        kk(krk::rmsnorm_fm(s->h_t + p.b0, Mp, m->lnf, RMS_EPS, HID, p.nb, s->hn_t + p.b0, Mp, p.st), "lnf");
+    });
+    timed(s, p, KRK_PROF_GEMM, [&] {
+        kk(krk::gemm_tiled(s->hn_t + p.b0, Mp, m->wte_t, VOC, s->logits + (size_t)p.b0 * VOC, VOC, p.M, VOC, HID,
+                           krk::EPI_STORE, false, p.tile_rows, p.st), "lm head");
     });
 }
 
+void lm_head(krk_state* s) { lm_head(s, Part{0, s->B, (int)s->Mp, s->m->stream, 0}); }
+
+void decode_embed(krk_state* s, const Part& p) {
+    const int Mp = (int)s->Mp;
+    timed(s, p, KRK_PROF_OTHER, [&] {
+        kk(krk::embed_fm(s->tok_d + p.b0, s->m->wte, VOC, HID, p.nb, s->h_t + p.b0, Mp, p.st), "embed");
+    });
+}
+
+// Layer l of one decode step for a slice of the batch (src/model.rs:626-783).
+void decode_layer(krk_state* s, int l, const uint8_t* active, int max_keys, const Part& p) {
+    const krk_model* m = s->m;
+    const LayerW& L = m->L[l];
+    const int Mp = (int)s->Mp, b0 = p.b0, nb = p.nb, M = p.M, tr = p.tile_rows;
+    cudaStream_t st = p.st;
+    const uint8_t* act = active ? active + b0 : nullptr;
+    float* h = s->h_t + b0;
+    float* hn = s->hn_t + b0;
+    auto gemm = [&](const float* A, const float* W, int N, int K, float* C, int ldc, int epi, bool fm, const char* w) {
+        timed(s, p, KRK_PROF_GEMM, [&] { kk(krk::gemm_tiled(A, Mp, W, N, C, ldc, M, N, K, epi, fm, tr, st), w); });
+    };
+    auto norm = [&](const float* x, const float* w, float eps, int K, float* out, const char* what) {
+        timed(s, p, KRK_PROF_NORM, [&] { kk(krk::rmsnorm_fm(x, Mp, w, eps, K, nb, out, Mp, st), what); });
+    };
+    if (is_mamba(l)) {  // src/model.rs:626-702
+        float* zx = s->zx + (size_t)b0 * DIP_PAD;
+        norm(h, L.ln, RMS_EPS, HID, hn, "ln");
+        gemm(hn, L.in_t, DIP_PAD, HID, zx, DIP_PAD, krk::EPI_STORE, false, "in_proj");
+        timed(s, p, KRK_PROF_CONV, [&] {
+            kk(krk::conv_step4(zx + OFF_X, DIP_PAD, s->conv[l] + (size_t)b0 * DXBC * 4, L.conv_w, L.conv_b, nb, DXBC,
+                               act, st), "conv");
+        });
+        krk::SsdStepArgs a{};
+        a.x = zx + OFF_X; a.x_sb = DIP_PAD;
+        a.bm = zx + OFF_B; a.cm = zx + OFF_C; a.bc_sb = DIP_PAD;
+        a.dt = zx + OFF_DT; a.dt_sb = DIP_PAD;
+        a.z = zx + OFF_Z; a.z_sb = DIP_PAD;
+        a.ssm = s->ssm[l] + (size_t)b0 * MH * MP * DS;
+        a.dt_bias = L.dt_bias; a.a_neg = L.a_neg; a.dsk = L.dsk;
+        a.y = s->y_t + b0; a.y_sb = 1; a.y_sc = Mp;
+        a.active = act;
+        a.B = nb; a.H = MH; a.P = MP; a.N = DS;
+        timed(s, p, KRK_PROF_SSD_STEP, [&] { kk(krk::ssd_step(a, false, st), "ssd step"); });
+        norm(s->y_t + b0, L.norm_w, MNORM_EPS, DI, s->yn_t + b0, "gated norm");
+        gemm(s->yn_t + b0, L.out_t, HID, DI, h, Mp, krk::EPI_RESIDUAL, true, "out_proj");
+    } else {  // src/model.rs:704-783
+        float* qkv = s->qkv + (size_t)b0 * QKV;
+        norm(h, L.ln1, RMS_EPS, HID, hn, "ln1");
+        gemm(hn, L.qkv_t, QKV, HID, qkv, QKV, krk::EPI_STORE, false, "wqkv");
+        krk::AttnDecodeArgs a{};
+        a.q = qkv; a.k = qkv + HID; a.v = qkv + 2 * HID; a.in_sb = QKV; a.in_sh = HD;
+        a.c_sb = (int64_t)s->ctx * HID; a.c_sh = HD; a.c_st = HID;
+        a.kc = s->kc[l] + (size_t)b0 * a.c_sb; a.vc = s->vc[l] + (size_t)b0 * a.c_sb;
+        a.pos = s->pos_d + b0; a.active = act;
+        a.out = s->ao_t + b0; a.o_sb = 1; a.o_sh = (int64_t)HD * Mp; a.o_sd = Mp;
+        const size_t max_splits = (size_t)(s->ctx + s->attn_split - 1) / s->attn_split;
+        a.work = s->attn_work + (size_t)b0 * NH * max_splits * (HD + 2);
+        a.B = nb; a.H = NH; a.dh = HD; a.ctx = s->ctx; a.split = s->attn_split; a.theta = THETA;
+        a.rope = s->rope;
+        a.max_keys = max_keys;
+        timed(s, p, KRK_PROF_ATTN_DECODE, [&] { kk(krk::attn_decode(a, st), "attention"); });
+        gemm(s->ao_t + b0, L.wo_t, HID, HID, h, Mp, krk::EPI_RESIDUAL, true, "wo");
+        norm(h, L.ln2, RMS_EPS, HID, hn, "ln2");
+        gemm(hn, L.fc1_t, INTER, HID, s->mlp_t + b0, Mp, krk::EPI_GELU, true, "fc1");
+        gemm(s->mlp_t + b0, L.fc2_t, HID, INTER, h, Mp, krk::EPI_RESIDUAL, true, "fc2");
+    }
+}
+
 // One decode step for all sequences: tokens in tok_d, positions in pos_d
-// (src/model.rs:586-624).  Does not advance positions.
-// max_keys: an upper bound on pos + 1 over the batch (the attention grid covers
-// no key block beyond it).
+// (src/model.rs:586-624).  Does not advance positions.  max_keys is an upper
+// bound on pos + 1 over the batch (the attention grid covers no key block
+// beyond it).
+//
+// A batch of 256 or more sequences runs as two halves on two streams, layer by
+// layer.  The halves are independent, so while one half's projections keep the
+// FP32 pipes busy the other half's SSD update or attention streams its state
+// through HBM, and each kernel's last partial wave is filled by the other half.
 void decode_forward(krk_state* s, const uint8_t* active, int max_keys) {
     const krk_model* m = s->m;
-    cudaStream_t st = m->stream;
     const int B = s->B, Mp = (int)s->Mp;
-    timed(s, KRK_PROF_OTHER, [&] { kk(krk::embed_fm(s->tok_d, m->wte, VOC, HID, B, s->h_t, Mp, st), "embed"); });
-    for (int l = 0; l < NL; ++l) {
-        const LayerW& L = m->L[l];
-        if (is_mamba(l)) {  // src/model.rs:626-702
-            timed(s, KRK_PROF_NORM, [&] { kk(krk::rmsnorm_fm(s->h_t, Mp, L.ln, RMS_EPS, HID, B, s->hn_t, Mp, st), "ln"); });
-            timed(s, KRK_PROF_GEMM, [&] { kk(krk::gemm(s->hn_t, Mp, L.in_t, DIP_PAD, s->zx, DIP_PAD, Mp, DIP_PAD, HID, krk::EPI_STORE, false, st),
-               "in_proj"); });
-            timed(s, KRK_PROF_CONV, [&] { kk(krk::conv_step4(s->zx + OFF_X, DIP_PAD, s->conv[l], L.conv_w, L.conv_b, B, DXBC, active, st), "conv"); });
-            krk::SsdStepArgs a{};
-            a.x = s->zx + OFF_X; a.x_sb = DIP_PAD;
-            a.bm = s->zx + OFF_B; a.cm = s->zx + OFF_C; a.bc_sb = DIP_PAD;
-            a.dt = s->zx + OFF_DT; a.dt_sb = DIP_PAD;
-            a.z = s->zx + OFF_Z; a.z_sb = DIP_PAD;
-            a.ssm = s->ssm[l];
-            a.dt_bias = L.dt_bias; a.a_neg = L.a_neg; a.dsk = L.dsk;
-            a.y = s->y_t; a.y_sb = 1; a.y_sc = Mp;
-            a.active = active;
-            a.B = B; a.H = MH; a.P = MP; a.N = DS;
-            timed(s, KRK_PROF_SSD_STEP, [&] { kk(krk::ssd_step(a, false, st), "ssd step"); });
-            timed(s, KRK_PROF_NORM, [&] { kk(krk::rmsnorm_fm(s->y_t, Mp, L.norm_w, MNORM_EPS, DI, B, s->yn_t, Mp, st), "gated norm"); });
-            timed(s, KRK_PROF_GEMM, [&] { kk(krk::gemm(s->yn_t, Mp, L.out_t, HID, s->h_t, Mp, Mp, HID, DI, krk::EPI_RESIDUAL, true, st), "out_proj"); });
-        } else {  // src/model.rs:704-783
-            timed(s, KRK_PROF_NORM, [&] { kk(krk::rmsnorm_fm(s->h_t, Mp, L.ln1, RMS_EPS, HID, B, s->hn_t, Mp, st), "ln1"); });
-            timed(s, KRK_PROF_GEMM, [&] { kk(krk::gemm(s->hn_t, Mp, L.qkv_t, QKV, s->qkv, QKV, Mp, QKV, HID, krk::EPI_STORE, false, st), "wqkv"); });
-            krk::AttnDecodeArgs a{};
-            a.q = s->qkv; a.k = s->qkv + HID; a.v = s->qkv + 2 * HID; a.in_sb = QKV; a.in_sh = HD;
-            a.kc = s->kc[l]; a.vc = s->vc[l]; a.c_sb = (int64_t)s->ctx * HID; a.c_sh = HD; a.c_st = HID;
-            a.pos = s->pos_d; a.active = active;
-            a.out = s->ao_t; a.o_sb = 1; a.o_sh = (int64_t)HD * Mp; a.o_sd = Mp;
-            a.work = s->attn_work;
-            a.B = B; a.H = NH; a.dh = HD; a.ctx = s->ctx; a.split = s->attn_split; a.theta = THETA;
-            a.rope = s->rope;
-            a.max_keys = max_keys;
-            timed(s, KRK_PROF_ATTN_DECODE, [&] { kk(krk::attn_decode(a, st), "attention"); });
-            timed(s, KRK_PROF_GEMM, [&] { kk(krk::gemm(s->ao_t, Mp, L.wo_t, HID, s->h_t, Mp, Mp, HID, HID, krk::EPI_RESIDUAL, true, st), "wo"); });
-            timed(s, KRK_PROF_NORM, [&] { kk(krk::rmsnorm_fm(s->h_t, Mp, L.ln2, RMS_EPS, HID, B, s->hn_t, Mp, st), "ln2"); });
-            timed(s, KRK_PROF_GEMM, [&] { kk(krk::gemm(s->hn_t, Mp, L.fc1_t, INTER, s->mlp_t, Mp, Mp, INTER, HID, krk::EPI_GELU, true, st), "fc1"); });
-            timed(s, KRK_PROF_GEMM, [&] { kk(krk::gemm(s->mlp_t, Mp, L.fc2_t, HID, s->h_t, Mp, Mp, HID, INTER, krk::EPI_RESIDUAL, true, st), "fc2"); });
-        }
+    Part parts[2];
+    int np = 1;
+    if (Mp >= 256 && s->ev_fork) {
+        const int h = (int)round_up(Mp / 2, 64);
+        parts[0] = Part{0, std::min(h, B), h, m->stream, 64};
+        parts[1] = Part{h, B - h, Mp - h, m->stream2, 64};
+        np = B > h ? 2 : 1;
+    } else {
+        parts[0] = Part{0, B, Mp, m->stream, 0};
     }
-    lm_head(s);
+    if (np == 2) {
+        kk(cudaEventRecord(s->ev_fork, m->stream), "fork");
+        kk(cudaStreamWaitEvent(m->stream2, s->ev_fork, 0), "fork");
+    }
+    for (int i = 0; i < np; ++i) decode_embed(s, parts[i]);
+    for (int l = 0; l < NL; ++l)
+        for (int i = 0; i < np; ++i) decode_layer(s, l, active, max_keys, parts[i]);
+    for (int i = 0; i < np; ++i) lm_head(s, parts[i]);
+    if (np == 2) {
+        kk(cudaEventRecord(s->ev_join, m->stream2), "join");
+        kk(cudaStreamWaitEvent(m->stream, s->ev_join, 0), "join");
+    }
 }
 
 // Prefill of sequences [g0, g0+S) whose packed tokens are already in pre.tok etc.
@@ -742,9 +822,11 @@ int krk_model_load(const char* path, int device, krk_model** out) {
         m->device = device;
         ck(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking), "stream create");
         try {
+            ck(cudaStreamCreateWithFlags(&m->stream2, cudaStreamNonBlocking), "stream create");
             upload_weights(m.get(), hw);
         } catch (...) {
             m->arena.release();
+            if (m->stream2) cudaStreamDestroy(m->stream2);
             cudaStreamDestroy(m->stream);
             throw;
         }
@@ -758,7 +840,9 @@ int krk_model_free(krk_model* m) {
     return guarded([&]() -> int {
         DeviceGuard g(m->device);
         cudaStreamSynchronize(m->stream);
+        cudaStreamSynchronize(m->stream2);
         m->arena.release();
+        cudaStreamDestroy(m->stream2);
         cudaStreamDestroy(m->stream);
         delete m;
         return KRK_OK;
@@ -795,6 +879,9 @@ int krk_state_free(krk_state* s) {
     return guarded([&]() -> int {
         DeviceGuard g(s->m->device);
         cudaStreamSynchronize(s->m->stream);
+        cudaStreamSynchronize(s->m->stream2);
+        if (s->ev_fork) cudaEventDestroy(s->ev_fork);
+        if (s->ev_join) cudaEventDestroy(s->ev_join);
         s->pre.arena.release();
         s->hist_arena.release();
         s->arena.release();
@@ -981,6 +1068,7 @@ int krk_state_profile(krk_state* s, int enable) {
         for (int i = 0; i < KRK_PROF_CLASSES; ++i) {
             s->prof.ms[i] = 0.0;
             s->prof.n[i] = 0;
+            s->prof.units[i] = 0;
         }
         return KRK_OK;
     });
@@ -991,6 +1079,12 @@ int krk_state_profile_read(const krk_state* s, int cls, double* total_ms, int64_
         return fail(KRK_INVALID, "bad profile arguments");
     *total_ms = s->prof.ms[cls];
     *launches = s->prof.n[cls];
+    return KRK_OK;
+}
+
+int krk_state_profile_units(const krk_state* s, int cls, int64_t* units) {
+    if (!s || cls < 0 || cls >= KRK_PROF_CLASSES || !units) return fail(KRK_INVALID, "bad profile arguments");
+    *units = s->prof.units[cls];
     return KRK_OK;
 }
 

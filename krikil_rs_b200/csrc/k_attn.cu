@@ -204,126 +204,183 @@ __global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(AttnDecodeArgs 
     }
 }
 
-// One 64-key block per CTA (split == AD_TILE): the K and V rows of the block
-// are requested together at entry, so the V copy is in flight while the scores
-// are computed and each CTA waits on memory once; the many small CTAs (5-6 per
-// SM) keep HBM busy between them.  Same arithmetic as attn_decode_kernel.
+// Split of 16*NW keys per CTA, 16 keys per warp, everything warp-private
+// until the CTA's final merge: each warp requests its K and V rows at entry
+// (V stays in flight while the scores run), ropes its own copy of q, computes
+// its scores with two lanes per key, its softmax partial (max, sum) with
+// shuffles and its PV partial; the NW partials are merged after the CTA's only
+// barrier.
+//
+// The score of key j is the reference dot (src/math.rs:89-124) split across a
+// lane pair: the even lane accumulates FMA lanes 0-3 (first float4 of every
+// 8-float chunk), the odd lane lanes 4-7, and the even lane folds
+// ((l0+l4)+(l2+l6)) + ((l1+l5)+(l3+l7)) and adds the unfused tail -- the same
+// rounding as the single-thread dot.
+constexpr int AW_KEYS = 16;  // keys per warp
+
 template <int DH>
-size_t adt_smem_bytes() {
-    return sizeof(float) * (3 * DH + 2 * AD_TILE + 2 * AD_TILE * AdLayout<DH>::KLD);
+struct AwLayout {
+    // K row stride in float4s = 2 (mod 4): the 8 lanes of one shared-memory
+    // phase (4 keys x 2 halves) hit 8 distinct 16-byte bank groups.
+    static constexpr int KLD = DH == 64 ? 72 : 88;
+    static constexpr int ND = (DH + 31) / 32;
+    // K rows, V rows, q, partial; rounded to whole float4s so every warp's
+    // region starts 16-byte aligned
+    static constexpr int WARP_FLOATS = (AW_KEYS * KLD + AW_KEYS * DH + DH + (DH + 2) + 3) / 4 * 4;
+};
+static_assert(AwLayout<64>::WARP_FLOATS % 4 == 0 && AwLayout<76>::WARP_FLOATS % 4 == 0, "alignment");
+static_assert(AwLayout<64>::KLD % 8 == 0 && (AwLayout<64>::KLD / 4) % 4 == 2, "K stride");
+static_assert((AwLayout<76>::KLD / 4) % 4 == 2 && AwLayout<76>::KLD >= 76, "K stride");
+
+template <int DH>
+size_t aw_smem_bytes(int nw) {
+    return sizeof(float) * (size_t)nw * AwLayout<DH>::WARP_FLOATS;
 }
 
-template <int DH>
-__global__ void __launch_bounds__(AD_THREADS) attn_decode_tile_kernel(AttnDecodeArgs a, int max_splits) {
-    using L = AdLayout<DH>;
-    constexpr int HALF = DH / 2;
-    static_assert(L::G * DH <= AD_TILE * L::KLD, "PV partials must fit in the K tile");
+template <int DH, int NW>
+__global__ void __launch_bounds__(NW * 32) attn_decode_warp_kernel(AttnDecodeArgs a, int max_splits) {
+    using L = AwLayout<DH>;
+    constexpr int HALF = DH / 2, DH4 = DH / 4, SPLIT = NW * AW_KEYS, CHUNKS = DH / 8;
     extern __shared__ __align__(16) float sm[];
-    float* kt = sm;                       // [AD_TILE][KLD]; PV partials after the scores
-    float* vt = kt + AD_TILE * L::KLD;    // [AD_TILE][KLD]
-    float* qs = vt + AD_TILE * L::KLD;
-    float* kn = qs + DH;
-    float* vn = kn + DH;
-    float* sc = vn + DH;                  // [AD_TILE]
-    float* scratch = sc + AD_TILE;        // [AD_TILE]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float* kt = sm + warp * L::WARP_FLOATS;  // [16][KLD]
+    float* vt = kt + AW_KEYS * L::KLD;       // [16][DH]
+    float* qw = vt + AW_KEYS * DH;           // [DH]
+    float* part = qw + DH;                   // [DH + 2]: o, max, sum
 
-    const int b = blockIdx.x, h = blockIdx.y, sp = blockIdx.z, tid = threadIdx.x;
+    const int b = blockIdx.x, h = blockIdx.y, sp = blockIdx.z;
     if (a.active && !a.active[b]) return;
     const int pos = a.pos[b];
     if (pos < 0 || pos >= a.ctx) return;  // the host rejects these before launch
     const int nkeys = pos + 1;
-    const int j0 = sp * AD_TILE;
-    if (j0 >= nkeys) return;
-    const int nk = min(AD_TILE, nkeys - j0);
-    const int nsplit = (nkeys + AD_TILE - 1) / AD_TILE;
+    const int j0 = sp * SPLIT;
+    if (j0 >= nkeys) return;  // uniform over the CTA
+    const int nsplit = (nkeys + SPLIT - 1) / SPLIT;
+    const int jw = j0 + warp * AW_KEYS;                // this warp's first key
+    const int nkw = max(0, min(AW_KEYS, nkeys - jw));  // and its key count
     const size_t cbase = (size_t)b * a.c_sb + (size_t)h * a.c_sh;
 
-    // Cached rows j0..j0+nk-1 except the new one (slot pos), K then V.
-    for (int i = tid; i < nk * L::DH4; i += AD_THREADS) {
-        const int r = i / L::DH4, c4 = i % L::DH4;
-        if (j0 + r != pos) cp_async16(kt + r * L::KLD + c4 * 4, a.kc + cbase + (size_t)(j0 + r) * a.c_st + c4 * 4);
+    for (int i = lane; i < nkw * DH4; i += 32) {
+        const int r = i / DH4, c4 = i % DH4;
+        if (jw + r != pos) cp_async16(kt + r * L::KLD + c4 * 4, a.kc + cbase + (size_t)(jw + r) * a.c_st + c4 * 4);
     }
     cp_async_commit();
-    for (int i = tid; i < nk * L::DH4; i += AD_THREADS) {
-        const int r = i / L::DH4, c4 = i % L::DH4;
-        if (j0 + r != pos) cp_async16(vt + r * L::KLD + c4 * 4, a.vc + cbase + (size_t)(j0 + r) * a.c_st + c4 * 4);
+    for (int i = lane; i < nkw * DH4; i += 32) {
+        const int r = i / DH4, c4 = i % DH4;
+        if (jw + r != pos) cp_async16(vt + r * DH + c4 * 4, a.vc + cbase + (size_t)(jw + r) * a.c_st + c4 * 4);
     }
     cp_async_commit();
 
+    // RoPE on q (every warp its own copy) and, in the warp holding slot pos,
+    // on the new k, which is appended with v (src/model.rs:721-733).
     const size_t in_off = (size_t)b * a.in_sb + (size_t)h * a.in_sh;
-    if (tid < DH) {
-        qs[tid] = a.q[in_off + tid];
-        kn[tid] = a.k[in_off + tid];
-        vn[tid] = a.v[in_off + tid];
-    }
-    __syncthreads();
-    if (tid < HALF) {  // src/model.rs:721-728
+    const bool owner = nkw > 0 && pos < jw + nkw;
+    const int rn = pos - jw;
+    for (int i = lane; i < HALF; i += 32) {
         float c, s;
         if (a.rope) {
-            const float2 cs = a.rope[(size_t)pos * HALF + tid];
+            const float2 cs = a.rope[(size_t)pos * HALF + i];
             c = cs.x;
             s = cs.y;
         } else {
-            rope_cs(tid, DH, pos, a.theta, c, s);
+            rope_cs(i, DH, pos, a.theta, c, s);
         }
-        rope_pair(qs[tid], qs[tid + HALF], c, s);
-        rope_pair(kn[tid], kn[tid + HALF], c, s);
+        float q0 = a.q[in_off + i], q1 = a.q[in_off + i + HALF];
+        rope_pair(q0, q1, c, s);
+        qw[i] = q0;
+        qw[i + HALF] = q1;
+        if (owner) {
+            float k0 = a.k[in_off + i], k1 = a.k[in_off + i + HALF];
+            rope_pair(k0, k1, c, s);
+            const float v0 = a.v[in_off + i], v1 = a.v[in_off + i + HALF];
+            kt[rn * L::KLD + i] = k0;
+            kt[rn * L::KLD + i + HALF] = k1;
+            vt[rn * DH + i] = v0;
+            vt[rn * DH + i + HALF] = v1;
+            float* kd = a.kc + cbase + (size_t)pos * a.c_st;
+            float* vd = a.vc + cbase + (size_t)pos * a.c_st;
+            kd[i] = k0;
+            kd[i + HALF] = k1;
+            vd[i] = v0;
+            vd[i + HALF] = v1;
+        }
     }
-    __syncthreads();
-    if (j0 + nk == nkeys && tid < DH) {  // KV append (src/model.rs:730-733) by the block holding slot pos
-        const int r = pos - j0;
-        kt[r * L::KLD + tid] = kn[tid];
-        vt[r * L::KLD + tid] = vn[tid];
-        a.kc[cbase + (size_t)pos * a.c_st + tid] = kn[tid];
-        a.vc[cbase + (size_t)pos * a.c_st + tid] = vn[tid];
-    }
-    cp_async_wait<1>();  // K rows of this thread landed
-    __syncthreads();
+    cp_async_wait<1>();
+    __syncwarp();
 
-    // scores (src/model.rs:742-748): dot(q_h, k_j) * (1/sqrt(dh))
+    // scores (src/model.rs:742-748): dot(q_h, k_j) * (1/sqrt(dh)), keys lane/2
     const float scale = 1.0f / sqrtf((float)DH);
-    float mx = -INFINITY;
-    if (tid < nk) {
-        const float sv = dot_ref(qs, kt + tid * L::KLD, DH) * scale;
-        sc[tid] = sv;
-        mx = sv;
+    const int r = lane >> 1, hf = lane & 1;
+    const bool valid = r < nkw;
+    float sv = -INFINITY;
+    {
+        const float* kr = kt + (valid ? r : 0) * L::KLD + 4 * hf;
+        const float* qr = qw + 4 * hf;
+        float l0 = 0.f, l1 = 0.f, l2 = 0.f, l3 = 0.f;
+#pragma unroll
+        for (int c = 0; c < CHUNKS; ++c) {
+            const float4 x = *reinterpret_cast<const float4*>(qr + 8 * c);
+            const float4 y = *reinterpret_cast<const float4*>(kr + 8 * c);
+            l0 = fmaf(x.x, y.x, l0); l1 = fmaf(x.y, y.y, l1);
+            l2 = fmaf(x.z, y.z, l2); l3 = fmaf(x.w, y.w, l3);
+        }
+        const float l4 = __shfl_xor_sync(0xffffffffu, l0, 1), l5 = __shfl_xor_sync(0xffffffffu, l1, 1);
+        const float l6 = __shfl_xor_sync(0xffffffffu, l2, 1), l7 = __shfl_xor_sync(0xffffffffu, l3, 1);
+        float d = ((l0 + l4) + (l2 + l6)) + ((l1 + l5) + (l3 + l7));
+        for (int i = CHUNKS * 8; i < DH; ++i) d = d + qw[i] * kt[(valid ? r : 0) * L::KLD + i];
+        d = __shfl_sync(0xffffffffu, d, lane & ~1);  // the even lane's fold
+        if (valid) sv = d * scale;
     }
-    // softmax over this block (src/math.rs:213-232)
-    const float m = block_reduce(mx, scratch, true);
-    float e = 0.0f;
-    if (tid < nk) {
-        e = expf(sc[tid] - m);
-        sc[tid] = e;
-    }
-    const float l = block_reduce(e, scratch + 32, false);
-    if (nsplit == 1 && tid < nk) sc[tid] = sc[tid] * (1.0f / l);
+    // softmax partial over the warp's keys (src/math.rs:213-232)
+    const float mw = warp_max(sv);
+    const float e = valid ? expf(sv - mw) : 0.0f;
+    const float lw = warp_sum(hf == 0 ? e : 0.0f);
     cp_async_wait<0>();
+    __syncwarp();
+
+    // out += w_j * v_j (src/model.rs:752-759) over the warp's keys, in order
+    float o[L::ND];
+#pragma unroll
+    for (int i = 0; i < L::ND; ++i) o[i] = 0.0f;
+    for (int k = 0; k < nkw; ++k) {
+        const float w = __shfl_sync(0xffffffffu, e, 2 * k);
+#pragma unroll
+        for (int i = 0; i < L::ND; ++i) {
+            const int d = lane + 32 * i;
+            if (d < DH) o[i] = o[i] + w * vt[k * DH + d];
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < L::ND; ++i) {
+        const int d = lane + 32 * i;
+        if (d < DH) part[d] = o[i];
+    }
+    if (lane == 0) {
+        part[DH] = nkw > 0 ? mw : -INFINITY;
+        part[DH + 1] = lw;
+    }
     __syncthreads();
 
-    // out += w_j * v_j (src/model.rs:752-759)
-    const int g = tid / L::DH4, d4 = tid % L::DH4;
-    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (g < L::G) {
-        for (int r = g; r < nk; r += L::G) {
-            const float w = sc[r];
-            const float4 vv = *reinterpret_cast<const float4*>(vt + r * L::KLD + d4 * 4);
-            o.x = o.x + w * vv.x;
-            o.y = o.y + w * vv.y;
-            o.z = o.z + w * vv.z;
-            o.w = o.w + w * vv.w;
+    // merge the warps' partials
+    for (int d = threadIdx.x; d < DH; d += NW * 32) {
+        float m = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) m = fmaxf(m, sm[w * L::WARP_FLOATS + AW_KEYS * (L::KLD + DH) + DH + DH]);
+        float acc = 0.0f, l = 0.0f;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) {
+            const float* pw = sm + w * L::WARP_FLOATS + AW_KEYS * (L::KLD + DH) + DH;
+            if (pw[DH] == -INFINITY) continue;  // a warp past the last key
+            const float f = expf(pw[DH] - m);
+            acc = acc + pw[d] * f;
+            l = l + pw[DH + 1] * f;
         }
-        *reinterpret_cast<float4*>(kt + g * DH + d4 * 4) = o;
-    }
-    __syncthreads();
-    if (tid < DH) {
-        float acc = kt[tid];
-        for (int gg = 1; gg < L::G; ++gg) acc = acc + kt[gg * DH + tid];
         if (nsplit == 1) {
-            a.out[(size_t)b * a.o_sb + (size_t)h * a.o_sh + (size_t)tid * a.o_sd] = acc;
+            a.out[(size_t)b * a.o_sb + (size_t)h * a.o_sh + (size_t)d * a.o_sd] = acc * (1.0f / l);
         } else {
             float* wp = a.work + (((size_t)b * a.H + h) * max_splits + sp) * (DH + 2);
-            wp[tid] = acc;
-            if (tid == 0) {
+            wp[d] = acc;
+            if (d == 0) {
                 wp[DH] = m;
                 wp[DH + 1] = l;
             }
@@ -471,13 +528,17 @@ cudaError_t attn_decode(const AttnDecodeArgs& a, cudaStream_t s) {
     const int keys = a.max_keys > 0 && a.max_keys < a.ctx ? a.max_keys : a.ctx;
     dim3 grid(a.B, a.H, (keys + a.split - 1) / a.split);
     cudaError_t e;
-    if (a.split == AD_TILE) {
-        const void* fn = a.dh == 76 ? (const void*)attn_decode_tile_kernel<76> : (const void*)attn_decode_tile_kernel<64>;
-        const size_t smem = a.dh == 76 ? adt_smem_bytes<76>() : adt_smem_bytes<64>();
-        static DeviceOnce once76, once64;
-        if ((e = (a.dh == 76 ? once76 : once64).set_smem(fn, smem)) != cudaSuccess) return e;
-        if (a.dh == 76) attn_decode_tile_kernel<76><<<grid, AD_THREADS, smem, s>>>(a, max_splits);
-        else attn_decode_tile_kernel<64><<<grid, AD_THREADS, smem, s>>>(a, max_splits);
+    if (a.split == 16 * 4 || a.split == 16 * 8) {
+        const int nw = a.split / 16;
+        const void* fn = a.dh == 76 ? (nw == 4 ? (const void*)attn_decode_warp_kernel<76, 4> : (const void*)attn_decode_warp_kernel<76, 8>)
+                                    : (nw == 4 ? (const void*)attn_decode_warp_kernel<64, 4> : (const void*)attn_decode_warp_kernel<64, 8>);
+        const size_t smem = a.dh == 76 ? aw_smem_bytes<76>(nw) : aw_smem_bytes<64>(nw);
+        static DeviceOnce once[4];
+        if ((e = once[(a.dh == 76 ? 2 : 0) + (nw == 8)].set_smem(fn, smem)) != cudaSuccess) return e;
+        if (a.dh == 76 && nw == 4) attn_decode_warp_kernel<76, 4><<<grid, 128, smem, s>>>(a, max_splits);
+        else if (a.dh == 76) attn_decode_warp_kernel<76, 8><<<grid, 256, smem, s>>>(a, max_splits);
+        else if (nw == 4) attn_decode_warp_kernel<64, 4><<<grid, 128, smem, s>>>(a, max_splits);
+        else attn_decode_warp_kernel<64, 8><<<grid, 256, smem, s>>>(a, max_splits);
     } else if (a.dh == 76) {
         static DeviceOnce once;
         const size_t smem = ad_smem_bytes<76>(a.split);

@@ -170,12 +170,14 @@ class PebbleState:
         check(lib.krk_state_profile(self._h, int(bool(enable))))
 
     def profile_read(self) -> dict:
-        """{class: (device ms, launches)} accumulated since profile()."""
+        """{class: (device ms, launches, decode sequences)} accumulated since
+        profile().  Kernel times of the two decode streams may overlap."""
         out = {}
         for i, name in enumerate(_lib.PROF_CLASSES):
-            ms, n = C.c_double(), C.c_int64()
+            ms, n, u = C.c_double(), C.c_int64(), C.c_int64()
             check(lib.krk_state_profile_read(self._h, i, C.byref(ms), C.byref(n)))
-            out[name] = (ms.value, n.value)
+            check(lib.krk_state_profile_units(self._h, i, C.byref(u)))
+            out[name] = (ms.value, n.value, u.value)
         return out
 
     def close(self) -> None:

@@ -205,7 +205,7 @@ def test_conv_ssd_scan_split_invariance_full_size():
 
 
 # ------------------------------------------------------------- attention
-@pytest.mark.parametrize("split", [64, 256, 2048])
+@pytest.mark.parametrize("split", [64, 128, 256, 2048])
 def test_rope_kv_attn_decode_full_size(split):
     """Config: q,k,v [64,8,1,64], positions ~U[0,2048), cache [64,8,2048,64]."""
     q, k, v, pos, kc, vc = synth.attn_decode_inputs()
@@ -221,9 +221,12 @@ def test_rope_kv_attn_decode_full_size(split):
         np.testing.assert_array_equal(gk[b, :, : pos[b]], kc[b, :, : pos[b]])  # history untouched
 
 
-@pytest.mark.parametrize("dh,ctx,posv", [(76, 16, [0, 15, 7]), (64, 300, [0, 63, 64, 299]), (76, 700, [699, 1, 256])])
-def test_rope_kv_attn_decode_edges(dh, ctx, posv):
-    """First slot, last slot, split boundaries, head dim 76 (19 float4s)."""
+@pytest.mark.parametrize("split", [64, 128])
+@pytest.mark.parametrize("dh,ctx,posv", [(76, 16, [0, 15, 7]), (64, 300, [0, 63, 64, 299]), (76, 700, [699, 1, 256]),
+                                         (64, 200, [15, 16, 17, 47, 48, 127, 128, 199]),
+                                         (76, 200, [15, 16, 31, 32, 63, 64, 65, 191])])
+def test_rope_kv_attn_decode_edges(dh, ctx, posv, split):
+    """First slot, last slot, 16-key warp and split boundaries, head dim 76 (19 float4s)."""
     rng = np.random.default_rng(dh + ctx)
     bsz, nh = len(posv), 8
     q = rng.standard_normal((bsz, nh, dh)).astype(np.float32)
@@ -232,9 +235,13 @@ def test_rope_kv_attn_decode_edges(dh, ctx, posv):
     kc = rng.standard_normal((bsz, nh, ctx, dh)).astype(np.float32)
     vc = rng.standard_normal((bsz, nh, ctx, dh)).astype(np.float32)
     pos = np.array(posv, np.int32)
-    out = K.rope_kv_attn_decode(cu(q), cu(k), cu(v), cu(kc), cu(vc), cu(pos), split=64)
-    ref = O.rope_kv_attn_decode(q, k, v, kc.copy(), vc.copy(), pos)
+    g_kc, g_vc = cu(kc), cu(vc)
+    out = K.rope_kv_attn_decode(cu(q), cu(k), cu(v), g_kc, g_vc, cu(pos), split=split)
+    o_kc, o_vc = kc.copy(), vc.copy()
+    ref = O.rope_kv_attn_decode(q, k, v, o_kc, o_vc, pos)
     np.testing.assert_allclose(np_(out), ref, atol=1e-4, rtol=1e-5)
+    np.testing.assert_allclose(np_(g_kc), o_kc, atol=1e-5, rtol=1e-5)  # appended roped k, history untouched
+    np.testing.assert_array_equal(np_(g_vc), o_vc)
 
 
 # ------------------------------------------------------------- sampling

@@ -170,3 +170,32 @@ def test_c5_subset_token_streams(models):
     for b in (0, 15):
         ref, _ = O.generate_greedy(orc, O.OracleState(2048), prompts[b].tolist(), 256, eos=None)
         assert got[b] == ref, b
+
+
+def test_large_batch_halves_match_single_sequences(models):
+    """A batch of 256+ sequences decodes as two halves on two streams; every
+    sequence's logits equal (bitwise) those of the same sequence run alone, on
+    both sides of the split, and match the oracle."""
+    gpu, orc = models
+    bsz = 260
+    rng = np.random.default_rng(11)
+    lens = rng.integers(1, 40, bsz)
+    prompts = [rng.integers(0, 2048, n).astype(np.uint32).tolist() for n in lens]
+    st = PebbleState(gpu, 64, batch=bsz)
+    gpu.prefill_batch(prompts, st)
+    picks = (0, 127, 128, 200, bsz - 1)
+    alone = {b: PebbleState(gpu, 64) for b in picks}
+    for b in picks:
+        gpu.forward_prefill(prompts[b], alone[b])
+    ost = O.OracleState(64)
+    O.forward_prefill(orc, ost, prompts[bsz - 1])
+    for step in range(3):
+        toks = [(29 * b + 7 * step) % 2048 for b in range(bsz)]
+        lg = gpu.step_batch(toks, st)
+        for b in picks:
+            np.testing.assert_array_equal(lg[b], gpu.forward_step(toks[b], alone[b]), err_msg=f"seq {b}")
+        close(lg[bsz - 1], O.forward_step(orc, ost, toks[bsz - 1]), f"step {step}")
+    got = gpu.generate_greedy(prompts, st, 6, stop_at_eos=False)
+    for b in (3, 255):
+        ref, _ = O.generate_greedy(orc, O.OracleState(64), prompts[b], 6, eos=None)
+        assert got[b] == ref, b
