@@ -10,6 +10,9 @@
 // a full 64x32 output tile of partial sums in registers (8x8 per thread); the
 // eight warp tiles are folded in the reference's order through shared memory in
 // the epilogue.  The result is bit-identical to the reference gemv for any M.
+// The multiply-adds are issued as packed pairs (__ffma2_rn, sm_100): each
+// component is rounded exactly as fmaf, and one instruction does two, which
+// halves the issue slots the FP32 pipes need.
 //
 // Operands: A feature-major (At[k][m], contiguous along m) and W K-major
 // (Wt[k][n], contiguous along n), so that the rows of both are dense runs that
@@ -85,11 +88,12 @@ __global__ void __launch_bounds__(NT, Tile<BM>::MIN_CTAS)
         cp_async16(Ws + r * BN + c4 * 4, Wt + (size_t)(k0 + 8 * r) * ldw + n0 + c4 * 4);
     };
 
-    float acc[TM][8];
+    // acc2[i][c] holds the partial sums of rows row_of(2i), row_of(2i + 1), column col_of(c)
+    float2 acc2[TM / 2][8];
 #pragma unroll
-    for (int i = 0; i < TM; ++i)
+    for (int i = 0; i < TM / 2; ++i)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
+        for (int c = 0; c < 8; ++c) acc2[i][c] = make_float2(0.0f, 0.0f);
 
 #pragma unroll
     for (int s = 0; s < WSTAGE - 1; ++s) {
@@ -108,23 +112,27 @@ __global__ void __launch_bounds__(NT, Tile<BM>::MIN_CTAS)
         const float* Ws = As + WROWS * BM;
 #pragma unroll
         for (int i = 0; i < WROWS; ++i) {  // k = kb*32 + warp + 8i: this warp's lane of the reference dot
-            float a[TM];
+            float2 a[TM / 2];
             {
                 const float4 a0 = *reinterpret_cast<const float4*>(As + i * BM + lm * 4);
-                a[0] = a0.x; a[1] = a0.y; a[2] = a0.z; a[3] = a0.w;
+                a[0] = make_float2(a0.x, a0.y);
+                a[1] = make_float2(a0.z, a0.w);
                 if (TM == 8) {
                     const float4 a1 = *reinterpret_cast<const float4*>(As + i * BM + 32 + lm * 4);
-                    a[TM == 8 ? 4 : 0] = a1.x; a[TM == 8 ? 5 : 1] = a1.y;
-                    a[TM == 8 ? 6 : 2] = a1.z; a[TM == 8 ? 7 : 3] = a1.w;
+                    a[TM == 8 ? 2 : 0] = make_float2(a1.x, a1.y);
+                    a[TM == 8 ? 3 : 1] = make_float2(a1.z, a1.w);
                 }
             }
             const float4 w0 = *reinterpret_cast<const float4*>(Ws + i * BN + ln * 4);
             const float4 w1 = *reinterpret_cast<const float4*>(Ws + i * BN + 16 + ln * 4);
             const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+            // two fused multiply-adds per instruction, each rounded as fmaf
 #pragma unroll
-            for (int r = 0; r < TM; ++r)
+            for (int c = 0; c < 8; ++c) {
+                const float2 wc = make_float2(w[c], w[c]);
 #pragma unroll
-                for (int c = 0; c < 8; ++c) acc[r][c] = fmaf(a[r], w[c], acc[r][c]);
+                for (int r = 0; r < TM / 2; ++r) acc2[r][c] = __ffma2_rn(a[r], wc, acc2[r][c]);
+            }
         }
     }
     cp_async_wait<0>();
@@ -132,24 +140,25 @@ __global__ void __launch_bounds__(NT, Tile<BM>::MIN_CTAS)
 
     // Spill the eight lane-partial tiles, laid out along the output's
     // contiguous dimension.
+    auto acc = [&](int r, int c) -> float { return (r & 1) ? acc2[r >> 1][c].y : acc2[r >> 1][c].x; };
     float* red = sm;
     if (!OUT_FM) {
         float* base = red + warp * (BM * RLD_BM);
 #pragma unroll
         for (int r = 0; r < TM; ++r) {
             float* d = base + row_of<BM>(lm, r) * RLD_BM;
-            *reinterpret_cast<float4*>(d + ln * 4) = make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
-            *reinterpret_cast<float4*>(d + 16 + ln * 4) = make_float4(acc[r][4], acc[r][5], acc[r][6], acc[r][7]);
+            *reinterpret_cast<float4*>(d + ln * 4) = make_float4(acc(r, 0), acc(r, 1), acc(r, 2), acc(r, 3));
+            *reinterpret_cast<float4*>(d + 16 + ln * 4) = make_float4(acc(r, 4), acc(r, 5), acc(r, 6), acc(r, 7));
         }
     } else {
         float* base = red + warp * (BN * T::RLD_FM);
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
             float* d = base + col_of(ln, c) * T::RLD_FM;
-            *reinterpret_cast<float4*>(d + lm * 4) = make_float4(acc[0][c], acc[1][c], acc[2][c], acc[3][c]);
+            *reinterpret_cast<float4*>(d + lm * 4) = make_float4(acc(0, c), acc(1, c), acc(2, c), acc(3, c));
             if (TM == 8)
                 *reinterpret_cast<float4*>(d + 32 + lm * 4) = make_float4(
-                    acc[TM == 8 ? 4 : 0][c], acc[TM == 8 ? 5 : 1][c], acc[TM == 8 ? 6 : 2][c], acc[TM == 8 ? 7 : 3][c]);
+                    acc(TM == 8 ? 4 : 0, c), acc(TM == 8 ? 5 : 1, c), acc(TM == 8 ? 6 : 2, c), acc(TM == 8 ? 7 : 3, c));
         }
     }
     __syncthreads();
