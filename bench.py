@@ -275,14 +275,14 @@ def run_ours(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
     torch.cuda.set_device(local)
 
-    from krikil_rs_b200 import PebbleModel, PebbleState, launch_count, synth
+    from krikil_rs_b200 import PebbleModel, PebbleState, launch_count, replicas, synth
     from krikil_rs_b200._lib import check, lib
 
     peak, peak_kind = measured_peaks()
     path = synth.weights_file(0)
     model = PebbleModel.load_safetensors(path, device=local)
     seqs, plen, new = args.seqs, args.prompt_len, args.new_tokens
-    prompts = synth.decode_prompts(world * seqs, plen, seed=1)[rank * seqs:(rank + 1) * seqs]
+    prompts = replicas.shard(synth.decode_prompts(world * seqs, plen, seed=1), world, rank)
     state = PebbleState(model, args.ctx, batch=seqs)
 
     # pinned host buffers for the end-to-end calls
@@ -319,16 +319,9 @@ def run_ours(args):
     prof = state.profile_read()
     state.profile(False)
     dev_ms = prof["device_total"][0]
+    (e2e_ms, dev_ms), total_tokens = replicas.reduce_timings(dist, "cuda", [e2e_ms, dev_ms], gen_tokens)
     if world > 1:
-        t = torch.tensor([e2e_ms, dev_ms], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms, dev_ms = float(t[0]), float(t[1])
-        g = torch.tensor([gen_tokens], dtype=torch.int64, device="cuda")
-        dist.all_reduce(g)
-        total_tokens = int(g[0])
         dist.barrier()
-    else:
-        total_tokens = gen_tokens
     expect = world * seqs * min(new, args.ctx - plen + 1) * args.steps
     assert total_tokens == expect, (total_tokens, expect)
 

@@ -88,12 +88,14 @@ __global__ void __launch_bounds__(NT, Tile<BM>::MIN_CTAS)
         cp_async16(Ws + r * BN + c4 * 4, Wt + (size_t)(k0 + 8 * r) * ldw + n0 + c4 * 4);
     };
 
-    // acc2[i][c] holds the partial sums of rows row_of(2i), row_of(2i + 1), column col_of(c)
-    float2 acc2[TM / 2][8];
+    // Partial sums in pairs, one __ffma2_rn per pair.  Batch-major output pairs
+    // rows: acc2[i*8 + c] = rows (2i, 2i+1) of column c; feature-major output
+    // pairs columns: acc2[r*4 + j] = columns (2j, 2j+1) of row r (indices of
+    // row_of / col_of).  The two forms differ only in register allocation.
+    constexpr bool PAIR_ROWS = !OUT_FM;
+    float2 acc2[TM * 4];
 #pragma unroll
-    for (int i = 0; i < TM / 2; ++i)
-#pragma unroll
-        for (int c = 0; c < 8; ++c) acc2[i][c] = make_float2(0.0f, 0.0f);
+    for (int i = 0; i < TM * 4; ++i) acc2[i] = make_float2(0.0f, 0.0f);
 
 #pragma unroll
     for (int s = 0; s < WSTAGE - 1; ++s) {
@@ -112,26 +114,36 @@ __global__ void __launch_bounds__(NT, Tile<BM>::MIN_CTAS)
         const float* Ws = As + WROWS * BM;
 #pragma unroll
         for (int i = 0; i < WROWS; ++i) {  // k = kb*32 + warp + 8i: this warp's lane of the reference dot
-            float2 a[TM / 2];
+            float a[TM];
             {
                 const float4 a0 = *reinterpret_cast<const float4*>(As + i * BM + lm * 4);
-                a[0] = make_float2(a0.x, a0.y);
-                a[1] = make_float2(a0.z, a0.w);
+                a[0] = a0.x; a[1] = a0.y; a[2] = a0.z; a[3] = a0.w;
                 if (TM == 8) {
                     const float4 a1 = *reinterpret_cast<const float4*>(As + i * BM + 32 + lm * 4);
-                    a[TM == 8 ? 2 : 0] = make_float2(a1.x, a1.y);
-                    a[TM == 8 ? 3 : 1] = make_float2(a1.z, a1.w);
+                    a[TM == 8 ? 4 : 0] = a1.x; a[TM == 8 ? 5 : 1] = a1.y;
+                    a[TM == 8 ? 6 : 2] = a1.z; a[TM == 8 ? 7 : 3] = a1.w;
                 }
             }
             const float4 w0 = *reinterpret_cast<const float4*>(Ws + i * BN + ln * 4);
             const float4 w1 = *reinterpret_cast<const float4*>(Ws + i * BN + 16 + ln * 4);
             const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
             // two fused multiply-adds per instruction, each rounded as fmaf
+            if (PAIR_ROWS) {
 #pragma unroll
-            for (int c = 0; c < 8; ++c) {
-                const float2 wc = make_float2(w[c], w[c]);
+                for (int c = 0; c < 8; ++c) {
+                    const float2 wc = make_float2(w[c], w[c]);
 #pragma unroll
-                for (int r = 0; r < TM / 2; ++r) acc2[r][c] = __ffma2_rn(a[r], wc, acc2[r][c]);
+                    for (int r = 0; r < TM / 2; ++r)
+                        acc2[r * 8 + c] = __ffma2_rn(make_float2(a[2 * r], a[2 * r + 1]), wc, acc2[r * 8 + c]);
+                }
+            } else {
+#pragma unroll
+                for (int r = 0; r < TM; ++r) {
+                    const float2 ar = make_float2(a[r], a[r]);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                        acc2[r * 4 + j] = __ffma2_rn(ar, make_float2(w[2 * j], w[2 * j + 1]), acc2[r * 4 + j]);
+                }
             }
         }
     }
@@ -140,7 +152,10 @@ __global__ void __launch_bounds__(NT, Tile<BM>::MIN_CTAS)
 
     // Spill the eight lane-partial tiles, laid out along the output's
     // contiguous dimension.
-    auto acc = [&](int r, int c) -> float { return (r & 1) ? acc2[r >> 1][c].y : acc2[r >> 1][c].x; };
+    auto acc = [&](int r, int c) -> float {
+        if (PAIR_ROWS) return (r & 1) ? acc2[(r >> 1) * 8 + c].y : acc2[(r >> 1) * 8 + c].x;
+        return (c & 1) ? acc2[r * 4 + (c >> 1)].y : acc2[r * 4 + (c >> 1)].x;
+    };
     float* red = sm;
     if (!OUT_FM) {
         float* base = red + warp * (BM * RLD_BM);
