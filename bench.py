@@ -218,6 +218,27 @@ def kernel_table(torch, peak, scan_t=2048):
         if extra:
             res[name].update(extra)
 
+    # projections at the decode shapes of one 1024-sequence step (nominal FP32 peak)
+    fp32_peak = 148 * 128 * 2 * 1.965e9
+    g = torch.Generator(device=dev).manual_seed(0)
+    # bring the clocks up from idle before the first timing (about 0.5 s of work)
+    a = torch.randn(608, 1024, device=dev, generator=g)
+    wt = torch.randn(608, 2720, device=dev, generator=g)
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < 0.5:
+        for _ in range(20):
+            K.gemm(a, wt)
+        torch.cuda.synchronize()
+    for name, m, n, kd, epi, fm in (("in_proj", 1024, 2720, 608, 0, False), ("fc2", 1024, 608, 2432, 1, True)):
+        a = torch.randn(kd, m, device=dev, generator=g)
+        wt = torch.randn(kd, n, device=dev, generator=g)
+        c = torch.zeros((n, m) if fm else (m, n), device=dev)
+        ms = timeit(lambda: K.gemm(a, wt, epilogue=epi, out_fm=fm, c=c))
+        fl = 2 * m * n * kd
+        res[f"gemm_{name}[{m}x{n}x{kd}]"] = {"ms": round(ms, 4), "tflops": round(fl / (ms * 1e-3) / 1e12, 2),
+                                            "fp32_frac_nominal": round(fl / (ms * 1e-3) / fp32_peak, 3)}
+        del a, wt, c
+
     x, z, r, w = (torch.from_numpy(a).to(dev) for a in synth.fused_norm_inputs())
     y = torch.empty_like(x)
     put("gated_rmsnorm_residual[16384,512]", 4 * x.numel() * 4 + w.numel() * 4,

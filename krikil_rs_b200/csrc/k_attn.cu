@@ -33,16 +33,14 @@ KRK_DEV void rope_pair(float& x0, float& x1, float c, float s) {
     x0 = a * c - b * s;
     x1 = a * s + b * c;
 }
-// The f32 operations are the reference's; powf, cosf and sinf are evaluated in
-// double precision and rounded once to f32 (a correctly rounded result, which
-// is what the host libm returns for all but rare arguments), because the angle
-// pos * invf reaches ~2047 rad and f32 library errors of a few ulps would show.
-KRK_DEV void rope_cs(int i, int dh, int pos, float theta, float& c, float& s) {
-    const float e = ((float)i * 2.0f) / (float)dh;
-    const float invf = 1.0f / (float)pow((double)theta, (double)e);
-    const float ang = (float)pos * invf;
-    c = (float)cos((double)ang);
-    s = (float)sin((double)ang);
+// (cos, sin) of pair i at position pos (src/math.rs:243-247): the angle is the
+// reference's f32 product pos * inv_freq[i], with inv_freq[i] = 1/powf(theta,
+// 2i/dh) computed on the host by the same libm powf the reference calls (the
+// angle reaches ~2047 rad, so inv_freq must be exact: one ulp of it moves the
+// angle by ~1e-4), and cos/sin from CUDA's sincosf (within 2 ulp).
+KRK_DEV void rope_cs(const RopeFreqs& fr, int i, int pos, float& c, float& s) {
+    const float ang = (float)pos * fr.f[i];
+    sincosf(ang, &s, &c);
 }
 
 constexpr int AD_THREADS = 128;
@@ -109,7 +107,7 @@ __global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(AttnDecodeArgs 
             c = cs.x;
             s = cs.y;
         } else {
-            rope_cs(tid, DH, pos, a.theta, c, s);
+            rope_cs(a.freq, tid, pos, c, s);
         }
         rope_pair(qs[tid], qs[tid + HALF], c, s);
         rope_pair(kn[tid], kn[tid + HALF], c, s);
@@ -283,7 +281,7 @@ __global__ void __launch_bounds__(NW * 32) attn_decode_warp_kernel(AttnDecodeArg
             c = cs.x;
             s = cs.y;
         } else {
-            rope_cs(i, DH, pos, a.theta, c, s);
+            rope_cs(a.freq, i, pos, c, s);
         }
         float q0 = a.q[in_off + i], q1 = a.q[in_off + i + HALF];
         rope_pair(q0, q1, c, s);
@@ -416,7 +414,8 @@ __global__ void attn_combine_kernel(AttnDecodeArgs a, int max_splits) {
 __global__ void rope_kv_prefill_kernel(float* __restrict__ qkv, int64_t q_rs, float* __restrict__ kc,
                                        float* __restrict__ vc, int64_t c_sb, int64_t c_sh, int64_t c_st,
                                        const int32_t* __restrict__ cu, const int32_t* __restrict__ start, int S,
-                                       int H, int dh, int total_rows, float theta, const float2* __restrict__ rope) {
+                                       int H, int dh, int total_rows, const RopeFreqs freq,
+                                       const float2* __restrict__ rope) {
     const int half = dh / 2;
     const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (gid >= (int64_t)total_rows * H * half) return;
@@ -436,7 +435,7 @@ __global__ void rope_kv_prefill_kernel(float* __restrict__ qkv, int64_t q_rs, fl
         c = cs.x;
         s = cs.y;
     } else {
-        rope_cs(i, dh, pos, theta, c, s);
+        rope_cs(freq, i, pos, c, s);
     }
     float* qr = qkv + (size_t)row * q_rs + (size_t)h * dh;
     float* kr = qkv + (size_t)row * q_rs + (size_t)H * dh + (size_t)h * dh;
@@ -513,12 +512,21 @@ __global__ void attn_prefill_kernel(const float* __restrict__ qkv, int64_t q_rs,
 
 }  // namespace
 
+RopeFreqs rope_freqs(int dh, float theta) {
+    RopeFreqs r{};
+    for (int i = 0; i < dh / 2 && i < ROPE_MAX_PAIRS; ++i)
+        r.f[i] = 1.0f / powf(theta, ((float)i * 2.0f) / (float)dh);  // src/math.rs:243-245, host libm
+    return r;
+}
+
 size_t attn_decode_work_floats(int B, int H, int dh, int ctx, int split) {
     const int ms = (ctx + split - 1) / split;
     return (size_t)B * H * ms * (dh + 2);
 }
 
-cudaError_t attn_decode(const AttnDecodeArgs& a, cudaStream_t s) {
+cudaError_t attn_decode(const AttnDecodeArgs& args, cudaStream_t s) {
+    AttnDecodeArgs a = args;
+    if (!a.rope) a.freq = rope_freqs(a.dh, a.theta);
     if (a.B <= 0 || a.H <= 0 || a.ctx <= 0 || a.split <= 0 || a.split % 64 || (a.dh != 64 && a.dh != 76) ||
         (a.c_sb & 3) || (a.c_sh & 3) || (a.c_st & 3) || (((uintptr_t)a.kc | (uintptr_t)a.vc) & 15))
         return cudaErrorInvalidValue;
@@ -565,11 +573,12 @@ cudaError_t attn_decode(const AttnDecodeArgs& a, cudaStream_t s) {
 cudaError_t rope_kv_prefill(float* qkv, int64_t q_rs, float* kc, float* vc, int64_t c_sb, int64_t c_sh,
                             int64_t c_st, const int32_t* cu_seqlens, const int32_t* start, int S, int H, int dh,
                             int total_rows, float theta, const float2* rope, cudaStream_t s) {
-    if (S <= 0 || H <= 0 || dh <= 0 || (dh & 1) || total_rows <= 0) return cudaErrorInvalidValue;
+    if (S <= 0 || H <= 0 || dh <= 0 || (dh & 1) || dh > 2 * ROPE_MAX_PAIRS || total_rows <= 0)
+        return cudaErrorInvalidValue;
     const int64_t n = (int64_t)total_rows * H * (dh / 2);
     rope_kv_prefill_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(qkv, q_rs, kc, vc, c_sb, c_sh, c_st,
                                                                        cu_seqlens, start, S, H, dh, total_rows,
-                                                                       theta, rope);
+                                                                       rope_freqs(dh, theta), rope);
     add_launches(1);
     return cudaGetLastError();
 }

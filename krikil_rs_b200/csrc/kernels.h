@@ -93,6 +93,13 @@ cudaError_t ssd_scan(const SsdScanArgs& a, bool conv, cudaStream_t s);
 // Decode: per sequence b and head h, RoPE on q and the new k at position pos[b],
 // append k,v at slot pos[b], softmax(q.K^T/sqrt(dh)).V over slots 0..pos[b].
 // Cache element (b,h,t,d) at cache[b*c_sb + h*c_sh + t*c_st + d].
+// RoPE inverse frequencies 1/theta^(2i/dh) from the host libm (i < dh/2 <= 64).
+constexpr int ROPE_MAX_PAIRS = 64;
+struct RopeFreqs {
+    float f[ROPE_MAX_PAIRS];
+};
+RopeFreqs rope_freqs(int dh, float theta);
+
 struct AttnDecodeArgs {
     const float* q; const float* k; const float* v; int64_t in_sb; int64_t in_sh;  // (b,h,d) at b*in_sb + h*in_sh + d
     float* kc; float* vc; int64_t c_sb; int64_t c_sh; int64_t c_st;
@@ -104,6 +111,7 @@ struct AttnDecodeArgs {
     float theta;
     const float2* rope;                      // optional (cos, sin) table [ctx][dh/2]; null: computed in-kernel
     int max_keys;                            // > 0: no sequence has pos + 1 above this; 0: unknown (ctx)
+    RopeFreqs freq;                          // filled by attn_decode() when rope is null
 };
 size_t attn_decode_work_floats(int B, int H, int dh, int ctx, int split);
 cudaError_t attn_decode(const AttnDecodeArgs& a, cudaStream_t s);
