@@ -39,6 +39,7 @@ sys.path.insert(0, ROOT)
 HID, VOC, INTER, DIP, DI, QKV = 608, 2048, 2432, 2707, 1216, 1824
 MAMBA_LAYERS, ATTN_LAYERS = 6, 2
 SSD_STATE_FLOATS = 19 * 64 * 128
+SSD_TRAFFIC_PER_SEQ = 263.7e6 / 256  # measured: DRAM bytes per sequence of one ssd_step launch
 METRIC = "decode tokens/s (batched greedy, Pebble-25M architecture, fp32)"
 
 
@@ -388,7 +389,11 @@ def run_ours(args):
                 "ms_per_step": e2e_ms / args.steps},
         "roofline": {"kernel": "ssd_step (decode SSD update + gate)", "bound": "hbm",
                      "achieved": round(ssd_gbs, 1), "peak": peak, "unit": "GB/s", "frac": round(ssd_gbs / peak, 3),
-                     "traffic": None, "peak_kind": peak_kind,
+                     # ncu DRAM read + write of the model's ssd_step per decode sequence
+                     # (1.030 MB; 256-sequence launches), scaled to this launch size
+                     "traffic": int(SSD_TRAFFIC_PER_SEQ * ssd_seqs / max(ssd_n, 1)),
+                     "traffic_source": "ncu dram__bytes_read+write, 256-sequence launches, scaled",
+                     "peak_kind": peak_kind,
                      "algorithmic_bytes_per_launch": int(ssd_bytes / max(ssd_n, 1)),
                      "launches": ssd_n, "avg_launch_us": round(ssd_ms * 1e3 / max(ssd_n, 1), 2)},
         "roofline_gemm": {"kernel": "gemm_lane8 (fp32 SIMT projections)", "bound": "fp32",

@@ -143,12 +143,17 @@ __global__ void conv_prefill4_kernel(const float* __restrict__ xin, int64_t x_rs
 }
 
 // ---------------------------------------------------------------------------
-// Prefill scan: one CTA per (sequence, head), 256 threads; thread (p, q) keeps
-// state row p, columns n = 16j + 4q + e (j < 8, e < 4) in registers for the
-// whole sequence.  Tokens are staged CH at a time in shared memory (x, gate,
-// B, C, dt, dA); y of the chunk is buffered and written coalesced.  The state
-// update uses one FMA per element (s = fma(s, dA, B*xdt)) and y four partial
-// FMA chains, so results agree with the sequential reference within rounding.
+// Prefill scan: one CTA per (sequence, head), 256 threads; thread (pp, q)
+// keeps state rows p = pp and pp + 32, columns n = 32j + 4q + e (j < 4, e < 4)
+// in registers for the whole sequence.  The eight lanes q of a row read
+// disjoint 16-byte pieces of the token's B and C rows, so each shared-memory
+// phase serves 128 distinct bytes (the kernel is bound by shared-memory
+// bandwidth, not by its FMAs).  Tokens are staged CH at a time in shared memory
+// (x, gate, B, C, dt, dA); y of the chunk is buffered and written coalesced.
+// The state update uses one FMA per element (s = fma(s, dA, B*xdt)), issued as
+// packed pairs (__fmul2_rn / __ffma2_rn round each component like the scalar
+// forms), and y partial FMA chains reduced over the eight lanes, so results
+// agree with the sequential reference within rounding.
 // CONV: conv + SiLU of the head's 64 x channels on a 3-slot state is applied
 // while staging, by threads 0..63, each owning one channel's window.
 // ---------------------------------------------------------------------------
@@ -169,19 +174,23 @@ __global__ void __launch_bounds__(256) ssd_scan_kernel(SsdScanArgs a) {
     float* sy = sda + SCAN_CH;            // [P][CH+1]
 
     const int h = blockIdx.x, sq = blockIdx.y;  // heads of a sequence adjacent: B, C shared in L2
-    const int tid = threadIdx.x, p = tid >> 2, q = tid & 3;
+    const int tid = threadIdx.x, pp = tid >> 3, q = tid & 7;
     const int r0 = a.cu_seqlens ? a.cu_seqlens[sq] : sq * a.uniform_len;
     const int r1 = a.cu_seqlens ? a.cu_seqlens[sq + 1] : (sq + 1) * a.uniform_len;
     const float dtb = a.dt_bias[h], an = a.a_neg[h], dsk = a.dsk[h];
     const int c0 = h * SSD_P;
 
-    float* st = a.ssm + (((size_t)sq * a.H + h) * SSD_P + p) * SSD_N + 4 * q;
-    float s[32];
+    // s[r][2j + k]: row pp + 32r, columns 32j + 4q + 2k, +1
+    float* st = a.ssm + (((size_t)sq * a.H + h) * SSD_P + pp) * SSD_N + 4 * q;
+    float2 s[2][8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        float4 v = *reinterpret_cast<const float4*>(st + 16 * j);
-        s[4 * j] = v.x; s[4 * j + 1] = v.y; s[4 * j + 2] = v.z; s[4 * j + 3] = v.w;
-    }
+    for (int r = 0; r < 2; ++r)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float4 v = *reinterpret_cast<const float4*>(st + r * 32 * SSD_N + 32 * j);
+            s[r][2 * j] = make_float2(v.x, v.y);
+            s[r][2 * j + 1] = make_float2(v.z, v.w);
+        }
     float cw0 = 0.f, cw1 = 0.f, cw2 = 0.f, cw3 = 0.f, cb = 0.f, w0 = 0.f, w1 = 0.f, w2 = 0.f;
     float* cst = nullptr;
     if (CONV && tid < SSD_P) {
@@ -232,32 +241,40 @@ __global__ void __launch_bounds__(256) ssd_scan_kernel(SsdScanArgs a) {
             __syncthreads();
         }
         for (int t = 0; t < nt; ++t) {
-            const float dA = sda[t];
-            const float xv = sx[t * SSD_P + p];
-            const float xdt = xv * sdt[t];
+            const float dA = sda[t], dtv = sdt[t];
+            const float2 dA2 = make_float2(dA, dA);
             const float* Bt = sB + t * SSD_N + 4 * q;
             const float* Ct = sC + t * SSD_N + 4 * q;
-            float y0 = 0.f, y1 = 0.f, y2 = 0.f, y3 = 0.f;
+            float4 bv[4], cv[4];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const float4 bv = *reinterpret_cast<const float4*>(Bt + 16 * j);
-                const float4 cv = *reinterpret_cast<const float4*>(Ct + 16 * j);
-                s[4 * j] = fmaf(s[4 * j], dA, bv.x * xdt);
-                s[4 * j + 1] = fmaf(s[4 * j + 1], dA, bv.y * xdt);
-                s[4 * j + 2] = fmaf(s[4 * j + 2], dA, bv.z * xdt);
-                s[4 * j + 3] = fmaf(s[4 * j + 3], dA, bv.w * xdt);
-                y0 = fmaf(s[4 * j], cv.x, y0);
-                y1 = fmaf(s[4 * j + 1], cv.y, y1);
-                y2 = fmaf(s[4 * j + 2], cv.z, y2);
-                y3 = fmaf(s[4 * j + 3], cv.w, y3);
+            for (int j = 0; j < 4; ++j) {
+                bv[j] = *reinterpret_cast<const float4*>(Bt + 32 * j);
+                cv[j] = *reinterpret_cast<const float4*>(Ct + 32 * j);
             }
-            float y = (y0 + y1) + (y2 + y3);
-            y += __shfl_xor_sync(0xffffffffu, y, 1);
-            y += __shfl_xor_sync(0xffffffffu, y, 2);
-            if (q == 0) {
-                float yv = y + dsk * xv;
-                if (GATE) yv = yv * sg[t * SSD_P + p];
-                sy[p * SCAN_YLD + t] = yv;
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                const float xv = sx[t * SSD_P + pp + 32 * r];
+                const float xdt = xv * dtv;
+                const float2 xdt2 = make_float2(xdt, xdt);
+                float2 y01 = make_float2(0.f, 0.f), y23 = make_float2(0.f, 0.f);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    s[r][2 * j] = __ffma2_rn(s[r][2 * j], dA2, __fmul2_rn(make_float2(bv[j].x, bv[j].y), xdt2));
+                    s[r][2 * j + 1] =
+                        __ffma2_rn(s[r][2 * j + 1], dA2, __fmul2_rn(make_float2(bv[j].z, bv[j].w), xdt2));
+                    y01 = __ffma2_rn(s[r][2 * j], make_float2(cv[j].x, cv[j].y), y01);
+                    y23 = __ffma2_rn(s[r][2 * j + 1], make_float2(cv[j].z, cv[j].w), y23);
+                }
+                float y = (y01.x + y01.y) + (y23.x + y23.y);
+                y += __shfl_xor_sync(0xffffffffu, y, 1);
+                y += __shfl_xor_sync(0xffffffffu, y, 2);
+                y += __shfl_xor_sync(0xffffffffu, y, 4);
+                if (q == 0) {
+                    const int p = pp + 32 * r;
+                    float yv = y + dsk * xv;
+                    if (GATE) yv = yv * sg[t * SSD_P + p];
+                    sy[p * SCAN_YLD + t] = yv;
+                }
             }
         }
         __syncthreads();
@@ -274,8 +291,11 @@ __global__ void __launch_bounds__(256) ssd_scan_kernel(SsdScanArgs a) {
         }
     }
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
-        *reinterpret_cast<float4*>(st + 16 * j) = make_float4(s[4 * j], s[4 * j + 1], s[4 * j + 2], s[4 * j + 3]);
+    for (int r = 0; r < 2; ++r)
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            *reinterpret_cast<float4*>(st + r * 32 * SSD_N + 32 * j) =
+                make_float4(s[r][2 * j].x, s[r][2 * j].y, s[r][2 * j + 1].x, s[r][2 * j + 1].y);
     if (CONV && tid < SSD_P) {
         cst[0] = w0; cst[1] = w1; cst[2] = w2;
     }
