@@ -385,7 +385,7 @@ def run_ours(args):
         "config": dict(workload_config(args), parallelism=f"replicas x{world} (no collectives)"),
         "e2e": {"value": total_tokens / (e2e_ms * 1e-3), "unit": "tokens/s",
                 "h2d_bytes_per_step": int(toks_h.numel() * 4 + lens_h.numel() * 4),
-                "d2h_bytes_per_step": int(out_h.numel() * 4 + n_h.numel() * 4 + seqs * 4),
+                "d2h_bytes_per_step": int(out_h.numel() * 4 + n_h.numel() * 4 + seqs * 4 + 4),
                 "ms_per_step": e2e_ms / args.steps},
         "roofline": {"kernel": "ssd_step (decode SSD update + gate)", "bound": "hbm",
                      "achieved": round(ssd_gbs, 1), "peak": peak, "unit": "GB/s", "frac": round(ssd_gbs / peak, 3),

@@ -171,6 +171,9 @@ enum {
     KRK_PROF_OTHER = 8,        /* embedding, RoPE prefill, sampling, bookkeeping */
     KRK_PROF_CLASSES = 9
 };
+/* enable: 0 off, 1 every kernel class and the whole-call total, 2 the
+ * whole-call total only (two events per call: no per-kernel event records and
+ * no per-kernel readback after the call). */
 KRK_API int krk_state_profile(krk_state* state, int enable);
 KRK_API int krk_state_profile_read(const krk_state* state, int cls, double* total_ms, int64_t* launches);
 /* Decode sequences processed by the timed launches of a class (the sum over

@@ -133,6 +133,7 @@ namespace {
 // Per-kernel-class CUDA-event timing of a state's calls (krk_state_profile).
 struct Prof {
     bool on = false;
+    bool per_kernel = false;  // false: only the KRK_PROF_DEVICE_TOTAL bracket
     bool total_open = false;
     cudaEvent_t total_start = nullptr;
     std::vector<cudaEvent_t> pool;
@@ -195,6 +196,7 @@ struct krk_state {
     int32_t* tlimit_d = nullptr;
     int32_t* slimit_d = nullptr;
     int32_t* step_d = nullptr;
+    int32_t* err_d = nullptr;  // set by a decode attention kernel whose K/V copy wait timed out
     float *h_t, *hn_t, *zx, *y_t, *yn_t, *qkv, *ao_t, *mlp_t, *logits, *attn_work;
     float2* rope = nullptr;  // (cos, sin) per [position][pair], from the host libm as src/math.rs:243-247
     int attn_split = 2048;
@@ -329,7 +331,7 @@ void create_state(krk_state* s, const krk_model* m, int B, int ctx) {
         }
     }
     b.add<int32_t>(B); b.add<uint8_t>(B); b.add<uint32_t>((size_t)B * SEEN_WORDS); b.add<uint32_t>(Mp);
-    b.add<int32_t>(B); b.add<int32_t>(B); b.add<int32_t>(1);
+    b.add<int32_t>(B); b.add<int32_t>(B); b.add<int32_t>(1); b.add<int32_t>(1);
     b.add<float>(HID * Mp); b.add<float>(HID * Mp); b.add<float>(Mp * DIP_PAD); b.add<float>(DI * Mp);
     b.add<float>(DI * Mp); b.add<float>(Mp * QKV); b.add<float>(HID * Mp); b.add<float>(INTER * Mp);
     b.add<float>(Mp * VOC); b.add<float>(work); b.add<float2>((size_t)ctx * (HD / 2));
@@ -350,6 +352,7 @@ void create_state(krk_state* s, const krk_model* m, int B, int ctx) {
     s->tlimit_d = s->arena.take<int32_t>(B);
     s->slimit_d = s->arena.take<int32_t>(B);
     s->step_d = s->arena.take<int32_t>(1);
+    s->err_d = s->arena.take<int32_t>(1);
     s->h_t = s->arena.take<float>(HID * Mp);
     s->hn_t = s->arena.take<float>(HID * Mp);
     s->zx = s->arena.take<float>(Mp * DIP_PAD);
@@ -424,7 +427,7 @@ void zero_pad_cols(float* buf, int64_t ld, int64_t valid, int rows, cudaStream_t
 // the number of decode sequences the launch processes (0 elsewhere).
 template <typename F>
 void timed_on(krk_state* s, cudaStream_t st, int cls, int64_t units, F&& f) {
-    if (!s->prof.on) {
+    if (!s->prof.on || !s->prof.per_kernel) {
         f();
         return;
     }
@@ -466,6 +469,13 @@ void prof_collect(krk_state* s) {
         s->prof.units[p.cls] += p.units;
     }
     s->prof.clear_events();
+}
+
+// Event pairs are read back lazily (reading each pair costs host time between
+// calls that the device would spend idle): at krk_state_profile_read, or once
+// many are pending.
+void prof_collect_if_large(krk_state* s) {
+    if (s->prof.pending.size() > 400000) prof_collect(s);
 }
 
 // ------------------------------------------------------------------ forward
@@ -556,6 +566,7 @@ void decode_layer(krk_state* s, int l, const uint8_t* active, int max_keys, cons
         a.B = nb; a.H = NH; a.dh = HD; a.ctx = s->ctx; a.split = s->attn_split; a.theta = THETA;
         a.rope = s->rope;
         a.max_keys = max_keys;
+        a.err = s->err_d;
         timed(s, p, KRK_PROF_ATTN_DECODE, [&] { kk(krk::attn_decode(a, st), "attention"); });
         gemm(s->ao_t + b0, L.wo_t, HID, HID, h, Mp, krk::EPI_RESIDUAL, true, "wo");
         norm(h, L.ln2, RMS_EPS, HID, hn, "ln2");
@@ -924,9 +935,17 @@ int krk_prefill(const krk_model* m, krk_state* s, const uint32_t* tokens, const 
         total_end(s);
         rc = copy_logits(s, logits_out);
         kk(cudaStreamSynchronize(m->stream), "prefill");
-        prof_collect(s);
+        prof_collect_if_large(s);
         return rc;
     });
+}
+
+// A decode attention kernel gave up waiting for its K/V copies (bounded
+// waits; the outputs of that step are not valid).  Clears the flag.
+static int device_wait_error(krk_state* s) {
+    kk(cudaMemsetAsync(s->err_d, 0, 4, s->m->stream), "status reset");
+    kk(cudaStreamSynchronize(s->m->stream), "status reset");
+    return fail(KRK_CUDA, "decode attention: a K/V copy wait timed out; outputs of this call are not valid");
 }
 
 int krk_step(const krk_model* m, krk_state* s, const uint32_t* tokens, float* logits_out) {
@@ -950,8 +969,11 @@ int krk_step(const krk_model* m, krk_state* s, const uint32_t* tokens, float* lo
         total_end(s);
         int rc = KRK_OK;
         if (logits_out) rc = copy_logits(s, logits_out);
+        int32_t err_h = 0;
+        kk(cudaMemcpyAsync(&err_h, s->err_d, 4, cudaMemcpyDeviceToHost, st), "d2h status");
         kk(cudaStreamSynchronize(st), "step");
-        prof_collect(s);
+        prof_collect_if_large(s);
+        if (err_h) return device_wait_error(s);
         return rc;
     });
 }
@@ -1013,8 +1035,11 @@ int krk_generate_greedy(const krk_model* m, krk_state* s, const uint32_t* prompt
         std::vector<int32_t> pos(B);
         kk(cudaMemcpyAsync(hist.data(), s->hist_d, hist.size() * 4, cudaMemcpyDeviceToHost, st), "d2h tokens");
         kk(cudaMemcpyAsync(pos.data(), s->pos_d, B * 4, cudaMemcpyDeviceToHost, st), "d2h pos");
+        int32_t err_h = 0;
+        kk(cudaMemcpyAsync(&err_h, s->err_d, 4, cudaMemcpyDeviceToHost, st), "d2h status");
         kk(cudaStreamSynchronize(st), "generate");
-        prof_collect(s);
+        prof_collect_if_large(s);
+        if (err_h) return device_wait_error(s);
         for (int b = 0; b < B; ++b) {
             int n = 0;
             for (int i = 0; i < tlimit[b]; ++i) {
@@ -1065,6 +1090,7 @@ int krk_state_profile(krk_state* s, int enable) {
         kk(cudaStreamSynchronize(s->m->stream), "profile");
         s->prof.clear_events();
         s->prof.on = enable != 0;
+        s->prof.per_kernel = enable == 1;
         for (int i = 0; i < KRK_PROF_CLASSES; ++i) {
             s->prof.ms[i] = 0.0;
             s->prof.n[i] = 0;
@@ -1074,18 +1100,35 @@ int krk_state_profile(krk_state* s, int enable) {
     });
 }
 
+// Folds the event pairs still pending (the state's calls have all returned, so
+// their streams are idle once synchronised).
+static void prof_settle(const krk_state* cs) {
+    krk_state* s = const_cast<krk_state*>(cs);  // the totals are a cache of the recorded events
+    if (s->prof.pending.empty()) return;
+    DeviceGuard g(s->m->device);
+    kk(cudaStreamSynchronize(s->m->stream), "profile");
+    kk(cudaStreamSynchronize(s->m->stream2), "profile");
+    prof_collect(s);
+}
+
 int krk_state_profile_read(const krk_state* s, int cls, double* total_ms, int64_t* launches) {
     if (!s || cls < 0 || cls >= KRK_PROF_CLASSES || !total_ms || !launches)
         return fail(KRK_INVALID, "bad profile arguments");
-    *total_ms = s->prof.ms[cls];
-    *launches = s->prof.n[cls];
-    return KRK_OK;
+    return guarded([&]() -> int {
+        prof_settle(s);
+        *total_ms = s->prof.ms[cls];
+        *launches = s->prof.n[cls];
+        return KRK_OK;
+    });
 }
 
 int krk_state_profile_units(const krk_state* s, int cls, int64_t* units) {
     if (!s || cls < 0 || cls >= KRK_PROF_CLASSES || !units) return fail(KRK_INVALID, "bad profile arguments");
-    *units = s->prof.units[cls];
-    return KRK_OK;
+    return guarded([&]() -> int {
+        prof_settle(s);
+        *units = s->prof.units[cls];
+        return KRK_OK;
+    });
 }
 
 int krk_launch_count(uint64_t* count) {

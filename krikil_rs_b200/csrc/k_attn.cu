@@ -203,8 +203,9 @@ __global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(AttnDecodeArgs 
 }
 
 // Split of 16*NW keys per CTA, 16 keys per warp, everything warp-private
-// until the CTA's final merge: each warp requests its K and V rows at entry
-// (V stays in flight while the scores run), ropes its own copy of q, computes
+// until the CTA's final merge: each warp requests its K and V rows at entry as
+// bulk copies (one per lane and row, completing on two mbarriers; V stays in
+// flight while the scores run), ropes its own copy of q, computes
 // its scores with two lanes per key, its softmax partial (max, sum) with
 // shuffles and its PV partial; the NW partials are merged after the CTA's only
 // barrier.
@@ -215,6 +216,7 @@ __global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(AttnDecodeArgs 
 // ((l0+l4)+(l2+l6)) + ((l1+l5)+(l3+l7)) and adds the unfused tail -- the same
 // rounding as the single-thread dot.
 constexpr int AW_KEYS = 16;  // keys per warp
+constexpr int AW_WAIT_POLLS = 1 << 20;  // mbarrier polls before a copy wait gives up
 
 template <int DH>
 struct AwLayout {
@@ -222,9 +224,9 @@ struct AwLayout {
     // phase (4 keys x 2 halves) hit 8 distinct 16-byte bank groups.
     static constexpr int KLD = DH == 64 ? 72 : 88;
     static constexpr int ND = (DH + 31) / 32;
-    // K rows, V rows, q, partial; rounded to whole float4s so every warp's
-    // region starts 16-byte aligned
-    static constexpr int WARP_FLOATS = (AW_KEYS * KLD + AW_KEYS * DH + DH + (DH + 2) + 3) / 4 * 4;
+    // two mbarriers (16 B), K rows, V rows, q, partial; rounded to whole
+    // float4s so every warp's region starts 16-byte aligned
+    static constexpr int WARP_FLOATS = (4 + AW_KEYS * KLD + AW_KEYS * DH + DH + (DH + 2) + 3) / 4 * 4;
 };
 static_assert(AwLayout<64>::WARP_FLOATS % 4 == 0 && AwLayout<76>::WARP_FLOATS % 4 == 0, "alignment");
 static_assert(AwLayout<64>::KLD % 8 == 0 && (AwLayout<64>::KLD / 4) % 4 == 2, "K stride");
@@ -235,14 +237,15 @@ size_t aw_smem_bytes(int nw) {
     return sizeof(float) * (size_t)nw * AwLayout<DH>::WARP_FLOATS;
 }
 
-template <int DH, int NW>
+template <int DH, int NW, bool BULK>
 __global__ void __launch_bounds__(NW * 32) attn_decode_warp_kernel(AttnDecodeArgs a, int max_splits) {
     using L = AwLayout<DH>;
     constexpr int HALF = DH / 2, DH4 = DH / 4, SPLIT = NW * AW_KEYS, CHUNKS = DH / 8;
     extern __shared__ __align__(16) float sm[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    float* kt = sm + warp * L::WARP_FLOATS;  // [16][KLD]
-    float* vt = kt + AW_KEYS * L::KLD;       // [16][DH]
+    uint64_t* bar = reinterpret_cast<uint64_t*>(sm + warp * L::WARP_FLOATS);  // [2]: K rows, V rows
+    float* kt = sm + warp * L::WARP_FLOATS + 4;  // [16][KLD]
+    float* vt = kt + AW_KEYS * L::KLD;           // [16][DH]
     float* qw = vt + AW_KEYS * DH;           // [DH]
     float* part = qw + DH;                   // [DH + 2]: o, max, sum
 
@@ -258,22 +261,48 @@ __global__ void __launch_bounds__(NW * 32) attn_decode_warp_kernel(AttnDecodeArg
     const int nkw = max(0, min(AW_KEYS, nkeys - jw));  // and its key count
     const size_t cbase = (size_t)b * a.c_sb + (size_t)h * a.c_sh;
 
-    for (int i = lane; i < nkw * DH4; i += 32) {
-        const int r = i / DH4, c4 = i % DH4;
-        if (jw + r != pos) cp_async16(kt + r * L::KLD + c4 * 4, a.kc + cbase + (size_t)(jw + r) * a.c_st + c4 * 4);
+    // The cached rows of this warp's keys (all but the new slot pos).  BULK
+    // (cache rows apart, as the model's [ctx][heads*dh] rows): one bulk copy
+    // per row and lane, lanes 0-15 K and 16-31 V, each set completing on its
+    // own mbarrier.  Otherwise (rows back to back): 16-byte cp.async pieces,
+    // which the load units merge into whole lines, in two commit groups.
+    const bool owner = nkw > 0 && pos < jw + nkw;
+    const int rn = pos - jw;
+    constexpr uint32_t ROW_BYTES = DH * sizeof(float);
+    if (!BULK) {
+        for (int i = lane; i < nkw * DH4; i += 32) {
+            const int r = i / DH4, c4 = i % DH4;
+            if (jw + r != pos)
+                cp_async16(kt + r * L::KLD + c4 * 4, a.kc + cbase + (size_t)(jw + r) * a.c_st + c4 * 4);
+        }
+        cp_async_commit();
+        for (int i = lane; i < nkw * DH4; i += 32) {
+            const int r = i / DH4, c4 = i % DH4;
+            if (jw + r != pos) cp_async16(vt + r * DH + c4 * 4, a.vc + cbase + (size_t)(jw + r) * a.c_st + c4 * 4);
+        }
+        cp_async_commit();
+    } else if (nkw > 0) {
+        if (lane == 0) {
+            mbar_init(&bar[0], 1);
+            mbar_init(&bar[1], 1);
+            fence_mbar_init();
+            const uint32_t bytes = (uint32_t)(nkw - (owner ? 1 : 0)) * ROW_BYTES;
+            mbar_arrive_expect_tx(&bar[0], bytes);
+            mbar_arrive_expect_tx(&bar[1], bytes);
+        }
+        __syncwarp();
+        const int r = lane & 15;
+        if (r < nkw && jw + r != pos) {
+            if (lane < 16)
+                bulk_copy_g2s(kt + r * L::KLD, a.kc + cbase + (size_t)(jw + r) * a.c_st, ROW_BYTES, &bar[0]);
+            else
+                bulk_copy_g2s(vt + r * DH, a.vc + cbase + (size_t)(jw + r) * a.c_st, ROW_BYTES, &bar[1]);
+        }
     }
-    cp_async_commit();
-    for (int i = lane; i < nkw * DH4; i += 32) {
-        const int r = i / DH4, c4 = i % DH4;
-        if (jw + r != pos) cp_async16(vt + r * DH + c4 * 4, a.vc + cbase + (size_t)(jw + r) * a.c_st + c4 * 4);
-    }
-    cp_async_commit();
 
     // RoPE on q (every warp its own copy) and, in the warp holding slot pos,
     // on the new k, which is appended with v (src/model.rs:721-733).
     const size_t in_off = (size_t)b * a.in_sb + (size_t)h * a.in_sh;
-    const bool owner = nkw > 0 && pos < jw + nkw;
-    const int rn = pos - jw;
     for (int i = lane; i < HALF; i += 32) {
         float c, s;
         if (a.rope) {
@@ -303,7 +332,10 @@ __global__ void __launch_bounds__(NW * 32) attn_decode_warp_kernel(AttnDecodeArg
             vd[i + HALF] = v1;
         }
     }
-    cp_async_wait<1>();
+    // A bounded wait: a copy that never lands flags an error instead of hanging.
+    bool ok = true;
+    if (!BULK) cp_async_wait<1>();
+    else ok = nkw == 0 || mbar_wait_bounded(&bar[0], 0, AW_WAIT_POLLS);
     __syncwarp();
 
     // scores (src/model.rs:742-748): dot(q_h, k_j) * (1/sqrt(dh)), keys lane/2
@@ -333,7 +365,8 @@ __global__ void __launch_bounds__(NW * 32) attn_decode_warp_kernel(AttnDecodeArg
     const float mw = warp_max(sv);
     const float e = valid ? expf(sv - mw) : 0.0f;
     const float lw = warp_sum(hf == 0 ? e : 0.0f);
-    cp_async_wait<0>();
+    if (!BULK) cp_async_wait<0>();
+    else ok = ok && (nkw == 0 || mbar_wait_bounded(&bar[1], 0, AW_WAIT_POLLS));
     __syncwarp();
 
     // out += w_j * v_j (src/model.rs:752-759) over the warp's keys, in order
@@ -354,8 +387,9 @@ __global__ void __launch_bounds__(NW * 32) attn_decode_warp_kernel(AttnDecodeArg
         if (d < DH) part[d] = o[i];
     }
     if (lane == 0) {
-        part[DH] = nkw > 0 ? mw : -INFINITY;
-        part[DH + 1] = lw;
+        part[DH] = nkw > 0 && ok ? mw : -INFINITY;  // a timed-out warp contributes nothing
+        part[DH + 1] = ok ? lw : 0.0f;
+        if (!ok && a.err) atomicOr(a.err, 1);
     }
     __syncthreads();
 
@@ -363,11 +397,11 @@ __global__ void __launch_bounds__(NW * 32) attn_decode_warp_kernel(AttnDecodeArg
     for (int d = threadIdx.x; d < DH; d += NW * 32) {
         float m = -INFINITY;
 #pragma unroll
-        for (int w = 0; w < NW; ++w) m = fmaxf(m, sm[w * L::WARP_FLOATS + AW_KEYS * (L::KLD + DH) + DH + DH]);
+        for (int w = 0; w < NW; ++w) m = fmaxf(m, sm[w * L::WARP_FLOATS + 4 + AW_KEYS * (L::KLD + DH) + DH + DH]);
         float acc = 0.0f, l = 0.0f;
 #pragma unroll
         for (int w = 0; w < NW; ++w) {
-            const float* pw = sm + w * L::WARP_FLOATS + AW_KEYS * (L::KLD + DH) + DH;
+            const float* pw = sm + w * L::WARP_FLOATS + 4 + AW_KEYS * (L::KLD + DH) + DH;
             if (pw[DH] == -INFINITY) continue;  // a warp past the last key
             const float f = expf(pw[DH] - m);
             acc = acc + pw[d] * f;
@@ -383,6 +417,10 @@ __global__ void __launch_bounds__(NW * 32) attn_decode_warp_kernel(AttnDecodeArg
                 wp[DH + 1] = l;
             }
         }
+    }
+    if (BULK && !ok && nkw > 0) {  // give copies still in flight a last bounded chance before the CTA exits
+        mbar_wait_bounded(&bar[0], 0, AW_WAIT_POLLS);
+        mbar_wait_bounded(&bar[1], 0, AW_WAIT_POLLS);
     }
 }
 
@@ -538,15 +576,21 @@ cudaError_t attn_decode(const AttnDecodeArgs& args, cudaStream_t s) {
     cudaError_t e;
     if (a.split == 16 * 4 || a.split == 16 * 8) {
         const int nw = a.split / 16;
-        const void* fn = a.dh == 76 ? (nw == 4 ? (const void*)attn_decode_warp_kernel<76, 4> : (const void*)attn_decode_warp_kernel<76, 8>)
-                                    : (nw == 4 ? (const void*)attn_decode_warp_kernel<64, 4> : (const void*)attn_decode_warp_kernel<64, 8>);
+        const bool bulk = a.c_st != a.dh;
+        const void* fns[8] = {(const void*)attn_decode_warp_kernel<64, 4, false>,
+                              (const void*)attn_decode_warp_kernel<64, 4, true>,
+                              (const void*)attn_decode_warp_kernel<64, 8, false>,
+                              (const void*)attn_decode_warp_kernel<64, 8, true>,
+                              (const void*)attn_decode_warp_kernel<76, 4, false>,
+                              (const void*)attn_decode_warp_kernel<76, 4, true>,
+                              (const void*)attn_decode_warp_kernel<76, 8, false>,
+                              (const void*)attn_decode_warp_kernel<76, 8, true>};
+        const int v = (a.dh == 76 ? 4 : 0) + (nw == 8 ? 2 : 0) + (bulk ? 1 : 0);
         const size_t smem = a.dh == 76 ? aw_smem_bytes<76>(nw) : aw_smem_bytes<64>(nw);
-        static DeviceOnce once[4];
-        if ((e = once[(a.dh == 76 ? 2 : 0) + (nw == 8)].set_smem(fn, smem)) != cudaSuccess) return e;
-        if (a.dh == 76 && nw == 4) attn_decode_warp_kernel<76, 4><<<grid, 128, smem, s>>>(a, max_splits);
-        else if (a.dh == 76) attn_decode_warp_kernel<76, 8><<<grid, 256, smem, s>>>(a, max_splits);
-        else if (nw == 4) attn_decode_warp_kernel<64, 4><<<grid, 128, smem, s>>>(a, max_splits);
-        else attn_decode_warp_kernel<64, 8><<<grid, 256, smem, s>>>(a, max_splits);
+        static DeviceOnce once[8];
+        if ((e = once[v].set_smem(fns[v], smem)) != cudaSuccess) return e;
+        void* params[] = {&a, (void*)&max_splits};
+        if ((e = cudaLaunchKernel(fns[v], grid, dim3(nw * 32), params, smem, s)) != cudaSuccess) return e;
     } else if (a.dh == 76) {
         static DeviceOnce once;
         const size_t smem = ad_smem_bytes<76>(a.split);

@@ -112,6 +112,7 @@ struct AttnDecodeArgs {
     const float2* rope;                      // optional (cos, sin) table [ctx][dh/2]; null: computed in-kernel
     int max_keys;                            // > 0: no sequence has pos + 1 above this; 0: unknown (ctx)
     RopeFreqs freq;                          // filled by attn_decode() when rope is null
+    int* err;                                // nullable: bit 0 set if a K/V copy wait timed out
 };
 size_t attn_decode_work_floats(int B, int H, int dh, int ctx, int split);
 cudaError_t attn_decode(const AttnDecodeArgs& a, cudaStream_t s);

@@ -165,9 +165,10 @@ class PebbleState:
         check(lib.krk_state_export(self._h, seq, layer, what, _ptr(out), out.size))
         return out
 
-    def profile(self, enable: bool = True) -> None:
-        """Turn per-kernel-class CUDA-event timing of later calls on/off (resets totals)."""
-        check(lib.krk_state_profile(self._h, int(bool(enable))))
+    def profile(self, enable: bool = True, per_kernel: bool = True) -> None:
+        """Turn CUDA-event timing of later calls on/off (resets totals): per kernel
+        class and whole calls, or (per_kernel=False) whole calls only."""
+        check(lib.krk_state_profile(self._h, 0 if not enable else (1 if per_kernel else 2)))
 
     def profile_read(self) -> dict:
         """{class: (device ms, launches, decode sequences)} accumulated since
