@@ -533,10 +533,10 @@ void decode_layer(krk_state* s, int l, const uint8_t* active, int max_keys, cons
     if (is_mamba(l)) {  // src/model.rs:626-702
         float* zx = s->zx + (size_t)b0 * DIP_PAD;
         norm(h, L.ln, RMS_EPS, HID, hn, "ln");
-        gemm(hn, L.in_t, DIP_PAD, HID, zx, DIP_PAD, krk::EPI_STORE, false, "in_proj");
-        timed(s, p, KRK_PROF_CONV, [&] {
-            kk(krk::conv_step4(zx + OFF_X, DIP_PAD, s->conv[l] + (size_t)b0 * DXBC * 4, L.conv_w, L.conv_b, nb, DXBC,
-                               act, st), "conv");
+        // in_proj with the decode conv + SiLU of its x, B, C columns in the epilogue
+        krk::GemmConv cv{s->conv[l] + (size_t)b0 * DXBC * 4, L.conv_w, L.conv_b, act, nb, OFF_X, OFF_X + DXBC};
+        timed(s, p, KRK_PROF_GEMM, [&] {
+            kk(krk::gemm_conv(hn, Mp, L.in_t, DIP_PAD, zx, DIP_PAD, M, DIP_PAD, HID, tr, cv, st), "in_proj + conv");
         });
         krk::SsdStepArgs a{};
         a.x = zx + OFF_X; a.x_sb = DIP_PAD;

@@ -63,7 +63,7 @@ KRK_DEV int col_of(int ln, int c) { return (c < 4) ? ln * 4 + c : 16 + ln * 4 + 
 template <int BM, int EPI, bool OUT_FM>
 __global__ void __launch_bounds__(NT, Tile<BM>::MIN_CTAS)
     gemm_lane8_kernel(const float* __restrict__ At, int lda, const float* __restrict__ Wt, int ldw,
-                      float* __restrict__ C, int ldc, int K) {
+                      float* __restrict__ C, int ldc, int K, const GemmConv cv) {
     using T = Tile<BM>;
     constexpr int TM = T::TM;
     extern __shared__ __align__(16) float sm[];
@@ -199,7 +199,24 @@ __global__ void __launch_bounds__(NT, Tile<BM>::MIN_CTAS)
 #pragma unroll
         for (int w = 0; w < 8; ++w) l[w] = *reinterpret_cast<const float4*>(part + w * wstride);
         float4 v = fold8(l);
-        if (EPI == EPI_RESIDUAL) {
+        if (EPI == EPI_CONV) {  // src/model.rs:643-654 on the channels this tile holds
+            const int m = m0 + (idx >> 3), n = n0 + (idx & 7) * 4;
+            if (n >= cv.lo && n < cv.hi && m < cv.rows && (!cv.active || cv.active[m])) {
+                const int c = n - cv.lo;
+                float4* sp = reinterpret_cast<float4*>(cv.state + ((size_t)m * (cv.hi - cv.lo) + c) * 4);
+                const float4* wp = reinterpret_cast<const float4*>(cv.w) + c;
+                float xv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float4 st = sp[e], wv = wp[e];
+                    // after the shift the window is [st.y, st.z, st.w, x]
+                    const float val = st.y * wv.x + st.z * wv.y + st.w * wv.z + xv[e] * wv.w + cv.bias[c + e];
+                    sp[e] = make_float4(st.y, st.z, st.w, xv[e]);
+                    xv[e] = silu(val);
+                }
+                v = make_float4(xv[0], xv[1], xv[2], xv[3]);
+            }
+        } else if (EPI == EPI_RESIDUAL) {
             float4 o = *reinterpret_cast<const float4*>(out);  // x += out (src/model.rs:699-701)
             v = f4add(o, v);
         } else if (EPI == EPI_GELU) {
@@ -211,12 +228,12 @@ __global__ void __launch_bounds__(NT, Tile<BM>::MIN_CTAS)
 
 template <int BM, int EPI, bool OUT_FM>
 cudaError_t launch(const float* At, int lda, const float* Wt, int ldw, float* C, int ldc, int M, int N, int K,
-                   cudaStream_t s) {
+                   cudaStream_t s, const GemmConv& cv = GemmConv{}) {
     static DeviceOnce once;
     cudaError_t e = once.set_smem((const void*)gemm_lane8_kernel<BM, EPI, OUT_FM>, Tile<BM>::SMEM_BYTES);
     if (e != cudaSuccess) return e;
     dim3 grid(M / BM, N / BN);
-    gemm_lane8_kernel<BM, EPI, OUT_FM><<<grid, NT, Tile<BM>::SMEM_BYTES, s>>>(At, lda, Wt, ldw, C, ldc, K);
+    gemm_lane8_kernel<BM, EPI, OUT_FM><<<grid, NT, Tile<BM>::SMEM_BYTES, s>>>(At, lda, Wt, ldw, C, ldc, K, cv);
     add_launches(1);
     return cudaGetLastError();
 }
@@ -267,6 +284,18 @@ cudaError_t gemm_tiled(const float* At, int lda, const float* Wt, int ldw, float
         return cudaErrorInvalidValue;
     if (tile_rows == 32) return dispatch<32>(At, lda, Wt, ldw, C, ldc, M, N, K, epilogue, out_fm, s);
     return dispatch<64>(At, lda, Wt, ldw, C, ldc, M, N, K, epilogue, out_fm, s);
+}
+
+cudaError_t gemm_conv(const float* At, int lda, const float* Wt, int ldw, float* C, int ldc, int M, int N, int K,
+                      int tile_rows, const GemmConv& cv, cudaStream_t s) {
+    if (tile_rows == 0) tile_rows = gemm_tile_rows(M, N);
+    if (M <= 0 || N <= 0 || K <= 0 || (tile_rows != 32 && tile_rows != 64) || M % tile_rows || N % BN || K % BK ||
+        lda % 4 || ldw % 4 || ldc % 4 || lda < M || ldw < N || ldc < N || !cv.state || !cv.w || !cv.bias ||
+        cv.lo < 0 || cv.lo % BN || cv.hi % BN || cv.hi <= cv.lo || cv.hi > N || cv.rows < 0 || cv.rows > M ||
+        ((uintptr_t)At | (uintptr_t)Wt | (uintptr_t)C | (uintptr_t)cv.state | (uintptr_t)cv.w) % 16)
+        return cudaErrorInvalidValue;
+    if (tile_rows == 32) return launch<32, EPI_CONV, false>(At, lda, Wt, ldw, C, ldc, M, N, K, s, cv);
+    return launch<64, EPI_CONV, false>(At, lda, Wt, ldw, C, ldc, M, N, K, s, cv);
 }
 
 cudaError_t gemm(const float* At, int lda, const float* Wt, int ldw, float* C, int ldc, int M, int N, int K,

@@ -28,15 +28,31 @@ namespace {
 // Feature-major RMSNorm: out[k][m] = x[k][m] * scale(m) * w[k].
 //
 // One CTA owns 8 columns (sequences).  The [K][8] column block is staged into
-// shared memory with cp.async by all threads at once (a single memory round
-// trip), then thread m forms column m's sum of squares in exactly the
+// shared memory with cp.async in NORM_CHUNKS row chunks (each its own commit
+// group), and thread m forms column m's sum of squares in exactly the
 // reference's order -- x[k][m]^2 added for k = 0..K-1 one after the other
 // (src/math.rs:45-48), a latency-bound chain, hence few columns per CTA and
-// many CTAs -- and all threads write the normalised block (x * scale) * w
+// many CTAs -- chunk by chunk as the chunks land, so the chain overlaps the
+// loads.  Then all threads write the normalised block (x * scale) * w
 // (src/math.rs:51-53).  K <= 1216.
 // ---------------------------------------------------------------------------
 constexpr int NORM_COLS = 8;
 constexpr int NORM_MAXK = 1216;
+constexpr int NORM_CHUNKS = 8;
+
+// cp.async.wait_group with a run-time count n in [0, NORM_CHUNKS).
+KRK_DEV void cp_async_wait_upto(int n) {
+    switch (n) {
+        case 0: cp_async_wait<0>(); break;
+        case 1: cp_async_wait<1>(); break;
+        case 2: cp_async_wait<2>(); break;
+        case 3: cp_async_wait<3>(); break;
+        case 4: cp_async_wait<4>(); break;
+        case 5: cp_async_wait<5>(); break;
+        case 6: cp_async_wait<6>(); break;
+        default: cp_async_wait<7>(); break;
+    }
+}
 
 __global__ void __launch_bounds__(256) rmsnorm_fm_kernel(const float* __restrict__ x, int ldx,
                                                          const float* __restrict__ w, float eps, int K, int M,
@@ -47,27 +63,36 @@ __global__ void __launch_bounds__(256) rmsnorm_fm_kernel(const float* __restrict
     const int m0 = blockIdx.x * NORM_COLS;
     const int ncols = min(NORM_COLS, M - m0);
     const bool full = (ncols == NORM_COLS) && ((ldx & 3) == 0) && ((((uintptr_t)x) & 15) == 0);
+    const int kc = (K + NORM_CHUNKS - 1) / NORM_CHUNKS;  // rows per chunk
     if (full) {
-        for (int i = tid; i < K * (NORM_COLS / 4); i += 256) {
-            int k = i / (NORM_COLS / 4), c4 = i % (NORM_COLS / 4);
-            cp_async16(blk + k * NORM_COLS + c4 * 4, x + (size_t)k * ldx + m0 + c4 * 4);
+        for (int c = 0; c < NORM_CHUNKS; ++c) {
+            const int k0 = c * kc, nk = max(0, min(K, k0 + kc) - k0);
+            for (int i = tid; i < nk * (NORM_COLS / 4); i += 256) {
+                const int k = k0 + i / (NORM_COLS / 4), c4 = i % (NORM_COLS / 4);
+                cp_async16(blk + k * NORM_COLS + c4 * 4, x + (size_t)k * ldx + m0 + c4 * 4);
+            }
+            cp_async_commit();
         }
-        cp_async_commit();
-        cp_async_wait<0>();
     } else {
         for (int i = tid; i < K * NORM_COLS; i += 256) {
             int k = i / NORM_COLS, c = i % NORM_COLS;
             blk[i] = c < ncols ? x[(size_t)k * ldx + m0 + c] : 0.0f;
         }
     }
-    __syncthreads();
-    if (tid < NORM_COLS) {
-        float ss = 0.0f;
+    float ss = 0.0f;
+    for (int c = 0; c < NORM_CHUNKS; ++c) {
+        if (full) cp_async_wait_upto(NORM_CHUNKS - 1 - c);
+        __syncthreads();  // chunk c visible to the summing threads
+        if (tid < NORM_COLS) {
+            const int k1 = min(K, (c + 1) * kc);
 #pragma unroll 8
-        for (int k = 0; k < K; ++k) {
-            float v = blk[k * NORM_COLS + tid];
-            ss += v * v;
+            for (int k = c * kc; k < k1; ++k) {
+                const float v = blk[k * NORM_COLS + tid];
+                ss += v * v;
+            }
         }
+    }
+    if (tid < NORM_COLS) {
         float mean = ss / (float)K;
         scale_s[tid] = 1.0f / sqrtf(mean + eps);
     }

@@ -23,9 +23,25 @@ struct DeviceOnce {
 //   Wt: W stored K-major,       Wt[k*ldw + n]
 //   out_fm=false: C[m*ldc + n];  out_fm=true: C[n*ldc + m]
 // M % 32 == 0, N % 32 == 0, K % 32 == 0; leading dims % 4 == 0; 16-B aligned.
-enum GemmEpilogue { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_GELU = 2 };
+enum GemmEpilogue { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_GELU = 2, EPI_CONV = 3 };
+// EPI_CONV (batch-major output only): output columns [lo, hi) are the decode
+// conv channels; for rows m < rows whose active flag is set (or all, when
+// active is null), the epilogue shifts the channel's 4-slot state
+// state[(m*(hi-lo) + c)*4] and stores silu(conv) instead of the raw value --
+// conv_step4 fused into the projection that produces its input.
+struct GemmConv {
+    float* state;
+    const float* w;     // [hi-lo][4]
+    const float* bias;  // [hi-lo]
+    const uint8_t* active;
+    int rows, lo, hi;
+};
 cudaError_t gemm(const float* At, int lda, const float* Wt, int ldw, float* C, int ldc, int M, int N, int K,
                  int epilogue, bool out_fm, cudaStream_t s);
+// gemm_tiled() with the EPI_CONV epilogue (batch-major output; lo and hi
+// multiples of 32).
+cudaError_t gemm_conv(const float* At, int lda, const float* Wt, int ldw, float* C, int ldc, int M, int N, int K,
+                      int tile_rows, const GemmConv& cv, cudaStream_t s);
 // Rows per CTA tile (64 or 32) gemm() uses for an M x N output.
 int gemm_tile_rows(int M, int N);
 // gemm() with an explicit CTA tile height (32 or 64; 0 = gemm_tile_rows).
