@@ -163,7 +163,7 @@ constexpr size_t SCAN_SMEM =
     sizeof(float) * (SCAN_CH * SSD_P * 2 + SCAN_CH * SSD_N * 2 + SCAN_CH * 2 + SSD_P * SCAN_YLD);
 
 template <bool CONV, bool GATE>
-__global__ void __launch_bounds__(256) ssd_scan_kernel(SsdScanArgs a) {
+__global__ void __launch_bounds__(256, 3) ssd_scan_kernel(SsdScanArgs a) {
     extern __shared__ __align__(16) float sm[];
     float* sB = sm;                       // [CH][N]
     float* sC = sB + SCAN_CH * SSD_N;     // [CH][N]
@@ -245,33 +245,37 @@ __global__ void __launch_bounds__(256) ssd_scan_kernel(SsdScanArgs a) {
             const float2 dA2 = make_float2(dA, dA);
             const float* Bt = sB + t * SSD_N + 4 * q;
             const float* Ct = sC + t * SSD_N + 4 * q;
-            float4 bv[4], cv[4];
+            float xv[2];
+            float2 xdt[2], ya[2], yb[2];
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                xv[r] = sx[t * SSD_P + pp + 32 * r];
+                const float xd = xv[r] * dtv;
+                xdt[r] = make_float2(xd, xd);
+                ya[r] = make_float2(0.f, 0.f);
+                yb[r] = make_float2(0.f, 0.f);
+            }
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-                bv[j] = *reinterpret_cast<const float4*>(Bt + 32 * j);
-                cv[j] = *reinterpret_cast<const float4*>(Ct + 32 * j);
+                const float4 bv = *reinterpret_cast<const float4*>(Bt + 32 * j);
+                const float4 cv = *reinterpret_cast<const float4*>(Ct + 32 * j);
+#pragma unroll
+                for (int r = 0; r < 2; ++r) {
+                    s[r][2 * j] = __ffma2_rn(s[r][2 * j], dA2, __fmul2_rn(make_float2(bv.x, bv.y), xdt[r]));
+                    s[r][2 * j + 1] = __ffma2_rn(s[r][2 * j + 1], dA2, __fmul2_rn(make_float2(bv.z, bv.w), xdt[r]));
+                    ya[r] = __ffma2_rn(s[r][2 * j], make_float2(cv.x, cv.y), ya[r]);
+                    yb[r] = __ffma2_rn(s[r][2 * j + 1], make_float2(cv.z, cv.w), yb[r]);
+                }
             }
 #pragma unroll
             for (int r = 0; r < 2; ++r) {
-                const float xv = sx[t * SSD_P + pp + 32 * r];
-                const float xdt = xv * dtv;
-                const float2 xdt2 = make_float2(xdt, xdt);
-                float2 y01 = make_float2(0.f, 0.f), y23 = make_float2(0.f, 0.f);
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    s[r][2 * j] = __ffma2_rn(s[r][2 * j], dA2, __fmul2_rn(make_float2(bv[j].x, bv[j].y), xdt2));
-                    s[r][2 * j + 1] =
-                        __ffma2_rn(s[r][2 * j + 1], dA2, __fmul2_rn(make_float2(bv[j].z, bv[j].w), xdt2));
-                    y01 = __ffma2_rn(s[r][2 * j], make_float2(cv[j].x, cv[j].y), y01);
-                    y23 = __ffma2_rn(s[r][2 * j + 1], make_float2(cv[j].z, cv[j].w), y23);
-                }
-                float y = (y01.x + y01.y) + (y23.x + y23.y);
+                float y = (ya[r].x + ya[r].y) + (yb[r].x + yb[r].y);
                 y += __shfl_xor_sync(0xffffffffu, y, 1);
                 y += __shfl_xor_sync(0xffffffffu, y, 2);
                 y += __shfl_xor_sync(0xffffffffu, y, 4);
                 if (q == 0) {
                     const int p = pp + 32 * r;
-                    float yv = y + dsk * xv;
+                    float yv = y + dsk * xv[r];
                     if (GATE) yv = yv * sg[t * SSD_P + p];
                     sy[p * SCAN_YLD + t] = yv;
                 }
