@@ -199,3 +199,23 @@ def test_large_batch_halves_match_single_sequences(models):
     for b in (3, 255):
         ref, _ = O.generate_greedy(orc, O.OracleState(64), prompts[b], 6, eos=None)
         assert got[b] == ref, b
+
+
+def test_profile_modes(models):
+    """krk_state_profile: mode 1 times every kernel class (event pairs read back
+    when the totals are read), mode 2 only whole calls."""
+    gpu, _ = models
+    st = PebbleState(gpu, 64, batch=4)
+    prompts = [_prompt(5, seed=b) for b in range(4)]
+    st.profile(True, per_kernel=True)
+    gpu.generate_greedy(prompts, st, 4, stop_at_eos=False)
+    p = st.profile_read()
+    assert p["device_total"][0] > 0 and p["device_total"][1] == 1
+    assert p["gemm"][1] > 0 and p["ssd_step"][1] > 0 and p["attn_decode"][1] > 0
+    assert p["ssd_step"][2] == 4 * p["ssd_step"][1]  # 4 sequences per decode launch
+    st.profile(True, per_kernel=False)
+    gpu.generate_greedy(prompts, st, 4, stop_at_eos=False)
+    p = st.profile_read()
+    assert p["device_total"][0] > 0 and p["device_total"][1] == 1
+    assert all(v[1] == 0 for k, v in p.items() if k != "device_total")
+    st.profile(False)
