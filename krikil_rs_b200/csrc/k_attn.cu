@@ -250,25 +250,65 @@ __global__ void __launch_bounds__(NW * 32) attn_decode_warp_kernel(AttnDecodeArg
     float* part = qw + DH;                   // [DH + 2]: o, max, sum
 
     const int b = blockIdx.x, h = blockIdx.y, sp = blockIdx.z;
-    if (a.active && !a.active[b]) return;
-    const int pos = a.pos[b];
-    if (pos < 0 || pos >= a.ctx) return;  // the host rejects these before launch
-    const int nkeys = pos + 1;
     const int j0 = sp * SPLIT;
-    if (j0 >= nkeys) return;  // uniform over the CTA
-    const int nsplit = (nkeys + SPLIT - 1) / SPLIT;
-    const int jw = j0 + warp * AW_KEYS;                // this warp's first key
-    const int nkw = max(0, min(AW_KEYS, nkeys - jw));  // and its key count
+    const int jw = j0 + warp * AW_KEYS;  // this warp's first key
     const size_t cbase = (size_t)b * a.c_sb + (size_t)h * a.c_sh;
+    constexpr uint32_t ROW_BYTES = DH * sizeof(float);
 
-    // The cached rows of this warp's keys (all but the new slot pos).  BULK
-    // (cache rows apart, as the model's [ctx][heads*dh] rows): one bulk copy
-    // per row and lane, lanes 0-15 K and 16-31 V, each set completing on its
-    // own mbarrier.  Otherwise (rows back to back): 16-byte cp.async pieces,
-    // which the load units merge into whole lines, in two commit groups.
+    // BULK (cache rows apart, as the model's [ctx][heads*dh] rows): the copies
+    // go out before the sequence's position is known -- learning it takes a
+    // dependent global load -- one bulk copy per row and lane (lanes 0-15 K,
+    // 16-31 V, each set completing on its own mbarrier) for every row of the
+    // warp's block below the batch's key bound; rows past pos are masked in
+    // the scores and the new row pos is overwritten once the copies landed.
+    int nrows = 0;
+    if (BULK) {
+        const int rows_max = a.max_keys > 0 && a.max_keys < a.ctx ? a.max_keys : a.ctx;  // no pos + 1 exceeds it
+        nrows = max(0, min(AW_KEYS, rows_max - jw));
+        if (nrows > 0) {
+            if (lane == 0) {
+                mbar_init(&bar[0], 1);
+                mbar_init(&bar[1], 1);
+                fence_mbar_init();
+                mbar_arrive_expect_tx(&bar[0], (uint32_t)nrows * ROW_BYTES);
+                mbar_arrive_expect_tx(&bar[1], (uint32_t)nrows * ROW_BYTES);
+            }
+            __syncwarp();
+            const int r = lane & 15;
+            if (r < nrows) {
+                if (lane < 16)
+                    bulk_copy_g2s(kt + r * L::KLD, a.kc + cbase + (size_t)(jw + r) * a.c_st, ROW_BYTES, &bar[0]);
+                else
+                    bulk_copy_g2s(vt + r * DH, a.vc + cbase + (size_t)(jw + r) * a.c_st, ROW_BYTES, &bar[1]);
+            }
+        }
+    }
+    // Before leaving early, the copies of this warp land (bounded waits).
+    auto drain = [&]() {
+        if (BULK && nrows > 0) {
+            mbar_wait_bounded(&bar[0], 0, AW_WAIT_POLLS);
+            mbar_wait_bounded(&bar[1], 0, AW_WAIT_POLLS);
+        }
+    };
+    const bool live = !a.active || a.active[b];
+    const int pos = a.pos[b];
+    if (!live || pos < 0 || pos >= a.ctx) {  // the host rejects bad positions before launch
+        drain();
+        return;
+    }
+    const int nkeys = pos + 1;
+    if (j0 >= nkeys) {  // uniform over the CTA
+        drain();
+        return;
+    }
+    const int nsplit = (nkeys + SPLIT - 1) / SPLIT;
+    const int nkw = max(0, min(AW_KEYS, nkeys - jw));  // this warp's key count
     const bool owner = nkw > 0 && pos < jw + nkw;
     const int rn = pos - jw;
-    constexpr uint32_t ROW_BYTES = DH * sizeof(float);
+
+    // Otherwise (rows back to back): 16-byte cp.async pieces, which the load
+    // units merge into whole lines, in two commit groups; the row pos is
+    // written from registers instead.
     if (!BULK) {
         for (int i = lane; i < nkw * DH4; i += 32) {
             const int r = i / DH4, c4 = i % DH4;
@@ -281,29 +321,16 @@ __global__ void __launch_bounds__(NW * 32) attn_decode_warp_kernel(AttnDecodeArg
             if (jw + r != pos) cp_async16(vt + r * DH + c4 * 4, a.vc + cbase + (size_t)(jw + r) * a.c_st + c4 * 4);
         }
         cp_async_commit();
-    } else if (nkw > 0) {
-        if (lane == 0) {
-            mbar_init(&bar[0], 1);
-            mbar_init(&bar[1], 1);
-            fence_mbar_init();
-            const uint32_t bytes = (uint32_t)(nkw - (owner ? 1 : 0)) * ROW_BYTES;
-            mbar_arrive_expect_tx(&bar[0], bytes);
-            mbar_arrive_expect_tx(&bar[1], bytes);
-        }
-        __syncwarp();
-        const int r = lane & 15;
-        if (r < nkw && jw + r != pos) {
-            if (lane < 16)
-                bulk_copy_g2s(kt + r * L::KLD, a.kc + cbase + (size_t)(jw + r) * a.c_st, ROW_BYTES, &bar[0]);
-            else
-                bulk_copy_g2s(vt + r * DH, a.vc + cbase + (size_t)(jw + r) * a.c_st, ROW_BYTES, &bar[1]);
-        }
     }
 
     // RoPE on q (every warp its own copy) and, in the warp holding slot pos,
     // on the new k, which is appended with v (src/model.rs:721-733).
     const size_t in_off = (size_t)b * a.in_sb + (size_t)h * a.in_sh;
-    for (int i = lane; i < HALF; i += 32) {
+    float kn[2][2], vn[2][2];  // the new row's pairs (i = lane, lane + 32)
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+        const int i = lane + 32 * t;
+        if (i >= HALF) break;
         float c, s;
         if (a.rope) {
             const float2 cs = a.rope[(size_t)pos * HALF + i];
@@ -320,10 +347,14 @@ __global__ void __launch_bounds__(NW * 32) attn_decode_warp_kernel(AttnDecodeArg
             float k0 = a.k[in_off + i], k1 = a.k[in_off + i + HALF];
             rope_pair(k0, k1, c, s);
             const float v0 = a.v[in_off + i], v1 = a.v[in_off + i + HALF];
-            kt[rn * L::KLD + i] = k0;
-            kt[rn * L::KLD + i + HALF] = k1;
-            vt[rn * DH + i] = v0;
-            vt[rn * DH + i + HALF] = v1;
+            kn[t][0] = k0; kn[t][1] = k1;
+            vn[t][0] = v0; vn[t][1] = v1;
+            if (!BULK) {
+                kt[rn * L::KLD + i] = k0;
+                kt[rn * L::KLD + i + HALF] = k1;
+                vt[rn * DH + i] = v0;
+                vt[rn * DH + i + HALF] = v1;
+            }
             float* kd = a.kc + cbase + (size_t)pos * a.c_st;
             float* vd = a.vc + cbase + (size_t)pos * a.c_st;
             kd[i] = k0;
@@ -334,8 +365,21 @@ __global__ void __launch_bounds__(NW * 32) attn_decode_warp_kernel(AttnDecodeArg
     }
     // A bounded wait: a copy that never lands flags an error instead of hanging.
     bool ok = true;
-    if (!BULK) cp_async_wait<1>();
-    else ok = nkw == 0 || mbar_wait_bounded(&bar[0], 0, AW_WAIT_POLLS);
+    if (!BULK) {
+        cp_async_wait<1>();
+    } else {
+        ok = nrows == 0 || mbar_wait_bounded(&bar[0], 0, AW_WAIT_POLLS);
+        if (owner) {  // the copied row pos is the cache's old content
+#pragma unroll
+            for (int t = 0; t < 2; ++t) {
+                const int i = lane + 32 * t;
+                if (i < HALF) {
+                    kt[rn * L::KLD + i] = kn[t][0];
+                    kt[rn * L::KLD + i + HALF] = kn[t][1];
+                }
+            }
+        }
+    }
     __syncwarp();
 
     // scores (src/model.rs:742-748): dot(q_h, k_j) * (1/sqrt(dh)), keys lane/2
@@ -365,8 +409,21 @@ __global__ void __launch_bounds__(NW * 32) attn_decode_warp_kernel(AttnDecodeArg
     const float mw = warp_max(sv);
     const float e = valid ? expf(sv - mw) : 0.0f;
     const float lw = warp_sum(hf == 0 ? e : 0.0f);
-    if (!BULK) cp_async_wait<0>();
-    else ok = ok && (nkw == 0 || mbar_wait_bounded(&bar[1], 0, AW_WAIT_POLLS));
+    if (!BULK) {
+        cp_async_wait<0>();
+    } else {
+        ok = (nrows == 0 || mbar_wait_bounded(&bar[1], 0, AW_WAIT_POLLS)) && ok;
+        if (owner) {
+#pragma unroll
+            for (int t = 0; t < 2; ++t) {
+                const int i = lane + 32 * t;
+                if (i < HALF) {
+                    vt[rn * DH + i] = vn[t][0];
+                    vt[rn * DH + i + HALF] = vn[t][1];
+                }
+            }
+        }
+    }
     __syncwarp();
 
     // out += w_j * v_j (src/model.rs:752-759) over the warp's keys, in order
@@ -418,10 +475,7 @@ __global__ void __launch_bounds__(NW * 32) attn_decode_warp_kernel(AttnDecodeArg
             }
         }
     }
-    if (BULK && !ok && nkw > 0) {  // give copies still in flight a last bounded chance before the CTA exits
-        mbar_wait_bounded(&bar[0], 0, AW_WAIT_POLLS);
-        mbar_wait_bounded(&bar[1], 0, AW_WAIT_POLLS);
-    }
+    if (!ok) drain();  // give copies still in flight a last bounded chance before the CTA exits
 }
 
 // Merges the per-split (max, sum, unnormalised out) partials of one (b, h).
