@@ -26,9 +26,18 @@ constexpr int SSD_N = 128;  // d_state (src/model.rs:22)
 template <bool CONV>
 __global__ void __launch_bounds__(128) ssd_step_kernel(SsdStepArgs a) {
     const int b = blockIdx.x, h = blockIdx.y;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    // The first 8 of this warp's 16 state rows are requested before anything
+    // else (the active flag and the x, B, C, dt reads would otherwise put two
+    // dependent round trips in front of the state stream); the other 8 after
+    // the first are consumed (16 up front would cost occupancy: 122 registers).
+    float* st = a.ssm + ((size_t)b * a.H + h) * (SSD_P * SSD_N) + lane * 4;
+    const int pb = warp * 16;
+    float4 s0[8], s1[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s0[i] = __ldcs(reinterpret_cast<const float4*>(st + (pb + i) * SSD_N));
     if (a.active && !a.active[b]) return;
     __shared__ float xs[SSD_P], gs[SSD_P];
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int c0 = h * SSD_P;
     if (tid < SSD_P) {
         const int c = c0 + tid;
@@ -56,14 +65,15 @@ __global__ void __launch_bounds__(128) ssd_step_kernel(SsdStepArgs a) {
     const float4 C4 = *reinterpret_cast<const float4*>(a.cm + (size_t)b * a.bc_sb + lane * 4);
     __syncthreads();
 
-    float* st = a.ssm + ((size_t)b * a.H + h) * (SSD_P * SSD_N) + lane * 4;
     const bool gate = a.z != nullptr;
 #pragma unroll
     for (int r0 = 0; r0 < 16; r0 += 8) {
-        const int pbase = warp * 16 + r0;
-        float4 s[8];
+        const int pbase = pb + r0;
+        if (r0 == 8) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) s[i] = __ldcs(reinterpret_cast<const float4*>(st + (pbase + i) * SSD_N));
+            for (int i = 0; i < 8; ++i) s1[i] = __ldcs(reinterpret_cast<const float4*>(st + (pb + 8 + i) * SSD_N));
+        }
+        float4* s = r0 == 0 ? s0 : s1;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             const int p = pbase + i;
