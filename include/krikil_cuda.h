@@ -171,6 +171,12 @@ enum {
     KRK_PROF_OTHER = 8,        /* embedding, RoPE prefill, sampling, bookkeeping */
     KRK_PROF_CLASSES = 9
 };
+/* Decode scheduling (no reference counterpart): with n = 2 (the default) a
+ * decode batch of 256+ sequences runs as two halves on two streams so that one
+ * half's projections overlap the other half's HBM-bound kernels; n = 1 runs it
+ * on the model stream alone.  Results are identical either way. */
+KRK_API int krk_state_set_decode_streams(krk_state* state, int n);
+
 /* enable: 0 off, 1 every kernel class and the whole-call total, 2 the
  * whole-call total only (two events per call: no per-kernel event records and
  * no per-kernel readback after the call). */

@@ -200,6 +200,7 @@ struct krk_state {
     float *h_t, *hn_t, *zx, *y_t, *yn_t, *qkv, *ao_t, *mlp_t, *logits, *attn_work;
     float2* rope = nullptr;  // (cos, sin) per [position][pair], from the host libm as src/math.rs:243-247
     int attn_split = 2048;
+    int decode_streams = 2;  // 2: batches of 256+ decode as two halves on two streams
     std::vector<int64_t> pos_h;
     PrefillWs pre;
     Prof prof;
@@ -589,7 +590,7 @@ void decode_forward(krk_state* s, const uint8_t* active, int max_keys) {
     const int B = s->B, Mp = (int)s->Mp;
     Part parts[2];
     int np = 1;
-    if (Mp >= 256 && s->ev_fork) {
+    if (Mp >= 256 && s->ev_fork && s->decode_streams == 2) {
         const int h = (int)round_up(Mp / 2, 64);
         parts[0] = Part{0, std::min(h, B), h, m->stream, 64};
         parts[1] = Part{h, B - h, Mp - h, m->stream2, 64};
@@ -1081,6 +1082,12 @@ int krk_state_export(const krk_state* s, int seq, int layer, int what, float* ou
         kk(cudaStreamSynchronize(s->m->stream), "export");
         return KRK_OK;
     });
+}
+
+int krk_state_set_decode_streams(krk_state* s, int n) {
+    if (!s || (n != 1 && n != 2)) return fail(KRK_INVALID, "decode streams must be 1 or 2");
+    s->decode_streams = n;
+    return KRK_OK;
 }
 
 int krk_state_profile(krk_state* s, int enable) {

@@ -111,7 +111,7 @@ __global__ void __launch_bounds__(256) rmsnorm_fm_kernel(const float* __restrict
 // The sum of squares is per-lane sequential then a warp tree.
 // ---------------------------------------------------------------------------
 template <int VPL, bool GATED>
-__global__ void __launch_bounds__(256) rownorm_kernel(const float* __restrict__ x, const float* __restrict__ z,
+__global__ void __launch_bounds__(256, VPL <= 4 ? 3 : 1) rownorm_kernel(const float* __restrict__ x, const float* __restrict__ z,
                                                       const float* __restrict__ res, const float* __restrict__ w,
                                                       float eps, int64_t rows, float* __restrict__ y) {
     constexpr int DIM = 128 * VPL;
@@ -182,12 +182,20 @@ cudaError_t launch_rownorm(const float* x, const float* z, const float* res, con
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    int64_t want = (rows + 7) / 8;
-    int64_t cap = (int64_t)sms * 8;
-    int grid = (int)(want < cap ? want : cap);
+    // one wave of resident CTAs whose warps stride over the rows
+    const int64_t want = (rows + 7) / 8;
+    auto grid_for = [&](const void* fn) {
+        int per_sm = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, 256, 0) != cudaSuccess || per_sm < 1) per_sm = 1;
+        const int64_t cap = (int64_t)sms * per_sm;
+        return (int)(want < cap ? want : cap);
+    };
     switch (dim / 128) {
-#define KRK_CASE(V) \
-    case V: rownorm_kernel<V, GATED><<<grid, 256, 0, s>>>(x, z, res, w, eps, rows, y); break;
+#define KRK_CASE(V)                                                                                 \
+    case V:                                                                                         \
+        rownorm_kernel<V, GATED><<<grid_for((const void*)rownorm_kernel<V, GATED>), 256, 0, s>>>( \
+            x, z, res, w, eps, rows, y);                                                            \
+        break;
         KRK_CASE(1) KRK_CASE(2) KRK_CASE(3) KRK_CASE(4) KRK_CASE(5) KRK_CASE(6) KRK_CASE(7) KRK_CASE(8)
 #undef KRK_CASE
         default: return cudaErrorInvalidValue;

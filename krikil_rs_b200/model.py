@@ -165,6 +165,10 @@ class PebbleState:
         check(lib.krk_state_export(self._h, seq, layer, what, _ptr(out), out.size))
         return out
 
+    def set_decode_streams(self, n: int) -> None:
+        """2 (default): decode batches of 256+ as two halves on two streams; 1: one stream."""
+        check(lib.krk_state_set_decode_streams(self._h, int(n)))
+
     def profile(self, enable: bool = True, per_kernel: bool = True) -> None:
         """Turn CUDA-event timing of later calls on/off (resets totals): per kernel
         class and whole calls, or (per_kernel=False) whole calls only."""
