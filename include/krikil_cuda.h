@@ -142,6 +142,19 @@ KRK_API int krk_generate_greedy(const krk_model* model, krk_state* state, const 
                                 const int32_t* lens, int max_new_tokens, float repetition_penalty, int stop_at_eos,
                                 uint32_t* tokens_out, int32_t* n_out);
 
+/* The same loop with Sampler::sample at any temperature (src/sampler.rs:43-152):
+ * repetition penalty, logits * (1/temperature), candidates sorted by logit
+ * (equal logits by ascending id), top_k (0 = all), softmax, top_p (1 = all)
+ * with renormalisation, then the first candidate whose running probability
+ * reaches r = Rng::gen::<f32>().  Sequence b draws from its own
+ * StdRng::seed_from_u64(seeds[b]) stream (rand 0.8's ChaCha12), as a reference
+ * Sampler built with config.seed = Some(seeds[b]); one word per pick.
+ * temperature <= 1e-6 is krk_generate_greedy (seeds may then be NULL). */
+KRK_API int krk_generate_sample(const krk_model* model, krk_state* state, const uint32_t* prompts,
+                                const int32_t* lens, int max_new_tokens, float temperature, float top_p, int top_k,
+                                float repetition_penalty, const uint64_t* seeds, int stop_at_eos,
+                                uint32_t* tokens_out, int32_t* n_out);
+
 /* Test hook: copies one sequence's layer state to host memory.
  *   what 0: conv state [1472][4] (Mamba layers)   what 1: SSD state [19][64][128]
  *   what 2: K cache [max_ctx][608] (attention)     what 3: V cache [max_ctx][608]
@@ -291,6 +304,18 @@ KRK_API int krk_k_rope_kv_attn_decode_noalloc(const float* q, const float* k, co
  * penalty 1 disables it), then the first maximum; tok [B]. */
 KRK_API int krk_k_greedy(const float* logits, int64_t ld, int vocab, int B, uint32_t* seen, float penalty,
                          uint32_t* tok, void* stream);
+
+/* One pick per row as krk_generate_sample does it (src/sampler.rs:43-152,
+ * vocab <= 4096): rng_state [B][10] (device) is each row's sampler state, from
+ * krk_rng_seed_state, advanced by one word per row; the pick's bit is set in
+ * seen when seen is not NULL.  temperature <= 1e-6 is krk_k_greedy. */
+KRK_API int krk_k_sample(const float* logits, int64_t ld, int vocab, int B, uint32_t* seen, float temperature,
+                         float top_p, int top_k, float penalty, uint32_t* rng_state, uint32_t* tok, void* stream);
+
+/* StdRng::seed_from_u64(seed) as sampler state: 8 ChaCha12 key words from
+ * rand_core's PCG32 expansion, then the next keystream word's index (0, 0);
+ * host memory, 10 words. */
+KRK_API int krk_rng_seed_state(uint64_t seed, uint32_t* state10);
 
 #ifdef __cplusplus
 }

@@ -197,6 +197,7 @@ struct krk_state {
     int32_t* slimit_d = nullptr;
     int32_t* step_d = nullptr;
     int32_t* err_d = nullptr;  // set by a decode attention kernel whose K/V copy wait timed out
+    uint32_t* rng_d = nullptr;  // [B][10] sampler random state (stochastic generation)
     float *h_t, *hn_t, *zx, *y_t, *yn_t, *qkv, *ao_t, *mlp_t, *logits, *attn_work;
     float2* rope = nullptr;  // (cos, sin) per [position][pair], from the host libm as src/math.rs:243-247
     int attn_split = 2048;
@@ -332,7 +333,7 @@ void create_state(krk_state* s, const krk_model* m, int B, int ctx) {
         }
     }
     b.add<int32_t>(B); b.add<uint8_t>(B); b.add<uint32_t>((size_t)B * SEEN_WORDS); b.add<uint32_t>(Mp);
-    b.add<int32_t>(B); b.add<int32_t>(B); b.add<int32_t>(1); b.add<int32_t>(1);
+    b.add<int32_t>(B); b.add<int32_t>(B); b.add<int32_t>(1); b.add<int32_t>(1); b.add<uint32_t>((size_t)B * 10);
     b.add<float>(HID * Mp); b.add<float>(HID * Mp); b.add<float>(Mp * DIP_PAD); b.add<float>(DI * Mp);
     b.add<float>(DI * Mp); b.add<float>(Mp * QKV); b.add<float>(HID * Mp); b.add<float>(INTER * Mp);
     b.add<float>(Mp * VOC); b.add<float>(work); b.add<float2>((size_t)ctx * (HD / 2));
@@ -354,6 +355,7 @@ void create_state(krk_state* s, const krk_model* m, int B, int ctx) {
     s->slimit_d = s->arena.take<int32_t>(B);
     s->step_d = s->arena.take<int32_t>(1);
     s->err_d = s->arena.take<int32_t>(1);
+    s->rng_d = s->arena.take<uint32_t>((size_t)B * 10);
     s->h_t = s->arena.take<float>(HID * Mp);
     s->hn_t = s->arena.take<float>(HID * Mp);
     s->zx = s->arena.take<float>(Mp * DIP_PAD);
@@ -979,12 +981,46 @@ int krk_step(const krk_model* m, krk_state* s, const uint32_t* tokens, float* lo
     });
 }
 
+// Sampler settings of a generation call (src/sampler.rs:5-13); temperature
+// <= 1e-6 is the greedy branch and needs no seeds.
+struct SampleCfg {
+    float temperature = 0.0f, top_p = 1.0f;
+    int top_k = 0;
+    const uint64_t* seeds = nullptr;  // [B]
+};
+
+static int generate_impl(const krk_model* m, krk_state* s, const uint32_t* prompts, const int32_t* lens,
+                         int max_new_tokens, float repetition_penalty, const SampleCfg& cfg, int stop_at_eos,
+                         uint32_t* tokens_out, int32_t* n_out);
+
 int krk_generate_greedy(const krk_model* m, krk_state* s, const uint32_t* prompts, const int32_t* lens,
                         int max_new_tokens, float repetition_penalty, int stop_at_eos, uint32_t* tokens_out,
                         int32_t* n_out) {
+    return generate_impl(m, s, prompts, lens, max_new_tokens, repetition_penalty, SampleCfg{}, stop_at_eos,
+                         tokens_out, n_out);
+}
+
+int krk_generate_sample(const krk_model* m, krk_state* s, const uint32_t* prompts, const int32_t* lens,
+                        int max_new_tokens, float temperature, float top_p, int top_k, float repetition_penalty,
+                        const uint64_t* seeds, int stop_at_eos, uint32_t* tokens_out, int32_t* n_out) {
+    SampleCfg cfg;
+    cfg.temperature = temperature;
+    cfg.top_p = top_p;
+    cfg.top_k = top_k;
+    cfg.seeds = seeds;
+    return generate_impl(m, s, prompts, lens, max_new_tokens, repetition_penalty, cfg, stop_at_eos, tokens_out,
+                         n_out);
+}
+
+static int generate_impl(const krk_model* m, krk_state* s, const uint32_t* prompts, const int32_t* lens,
+                         int max_new_tokens, float repetition_penalty, const SampleCfg& cfg, int stop_at_eos,
+                         uint32_t* tokens_out, int32_t* n_out) {
     return guarded([&]() -> int {
         if (!m || !s || s->m != m) return fail(KRK_INVALID, "null handle or state of another model");
         if (max_new_tokens <= 0 || !tokens_out || !n_out) return fail(KRK_INVALID, "bad output arguments");
+        const bool stochastic = cfg.temperature > 1e-6f;
+        if (stochastic && !cfg.seeds) return fail(KRK_INVALID, "sampling with temperature > 0 needs seeds");
+        if (stochastic && !(cfg.temperature == cfg.temperature)) return fail(KRK_INVALID, "bad temperature");
         DeviceGuard g(m->device);
         cudaStream_t st = m->stream;
         const int B = s->B;
@@ -1016,20 +1052,27 @@ int krk_generate_greedy(const krk_model* m, krk_state* s, const uint32_t* prompt
         kk(cudaMemsetAsync(s->active_d, 1, B, st), "active");
         kk(cudaMemsetAsync(s->step_d, 0, 4, st), "step");
         kk(cudaMemsetAsync(s->hist_d, 0xff, (size_t)max_picks * B * 4, st), "hist");
+        std::vector<uint32_t> rng;
+        if (stochastic) {  // Sampler::new with config.seed (src/sampler.rs:34-40), one per sequence
+            rng.resize((size_t)B * 10);
+            for (int b = 0; b < B; ++b) krk::rng_seed_state(cfg.seeds[b], rng.data() + (size_t)b * 10);
+            kk(cudaMemcpyAsync(s->rng_d, rng.data(), rng.size() * 4, cudaMemcpyHostToDevice, st), "h2d rng");
+        }
         krk::GreedyArgs ga{};
+        ga.temperature = cfg.temperature; ga.top_p = cfg.top_p; ga.top_k = cfg.top_k; ga.rng = s->rng_d;
         ga.logits = s->logits; ga.ld = VOC; ga.vocab = VOC; ga.B = B;
         ga.seen = s->seen_d; ga.penalty = repetition_penalty;
         ga.tok = s->tok_d; ga.active = s->active_d; ga.hist = s->hist_d; ga.step = s->step_d;
         ga.tlimit = s->tlimit_d; ga.slimit = s->slimit_d; ga.stop_eos = stop_at_eos; ga.eos = KRK_EOS_TOKEN;
         ga.pos = nullptr;
         // first pick from the prefill logits (src/generate.rs:81-82)
-        timed(s, KRK_PROF_OTHER, [&] { kk(krk::greedy(ga, st), "greedy"); });
+        timed(s, KRK_PROF_OTHER, [&] { kk(krk::sample(ga, st), "sample"); });
         ga.pos = s->pos_d;
         // step i runs every active sequence at position pos_h[b] + i at most
         const int64_t pos0 = *std::max_element(s->pos_h.begin(), s->pos_h.end());
         for (int i = 0; i < max_steps; ++i) {
             decode_forward(s, s->active_d, (int)(pos0 + i + 1));
-            timed(s, KRK_PROF_OTHER, [&] { kk(krk::greedy(ga, st), "greedy"); });
+            timed(s, KRK_PROF_OTHER, [&] { kk(krk::sample(ga, st), "sample"); });
         }
         total_end(s);
         std::vector<uint32_t> hist((size_t)max_picks * B);
@@ -1241,6 +1284,22 @@ int krk_k_greedy(const float* logits, int64_t ld, int vocab, int B, uint32_t* se
     krk::GreedyArgs a{};
     a.logits = logits; a.ld = ld; a.vocab = vocab; a.B = B; a.seen = seen; a.penalty = penalty; a.tok = tok;
     return cuda_status(krk::greedy(a, (cudaStream_t)stream), "greedy");
+}
+
+int krk_k_sample(const float* logits, int64_t ld, int vocab, int B, uint32_t* seen, float temperature,
+                 float top_p, int top_k, float penalty, uint32_t* rng_state, uint32_t* tok, void* stream) {
+    if (temperature > 1e-6f && !rng_state) return fail(KRK_INVALID, "sampling needs a random state");
+    krk::GreedyArgs a{};
+    a.logits = logits; a.ld = ld; a.vocab = vocab; a.B = B; a.seen = seen;
+    a.penalty = penalty; a.tok = tok;
+    a.temperature = temperature; a.top_p = top_p; a.top_k = top_k; a.rng = rng_state;
+    return cuda_status(krk::sample(a, (cudaStream_t)stream), "sample");
+}
+
+int krk_rng_seed_state(uint64_t seed, uint32_t* state10) {
+    if (!state10) return fail(KRK_INVALID, "null state");
+    krk::rng_seed_state(seed, state10);
+    return KRK_OK;
 }
 
 }  // extern "C"

@@ -163,8 +163,17 @@ struct GreedyArgs {
     uint8_t* active;
     uint32_t* hist; int32_t* step; int32_t* pos; const int32_t* tlimit; const int32_t* slimit;
     int stop_eos; uint32_t eos;
+    // stochastic sampling (src/sampler.rs:83-152) when temperature > 1e-6
+    float temperature; float top_p; int top_k;
+    uint32_t* rng;  // [B][10]: ChaCha12 key (8 words), index of the next keystream word (lo, hi)
 };
 cudaError_t greedy(const GreedyArgs& a, cudaStream_t s);
+// greedy() when temperature <= 1e-6, else the stochastic pick with the same
+// bookkeeping (vocab <= 4096).
+cudaError_t sample(const GreedyArgs& a, cudaStream_t s);
+// StdRng::seed_from_u64 (rand_core 0.6 over rand_chacha 0.3's ChaCha12):
+// the sampler state [10] for `seed`, on the host.
+void rng_seed_state(uint64_t seed, uint32_t st[10]);
 // Sets the seen bit of each packed row's token for its sequence.
 cudaError_t mark_seen(const uint32_t* tok, const int32_t* row_seq, int rows, uint32_t* seen, int words,
                       cudaStream_t s);

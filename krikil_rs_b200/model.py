@@ -11,6 +11,7 @@ sequences in one state.
 from __future__ import annotations
 
 import ctypes as C
+import os
 import time
 from dataclasses import dataclass, field
 from typing import List, Optional, Sequence
@@ -118,6 +119,28 @@ class PebbleModel:
                                       _ptr(out), _ptr(n)))
         return [out[b, : n[b]].tolist() for b in range(state.batch)]
 
+    def generate_sample(self, prompts: Sequence[Sequence[int]], state: "PebbleState", max_new_tokens: int,
+                        temperature: float, top_p: float = 1.0, top_k: int = 0, repetition_penalty: float = 1.0,
+                        seeds: Optional[Sequence[int]] = None, stop_at_eos: bool = True) -> List[List[int]]:
+        """Batched generation with the stochastic sampler on the device (see
+        krk_generate_sample); sequence b draws from StdRng::seed_from_u64(seeds[b])."""
+        if len(prompts) != state.batch:
+            raise ValueError(f"{len(prompts)} prompts for a state of batch {state.batch}")
+        if seeds is None:
+            seeds = [int.from_bytes(os.urandom(8), "little") for _ in range(state.batch)]
+        sd = np.ascontiguousarray(np.array([int(x) & 0xFFFFFFFFFFFFFFFF for x in seeds], dtype=np.uint64))
+        if sd.size != state.batch:
+            raise ValueError(f"{sd.size} seeds for a state of batch {state.batch}")
+        lens = np.array([len(p) for p in prompts], dtype=np.int32)
+        toks = _pack(prompts)
+        out = np.zeros((state.batch, max_new_tokens), np.uint32)
+        n = np.zeros(state.batch, np.int32)
+        check(lib.krk_generate_sample(self._h, state._h, _ptr(toks) if toks.size else None, _ptr(lens),
+                                      int(max_new_tokens), float(temperature), float(top_p), int(top_k),
+                                      float(repetition_penalty), _ptr(sd), int(bool(stop_at_eos)), _ptr(out),
+                                      _ptr(n)))
+        return [out[b, : n[b]].tolist() for b in range(state.batch)]
+
 
 def _u32(tokens) -> np.ndarray:
     a = np.asarray(tokens, dtype=np.int64)
@@ -200,7 +223,8 @@ class PebbleState:
 # ------------------------------------------------------------------ generation
 @dataclass
 class SamplerConfig:
-    """src/sampler.rs:5-26.  Only temperature <= 1e-6 (greedy) runs here."""
+    """src/sampler.rs:5-26.  seed None draws a seed from the OS, as the
+    reference's StdRng::from_entropy."""
 
     temperature: float = 0.7
     top_p: float = 0.95
@@ -232,7 +256,7 @@ class GenerationResult:
 
 
 class GenerationEngine:
-    """src/generate.rs:36-133 for one sequence, greedy decoding."""
+    """src/generate.rs:36-133 for one sequence."""
 
     def __init__(self, model: PebbleModel):
         self.model = model
@@ -241,7 +265,20 @@ class GenerationEngine:
                  on_token=None) -> GenerationResult:
         sc = options.sampler_config
         if sc.temperature > 1e-6:
-            raise NotImplementedError("only greedy decoding (temperature <= 1e-6) runs on the GPU path")
+            # the whole loop on the device (krk_generate_sample), then the callbacks
+            if state.batch != 1:
+                raise ValueError("GenerationEngine.generate runs one sequence")
+            if sc.eos_token_id != EOS_TOKEN:
+                raise ValueError(f"the device loop stops at token {EOS_TOKEN}")
+            t0 = time.perf_counter()
+            out = self.model.generate_sample([list(prompt_tokens)], state, options.max_new_tokens, sc.temperature,
+                                             sc.top_p, sc.top_k, sc.repetition_penalty,
+                                             None if sc.seed is None else [sc.seed])[0]
+            dt = time.perf_counter() - t0
+            for t in out:
+                if on_token:
+                    on_token(t)
+            return GenerationResult(out, 0.0, dt, len(prompt_tokens), len(out), len(out) / dt if dt > 0 else 0.0)
         state.reset()
         all_tokens = list(int(t) for t in prompt_tokens)
         t0 = time.perf_counter()

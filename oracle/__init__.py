@@ -65,6 +65,14 @@ lib.orc_rms_norm_rows.argtypes = [_fp, _fp, C.c_float, _fp, C.c_int64, C.c_int]
 lib.orc_rope_kv_attn_decode.argtypes = [_fp, _fp, _fp, _fp, _fp, _i32p, _fp] + [C.c_int] * 4 + [C.c_float]
 lib.orc_conv_ssd_step.argtypes = [_fp] * 12 + [C.c_int] * 4
 lib.orc_conv_ssd_scan.argtypes = [_fp] * 12 + [C.c_int] * 5
+lib.orc_chacha_block.argtypes = [_u32p, C.c_int, _u32p]
+lib.orc_rng_seed.argtypes = [C.c_uint64, _u32p]
+lib.orc_rng_next_u32.restype = C.c_uint32
+lib.orc_rng_next_u32.argtypes = [_u32p]
+lib.orc_rng_f32.restype = C.c_float
+lib.orc_rng_f32.argtypes = [_u32p]
+lib.orc_sample.restype = C.c_uint32
+lib.orc_sample.argtypes = [_fp, C.c_int, _u32p, C.c_int, C.c_float, C.c_float, C.c_int, C.c_float, _u32p]
 lib.orc_num_threads.restype = C.c_int
 lib.orc_set_num_threads.argtypes = [C.c_int]
 
@@ -147,6 +155,41 @@ def sample_greedy(logits, context: Sequence[int], penalty: float = 1.0) -> int:
     ctx = np.ascontiguousarray(np.array(context, dtype=np.uint32))
     scratch = np.empty_like(lg)
     return int(lib.orc_sample_greedy(_p(lg), lg.size, ctx.ctypes.data_as(_u32p), ctx.size, penalty, _p(scratch)))
+
+
+# ------------------------------------------------------- stochastic sampling
+def chacha_block(words: Sequence[int], rounds: int) -> List[int]:
+    """The ChaCha block function on 16 input words (test hook)."""
+    inp = np.ascontiguousarray(np.array(words, dtype=np.uint32))
+    out = np.empty(16, np.uint32)
+    lib.orc_chacha_block(inp.ctypes.data_as(_u32p), rounds, out.ctypes.data_as(_u32p))
+    return out.tolist()
+
+
+class Rng:
+    """StdRng::seed_from_u64(seed) restated (see krikil_oracle.c): ten u32 words,
+    the ChaCha12 key and the index of the next keystream word."""
+
+    def __init__(self, seed: int):
+        self.state = np.zeros(10, np.uint32)
+        lib.orc_rng_seed(seed & 0xFFFFFFFFFFFFFFFF, self.state.ctypes.data_as(_u32p))
+
+    def next_u32(self) -> int:
+        return int(lib.orc_rng_next_u32(self.state.ctypes.data_as(_u32p)))
+
+    def gen_f32(self) -> float:
+        return float(lib.orc_rng_f32(self.state.ctypes.data_as(_u32p)))
+
+
+def sample(logits, context: Sequence[int], temperature: float, top_p: float, top_k: int, penalty: float,
+           rng: Rng) -> int:
+    """Sampler::sample (src/sampler.rs:43-152); temperature <= 1e-6 is the greedy branch."""
+    if temperature <= 1e-6:
+        return sample_greedy(logits, context, penalty)
+    lg = np.ascontiguousarray(logits, np.float32)
+    ctx = np.ascontiguousarray(np.array(context, dtype=np.uint32))
+    return int(lib.orc_sample(_p(lg), lg.size, ctx.ctypes.data_as(_u32p), ctx.size, temperature, top_p, top_k,
+                              penalty, rng.state.ctypes.data_as(_u32p)))
 
 
 # ------------------------------------------------------- synthetic layer ops
@@ -273,6 +316,28 @@ def forward_step(model: OracleModel, state: OracleState, token: int) -> np.ndarr
     if rc:
         raise OracleError(rc)
     return logits
+
+
+def generate_sample(model: OracleModel, state: OracleState, prompt, max_new_tokens: int, temperature: float,
+                    top_p: float, top_k: int, repetition_penalty: float, seed: int, eos: Optional[int] = 0):
+    """GenerationEngine::generate_with_callback (src/generate.rs:65-114) with a
+    Sampler seeded by `seed` (src/sampler.rs:35-40).  ``eos=None`` ignores EOS."""
+    state.reset()
+    rng = Rng(seed)
+    all_tokens = [int(t) for t in prompt]
+    lg = forward_prefill(model, state, prompt)
+    nxt = sample(lg, all_tokens, temperature, top_p, top_k, repetition_penalty, rng)
+    out = []
+    while len(out) < max_new_tokens:
+        if eos is not None and nxt == eos:
+            break
+        out.append(nxt)
+        all_tokens.append(nxt)
+        if state.current_pos >= state.context_limit:
+            break
+        lg = forward_step(model, state, nxt)
+        nxt = sample(lg, all_tokens, temperature, top_p, top_k, repetition_penalty, rng)
+    return out
 
 
 def generate_greedy(model: OracleModel, state: OracleState, prompt, max_new_tokens: int,

@@ -416,6 +416,164 @@ EXPORT uint32_t orc_sample_greedy(const float *logits, int vocab, const uint32_t
 }
 
 /* ------------------------------------------------------------------------- */
+/* Stochastic sampling (src/sampler.rs:83-152) and its random stream.          */
+/*                                                                             */
+/* The reference draws from rand 0.8's StdRng, which is rand_chacha 0.3's      */
+/* ChaCha12Rng, seeded by rand_core 0.6's SeedableRng::seed_from_u64; neither  */
+/* crate's source is in the reference tree.  Restated from the published       */
+/* algorithms:                                                                 */
+/*   - seed_from_u64: 8 key words from a PCG32 (XSH-RR) sequence: the 64-bit   */
+/*     state advances first (state = state*6364136223846793005 +               */
+/*     11634580027462260723), the output is ((state>>18)^state)>>27 rotated    */
+/*     right by state>>59, stored little-endian;                               */
+/*   - ChaCha with 12 rounds (6 column + diagonal double rounds), the          */
+/*     "expand 32-byte k" constants, a 64-bit block counter in words 12-13     */
+/*     and a zero 64-bit stream id in words 14-15; next_u32 returns the        */
+/*     keystream's 32-bit words in order (block n/16, word n%16);              */
+/*   - Rng::gen::<f32>() (Standard): (next_u32 >> 8) * 2^-24, in [0, 1).       */
+/* The ChaCha block function is checked against the published ChaCha20 test   */
+/* vectors (same code with 20 rounds); the PCG expansion and the f32           */
+/* conversion have no vectors here, so the seeded stream is unpinned against   */
+/* the reference.                                                              */
+/* ------------------------------------------------------------------------- */
+static uint32_t rotl32(uint32_t x, int r) { return (x << r) | (x >> (32 - r)); }
+
+#define QR(a, b, c, d)                                                                                   \
+    do {                                                                                                 \
+        a += b; d ^= a; d = rotl32(d, 16);                                                               \
+        c += d; b ^= c; b = rotl32(b, 12);                                                               \
+        a += b; d ^= a; d = rotl32(d, 8);                                                                \
+        c += d; b ^= c; b = rotl32(b, 7);                                                                \
+    } while (0)
+
+/* One ChaCha block: 16 input words (constants, key, counter, stream) -> out. */
+EXPORT void orc_chacha_block(const uint32_t in[16], int rounds, uint32_t out[16]) {
+    uint32_t x[16];
+    memcpy(x, in, sizeof(x));
+    for (int r = 0; r < rounds; r += 2) {
+        QR(x[0], x[4], x[8], x[12]);
+        QR(x[1], x[5], x[9], x[13]);
+        QR(x[2], x[6], x[10], x[14]);
+        QR(x[3], x[7], x[11], x[15]);
+        QR(x[0], x[5], x[10], x[15]);
+        QR(x[1], x[6], x[11], x[12]);
+        QR(x[2], x[7], x[8], x[13]);
+        QR(x[3], x[4], x[9], x[14]);
+    }
+    for (int i = 0; i < 16; i++) out[i] = x[i] + in[i];
+}
+
+/* Sampler random state: key[8], then the index of the next keystream word
+ * (lo, hi). */
+EXPORT void orc_rng_seed(uint64_t seed, uint32_t st[10]) {
+    uint64_t s = seed;
+    for (int i = 0; i < 8; i++) {
+        s = s * 6364136223846793005ULL + 11634580027462260723ULL;
+        const uint32_t xs = (uint32_t)(((s >> 18) ^ s) >> 27);
+        const uint32_t rot = (uint32_t)(s >> 59);
+        st[i] = (xs >> rot) | (xs << ((32 - rot) & 31));
+    }
+    st[8] = 0;
+    st[9] = 0;
+}
+
+EXPORT uint32_t orc_rng_next_u32(uint32_t st[10]) {
+    const uint64_t n = (uint64_t)st[8] | ((uint64_t)st[9] << 32);
+    const uint64_t blk = n >> 4;
+    uint32_t in[16] = {0x61707865u, 0x3320646eu, 0x79622d32u, 0x6b206574u};
+    for (int i = 0; i < 8; i++) in[4 + i] = st[i];
+    in[12] = (uint32_t)blk;
+    in[13] = (uint32_t)(blk >> 32);
+    in[14] = 0;
+    in[15] = 0;
+    uint32_t out[16];
+    orc_chacha_block(in, 12, out);
+    const uint64_t n1 = n + 1;
+    st[8] = (uint32_t)n1;
+    st[9] = (uint32_t)(n1 >> 32);
+    return out[n & 15];
+}
+
+EXPORT float orc_rng_f32(uint32_t st[10]) { return (float)(orc_rng_next_u32(st) >> 8) * (1.0f / 16777216.0f); }
+
+typedef struct {
+    float v;
+    uint32_t id;
+} OrcCand;
+
+/* Descending by value; equal values (which the reference's unstable sort
+ * leaves in an unspecified order) by ascending id; NaN after everything. */
+static int cand_cmp(const void *pa, const void *pb) {
+    const OrcCand *a = pa, *b = pb;
+    const int na = isnan(a->v), nb = isnan(b->v);
+    if (na || nb) return na == nb ? (a->id < b->id ? -1 : (a->id > b->id)) : (na ? 1 : -1);
+    if (a->v > b->v) return -1;
+    if (a->v < b->v) return 1;
+    return a->id < b->id ? -1 : (a->id > b->id);
+}
+
+/* src/sampler.rs:43-152 with temperature > 1e-6 (the greedy branch is
+ * orc_sample_greedy).  rng: the state above, advanced by one word. */
+EXPORT uint32_t orc_sample(const float *logits, int vocab, const uint32_t *ctx, int nctx, float temperature, float top_p,
+                           int top_k, float penalty, uint32_t rng[10]) {
+    float *m = malloc(sizeof(float) * (size_t)vocab);
+    memcpy(m, logits, sizeof(float) * (size_t)vocab);
+    if (fabsf(penalty - 1.0f) > 1e-4f) { /* :50-66 */
+        unsigned char *seen = calloc((size_t)vocab, 1);
+        for (int i = 0; i < nctx; i++)
+            if (ctx[i] < (uint32_t)vocab) seen[ctx[i]] = 1;
+        for (int t = 0; t < vocab; t++)
+            if (seen[t]) m[t] = m[t] > 0.0f ? m[t] / penalty : m[t] * penalty;
+        free(seen);
+    }
+    const float inv_temp = 1.0f / temperature; /* :82-86 */
+    OrcCand *c = malloc(sizeof(OrcCand) * (size_t)vocab);
+    for (int i = 0; i < vocab; i++) {
+        c[i].v = m[i] * inv_temp;
+        c[i].id = (uint32_t)i;
+    }
+    qsort(c, (size_t)vocab, sizeof(OrcCand), cand_cmp); /* :88-96 */
+    int n = (top_k > 0 && top_k < vocab) ? top_k : vocab; /* :98-101 */
+    const float mx = c[0].v;                                /* :103-118 */
+    float sum = 0.0f;
+    for (int i = 0; i < n; i++) {
+        c[i].v = expf(c[i].v - mx);
+        sum += c[i].v;
+    }
+    const float inv_sum = 1.0f / sum;
+    for (int i = 0; i < n; i++) c[i].v *= inv_sum;
+    if (top_p < 1.0f) { /* :120-139 */
+        float cum = 0.0f;
+        int cut = n;
+        for (int i = 0; i < n; i++) {
+            cum += c[i].v;
+            if (cum >= top_p) {
+                cut = i + 1 < n ? i + 1 : n;
+                break;
+            }
+        }
+        n = cut;
+        float ns = 0.0f;
+        for (int i = 0; i < n; i++) ns += c[i].v;
+        const float inv_ns = 1.0f / ns;
+        for (int i = 0; i < n; i++) c[i].v *= inv_ns;
+    }
+    const float r = orc_rng_f32(rng); /* :141-151 */
+    float acc = 0.0f;
+    uint32_t pick = c[0].id;
+    for (int i = 0; i < n; i++) {
+        acc += c[i].v;
+        if (r <= acc) {
+            pick = c[i].id;
+            break;
+        }
+    }
+    free(c);
+    free(m);
+    return pick;
+}
+
+/* ------------------------------------------------------------------------- */
 /* Stand-alone forms of the fused layer ops, on the synthetic benchmark       */
 /* layouts.  Each is the reference's arithmetic for that op, generalised to   */
 /* the benchmark's sizes.                                                     */

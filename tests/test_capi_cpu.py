@@ -101,3 +101,12 @@ def test_synth_safetensors_roundtrip(tmp_path):
     w2 = synth.make_weights(0)
     assert all(np.array_equal(w[k], w2[k]) for k in w)
     assert (w["blocks.0.mixer.A_log"] >= 0).all() and (w["blocks.0.mixer.A_log"] <= np.log(16)).all()
+
+
+def test_rng_seed_state_matches_oracle():
+    """krk_rng_seed_state (host) = the oracle's StdRng::seed_from_u64 restatement."""
+    import oracle as O
+    for seed in (0, 1, 42, 2**63 + 5, 2**64 - 1):
+        st = np.zeros(10, np.uint32)
+        assert lib.krk_rng_seed_state(seed, st.ctypes.data) == _lib.OK
+        np.testing.assert_array_equal(st, O.Rng(seed).state)

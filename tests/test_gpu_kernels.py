@@ -13,7 +13,7 @@ pytestmark = pytest.mark.gpu
 if not torch.cuda.is_available():  # pragma: no cover
     pytest.skip("no CUDA device", allow_module_level=True)
 
-from krikil_rs_b200 import kernels as K  # noqa: E402
+from krikil_rs_b200 import _lib, kernels as K  # noqa: E402
 
 DEV = torch.device("cuda:0")
 
@@ -245,6 +245,36 @@ def test_rope_kv_attn_decode_edges(dh, ctx, posv, split):
 
 
 # ------------------------------------------------------------- sampling
+@pytest.mark.parametrize("temp,top_p,top_k,pen", [(0.7, 0.95, 50, 1.2), (1.0, 1.0, 0, 1.0), (0.5, 0.5, 0, 1.0),
+                                                  (1.3, 0.9, 5, 1.5), (2.0, 1.0, 2048, 1.0)])
+def test_stochastic_sample_matches_oracle(temp, top_p, top_k, pen):
+    """krk_k_sample against the oracle's Sampler::sample restatement: 6 rows, 40
+    picks each from the rows' own seeded streams (crossing ChaCha block
+    boundaries), the picks fed back into the penalty set."""
+    rng_np = np.random.default_rng(21)
+    B, V = 6, 2048
+    lg = (rng_np.standard_normal((B, V)) * 3).astype(np.float32)
+    ctx = [list(rng_np.integers(0, V, 20)) for _ in range(B)]
+    seen = np.zeros((B, V // 32), np.uint32)
+    for b in range(B):
+        for t in ctx[b]:
+            seen[b, t >> 5] |= np.uint32(1 << (t & 31))
+    seeds = [3, 99, 2**40 + 7, 0, 12345, 2**63]
+    orng = [O.Rng(s_) for s_ in seeds]
+    st = np.stack([O.Rng(s_).state for s_ in seeds]).astype(np.uint32)
+    g_lg, g_seen, g_st = cu(lg), torch.from_numpy(seen.view(np.int32)).to("cuda"), torch.from_numpy(st.view(np.int32)).to("cuda")
+    tok = torch.zeros(B, dtype=torch.int32, device="cuda")
+    for it in range(40):
+        rc = _lib.lib.krk_k_sample(g_lg.data_ptr(), V, V, B, g_seen.data_ptr(), temp, top_p, top_k, pen,
+                                   g_st.data_ptr(), tok.data_ptr(), torch.cuda.current_stream().cuda_stream)
+        assert rc == _lib.OK
+        got = np_(tok).view(np.uint32).tolist()
+        for b in range(B):
+            want = O.sample(lg[b], ctx[b], temp, top_p, top_k, pen, orng[b])
+            assert got[b] == want, (it, b, got[b], want)
+            ctx[b].append(want)
+    np.testing.assert_array_equal(np_(g_st).view(np.uint32), np.stack([r.state for r in orng]))
+
 def test_greedy_matches_sampler():
     rng = np.random.default_rng(6)
     lg = rng.standard_normal((5, 2048)).astype(np.float32)

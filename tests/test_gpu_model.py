@@ -239,3 +239,22 @@ def test_one_or_two_decode_streams_identical(models):
         np.testing.assert_array_equal(a_, b_)
     with pytest.raises(KrikilError):
         PebbleState(gpu, 8).set_decode_streams(3)
+
+
+def test_generate_sample_device_matches_oracle(models):
+    """krk_generate_sample against the oracle's generate loop with a seeded
+    Sampler per sequence: identical token streams (ragged prompts, EOS on)."""
+    gpu, orc = models
+    prompts = [_prompt(n, seed=50 + n) for n in (3, 9, 17)]
+    seeds = [42, 7, 2**33 + 1]
+    st = PebbleState(gpu, 96, batch=len(prompts))
+    for temp, top_p, top_k, pen in ((0.7, 0.95, 50, 1.2), (1.0, 1.0, 0, 1.0)):
+        got = gpu.generate_sample(prompts, st, 12, temp, top_p, top_k, pen, seeds, stop_at_eos=True)
+        for b, p in enumerate(prompts):
+            ref = O.generate_sample(orc, O.OracleState(96), p, 12, temp, top_p, top_k, pen, seeds[b], eos=0)
+            assert got[b] == ref, (b, temp)
+    eng = GenerationEngine(gpu)
+    st1 = PebbleState(gpu, 64)
+    cfg = SamplerConfig(temperature=0.8, top_p=0.9, top_k=20, repetition_penalty=1.1, seed=5)
+    res = eng.generate(prompts[0], st1, GenerationOptions(max_new_tokens=10, sampler_config=cfg))
+    assert res.generated_tokens == O.generate_sample(orc, O.OracleState(64), prompts[0], 10, 0.8, 0.9, 20, 1.1, 5)

@@ -163,3 +163,48 @@ def test_oracle_matches_reference_golden_logits():
     assert int(np.argmax(lg)) == int(np.argmax(pre["logits"]))
     lg2 = O.forward_step(m, st, stp["step_token"])
     assert np.abs(lg2 - np.array(stp["logits"], np.float32)).max() < 1e-4
+
+
+# ---- stochastic sampler (src/sampler.rs:83-152) and its StdRng stream -------
+def test_chacha_block_published_vectors():
+    """The oracle's ChaCha block function (run with 20 rounds) against the
+    published ChaCha20 vectors: the all-zero key/nonce keystream and RFC 7539
+    section 2.3.2; ChaCha12, the reference's StdRng core, is the same code with
+    12 rounds."""
+    const = [0x61707865, 0x3320646E, 0x79622D32, 0x6B206574]
+    out = O.chacha_block(const + [0] * 12, 20)
+    assert out[:4] == [0xADE0B876, 0x903DF1A0, 0xE56A5D40, 0x28BD8653]
+    key = [int.from_bytes(bytes(range(4 * i, 4 * i + 4)), "little") for i in range(8)]
+    nonce = bytes.fromhex("000000090000004a00000000")
+    words = const + key + [1] + [int.from_bytes(nonce[4 * i:4 * i + 4], "little") for i in range(3)]
+    ser = b"".join(w.to_bytes(4, "little") for w in O.chacha_block(words, 20))
+    assert ser[:16].hex() == "10f1e7e4d13b5915500fdd1fa32071c4"
+
+
+def test_rng_stream_deterministic_and_uniform():
+    a, b = O.Rng(42), O.Rng(42)
+    xs = [a.gen_f32() for _ in range(4000)]
+    assert xs == [b.gen_f32() for _ in range(4000)]
+    assert all(0.0 <= x < 1.0 for x in xs) and abs(np.mean(xs) - 0.5) < 0.02
+    assert O.Rng(43).next_u32() != O.Rng(42).next_u32()
+
+
+def test_sampling_deterministic_with_seed():
+    """src/sampler.rs:185-201: two samplers with seed 42 pick the same token."""
+    lg = np.array([1.0, 2.0, 3.0, 4.0, 5.0, 6.0], np.float32)
+    t1 = O.sample(lg, [], 0.7, 0.9, 10, 1.0, O.Rng(42))
+    t2 = O.sample(lg, [], 0.7, 0.9, 10, 1.0, O.Rng(42))
+    assert t1 == t2 and 0 <= t1 < 6
+
+
+def test_sampling_filters_and_distribution():
+    lg = np.array([0.5, 2.0, 1.0, -1.0, 1.5], np.float32)
+    rng = O.Rng(7)
+    assert {O.sample(lg, [], 1.0, 1.0, 1, 1.0, rng) for _ in range(50)} == {1}  # top-k 1 = argmax
+    assert {O.sample(lg, [], 1.0, 1e-3, 0, 1.0, rng) for _ in range(50)} == {1}  # tiny top-p keeps one
+    assert {O.sample(lg, [], 1.0, 0.9, 2, 1.0, rng) for _ in range(200)} <= {1, 4}
+    counts = np.bincount([O.sample(lg, [], 1.0, 1.0, 0, 1.0, rng) for _ in range(20000)], minlength=5)
+    p = np.exp(lg - lg.max())
+    p /= p.sum()
+    assert np.abs(counts / counts.sum() - p).max() < 0.015
+    assert O.sample(lg, [1], 0.0, 1.0, 0, 3.0, rng) == 4  # temperature 0: greedy after the penalty
