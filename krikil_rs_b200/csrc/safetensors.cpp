@@ -1,5 +1,10 @@
 #include "safetensors.h"
 
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
 #include <stdio.h>
 #include <string.h>
 
@@ -154,37 +159,49 @@ struct Json {
 
 }  // namespace
 
+void SafeTensorsFile::unmap() {
+    if (base_) munmap(const_cast<uint8_t*>(base_), size_);
+    base_ = nullptr;
+    size_ = 0;
+}
+
 bool SafeTensorsFile::open(const std::string& path, std::string& err) {
-    FILE* f = fopen(path.c_str(), "rb");
-    if (!f) {
+    unmap();
+    const int fd = ::open(path.c_str(), O_RDONLY);
+    if (fd < 0) {
         err = "Failed to open model file: " + path;
         return false;
     }
-    fseek(f, 0, SEEK_END);
-    long sz = ftell(f);
-    fseek(f, 0, SEEK_SET);
-    if (sz < 8) {
-        fclose(f);
-        err = "Failed to parse safetensors from " + path + ": file too short";
-        return false;
-    }
-    bytes_.resize((size_t)sz);
-    size_t got = fread(bytes_.data(), 1, (size_t)sz, f);
-    fclose(f);
-    if (got != (size_t)sz) {
+    struct stat st;
+    if (fstat(fd, &st) != 0) {
+        ::close(fd);
         err = "Failed to read model file: " + path;
         return false;
     }
+    const size_t sz = (size_t)st.st_size;
+    if (sz < 8) {
+        ::close(fd);
+        err = "Failed to parse safetensors from " + path + ": file too short";
+        return false;
+    }
+    void* p = mmap(nullptr, sz, PROT_READ, MAP_PRIVATE, fd, 0);
+    ::close(fd);
+    if (p == MAP_FAILED) {
+        err = "Failed to read model file: " + path;
+        return false;
+    }
+    madvise(p, sz, MADV_SEQUENTIAL);
+    base_ = static_cast<const uint8_t*>(p);
+    size_ = sz;
     uint64_t hlen = 0;
-    for (int i = 7; i >= 0; --i) hlen = (hlen << 8) | bytes_[i];
+    for (int i = 7; i >= 0; --i) hlen = (hlen << 8) | base_[i];
     if (hlen > (uint64_t)sz - 8) {
         err = "Failed to parse safetensors from " + path + ": header length exceeds file";
         return false;
     }
     data_off_ = 8 + (size_t)hlen;
     const uint64_t data_len = (uint64_t)sz - data_off_;
-    Json js{reinterpret_cast<const char*>(bytes_.data()) + 8, reinterpret_cast<const char*>(bytes_.data()) + 8 + hlen,
-            ""};
+    Json js{reinterpret_cast<const char*>(base_) + 8, reinterpret_cast<const char*>(base_) + 8 + hlen, ""};
     tensors_.clear();
     bool ok = js.lit('{');
     if (ok && !js.lit('}')) {

@@ -17,8 +17,14 @@ struct TensorInfo {
     uint64_t begin = 0, end = 0;  // byte offsets into the data section
 };
 
+// The file is mapped read-only (no copy of the tensor bytes on the host); the
+// mapping lives as long as the object.
 class SafeTensorsFile {
 public:
+    SafeTensorsFile() = default;
+    SafeTensorsFile(const SafeTensorsFile&) = delete;
+    SafeTensorsFile& operator=(const SafeTensorsFile&) = delete;
+    ~SafeTensorsFile() { unmap(); }
     // Returns false and sets err on failure (missing file, short read,
     // malformed header, offsets outside the data section).
     bool open(const std::string& path, std::string& err);
@@ -27,10 +33,12 @@ public:
         auto it = tensors_.find(name);
         return it == tensors_.end() ? nullptr : &it->second;
     }
-    const uint8_t* data(const TensorInfo& t) const { return bytes_.data() + data_off_ + t.begin; }
+    const uint8_t* data(const TensorInfo& t) const { return base_ + data_off_ + t.begin; }
 
 private:
-    std::vector<uint8_t> bytes_;
+    void unmap();
+    const uint8_t* base_ = nullptr;
+    size_t size_ = 0;
     size_t data_off_ = 0;
     std::map<std::string, TensorInfo> tensors_;
 };
