@@ -118,9 +118,6 @@ __global__ void __launch_bounds__(256, VPL <= 4 ? 3 : 1) rownorm_kernel(const fl
     const int lane = threadIdx.x & 31;
     const int64_t warp_global = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-    float4 wv[VPL];
-#pragma unroll
-    for (int i = 0; i < VPL; ++i) wv[i] = __ldg(reinterpret_cast<const float4*>(w) + lane + 32 * i);
     for (int64_t r = warp_global; r < rows; r += nwarps) {
         const float4* xr = reinterpret_cast<const float4*>(x + r * DIM);
         float4 g[VPL], rr[VPL];
@@ -157,11 +154,12 @@ __global__ void __launch_bounds__(256, VPL <= 4 ? 3 : 1) rownorm_kernel(const fl
         float4* yr = reinterpret_cast<float4*>(y + r * DIM);
 #pragma unroll
         for (int i = 0; i < VPL; ++i) {
+            const float4 wv = __ldg(reinterpret_cast<const float4*>(w) + lane + 32 * i);  // L1-resident
             float4 o;
-            o.x = g[i].x * scale * wv[i].x;
-            o.y = g[i].y * scale * wv[i].y;
-            o.z = g[i].z * scale * wv[i].z;
-            o.w = g[i].w * scale * wv[i].w;
+            o.x = g[i].x * scale * wv.x;
+            o.y = g[i].y * scale * wv.y;
+            o.z = g[i].z * scale * wv.z;
+            o.w = g[i].w * scale * wv.w;
             if (GATED) {
                 o.x = o.x + rr[i].x;
                 o.y = o.y + rr[i].y;
