@@ -258,3 +258,21 @@ def test_generate_sample_device_matches_oracle(models):
     cfg = SamplerConfig(temperature=0.8, top_p=0.9, top_k=20, repetition_penalty=1.1, seed=5)
     res = eng.generate(prompts[0], st1, GenerationOptions(max_new_tokens=10, sampler_config=cfg))
     assert res.generated_tokens == O.generate_sample(orc, O.OracleState(64), prompts[0], 10, 0.8, 0.9, 20, 1.1, 5)
+
+
+def test_large_batch_generation_to_context_limit(models):
+    """260 sequences (two decode streams) generating until the context limit,
+    with EOS stops on: ragged positions near the end of the cache exercise the
+    attention's key bound and the per-sequence stop bookkeeping."""
+    gpu, orc = models
+    bsz, ctx = 260, 40
+    rng = np.random.default_rng(17)
+    lens = rng.integers(1, ctx + 1, bsz)
+    prompts = [rng.integers(0, 2048, int(n)).astype(np.uint32).tolist() for n in lens]
+    st = PebbleState(gpu, ctx, batch=bsz)
+    got = gpu.generate_greedy(prompts, st, 64, repetition_penalty=1.1, stop_at_eos=True)
+    for b in (0, 129, 130, 259, int(np.argmax(lens)), int(np.argmin(lens))):
+        ref, _ = O.generate_greedy(orc, O.OracleState(ctx), prompts[b], 64, repetition_penalty=1.1, eos=0)
+        assert got[b] == ref, b
+    for b in range(bsz):
+        assert len(got[b]) <= ctx - lens[b] + 1
