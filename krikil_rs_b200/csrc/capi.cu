@@ -230,87 +230,109 @@ HostTensor get_tensor(const krk::SafeTensorsFile& f, const std::string& name, si
     return {reinterpret_cast<const float*>(f.data(*t)), n};  // x86 host: little-endian, unaligned loads are fine
 }
 
-// rows x cols (row-major) -> [cols][ld] (transposed, columns padded with zeros)
-std::vector<float> transpose_pad(const float* w, int rows, int cols, int ld) {
-    std::vector<float> out((size_t)cols * ld, 0.0f);
-    for (int r = 0; r < rows; ++r) {
-        const float* src = w + (size_t)r * cols;
-        for (int c = 0; c < cols; ++c) {
-            float v;
-            memcpy(&v, src + c, 4);
-            out[(size_t)c * ld + r] = v;
-        }
-    }
-    return out;
-}
-
 std::vector<float> copy_vec(const HostTensor& t) {
     std::vector<float> v(t.n);
     memcpy(v.data(), t.p, t.n * 4);
     return v;
 }
 
+// What upload_weights copies: a tensor straight from the mapped file (plain),
+// a [rows][cols] tensor to be transposed on the device into [cols][ld] (the
+// K-major layout of the projections), or a host-computed vector.
 struct HostWeights {
     struct Upload {
         float** dst;
-        std::vector<float> data;
+        const float* src = nullptr;  // in the mapped file
+        size_t n = 0;                // floats at src (plain / transposed) or in data
+        int rows = 0, cols = 0, ld = 0;  // ld > 0: transposed
+        std::vector<float> data;         // host-computed
+        size_t dst_floats() const { return ld > 0 ? (size_t)cols * ld : (data.empty() ? n : data.size()); }
     };
+    krk::SafeTensorsFile file;  // mapped until the upload is done
     std::vector<Upload> ups;
 };
 
-// Reads and checks every tensor (src/model.rs:256-294) and prepares the device
-// layouts on the host; touches no device.
+// Reads and checks every tensor (src/model.rs:256-294); touches no device.
 void read_weights(krk_model* m, const std::string& path, HostWeights& hw) {
-    krk::SafeTensorsFile f;
+    krk::SafeTensorsFile& f = hw.file;
     std::string err;
     if (!f.open(path, err)) throw KrkError{KRK_IO, err};
-    auto add = [&](float** dst, std::vector<float>&& v) { hw.ups.push_back({dst, std::move(v)}); };
+    auto plain = [&](float** dst, const HostTensor& t) {
+        HostWeights::Upload u;
+        u.dst = dst; u.src = t.p; u.n = t.n;
+        hw.ups.push_back(std::move(u));
+    };
+    auto transposed = [&](float** dst, const HostTensor& t, int rows, int cols, int ld) {
+        HostWeights::Upload u;
+        u.dst = dst; u.src = t.p; u.n = t.n; u.rows = rows; u.cols = cols; u.ld = ld;
+        hw.ups.push_back(std::move(u));
+    };
 
     HostTensor wte = get_tensor(f, "wte.weight", (size_t)VOC * HID);
-    HostTensor lnf = get_tensor(f, "lnf.weight", HID);
-    add(&m->wte, copy_vec(wte));
-    add(&m->wte_t, transpose_pad(wte.p, VOC, HID, VOC));
-    add(&m->lnf, copy_vec(lnf));
+    plain(&m->wte, wte);
+    transposed(&m->wte_t, wte, VOC, HID, VOC);
+    plain(&m->lnf, get_tensor(f, "lnf.weight", HID));
     for (int i = 0; i < NL; ++i) {
         const std::string p = "blocks." + std::to_string(i) + ".";
         LayerW& L = m->L[i];
         if (is_mamba(i)) {
-            add(&L.ln, copy_vec(get_tensor(f, p + "ln.weight", HID)));
-            HostTensor inp = get_tensor(f, p + "mixer.in_proj.weight", (size_t)DIP * HID);
-            add(&L.in_t, transpose_pad(inp.p, DIP, HID, DIP_PAD));
-            add(&L.conv_w, copy_vec(get_tensor(f, p + "mixer.conv1d.weight", (size_t)DXBC * 4)));
-            add(&L.conv_b, copy_vec(get_tensor(f, p + "mixer.conv1d.bias", DXBC)));
-            add(&L.dt_bias, copy_vec(get_tensor(f, p + "mixer.dt_bias", MH)));
-            std::vector<float> alog = copy_vec(get_tensor(f, p + "mixer.A_log", MH));
-            for (float& v : alog) v = -expf(v);  // A = -exp(A_log) (src/model.rs:273-274)
-            add(&L.a_neg, std::move(alog));
-            add(&L.dsk, copy_vec(get_tensor(f, p + "mixer.D", MH)));
-            add(&L.norm_w, copy_vec(get_tensor(f, p + "mixer.norm.weight", DI)));
-            HostTensor outp = get_tensor(f, p + "mixer.out_proj.weight", (size_t)HID * DI);
-            add(&L.out_t, transpose_pad(outp.p, HID, DI, HID));
+            plain(&L.ln, get_tensor(f, p + "ln.weight", HID));
+            transposed(&L.in_t, get_tensor(f, p + "mixer.in_proj.weight", (size_t)DIP * HID), DIP, HID, DIP_PAD);
+            plain(&L.conv_w, get_tensor(f, p + "mixer.conv1d.weight", (size_t)DXBC * 4));
+            plain(&L.conv_b, get_tensor(f, p + "mixer.conv1d.bias", DXBC));
+            plain(&L.dt_bias, get_tensor(f, p + "mixer.dt_bias", MH));
+            HostWeights::Upload a;
+            a.dst = &L.a_neg;
+            a.data = copy_vec(get_tensor(f, p + "mixer.A_log", MH));
+            for (float& v : a.data) v = -expf(v);  // A = -exp(A_log) (src/model.rs:273-274), host libm
+            hw.ups.push_back(std::move(a));
+            plain(&L.dsk, get_tensor(f, p + "mixer.D", MH));
+            plain(&L.norm_w, get_tensor(f, p + "mixer.norm.weight", DI));
+            transposed(&L.out_t, get_tensor(f, p + "mixer.out_proj.weight", (size_t)HID * DI), HID, DI, HID);
         } else {
-            add(&L.ln1, copy_vec(get_tensor(f, p + "ln1.weight", HID)));
-            HostTensor wqkv = get_tensor(f, p + "wqkv.weight", (size_t)QKV * HID);
-            add(&L.qkv_t, transpose_pad(wqkv.p, QKV, HID, QKV));
-            HostTensor wo = get_tensor(f, p + "wo.weight", (size_t)HID * HID);
-            add(&L.wo_t, transpose_pad(wo.p, HID, HID, HID));
-            add(&L.ln2, copy_vec(get_tensor(f, p + "ln2.weight", HID)));
-            HostTensor fc1 = get_tensor(f, p + "fc1.weight", (size_t)INTER * HID);
-            add(&L.fc1_t, transpose_pad(fc1.p, INTER, HID, INTER));
-            HostTensor fc2 = get_tensor(f, p + "fc2.weight", (size_t)HID * INTER);
-            add(&L.fc2_t, transpose_pad(fc2.p, HID, INTER, HID));
+            plain(&L.ln1, get_tensor(f, p + "ln1.weight", HID));
+            transposed(&L.qkv_t, get_tensor(f, p + "wqkv.weight", (size_t)QKV * HID), QKV, HID, QKV);
+            transposed(&L.wo_t, get_tensor(f, p + "wo.weight", (size_t)HID * HID), HID, HID, HID);
+            plain(&L.ln2, get_tensor(f, p + "ln2.weight", HID));
+            transposed(&L.fc1_t, get_tensor(f, p + "fc1.weight", (size_t)INTER * HID), INTER, HID, INTER);
+            transposed(&L.fc2_t, get_tensor(f, p + "fc2.weight", (size_t)HID * INTER), HID, INTER, HID);
         }
     }
 }
 
+// Copies every tensor from the mapped file to the device; the projections go
+// through a staging buffer and are transposed by a kernel.
 void upload_weights(krk_model* m, HostWeights& hw) {
     Budget bud;
-    for (auto& u : hw.ups) bud.add<float>(u.data.size());
-    m->arena.reserve(bud.bytes);
+    size_t stage = 0;
     for (auto& u : hw.ups) {
-        *u.dst = m->arena.take<float>(u.data.size());
-        ck(cudaMemcpy(*u.dst, u.data.data(), u.data.size() * 4, cudaMemcpyHostToDevice), "weight upload");
+        bud.add<float>(u.dst_floats());
+        if (u.ld > 0) stage = std::max(stage, u.n);
     }
+    m->arena.reserve(bud.bytes);
+    float* staging = nullptr;
+    if (stage) ck(cudaMalloc(&staging, stage * 4), "staging alloc");
+    try {
+        for (auto& u : hw.ups) {
+            *u.dst = m->arena.take<float>(u.dst_floats());
+            // all on the model stream: the copy into the staging buffer, the
+            // transpose that reads it, and the next copy that refills it
+            if (u.ld > 0) {
+                ck(cudaMemcpyAsync(staging, u.src, u.n * 4, cudaMemcpyHostToDevice, m->stream), "weight upload");
+                ck(krk::transpose_pad(staging, u.rows, u.cols, *u.dst, u.ld, m->stream), "weight transpose");
+            } else if (!u.data.empty()) {
+                ck(cudaMemcpyAsync(*u.dst, u.data.data(), u.data.size() * 4, cudaMemcpyHostToDevice, m->stream),
+                   "weight upload");
+            } else {
+                ck(cudaMemcpyAsync(*u.dst, u.src, u.n * 4, cudaMemcpyHostToDevice, m->stream), "weight upload");
+            }
+        }
+        ck(cudaStreamSynchronize(m->stream), "weight upload");
+    } catch (...) {
+        if (staging) cudaFree(staging);
+        throw;
+    }
+    if (staging) ck(cudaFree(staging), "staging free");
 }
 
 // ------------------------------------------------------------------ state

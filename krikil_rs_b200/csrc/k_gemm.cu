@@ -263,7 +263,31 @@ int sm_count() {
     return n;
 }
 
+// 32x32 tiles through shared memory (padded rows: no bank conflicts).
+__global__ void transpose_pad_kernel(const float* __restrict__ in, int rows, int cols, float* __restrict__ out,
+                                     int ld) {
+    __shared__ float t[32][33];
+    const int r0 = blockIdx.y * 32, c0 = blockIdx.x * 32;
+    for (int i = threadIdx.y; i < 32; i += 8) {
+        const int r = r0 + i, c = c0 + threadIdx.x;
+        t[i][threadIdx.x] = (r < rows && c < cols) ? in[(size_t)r * cols + c] : 0.0f;
+    }
+    __syncthreads();
+    for (int i = threadIdx.y; i < 32; i += 8) {
+        const int c = c0 + i, r = r0 + threadIdx.x;
+        if (c < cols && r < ld) out[(size_t)c * ld + r] = t[threadIdx.x][i];
+    }
+}
+
 }  // namespace
+
+cudaError_t transpose_pad(const float* in, int rows, int cols, float* out, int ld, cudaStream_t s) {
+    if (rows <= 0 || cols <= 0 || ld < rows) return cudaErrorInvalidValue;
+    dim3 grid((cols + 31) / 32, (ld + 31) / 32);
+    transpose_pad_kernel<<<grid, dim3(32, 8), 0, s>>>(in, rows, cols, out, ld);
+    add_launches(1);
+    return cudaGetLastError();
+}
 
 // Tile choice: 32-row tiles (3 CTAs per SM, ~10% lower FMA rate than the
 // 64-row tile at full occupancy, measured on B200) only when 64-row tiles would

@@ -42,6 +42,9 @@ cudaError_t gemm(const float* At, int lda, const float* Wt, int ldw, float* C, i
 // multiples of 32).
 cudaError_t gemm_conv(const float* At, int lda, const float* Wt, int ldw, float* C, int ldc, int M, int N, int K,
                       int tile_rows, const GemmConv& cv, cudaStream_t s);
+// out[c*ld + r] = in[r*cols + c] for r < rows, 0 for rows <= r < ld (c < cols):
+// a row-major weight [rows][cols] into the K-major layout the projections read.
+cudaError_t transpose_pad(const float* in, int rows, int cols, float* out, int ld, cudaStream_t s);
 // Rows per CTA tile (64 or 32) gemm() uses for an M x N output.
 int gemm_tile_rows(int M, int N);
 // gemm() with an explicit CTA tile height (32 or 64; 0 = gemm_tile_rows).
