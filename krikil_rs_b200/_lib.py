@@ -62,6 +62,18 @@ _SIGS = {
     "krk_k_rope_kv_attn_decode": (_i32, [_fp] * 8 + [_i32] * 5 + [_f32, _vp]),
     "krk_k_greedy": (_i32, [_fp, _i64, _i32, _i32, _vp, _f32, _vp, _vp]),
     "krk_k_rope_kv_attn_decode_noalloc": (_i32, [_fp] * 7 + [_i32] * 5 + [_f32, _vp]),
+    # include/krikil_text.h
+    "krk_tokenizer_load": (_i32, [C.c_char_p, C.POINTER(_vp)]),
+    "krk_tokenizer_free": (_i32, [_vp]),
+    "krk_tokenizer_encode": (_i32, [_vp, C.c_char_p, C.c_size_t, _vp, C.c_size_t, C.POINTER(C.c_size_t)]),
+    "krk_tokenizer_decode": (_i32, [_vp, _vp, C.c_size_t, _i32, C.c_char_p, C.c_size_t, C.POINTER(C.c_size_t)]),
+    "krk_tokenizer_token_to_id": (_i32, [_vp, C.c_char_p, C.POINTER(_i64)]),
+    "krk_tokenizer_eos_token_id": (_i32, [_vp, C.POINTER(C.c_uint32)]),
+    "krk_tokenizer_vocab_size": (_i32, [_vp, C.POINTER(C.c_size_t)]),
+    "krk_tokenizer_resolve_path": (_i32, [C.c_char_p, C.c_char_p, C.c_char_p, C.c_size_t, C.POINTER(C.c_size_t)]),
+    "krk_chat_template_render": (_i32, [C.c_char_p, C.POINTER(C.c_char_p), C.POINTER(C.c_char_p), C.c_size_t, _i32,
+                                        C.c_char_p, C.c_size_t, C.POINTER(C.c_size_t)]),
+    "krk_default_chat_template": (C.c_char_p, []),
 }
 
 for _name, (_res, _args) in _SIGS.items():
