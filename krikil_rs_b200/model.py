@@ -240,12 +240,15 @@ class GenerationOptions:
 
     max_new_tokens: int = 128
     sampler_config: SamplerConfig = field(default_factory=SamplerConfig)
-    stream_stdout: bool = False
+    stream_stdout: bool = True  # print each token's text (needs the engine's tokenizer)
 
 
 @dataclass
 class GenerationResult:
-    """src/generate.rs:25-34 (token ids; text decoding is not part of this path)."""
+    """src/generate.rs:25-34.  generated_text is the concatenated decode_token
+    text of the generated tokens (empty without a tokenizer).  The device
+    sampling loop runs prefill and decode in one call: its decode_duration
+    covers both."""
 
     generated_tokens: List[int]
     prefill_duration: float
@@ -253,16 +256,48 @@ class GenerationResult:
     prompt_token_count: int
     generated_token_count: int
     tokens_per_second: float
+    generated_text: str = ""
 
 
 class GenerationEngine:
-    """src/generate.rs:36-133 for one sequence."""
+    """src/generate.rs:36-133 for one sequence.  With a tokenizer (the
+    reference's GenerationEngine::new(&model, &tokenizer)) each token's text is
+    streamed to stdout (options.stream_stdout), passed to on_token and
+    collected in generated_text; without one, on_token receives token ids."""
 
-    def __init__(self, model: PebbleModel):
+    def __init__(self, model: PebbleModel, tokenizer=None):
         self.model = model
+        self.tokenizer = tokenizer
+
+    def generate_with_callback(self, prompt_tokens: Sequence[int], state: PebbleState, options: GenerationOptions,
+                               on_token) -> GenerationResult:
+        return self.generate(prompt_tokens, state, options, on_token)
+
+    def _emitter(self, options: GenerationOptions, on_token, text: List[str]):
+        tok = self.tokenizer
+
+        def emit(t: int) -> None:
+            if tok is None:
+                if on_token:
+                    on_token(t)
+                return
+            try:
+                s = tok.decode_token(t)
+            except KrikilError:  # src/generate.rs:89-92: a token that does not decode prints nothing
+                s = ""
+            if options.stream_stdout:
+                import sys
+                sys.stdout.write(s)
+                sys.stdout.flush()
+            if on_token:
+                on_token(s)
+            text.append(s)
+        return emit
 
     def generate(self, prompt_tokens: Sequence[int], state: PebbleState, options: GenerationOptions,
                  on_token=None) -> GenerationResult:
+        text: List[str] = []
+        emit = self._emitter(options, on_token, text)
         sc = options.sampler_config
         if sc.temperature > 1e-6:
             # the whole loop on the device (krk_generate_sample), then the callbacks
@@ -276,9 +311,9 @@ class GenerationEngine:
                                              None if sc.seed is None else [sc.seed])[0]
             dt = time.perf_counter() - t0
             for t in out:
-                if on_token:
-                    on_token(t)
-            return GenerationResult(out, 0.0, dt, len(prompt_tokens), len(out), len(out) / dt if dt > 0 else 0.0)
+                emit(t)
+            return GenerationResult(out, 0.0, dt, len(prompt_tokens), len(out), len(out) / dt if dt > 0 else 0.0,
+                                    "".join(text))
         state.reset()
         all_tokens = list(int(t) for t in prompt_tokens)
         t0 = time.perf_counter()
@@ -292,14 +327,14 @@ class GenerationEngine:
                 break
             out.append(nxt)
             all_tokens.append(nxt)
-            if on_token:
-                on_token(nxt)
+            emit(nxt)
             if state.current_pos >= state.context_limit:
                 break
             logits = self.model.forward_step(nxt, state)
             nxt = greedy_host(logits, all_tokens, sc.repetition_penalty)
         dec = time.perf_counter() - t1
-        return GenerationResult(out, prefill, dec, len(prompt_tokens), len(out), len(out) / dec if dec > 0 else 0.0)
+        return GenerationResult(out, prefill, dec, len(prompt_tokens), len(out), len(out) / dec if dec > 0 else 0.0,
+                                "".join(text))
 
 
 def greedy_host(logits: np.ndarray, context: Sequence[int], penalty: float) -> int:

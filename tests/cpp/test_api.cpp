@@ -3,7 +3,7 @@
 // src/generate.rs generation): run by tests/test_cpp_api.py, which compares
 // the values written to the output file against the oracle.
 //
-// usage: test_api <weights.safetensors> <out.bin>
+// usage: test_api <weights.safetensors> <out.bin> <tokenizer.json>
 // exit 0: all checks passed; 77: no CUDA device (only the loader checks ran);
 // 1: a check failed (message on stderr).
 #include <cstdio>
@@ -40,9 +40,25 @@ static void expect_error(F&& f, int status, const char* needle) {
 }
 
 int main(int argc, char** argv) {
-    if (argc != 3) {
-        std::fprintf(stderr, "usage: test_api <weights> <out>\n");
+    if (argc != 4) {
+        std::fprintf(stderr, "usage: test_api <weights> <out> <tokenizer.json>\n");
         return 2;
+    }
+    // text front end (src/tokenizer.rs, src/template.rs): host only
+    {
+        auto tok = krikil::PebbleTokenizer::from_file(argv[3]);
+        const auto tmpl = krikil::ChatTemplateEngine::default_template();
+        const std::string prompt = tmpl.render_user_prompt("What is the capital of France?");
+        CHECK(prompt == "user: What is the capital of France? assistant: ");
+        const auto ids = tok.encode(prompt);
+        CHECK(!ids.empty() && tok.decode(ids) == prompt);
+        CHECK(tok.eos_token_id() == krikil::DEFAULT_EOS_TOKEN_ID && tok.decode_token(0) == "<|eos|>");
+        CHECK(tmpl.render({krikil::ChatMessage::user("Hello"), krikil::ChatMessage::assistant("Hi there!")}, false) ==
+              "user: Hello assistant: Hi there! ");
+        expect_error([] { krikil::ChatTemplateEngine("{% if %}").render({}, false); }, KRK_INVALID,
+                     "Failed to parse Jinja chat template");
+        expect_error([] { krikil::PebbleTokenizer::from_file("/nonexistent/tokenizer.json"); }, KRK_IO,
+                     "Failed to load tokenizer from");
     }
     // load errors come before any device work (src/model.rs:233-240)
     expect_error([] { krikil::PebbleModel::load_safetensors("/nonexistent/model.safetensors"); }, KRK_IO,

@@ -30,7 +30,8 @@ def binary(tmp_path_factory):
 
 def _run(binary, tmp_path):
     out = str(tmp_path / "out.bin")
-    p = subprocess.run([binary, synth.weights_file(0), out], capture_output=True, text=True, timeout=600)
+    tok = os.path.join(ROOT, "tests", "golden", "tokenizer_small.json")
+    p = subprocess.run([binary, synth.weights_file(0), out, tok], capture_output=True, text=True, timeout=600)
     return p, out
 
 

@@ -244,8 +244,28 @@ def test_rope_kv_attn_decode_edges(dh, ctx, posv, split):
     np.testing.assert_array_equal(np_(g_vc), o_vc)
 
 
+@pytest.mark.parametrize("split,ctx", [(64, 2048), (128, 700), (256, 2048), (64, 64 * 65)])
+def test_rope_kv_attn_decode_split_merge(split, ctx):
+    """Split partials through the work buffer, up to 65 splits: the buffer
+    starts as garbage and is reused across calls with other positions; every
+    call must match the oracle."""
+    rng = np.random.default_rng(split + ctx)
+    bsz, nh, dh = 5, 3, 64
+    kc = rng.standard_normal((bsz, nh, ctx, dh)).astype(np.float32)
+    vc = rng.standard_normal((bsz, nh, ctx, dh)).astype(np.float32)
+    g_kc, g_vc = cu(kc), cu(vc)
+    work = torch.from_numpy(rng.integers(-2**31, 2**31, K.attn_work_floats(bsz, nh, dh, ctx, split),
+                                         dtype=np.int64).astype(np.int32)).to(DEV).view(torch.float32)
+    for call in range(3):
+        q, k, v = (rng.standard_normal((bsz, nh, dh)).astype(np.float32) for _ in range(3))
+        pos = np.array([ctx - 1 - call, call, ctx // 2, split - 1 + call, split + call], np.int32)
+        out = K.rope_kv_attn_decode(cu(q), cu(k), cu(v), g_kc, g_vc, cu(pos), split=split, work=work)
+        ref = O.rope_kv_attn_decode(q, k, v, kc, vc, pos)  # updates kc / vc like the device call
+        np.testing.assert_allclose(np_(out), ref, atol=1e-4, rtol=1e-5)
+
+
 # ------------------------------------------------------------- sampling
-@pytest.mark.parametrize("temp,top_p,top_k,pen", [(0.7, 0.95, 50, 1.2), (1.0, 1.0, 0, 1.0), (0.5, 0.5, 0, 1.0),
+@pytest.mark.parametrize("temp,top_p,top_k,pen",[(0.7, 0.95, 50, 1.2), (1.0, 1.0, 0, 1.0), (0.5, 0.5, 0, 1.0),
                                                   (1.3, 0.9, 5, 1.5), (2.0, 1.0, 2048, 1.0)])
 def test_stochastic_sample_matches_oracle(temp, top_p, top_k, pen):
     """krk_k_sample against the oracle's Sampler::sample restatement: 6 rows, 40

@@ -260,6 +260,27 @@ def test_generate_sample_device_matches_oracle(models):
     assert res.generated_tokens == O.generate_sample(orc, O.OracleState(64), prompts[0], 10, 0.8, 0.9, 20, 1.1, 5)
 
 
+def test_generation_engine_with_tokenizer(models):
+    """GenerationEngine::new(&model, &tokenizer) (src/generate.rs:41-133): each
+    token's decode_token text goes to the callback and into generated_text."""
+    import os
+    from krikil_rs_b200.text import PebbleTokenizer
+    gpu, orc = models
+    tok = PebbleTokenizer.from_file(os.path.join(os.path.dirname(__file__), "golden", "tokenizer_small.json"))
+    eng = GenerationEngine(gpu, tok)
+    ids = tok.encode("user: Hello there assistant: ")
+    for cfg in (SamplerConfig(temperature=0.0, repetition_penalty=1.2), SamplerConfig(seed=11)):
+        seen = []
+        res = eng.generate_with_callback(ids, PebbleState(gpu, 64), GenerationOptions(
+            max_new_tokens=12, sampler_config=cfg, stream_stdout=False), seen.append)
+        if cfg.temperature == 0.0:
+            ref, _ = O.generate_greedy(orc, O.OracleState(64), ids, 12, repetition_penalty=1.2, eos=0)
+        else:
+            ref = O.generate_sample(orc, O.OracleState(64), ids, 12, 0.7, 0.95, 50, 1.2, 11)
+        assert res.generated_tokens == ref
+        assert seen == [tok.decode_token(t) for t in ref] and res.generated_text == "".join(seen)
+
+
 def test_large_batch_generation_to_context_limit(models):
     """260 sequences (two decode streams) generating until the context limit,
     with EOS stops on: ragged positions near the end of the cache exercise the
