@@ -32,6 +32,14 @@ KRK_DEV float as_erf(float x) {
 // src/math.rs:17-21 (FRAC_1_SQRT_2 as an f32 constant)
 KRK_DEV float gelu(float x) { return 0.5f * x * (1.0f + as_erf(x * 0.70710678118654752f)); }
 
+// Programmatic dependent launch (sm_90+): a kernel launched with programmatic
+// stream serialization may be scheduled once every block of the kernel before
+// it has called pdl_trigger() (or exited); pdl_wait() then blocks until that
+// kernel has completed and its writes are visible.  Both are no-ops for
+// kernels launched without the attribute.
+KRK_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+KRK_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 KRK_DEV float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -82,6 +82,7 @@ __global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(AttnDecodeArgs 
     float* sc = red + AD_RED;
     float* tile = sc + a.split;
     float* scratch = tile + AD_TILE * L::KLD;
+    pdl_trigger();  // the combine kernel may be scheduled behind the last blocks
 
     const int b = blockIdx.x, h = blockIdx.y, sp = blockIdx.z, tid = threadIdx.x;
     if (a.active && !a.active[b]) return;
@@ -248,6 +249,7 @@ __global__ void __launch_bounds__(NW * 32) attn_decode_warp_kernel(AttnDecodeArg
     float* vt = kt + AW_KEYS * L::KLD;           // [16][DH]
     float* qw = vt + AW_KEYS * DH;           // [DH]
     float* part = qw + DH;                   // [DH + 2]: o, max, sum
+    pdl_trigger();  // the combine kernel may be scheduled behind the last blocks
 
     const int b = blockIdx.x, h = blockIdx.y, sp = blockIdx.z;
     const int j0 = sp * SPLIT;
@@ -479,6 +481,8 @@ __global__ void __launch_bounds__(NW * 32) attn_decode_warp_kernel(AttnDecodeArg
 }
 
 // Merges the per-split (max, sum, unnormalised out) partials of one (b, h).
+// Launched as a programmatic dependent of the split kernel: it reads the
+// positions while that kernel drains, then waits for its partials.
 __global__ void attn_combine_kernel(AttnDecodeArgs a, int max_splits) {
     const int b = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
     if (a.active && !a.active[b]) return;
@@ -486,6 +490,7 @@ __global__ void attn_combine_kernel(AttnDecodeArgs a, int max_splits) {
     if (pos < 0 || pos >= a.ctx) return;
     const int nsplit = (pos + a.split) / a.split;
     if (nsplit <= 1 || d >= a.dh) return;
+    pdl_wait();
     const float* wp = a.work + ((size_t)b * a.H + h) * max_splits * (a.dh + 2);
     float m = -INFINITY;
     for (int c = 0; c < nsplit; ++c) m = fmaxf(m, wp[c * (a.dh + 2) + a.dh]);
@@ -497,6 +502,66 @@ __global__ void attn_combine_kernel(AttnDecodeArgs a, int max_splits) {
         o = o + p[d] * e;
     }
     a.out[(size_t)b * a.o_sb + (size_t)h * a.o_sh + (size_t)d * a.o_sd] = o * (1.0f / l);
+}
+
+// The same merge for long caches (many splits per sequence): every load of a
+// pass is independent of the others -- thread c reads split c's max and sum,
+// and the weighted output sums run in groups of consecutive splits, one
+// thread per dim and group -- so it costs a few memory latencies however many
+// splits there are.  Also a programmatic dependent of the split kernel.
+constexpr int ACW_THREADS = 256;
+constexpr int ACW_MIN_SPLITS = 9;  // from this many splits per sequence on
+
+size_t acw_smem_bytes(int max_splits, int dh) {
+    return sizeof(float) * (2 * (size_t)max_splits + (size_t)(ACW_THREADS / dh) * dh);
+}
+
+__global__ void __launch_bounds__(ACW_THREADS) attn_combine_wide_kernel(AttnDecodeArgs a, int max_splits) {
+    extern __shared__ __align__(16) float cm[];
+    __shared__ float mred[ACW_THREADS / 32];
+    const int b = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
+    if (a.active && !a.active[b]) return;
+    const int pos = a.pos[b];
+    if (pos < 0 || pos >= a.ctx) return;
+    const int nsplit = (pos + a.split) / a.split;
+    if (nsplit <= 1) return;
+    pdl_wait();
+    const int dh = a.dh, st = dh + 2, groups = ACW_THREADS / dh;
+    float* wt = cm;               // [max_splits]: split max, then its weight
+    float* ls = cm + max_splits;  // [max_splits]: split sum
+    float* po = ls + max_splits;  // [groups][dh]: weighted output sums
+    const float* wp = a.work + ((size_t)b * a.H + h) * max_splits * st;
+    float m = -INFINITY;
+    for (int c = tid; c < nsplit; c += ACW_THREADS) {
+        const float mc = wp[(size_t)c * st + dh];
+        wt[c] = mc;
+        ls[c] = wp[(size_t)c * st + dh + 1];
+        m = fmaxf(m, mc);
+    }
+    m = warp_max(m);
+    if ((tid & 31) == 0) mred[tid >> 5] = m;
+    __syncthreads();
+    m = mred[0];
+#pragma unroll
+    for (int w = 1; w < ACW_THREADS / 32; ++w) m = fmaxf(m, mred[w]);
+    for (int c = tid; c < nsplit; c += ACW_THREADS) wt[c] = expf(wt[c] - m);
+    __syncthreads();
+    const int g = tid / dh, d = tid % dh;
+    if (g < groups) {
+        const int per = (nsplit + groups - 1) / groups;
+        const int c0 = g * per, c1 = min(nsplit, c0 + per);
+        float o = 0.0f;
+#pragma unroll 8
+        for (int c = c0; c < c1; ++c) o = o + wp[(size_t)c * st + d] * wt[c];
+        po[g * dh + d] = o;
+    }
+    __syncthreads();
+    if (tid < dh) {
+        float o = 0.0f, l = 0.0f;
+        for (int gg = 0; gg < groups; ++gg) o = o + po[gg * dh + tid];
+        for (int c = 0; c < nsplit; ++c) l = l + ls[c] * wt[c];
+        a.out[(size_t)b * a.o_sb + (size_t)h * a.o_sh + (size_t)tid * a.o_sd] = o * (1.0f / l);
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -661,7 +726,27 @@ cudaError_t attn_decode(const AttnDecodeArgs& args, cudaStream_t s) {
     add_launches(1);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     if (max_splits > 1) {
-        attn_combine_kernel<<<dim3(a.B, a.H), 128, 0, s>>>(a, max_splits);
+        // splits of the longest sequence: many take the wide merge
+        const bool wide = (keys + a.split - 1) / a.split >= ACW_MIN_SPLITS;
+        const size_t cs = wide ? acw_smem_bytes(max_splits, a.dh) : 0;
+        if (cs > 48 * 1024) {
+            if (cs > 226 * 1024) return cudaErrorInvalidValue;
+            static DeviceOnce once;
+            if ((e = once.set_smem((const void*)attn_combine_wide_kernel, 226 * 1024)) != cudaSuccess) return e;
+        }
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(a.B, a.H);
+        cfg.blockDim = dim3(wide ? ACW_THREADS : 128);
+        cfg.dynamicSmemBytes = cs;
+        cfg.stream = s;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        e = wide ? cudaLaunchKernelEx(&cfg, attn_combine_wide_kernel, a, max_splits)
+                 : cudaLaunchKernelEx(&cfg, attn_combine_kernel, a, max_splits);
+        if (e != cudaSuccess) return e;
         add_launches(1);
         e = cudaGetLastError();
     }
