@@ -58,6 +58,7 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
     ap.add_argument("--kernels-only", action="store_true", help="only the per-kernel table")
     ap.add_argument("--scan-t", type=int, default=2048, help="tokens of the conv+SSD scan case")
+    ap.add_argument("--decode-streams", type=int, default=3, help="parts of the decode batch on their own streams")
     return ap.parse_args()
 
 
@@ -207,7 +208,8 @@ def workload_config(args):
     return {"workload": "batched greedy decode of Pebble-25M (config.json dims), random-init seed 0",
             "seqs_per_gpu": args.seqs, "prompt_len": args.prompt_len, "new_tokens": args.new_tokens,
             "ctx": args.ctx, "eos": "ignored", "prompts": "U[0,2048) numpy seed 1",
-            "l2": "inputs larger than L2 (SSD state 3.8 GB + KV cache per GPU)"}
+            "l2": "inputs larger than L2 (SSD state 3.8 GB + KV cache per GPU)",
+            "decode_parts": getattr(args, "decode_streams", 3)}
 
 
 # ----------------------------------------------------------------- per-kernel table
@@ -321,6 +323,7 @@ def run_ours(args):
     seqs, plen, new = args.seqs, args.prompt_len, args.new_tokens
     prompts = replicas.shard(synth.decode_prompts(world * seqs, plen, seed=1), world, rank)
     state = PebbleState(model, args.ctx, batch=seqs)
+    state.set_decode_streams(args.decode_streams)
 
     # pinned host buffers for the end-to-end calls
     toks_h = torch.from_numpy(np.ascontiguousarray(prompts.reshape(-1).view(np.int32))).pin_memory()
@@ -356,13 +359,13 @@ def run_ours(args):
     prof = state.profile_read()
     state.profile(False)
     # One more call on a single stream (outside the timed region): the same
-    # kernels without the other half-batch beside them, for per-kernel rates.
+    # kernels without the batch's other parts beside them, for per-kernel rates.
     state.set_decode_streams(1)
     state.profile(True)
     generate()
     prof1 = state.profile_read()
     state.profile(False)
-    state.set_decode_streams(2)
+    state.set_decode_streams(args.decode_streams)
     dev_ms = prof["device_total"][0]
     (e2e_ms, dev_ms), total_tokens = replicas.reduce_timings(dist, "cuda", [e2e_ms, dev_ms], gen_tokens)
     if world > 1:
@@ -377,8 +380,8 @@ def run_ours(args):
 
     steps_per_gen = min(new, args.ctx - plen)
     # Per-class times are kernel times on their own stream; a decode batch of
-    # 256+ sequences runs as two concurrent halves, so these are per-launch
-    # rates under the other half's load, and the shares are of summed kernel time.
+    # 256+ sequences runs as concurrent parts, so these are per-launch rates
+    # under the other parts' load, and the shares are of summed kernel time.
     # dominant HBM kernel: the decode SSD update
     ssd_ms, ssd_n, ssd_seqs = prof["ssd_step"]
     ssd_bytes = ssd_step_bytes_per_launch(1) * ssd_seqs
@@ -417,7 +420,7 @@ def run_ours(args):
                      "traffic": int(SSD_TRAFFIC_PER_SEQ * ssd_seqs / max(ssd_n, 1)),
                      "traffic_source": "ncu dram__bytes_read+write, 256-sequence launches, scaled",
                      "peak_kind": peak_kind,
-                     "note": "live per-launch rate while the other half-batch's kernels share the GPU; "
+                     "note": "live per-launch rate while the other decode parts' kernels share the GPU; "
                              "see single_stream for the same kernel without them",
                      "algorithmic_bytes_per_launch": int(ssd_bytes / max(ssd_n, 1)),
                      "launches": ssd_n, "avg_launch_us": round(ssd_ms * 1e3 / max(ssd_n, 1), 2)},

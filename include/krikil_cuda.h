@@ -184,10 +184,12 @@ enum {
     KRK_PROF_OTHER = 8,        /* embedding, RoPE prefill, sampling, bookkeeping */
     KRK_PROF_CLASSES = 9
 };
-/* Decode scheduling (no reference counterpart): with n = 2 (the default) a
- * decode batch of 256+ sequences runs as two halves on two streams so that one
- * half's projections overlap the other half's HBM-bound kernels; n = 1 runs it
- * on the model stream alone.  Results are identical either way. */
+/* Decode scheduling (no reference counterpart): a decode batch of 256+
+ * sequences runs as up to n parts of whole 64-row tiles (at least two tiles
+ * each, sizes within one tile) on their own streams, so that one part's
+ * projections overlap the others' HBM-bound kernels; n = 3 is the default,
+ * n = 1 runs the batch on the model stream alone, n <= 4.  Results are
+ * identical for every n. */
 KRK_API int krk_state_set_decode_streams(krk_state* state, int n);
 
 /* enable: 0 off, 1 every kernel class and the whole-call total, 2 the
@@ -298,6 +300,17 @@ KRK_API int krk_k_rope_kv_attn_decode(const float* q, const float* k, const floa
 KRK_API int krk_k_rope_kv_attn_decode_noalloc(const float* q, const float* k, const float* v, float* kc, float* vc,
                                               const int32_t* pos, float* out, int B, int H, int dh, int ctx,
                                               int split, float theta, void* stream);
+
+/* Test hook of the copy-wait failure path (no counterpart in the reference).
+ * One warp arms a shared-memory mbarrier for a 16-byte bulk copy exactly as the
+ * decode attention arms it for its K/V rows, then waits with the same bounded
+ * wait, `polls` polls at most (1 .. 2^20).  copy != 0: the copy of src16
+ * (16-byte aligned device memory) is issued and lands, and *status (device)
+ * is left alone; copy == 0: no copy is issued, the wait runs out, and bit 0 of
+ * *status is set -- the status word krk_step / krk_generate_* read back after
+ * the attention kernels.  The kernel returns either way and the context stays
+ * usable. */
+KRK_API int krk_k_wait_probe(const float* src16, int polls, int copy, int32_t* status, void* stream);
 
 /* Greedy pick (src/sampler.rs:50-80) per row of logits [B][ld]: repetition
  * penalty on tokens whose bit is set in seen [B][vocab/32] (seen may be NULL;

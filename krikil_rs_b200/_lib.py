@@ -62,6 +62,7 @@ _SIGS = {
     "krk_k_rope_kv_attn_decode": (_i32, [_fp] * 8 + [_i32] * 5 + [_f32, _vp]),
     "krk_k_greedy": (_i32, [_fp, _i64, _i32, _i32, _vp, _f32, _vp, _vp]),
     "krk_k_rope_kv_attn_decode_noalloc": (_i32, [_fp] * 7 + [_i32] * 5 + [_f32, _vp]),
+    "krk_k_wait_probe": (_i32, [_fp, _i32, _i32, _vp, _vp]),
     # include/krikil_text.h
     "krk_tokenizer_load": (_i32, [C.c_char_p, C.POINTER(_vp)]),
     "krk_tokenizer_free": (_i32, [_vp]),

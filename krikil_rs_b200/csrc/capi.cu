@@ -122,7 +122,8 @@ struct LayerW {
 struct krk_model {
     int device = 0;
     cudaStream_t stream = nullptr;
-    cudaStream_t stream2 = nullptr;  // second half of a split decode batch
+    cudaStream_t stream2 = nullptr;  // second part of a split decode batch
+    cudaStream_t stream3 = nullptr, stream4 = nullptr;  // third and fourth parts
     Arena arena;
     float *wte = nullptr, *wte_t = nullptr, *lnf = nullptr;
     LayerW L[NL];
@@ -201,14 +202,15 @@ struct krk_state {
     float *h_t, *hn_t, *zx, *y_t, *yn_t, *qkv, *ao_t, *mlp_t, *logits, *attn_work;
     float2* rope = nullptr;  // (cos, sin) per [position][pair], from the host libm as src/math.rs:243-247
     int attn_split = 2048;
-    int decode_streams = 2;  // 2: batches of 256+ decode as two halves on two streams
+    int decode_streams = 3;  // decode batches of 256+ in up to this many parts on their own streams
     std::vector<int64_t> pos_h;
     PrefillWs pre;
     Prof prof;
     Arena hist_arena;
     int64_t hist_cap = 0;
     uint32_t* hist_d = nullptr;
-    cudaEvent_t ev_fork = nullptr, ev_join = nullptr;  // ordering of the two decode streams
+    cudaEvent_t ev_fork = nullptr, ev_join = nullptr;  // ordering of the decode streams
+    cudaEvent_t ev_join3 = nullptr, ev_join4 = nullptr;
 };
 
 namespace {
@@ -405,6 +407,8 @@ void create_state(krk_state* s, const krk_model* m, int B, int ctx) {
     s->pos_h.assign(B, 0);
     ck(cudaEventCreateWithFlags(&s->ev_fork, cudaEventDisableTiming), "event create");
     ck(cudaEventCreateWithFlags(&s->ev_join, cudaEventDisableTiming), "event create");
+    ck(cudaEventCreateWithFlags(&s->ev_join3, cudaEventDisableTiming), "event create");
+    ck(cudaEventCreateWithFlags(&s->ev_join4, cudaEventDisableTiming), "event create");
 }
 
 void ensure_prefill_ws(krk_state* s, int64_t tokens, int seqs) {
@@ -609,30 +613,44 @@ void decode_layer(krk_state* s, int l, const uint8_t* active, int max_keys, cons
 // layer.  The halves are independent, so while one half's projections keep the
 // FP32 pipes busy the other half's SSD update or attention streams its state
 // through HBM, and each kernel's last partial wave is filled by the other half.
-void decode_forward(krk_state* s, const uint8_t* active, int max_keys) {
+// The decode batch as one part, or split into up to decode_streams parts of
+// whole 64-row tiles (two tiles at least, sizes differing by one tile at most)
+// on the model's streams.
+int decode_parts(const krk_state* s, Part parts[4]) {
     const krk_model* m = s->m;
     const int B = s->B, Mp = (int)s->Mp;
-    Part parts[2];
-    int np = 1;
-    if (Mp >= 256 && s->ev_fork && s->decode_streams == 2) {
-        const int h = (int)round_up(Mp / 2, 64);
-        parts[0] = Part{0, std::min(h, B), h, m->stream, 64};
-        parts[1] = Part{h, B - h, Mp - h, m->stream2, 64};
-        np = B > h ? 2 : 1;
-    } else {
-        parts[0] = Part{0, B, Mp, m->stream, 0};
+    const int n = std::min(s->decode_streams, Mp / 128);  // parts of at least two tiles
+    cudaStream_t st[4] = {m->stream, m->stream2, m->stream3, m->stream4};
+    if (n >= 2 && s->ev_fork) {
+        const int tiles = Mp / 64;  // parts of tiles / n or tiles / n + 1 whole tiles, larger first
+        int np = 0, b0 = 0;
+        for (int i = 0; i < n && b0 < B; ++i) {
+            const int M = 64 * (tiles / n + (i < tiles % n ? 1 : 0));
+            parts[np++] = Part{b0, std::min(M, B - b0), M, st[i], 64};
+            b0 += M;
+        }
+        if (np >= 2) return np;
     }
-    if (np == 2) {
+    parts[0] = Part{0, B, Mp, m->stream, 0};
+    return 1;
+}
+
+void decode_forward(krk_state* s, const uint8_t* active, int max_keys) {
+    const krk_model* m = s->m;
+    Part parts[4];
+    const int np = decode_parts(s, parts);
+    cudaEvent_t joins[4] = {nullptr, s->ev_join, s->ev_join3, s->ev_join4};
+    if (np >= 2) {
         kk(cudaEventRecord(s->ev_fork, m->stream), "fork");
-        kk(cudaStreamWaitEvent(m->stream2, s->ev_fork, 0), "fork");
+        for (int i = 1; i < np; ++i) kk(cudaStreamWaitEvent(parts[i].st, s->ev_fork, 0), "fork");
     }
     for (int i = 0; i < np; ++i) decode_embed(s, parts[i]);
     for (int l = 0; l < NL; ++l)
         for (int i = 0; i < np; ++i) decode_layer(s, l, active, max_keys, parts[i]);
     for (int i = 0; i < np; ++i) lm_head(s, parts[i]);
-    if (np == 2) {
-        kk(cudaEventRecord(s->ev_join, m->stream2), "join");
-        kk(cudaStreamWaitEvent(m->stream, s->ev_join, 0), "join");
+    for (int i = 1; i < np; ++i) {
+        kk(cudaEventRecord(joins[i], parts[i].st), "join");
+        kk(cudaStreamWaitEvent(m->stream, joins[i], 0), "join");
     }
 }
 
@@ -859,10 +877,14 @@ int krk_model_load(const char* path, int device, krk_model** out) {
         ck(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking), "stream create");
         try {
             ck(cudaStreamCreateWithFlags(&m->stream2, cudaStreamNonBlocking), "stream create");
+            ck(cudaStreamCreateWithFlags(&m->stream3, cudaStreamNonBlocking), "stream create");
+            ck(cudaStreamCreateWithFlags(&m->stream4, cudaStreamNonBlocking), "stream create");
             upload_weights(m.get(), hw);
         } catch (...) {
             m->arena.release();
             if (m->stream2) cudaStreamDestroy(m->stream2);
+            if (m->stream3) cudaStreamDestroy(m->stream3);
+            if (m->stream4) cudaStreamDestroy(m->stream4);
             cudaStreamDestroy(m->stream);
             throw;
         }
@@ -877,8 +899,12 @@ int krk_model_free(krk_model* m) {
         DeviceGuard g(m->device);
         cudaStreamSynchronize(m->stream);
         cudaStreamSynchronize(m->stream2);
+        cudaStreamSynchronize(m->stream3);
+        cudaStreamSynchronize(m->stream4);
         m->arena.release();
         cudaStreamDestroy(m->stream2);
+        cudaStreamDestroy(m->stream3);
+        cudaStreamDestroy(m->stream4);
         cudaStreamDestroy(m->stream);
         delete m;
         return KRK_OK;
@@ -916,8 +942,12 @@ int krk_state_free(krk_state* s) {
         DeviceGuard g(s->m->device);
         cudaStreamSynchronize(s->m->stream);
         cudaStreamSynchronize(s->m->stream2);
+        cudaStreamSynchronize(s->m->stream3);
+        cudaStreamSynchronize(s->m->stream4);
         if (s->ev_fork) cudaEventDestroy(s->ev_fork);
         if (s->ev_join) cudaEventDestroy(s->ev_join);
+        if (s->ev_join3) cudaEventDestroy(s->ev_join3);
+        if (s->ev_join4) cudaEventDestroy(s->ev_join4);
         s->pre.arena.release();
         s->hist_arena.release();
         s->arena.release();
@@ -1150,7 +1180,7 @@ int krk_state_export(const krk_state* s, int seq, int layer, int what, float* ou
 }
 
 int krk_state_set_decode_streams(krk_state* s, int n) {
-    if (!s || (n != 1 && n != 2)) return fail(KRK_INVALID, "decode streams must be 1 or 2");
+    if (!s || n < 1 || n > 4) return fail(KRK_INVALID, "decode streams must be 1 to 4");
     s->decode_streams = n;
     return KRK_OK;
 }
@@ -1180,6 +1210,8 @@ static void prof_settle(const krk_state* cs) {
     DeviceGuard g(s->m->device);
     kk(cudaStreamSynchronize(s->m->stream), "profile");
     kk(cudaStreamSynchronize(s->m->stream2), "profile");
+    kk(cudaStreamSynchronize(s->m->stream3), "profile");
+    kk(cudaStreamSynchronize(s->m->stream4), "profile");
     prof_collect(s);
 }
 
@@ -1299,6 +1331,10 @@ int krk_k_rope_kv_attn_decode(const float* q, const float* k, const float* v, fl
     a.B = B; a.H = H; a.dh = dh; a.ctx = ctx; a.split = split <= 0 ? 256 : split; a.theta = theta;
     a.rope = nullptr;
     return cuda_status(krk::attn_decode(a, (cudaStream_t)stream), "rope_kv_attn_decode");
+}
+
+int krk_k_wait_probe(const float* src16, int polls, int copy, int32_t* status, void* stream) {
+    return cuda_status(krk::wait_probe(src16, polls, copy != 0, status, (cudaStream_t)stream), "wait_probe");
 }
 
 int krk_k_greedy(const float* logits, int64_t ld, int vocab, int B, uint32_t* seen, float penalty, uint32_t* tok,

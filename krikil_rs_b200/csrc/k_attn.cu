@@ -480,6 +480,26 @@ __global__ void __launch_bounds__(NW * 32) attn_decode_warp_kernel(AttnDecodeArg
     if (!ok) drain();  // give copies still in flight a last bounded chance before the CTA exits
 }
 
+// The failure path of the bounded copy waits, runnable on purpose: one warp
+// arms an mbarrier for a 16-byte bulk copy as attn_decode_warp_kernel arms its
+// K/V barriers and waits with the same bounded wait.  Without the copy nothing
+// ever completes the phase, the wait gives up after `polls` polls, and the
+// kernel flags it in *err as the attention kernel does, then returns (no copy
+// is in flight when the block exits).
+__global__ void wait_probe_kernel(const float* src, int polls, int copy, int* err) {
+    __shared__ __align__(16) float buf[4];
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_mbar_init();
+        mbar_arrive_expect_tx(&bar, (uint32_t)sizeof(buf));
+        if (copy) bulk_copy_g2s(buf, src, (uint32_t)sizeof(buf), &bar);
+    }
+    __syncwarp();
+    const bool ok = mbar_wait_bounded(&bar, 0, polls);
+    if (threadIdx.x == 0 && !ok && err) atomicOr(err, 1);
+}
+
 // Merges the per-split (max, sum, unnormalised out) partials of one (b, h).
 // Launched as a programmatic dependent of the split kernel: it reads the
 // positions while that kernel drains, then waits for its partials.
@@ -751,6 +771,13 @@ cudaError_t attn_decode(const AttnDecodeArgs& args, cudaStream_t s) {
         e = cudaGetLastError();
     }
     return e;
+}
+
+cudaError_t wait_probe(const float* src, int polls, bool copy, int* err, cudaStream_t s) {
+    if (polls < 1 || polls > AW_WAIT_POLLS || (copy && (!src || ((uintptr_t)src & 15)))) return cudaErrorInvalidValue;
+    wait_probe_kernel<<<1, 32, 0, s>>>(src, polls, copy ? 1 : 0, err);
+    add_launches(1);
+    return cudaGetLastError();
 }
 
 cudaError_t rope_kv_prefill(float* qkv, int64_t q_rs, float* kc, float* vc, int64_t c_sb, int64_t c_sh,

@@ -135,6 +135,10 @@ struct AttnDecodeArgs {
 };
 size_t attn_decode_work_floats(int B, int H, int dh, int ctx, int split);
 cudaError_t attn_decode(const AttnDecodeArgs& a, cudaStream_t s);
+// The bounded copy wait of the decode attention on one armed mbarrier: with
+// copy a 16-byte bulk copy of src lands; without, the wait runs out after
+// `polls` polls and bit 0 of *err is set.
+cudaError_t wait_probe(const float* src, int polls, bool copy, int* err, cudaStream_t s);
 
 // Prefill: RoPE q in place and k into the cache, v into the cache, for packed rows.
 // qkv(row) = qkv[row*q_rs + ...] with q | k | v of H*dh each; cache layout as above

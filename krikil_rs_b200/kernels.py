@@ -109,6 +109,13 @@ def attn_work_floats(b: int, h: int, dh: int, ctx: int, split: int = 0) -> int:
     return int(lib.krk_attn_work_floats(b, h, dh, ctx, split))
 
 
+def wait_probe(src16, status, polls: int, copy: bool) -> None:
+    """krk_k_wait_probe: the bounded copy wait with (copy) or without its copy;
+    bit 0 of status (int32, device) is set when the wait runs out."""
+    check(lib.krk_k_wait_probe(src16.data_ptr() if src16 is not None else None, polls, int(copy),
+                               status.data_ptr(), _stream()))
+
+
 def rope_kv_attn_decode(q, k, v, kc, vc, pos, split: int = 0, theta: float = 10000.0, work=None, out=None):
     """q,k,v [B,H,dh]; kc,vc [B,H,ctx,dh] (updated at pos); pos int32 [B]."""
     _f32(q, k, v, kc, vc, work, out)

@@ -189,7 +189,8 @@ class PebbleState:
         return out
 
     def set_decode_streams(self, n: int) -> None:
-        """2 (default): decode batches of 256+ as two halves on two streams; 1: one stream."""
+        """Decode batches of 256+ in up to n parts of whole 64-row tiles on their
+        own streams (3 by default, at most 4); 1: one stream."""
         check(lib.krk_state_set_decode_streams(self._h, int(n)))
 
     def profile(self, enable: bool = True, per_kernel: bool = True) -> None:

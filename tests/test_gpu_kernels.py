@@ -264,6 +264,35 @@ def test_rope_kv_attn_decode_split_merge(split, ctx):
         np.testing.assert_allclose(np_(out), ref, atol=1e-4, rtol=1e-5)
 
 
+def test_copy_wait_timeout_sets_status_and_context_survives():
+    """The bounded wait of the attention's K/V copies, made to run out on a
+    barrier whose copy is never issued: the kernel returns, the status word has
+    bit 0 set, and the context keeps working (the same wait with its copy
+    issued succeeds, and an attention call afterwards matches the oracle)."""
+    src = torch.arange(4, dtype=torch.float32, device=DEV)
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    K.wait_probe(src, status, polls=256, copy=True)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    K.wait_probe(None, status, polls=256, copy=False)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 1
+    status.zero_()
+    K.wait_probe(src, status, polls=256, copy=True)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    from krikil_rs_b200._lib import KrikilError
+    with pytest.raises(KrikilError):
+        K.wait_probe(src[1:], status, polls=256, copy=True)  # not 16-byte aligned: refused before launch
+    rng = np.random.default_rng(9)
+    q, k, v = (rng.standard_normal((2, 2, 64)).astype(np.float32) for _ in range(3))
+    kc, vc = (rng.standard_normal((2, 2, 128, 64)).astype(np.float32) for _ in range(2))
+    pos = np.array([5, 127], np.int32)
+    out = K.rope_kv_attn_decode(cu(q), cu(k), cu(v), cu(kc), cu(vc), cu(pos), split=64)
+    np.testing.assert_allclose(np_(out), O.rope_kv_attn_decode(q, k, v, kc.copy(), vc.copy(), pos), atol=1e-4,
+                               rtol=1e-5)
+
+
 # ------------------------------------------------------------- sampling
 @pytest.mark.parametrize("temp,top_p,top_k,pen",[(0.7, 0.95, 50, 1.2), (1.0, 1.0, 0, 1.0), (0.5, 0.5, 0, 1.0),
                                                   (1.3, 0.9, 5, 1.5), (2.0, 1.0, 2048, 1.0)])

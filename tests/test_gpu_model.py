@@ -221,24 +221,25 @@ def test_profile_modes(models):
     st.profile(False)
 
 
-def test_one_or_two_decode_streams_identical(models):
-    """krk_state_set_decode_streams: a 260-sequence batch decoded on one stream
-    or as two halves on two streams gives bitwise identical logits."""
+def test_decode_streams_identical(models):
+    """krk_state_set_decode_streams: a 520-sequence batch decoded on one stream,
+    as two halves, or as three parts of 192 rows gives bitwise identical logits."""
     gpu, _ = models
-    bsz = 260
+    bsz = 520
     rng = np.random.default_rng(12)
     prompts = [rng.integers(0, 2048, int(n)).astype(np.uint32).tolist() for n in rng.integers(1, 30, bsz)]
     out = []
-    for n in (1, 2):
+    for n in (1, 2, 3, 4):
         st = PebbleState(gpu, 64, batch=bsz)
         st.set_decode_streams(n)
         gpu.prefill_batch(prompts, st)
         lg = [gpu.step_batch([(13 * b + s) % 2048 for b in range(bsz)], st) for s in range(2)]
         out.append(lg)
-    for a_, b_ in zip(*out):
-        np.testing.assert_array_equal(a_, b_)
+    for other in out[1:]:
+        for a_, b_ in zip(out[0], other):
+            np.testing.assert_array_equal(a_, b_)
     with pytest.raises(KrikilError):
-        PebbleState(gpu, 8).set_decode_streams(3)
+        PebbleState(gpu, 8).set_decode_streams(5)
 
 
 def test_generate_sample_device_matches_oracle(models):
