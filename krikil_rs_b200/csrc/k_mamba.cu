@@ -153,24 +153,26 @@ __global__ void conv_prefill4_kernel(const float* __restrict__ xin, int64_t x_rs
 }
 
 // ---------------------------------------------------------------------------
-// Prefill scan: one CTA per (sequence, head), 256 threads; thread (pp, q)
-// keeps state rows p = pp and pp + 32, columns n = 32j + 4q + e (j < 4, e < 4)
-// in registers for the whole sequence.  The eight lanes q of a row read
-// disjoint 16-byte pieces of the token's B and C rows, so each shared-memory
-// phase serves 128 distinct bytes (the kernel is bound by shared-memory
-// bandwidth, not by its FMAs).  Tokens are staged CH at a time in shared memory
-// (x, gate, B, C, dt, dA); y of the chunk is buffered and written coalesced.
-// The state update uses one FMA per element (s = fma(s, dA, B*xdt)), issued as
-// packed pairs (__fmul2_rn / __ffma2_rn round each component like the scalar
-// forms), and y partial FMA chains reduced over the eight lanes, so results
-// agree with the sequential reference within rounding.
+// Prefill scan: one CTA per (sequence, head), 256 threads; warp w keeps state
+// columns n = 16w .. 16w+15 and lane l rows p = l and l + 32 in registers for
+// the whole sequence.  All lanes of a warp read the same 16-byte pieces of the
+// token's B and C rows, so those shared-memory loads are broadcasts (one
+// wavefront each), and the y partial of a row over the warp's 16 columns is a
+// per-lane FMA chain; the eight warps' partials meet in shared memory once per
+// chunk and are added in warp order.  Tokens are staged CH at a time in shared
+// memory (x, gate, B, C, dt, dA); y of the chunk is buffered and written
+// coalesced.  The state update uses one FMA per element
+// (s = fma(s, dA, B*xdt)), issued as packed pairs (__fmul2_rn / __ffma2_rn
+// round each component like the scalar forms), so results agree with the
+// sequential reference within rounding.
 // CONV: conv + SiLU of the head's 64 x channels on a 3-slot state is applied
 // while staging, by threads 0..63, each owning one channel's window.
 // ---------------------------------------------------------------------------
-constexpr int SCAN_CH = 32;
+constexpr int SCAN_CH = 16;
 constexpr int SCAN_YLD = SCAN_CH + 1;
-constexpr size_t SCAN_SMEM =
-    sizeof(float) * (SCAN_CH * SSD_P * 2 + SCAN_CH * SSD_N * 2 + SCAN_CH * 2 + SSD_P * SCAN_YLD);
+constexpr int SCAN_WARPS = 8;
+constexpr size_t SCAN_SMEM = sizeof(float) * (SCAN_CH * SSD_P * 2 + SCAN_CH * SSD_N * 2 + SCAN_CH * 2 +
+                                              SSD_P * SCAN_YLD + SCAN_CH * SCAN_WARPS * SSD_P);
 
 template <bool CONV, bool GATE>
 __global__ void __launch_bounds__(256, 3) ssd_scan_kernel(SsdScanArgs a) {
@@ -182,22 +184,23 @@ __global__ void __launch_bounds__(256, 3) ssd_scan_kernel(SsdScanArgs a) {
     float* sdt = sg + SCAN_CH * SSD_P;    // [CH]
     float* sda = sdt + SCAN_CH;           // [CH]
     float* sy = sda + SCAN_CH;            // [P][CH+1]
+    float* syp = sy + SSD_P * SCAN_YLD;   // [CH][warps][P]: y partials over each warp's columns
 
     const int h = blockIdx.x, sq = blockIdx.y;  // heads of a sequence adjacent: B, C shared in L2
-    const int tid = threadIdx.x, pp = tid >> 3, q = tid & 7;
+    const int tid = threadIdx.x, w = tid >> 5, l = tid & 31;
     const int r0 = a.cu_seqlens ? a.cu_seqlens[sq] : sq * a.uniform_len;
     const int r1 = a.cu_seqlens ? a.cu_seqlens[sq + 1] : (sq + 1) * a.uniform_len;
     const float dtb = a.dt_bias[h], an = a.a_neg[h], dsk = a.dsk[h];
     const int c0 = h * SSD_P;
 
-    // s[r][2j + k]: row pp + 32r, columns 32j + 4q + 2k, +1
-    float* st = a.ssm + (((size_t)sq * a.H + h) * SSD_P + pp) * SSD_N + 4 * q;
+    // s[r][k]: row l + 32r, columns 16w + 2k, +1
+    float* st = a.ssm + (((size_t)sq * a.H + h) * SSD_P + l) * SSD_N + 16 * w;
     float2 s[2][8];
 #pragma unroll
     for (int r = 0; r < 2; ++r)
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-            const float4 v = *reinterpret_cast<const float4*>(st + r * 32 * SSD_N + 32 * j);
+            const float4 v = *reinterpret_cast<const float4*>(st + r * 32 * SSD_N + 4 * j);
             s[r][2 * j] = make_float2(v.x, v.y);
             s[r][2 * j + 1] = make_float2(v.z, v.w);
         }
@@ -253,22 +256,20 @@ __global__ void __launch_bounds__(256, 3) ssd_scan_kernel(SsdScanArgs a) {
         for (int t = 0; t < nt; ++t) {
             const float dA = sda[t], dtv = sdt[t];
             const float2 dA2 = make_float2(dA, dA);
-            const float* Bt = sB + t * SSD_N + 4 * q;
-            const float* Ct = sC + t * SSD_N + 4 * q;
-            float xv[2];
+            const float* Bt = sB + t * SSD_N + 16 * w;
+            const float* Ct = sC + t * SSD_N + 16 * w;
             float2 xdt[2], ya[2], yb[2];
 #pragma unroll
             for (int r = 0; r < 2; ++r) {
-                xv[r] = sx[t * SSD_P + pp + 32 * r];
-                const float xd = xv[r] * dtv;
+                const float xd = sx[t * SSD_P + l + 32 * r] * dtv;
                 xdt[r] = make_float2(xd, xd);
                 ya[r] = make_float2(0.f, 0.f);
                 yb[r] = make_float2(0.f, 0.f);
             }
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-                const float4 bv = *reinterpret_cast<const float4*>(Bt + 32 * j);
-                const float4 cv = *reinterpret_cast<const float4*>(Ct + 32 * j);
+                const float4 bv = *reinterpret_cast<const float4*>(Bt + 4 * j);
+                const float4 cv = *reinterpret_cast<const float4*>(Ct + 4 * j);
 #pragma unroll
                 for (int r = 0; r < 2; ++r) {
                     s[r][2 * j] = __ffma2_rn(s[r][2 * j], dA2, __fmul2_rn(make_float2(bv.x, bv.y), xdt[r]));
@@ -278,18 +279,19 @@ __global__ void __launch_bounds__(256, 3) ssd_scan_kernel(SsdScanArgs a) {
                 }
             }
 #pragma unroll
-            for (int r = 0; r < 2; ++r) {
-                float y = (ya[r].x + ya[r].y) + (yb[r].x + yb[r].y);
-                y += __shfl_xor_sync(0xffffffffu, y, 1);
-                y += __shfl_xor_sync(0xffffffffu, y, 2);
-                y += __shfl_xor_sync(0xffffffffu, y, 4);
-                if (q == 0) {
-                    const int p = pp + 32 * r;
-                    float yv = y + dsk * xv[r];
-                    if (GATE) yv = yv * sg[t * SSD_P + p];
-                    sy[p * SCAN_YLD + t] = yv;
-                }
-            }
+            for (int r = 0; r < 2; ++r)
+                syp[(t * SCAN_WARPS + w) * SSD_P + l + 32 * r] = (ya[r].x + ya[r].y) + (yb[r].x + yb[r].y);
+        }
+        __syncthreads();
+        for (int i = tid; i < nt * SSD_P; i += 256) {  // y of the chunk: the warps' partials in order
+            const int t = i / SSD_P, p = i % SSD_P;
+            const float* yp = syp + t * SCAN_WARPS * SSD_P + p;
+            float y = yp[0];
+#pragma unroll
+            for (int ww = 1; ww < SCAN_WARPS; ++ww) y = y + yp[ww * SSD_P];
+            float yv = y + dsk * sx[t * SSD_P + p];
+            if (GATE) yv = yv * sg[t * SSD_P + p];
+            sy[p * SCAN_YLD + t] = yv;
         }
         __syncthreads();
         if (a.y_rs == 1) {  // feature-major output: each channel's rows are contiguous
@@ -308,7 +310,7 @@ __global__ void __launch_bounds__(256, 3) ssd_scan_kernel(SsdScanArgs a) {
     for (int r = 0; r < 2; ++r)
 #pragma unroll
         for (int j = 0; j < 4; ++j)
-            *reinterpret_cast<float4*>(st + r * 32 * SSD_N + 32 * j) =
+            *reinterpret_cast<float4*>(st + r * 32 * SSD_N + 4 * j) =
                 make_float4(s[r][2 * j].x, s[r][2 * j].y, s[r][2 * j + 1].x, s[r][2 * j + 1].y);
     if (CONV && tid < SSD_P) {
         cst[0] = w0; cst[1] = w1; cst[2] = w2;
