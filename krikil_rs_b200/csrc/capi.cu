@@ -38,6 +38,7 @@ constexpr int QKV = 3 * HID;
 constexpr float RMS_EPS = 1e-6f, MNORM_EPS = 1e-5f, THETA = 10000.0f;
 constexpr int SEEN_WORDS = VOC / 32;
 constexpr int64_t PREFILL_GROUP_TOKENS = 16384;
+constexpr int PREFILL_STREAMS = 3;  // prefill groups in flight at once, each on its own stream
 
 // Column offsets inside one in_proj output row: z | x | B | C | dt (src/model.rs:638-640, :656-658).
 constexpr int OFF_Z = 0, OFF_X = DI, OFF_B = DI + DI, OFF_C = DI + DI + DS, OFF_DT = DI + DXBC;
@@ -204,7 +205,7 @@ struct krk_state {
     int attn_split = 2048;
     int decode_streams = 3;  // decode batches of 256+ in up to this many parts on their own streams
     std::vector<int64_t> pos_h;
-    PrefillWs pre;
+    PrefillWs pre[PREFILL_STREAMS];  // one workspace per prefill stream
     Prof prof;
     Arena hist_arena;
     int64_t hist_cap = 0;
@@ -411,8 +412,13 @@ void create_state(krk_state* s, const krk_model* m, int B, int ctx) {
     ck(cudaEventCreateWithFlags(&s->ev_join4, cudaEventDisableTiming), "event create");
 }
 
-void ensure_prefill_ws(krk_state* s, int64_t tokens, int seqs) {
-    PrefillWs& w = s->pre;
+void sync_model_streams(const krk_model* m) {
+    for (cudaStream_t x : {m->stream, m->stream2, m->stream3, m->stream4})
+        if (x) ck(cudaStreamSynchronize(x), "stream sync");
+}
+
+void ensure_prefill_ws(krk_state* s, int k, int64_t tokens, int seqs) {
+    PrefillWs& w = s->pre[k];
     if (tokens <= w.cap_tokens && seqs <= w.cap_seqs) return;
     const int64_t T = round_up(std::max<int64_t>(tokens, w.cap_tokens), 64);
     const int S = std::max(seqs, w.cap_seqs);
@@ -422,7 +428,7 @@ void ensure_prefill_ws(krk_state* s, int64_t tokens, int seqs) {
     b.add<float>(INTER * T);
     b.add<uint32_t>(T); b.add<int32_t>(T); b.add<int32_t>(S + 1); b.add<int32_t>(S); b.add<int32_t>(S);
     b.add<int32_t>(S);
-    ck(cudaStreamSynchronize(s->m->stream), "prefill ws sync");
+    sync_model_streams(s->m);  // the old workspace may still be in use on any stream
     w.arena.reserve(b.bytes);
     w.x_t = w.arena.take<float>(HID * T);
     w.hn_t = w.arena.take<float>(HID * T);
@@ -655,10 +661,9 @@ void decode_forward(krk_state* s, const uint8_t* active, int max_keys) {
 }
 
 // Prefill of sequences [g0, g0+S) whose packed tokens are already in pre.tok etc.
-void prefill_group(krk_state* s, int g0, int S, int64_t rows) {
+void prefill_group(krk_state* s, int g0, int S, int64_t rows, PrefillWs& w, cudaStream_t st) {
     const krk_model* m = s->m;
-    cudaStream_t st = m->stream;
-    PrefillWs& w = s->pre;
+    auto timed = [&](krk_state* sp, int cls, auto&& f) { timed_on(sp, st, cls, 0, f); };
     const int T = (int)round_up(rows, 64);
     const int R = (int)rows;
     zero_pad_cols(w.x_t, T, R, HID, st);
@@ -730,40 +735,84 @@ int run_prefill(krk_state* s, const uint32_t* tokens, const int32_t* lens, bool 
         if (tokens[i] >= (uint32_t)VOC)
             return fail(KRK_BAD_TOKEN,
                         "Token ID " + std::to_string(tokens[i]) + " exceeds vocab size " + std::to_string(VOC));
-    cudaStream_t st = s->m->stream;
-    int64_t off = 0;
-    int g0 = 0;
-    while (g0 < B) {
-        int g1 = g0;
-        int64_t rows = 0;
-        while (g1 < B && (g1 == g0 || rows + lens[g1] <= PREFILL_GROUP_TOKENS)) rows += lens[g1++];
-        const int S = g1 - g0;
-        ensure_prefill_ws(s, rows, S);
-        PrefillWs& w = s->pre;
-        std::vector<int32_t> cu(S + 1), start(S), last(S), dst(S), row_seq(rows);
-        cu[0] = 0;
-        for (int i = 0; i < S; ++i) {
-            cu[i + 1] = cu[i] + lens[g0 + i];
-            start[i] = (int32_t)s->pos_h[g0 + i];
-            last[i] = cu[i + 1] - 1;
-            dst[i] = g0 + i;
-            for (int r = cu[i]; r < cu[i + 1]; ++r) row_seq[r] = i;
+    const krk_model* m = s->m;
+    cudaStream_t st = m->stream;
+    // Groups of whole sequences up to PREFILL_GROUP_TOKENS tokens.  They are
+    // independent (disjoint sequences, states and cache rows), so up to
+    // PREFILL_STREAMS of them run at once, group i on stream i % PREFILL_STREAMS
+    // with that stream's workspace: one group's projections overlap another's
+    // scan, attention and norms.  Stream order makes a workspace's reuse safe.
+    struct Group {
+        int g0, S;
+        int64_t rows, off;
+        std::vector<int32_t> cu, start, last, dst, row_seq;  // alive until the final sync
+    };
+    std::vector<Group> groups;
+    {
+        int64_t off = 0;
+        int g0 = 0;
+        while (g0 < B) {
+            int g1 = g0;
+            int64_t rows = 0;
+            while (g1 < B && (g1 == g0 || rows + lens[g1] <= PREFILL_GROUP_TOKENS)) rows += lens[g1++];
+            Group g;
+            g.g0 = g0; g.S = g1 - g0; g.rows = rows; g.off = off;
+            g.cu.resize(g.S + 1); g.start.resize(g.S); g.last.resize(g.S); g.dst.resize(g.S);
+            g.row_seq.resize(rows);
+            g.cu[0] = 0;
+            for (int i = 0; i < g.S; ++i) {
+                g.cu[i + 1] = g.cu[i] + lens[g0 + i];
+                g.start[i] = (int32_t)s->pos_h[g0 + i];
+                g.last[i] = g.cu[i + 1] - 1;
+                g.dst[i] = g0 + i;
+                for (int r = g.cu[i]; r < g.cu[i + 1]; ++r) g.row_seq[r] = i;
+            }
+            groups.push_back(std::move(g));
+            off += rows;
+            g0 = g1;
         }
-        kk(cudaMemcpyAsync(w.tok, tokens + off, rows * 4, cudaMemcpyHostToDevice, st), "h2d tokens");
-        kk(cudaMemcpyAsync(w.cu, cu.data(), (S + 1) * 4, cudaMemcpyHostToDevice, st), "h2d cu");
-        kk(cudaMemcpyAsync(w.start, start.data(), S * 4, cudaMemcpyHostToDevice, st), "h2d start");
-        kk(cudaMemcpyAsync(w.last, last.data(), S * 4, cudaMemcpyHostToDevice, st), "h2d last");
-        kk(cudaMemcpyAsync(w.dst, dst.data(), S * 4, cudaMemcpyHostToDevice, st), "h2d dst");
-        kk(cudaMemcpyAsync(w.row_seq, row_seq.data(), rows * 4, cudaMemcpyHostToDevice, st), "h2d row_seq");
-        total_begin(s);
-        prefill_group(s, g0, S, rows);
-        if (mark)
-            timed(s, KRK_PROF_OTHER, [&] { kk(krk::mark_seen(w.tok, w.row_seq, (int)rows, s->seen_d + (size_t)g0 * SEEN_WORDS, SEEN_WORDS, st),
-               "mark seen"); });
-        kk(cudaStreamSynchronize(st), "prefill group");  // the host vectors above go out of scope
-        off += rows;
-        g0 = g1;
     }
+    const int ns = std::min<int>(PREFILL_STREAMS, (int)groups.size());
+    cudaStream_t streams[PREFILL_STREAMS] = {m->stream, m->stream2, m->stream3};
+    for (int k = 0; k < ns; ++k) {
+        int64_t rows = 0;
+        int seqs = 0;
+        for (size_t i = k; i < groups.size(); i += ns) {
+            rows = std::max(rows, groups[i].rows);
+            seqs = std::max(seqs, groups[i].S);
+        }
+        ensure_prefill_ws(s, k, rows, seqs);
+    }
+    if (ns > 1) {
+        kk(cudaEventRecord(s->ev_fork, st), "fork");
+        for (int k = 1; k < ns; ++k) kk(cudaStreamWaitEvent(streams[k], s->ev_fork, 0), "fork");
+    }
+    for (size_t i = 0; i < groups.size(); ++i) {
+        const Group& g = groups[i];
+        const int k = (int)(i % ns);
+        cudaStream_t gs = streams[k];
+        PrefillWs& w = s->pre[k];
+        kk(cudaMemcpyAsync(w.tok, tokens + g.off, g.rows * 4, cudaMemcpyHostToDevice, gs), "h2d tokens");
+        kk(cudaMemcpyAsync(w.cu, g.cu.data(), (g.S + 1) * 4, cudaMemcpyHostToDevice, gs), "h2d cu");
+        kk(cudaMemcpyAsync(w.start, g.start.data(), g.S * 4, cudaMemcpyHostToDevice, gs), "h2d start");
+        kk(cudaMemcpyAsync(w.last, g.last.data(), g.S * 4, cudaMemcpyHostToDevice, gs), "h2d last");
+        kk(cudaMemcpyAsync(w.dst, g.dst.data(), g.S * 4, cudaMemcpyHostToDevice, gs), "h2d dst");
+        kk(cudaMemcpyAsync(w.row_seq, g.row_seq.data(), g.rows * 4, cudaMemcpyHostToDevice, gs), "h2d row_seq");
+        if (i == 0) total_begin(s);
+        prefill_group(s, g.g0, g.S, g.rows, w, gs);
+        if (mark)
+            timed_on(s, gs, KRK_PROF_OTHER, 0, [&] {
+                kk(krk::mark_seen(w.tok, w.row_seq, (int)g.rows, s->seen_d + (size_t)g.g0 * SEEN_WORDS, SEEN_WORDS,
+                                  gs),
+                   "mark seen");
+            });
+    }
+    cudaEvent_t joins[PREFILL_STREAMS] = {nullptr, s->ev_join, s->ev_join3};
+    for (int k = 1; k < ns; ++k) {
+        kk(cudaEventRecord(joins[k], streams[k]), "join");
+        kk(cudaStreamWaitEvent(st, joins[k], 0), "join");
+    }
+    kk(cudaStreamSynchronize(st), "prefill groups");  // the groups' host vectors go out of scope below
     lm_head(s);
     for (int b = 0; b < B; ++b) s->pos_h[b] += lens[b];
     std::vector<int32_t> p32(s->pos_h.begin(), s->pos_h.end());
@@ -948,7 +997,7 @@ int krk_state_free(krk_state* s) {
         if (s->ev_join) cudaEventDestroy(s->ev_join);
         if (s->ev_join3) cudaEventDestroy(s->ev_join3);
         if (s->ev_join4) cudaEventDestroy(s->ev_join4);
-        s->pre.arena.release();
+        for (auto& w : s->pre) w.arena.release();
         s->hist_arena.release();
         s->arena.release();
         delete s;

@@ -242,6 +242,29 @@ def test_decode_streams_identical(models):
         PebbleState(gpu, 8).set_decode_streams(5)
 
 
+def test_multi_group_prefill_on_streams(models):
+    """A 70-sequence prefill of ~49k tokens runs as several 16k-token groups on
+    up to three streams with their own workspaces: its logits and the next
+    decode step equal (bitwise) those of the same sequences prefilled ten at a
+    time (one group each), and two of them match the oracle."""
+    gpu, orc = models
+    rng = np.random.default_rng(31)
+    bsz, ctx = 70, 1024
+    prompts = [rng.integers(0, 2048, int(n)).astype(np.uint32).tolist() for n in rng.integers(600, 800, bsz)]
+    assert sum(len(p) for p in prompts) > 2 * 16384  # three groups at least
+    st = PebbleState(gpu, ctx, batch=bsz)
+    lg = gpu.prefill_batch(prompts, st)
+    nxt = [int(np.argmax(r)) for r in lg]
+    lg2 = gpu.step_batch(nxt, st)
+    for c0 in range(0, bsz, 10):
+        sub = PebbleState(gpu, ctx, batch=10)
+        np.testing.assert_array_equal(gpu.prefill_batch(prompts[c0:c0 + 10], sub), lg[c0:c0 + 10])
+        np.testing.assert_array_equal(gpu.step_batch(nxt[c0:c0 + 10], sub), lg2[c0:c0 + 10])
+    for b in (0, bsz - 1):
+        ref = O.forward_prefill(orc, O.OracleState(ctx), prompts[b])
+        np.testing.assert_allclose(lg[b], ref, atol=1e-4, rtol=1e-5)
+
+
 def test_generate_sample_device_matches_oracle(models):
     """krk_generate_sample against the oracle's generate loop with a seeded
     Sampler per sequence: identical token streams (ragged prompts, EOS on)."""
