@@ -143,8 +143,10 @@ def attn_decode_bytes(b, prompt, steps):
 
 
 def single_stream_summary(prof, seqs, plen, steps, tokens, peak, fp32_nominal):
-    """Per-kernel rates of one generate call with the decode on one stream."""
+    """Per-kernel rates of one generate call on one stream (decode and prefill);
+    shares are of the summed kernel time."""
     dev_ms = prof["device_total"][0]
+    kernel_ms = sum(v[0] for k, v in prof.items() if k != "device_total")
     ssd_ms, ssd_n, ssd_seqs = prof["ssd_step"]
     ssd_gbs = ssd_step_bytes_per_launch(1) * ssd_seqs / (ssd_ms * 1e-3) / 1e9
     gemm_tf = gemm_flops_per_generate(seqs, plen, steps) / (prof["gemm"][0] * 1e-3) / 1e12
@@ -154,7 +156,7 @@ def single_stream_summary(prof, seqs, plen, steps, tokens, peak, fp32_nominal):
                          "avg_launch_us": round(ssd_ms * 1e3 / max(ssd_n, 1), 2)},
             "gemm": {"achieved": round(gemm_tf, 2), "unit": "TFLOP/s", "frac_nominal": round(gemm_tf / fp32_nominal, 3)},
             "attn_decode": {"achieved": round(attn_gbs, 1), "unit": "GB/s", "frac": round(attn_gbs / peak, 3)},
-            "time_share": {k: round(v[0] / dev_ms, 4) for k, v in prof.items() if k != "device_total"}}
+            "time_share": {k: round(v[0] / kernel_ms, 4) for k, v in prof.items() if k != "device_total"}}
 
 
 # ----------------------------------------------------------------- CPU baseline

@@ -188,8 +188,9 @@ enum {
  * sequences runs as up to n parts of whole 64-row tiles (at least two tiles
  * each, sizes within one tile) on their own streams, so that one part's
  * projections overlap the others' HBM-bound kernels; n = 3 is the default,
- * n = 1 runs the batch on the model stream alone, n <= 4.  Results are
- * identical for every n. */
+ * n <= 4.  Prefills of more than 16,384 prompt tokens run up to three groups
+ * of whole sequences at once on the same streams.  n = 1 runs decode and
+ * prefill on the model stream alone.  Results are identical for every n. */
 KRK_API int krk_state_set_decode_streams(krk_state* state, int n);
 
 /* enable: 0 off, 1 every kernel class and the whole-call total, 2 the

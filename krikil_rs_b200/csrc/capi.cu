@@ -772,7 +772,8 @@ int run_prefill(krk_state* s, const uint32_t* tokens, const int32_t* lens, bool 
             g0 = g1;
         }
     }
-    const int ns = std::min<int>(PREFILL_STREAMS, (int)groups.size());
+    // decode_streams == 1 keeps the prefill on the model stream too
+    const int ns = s->decode_streams == 1 ? 1 : std::min<int>(PREFILL_STREAMS, (int)groups.size());
     cudaStream_t streams[PREFILL_STREAMS] = {m->stream, m->stream2, m->stream3};
     for (int k = 0; k < ns; ++k) {
         int64_t rows = 0;

@@ -190,7 +190,7 @@ class PebbleState:
 
     def set_decode_streams(self, n: int) -> None:
         """Decode batches of 256+ in up to n parts of whole 64-row tiles on their
-        own streams (3 by default, at most 4); 1: one stream."""
+        own streams (3 by default, at most 4); 1: decode and prefill on one stream."""
         check(lib.krk_state_set_decode_streams(self._h, int(n)))
 
     def profile(self, enable: bool = True, per_kernel: bool = True) -> None:
