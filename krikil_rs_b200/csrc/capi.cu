@@ -181,6 +181,7 @@ struct PrefillWs {
     float *x_t, *hn_t, *zx, *xbc, *y_t, *yn_t, *qkv, *ao_t, *mlp_t;
     uint32_t* tok;
     int32_t *row_seq, *cu, *start, *last, *dst;
+    int2* blk;  // prefill attention blocks: (sequence, first row)
 };
 
 }  // namespace
@@ -428,6 +429,7 @@ void ensure_prefill_ws(krk_state* s, int k, int64_t tokens, int seqs) {
     b.add<float>(INTER * T);
     b.add<uint32_t>(T); b.add<int32_t>(T); b.add<int32_t>(S + 1); b.add<int32_t>(S); b.add<int32_t>(S);
     b.add<int32_t>(S);
+    b.add<int2>(T + S);
     sync_model_streams(s->m);  // the old workspace may still be in use on any stream
     w.arena.reserve(b.bytes);
     w.x_t = w.arena.take<float>(HID * T);
@@ -445,6 +447,7 @@ void ensure_prefill_ws(krk_state* s, int k, int64_t tokens, int seqs) {
     w.start = w.arena.take<int32_t>(S);
     w.last = w.arena.take<int32_t>(S);
     w.dst = w.arena.take<int32_t>(S);
+    w.blk = w.arena.take<int2>(T + S);
     ck(cudaMemsetAsync(w.arena.base, 0, w.arena.cap, s->m->stream), "prefill ws memset");
     w.cap_tokens = T;
     w.cap_seqs = S;
@@ -661,7 +664,8 @@ void decode_forward(krk_state* s, const uint8_t* active, int max_keys) {
 }
 
 // Prefill of sequences [g0, g0+S) whose packed tokens are already in pre.tok etc.
-void prefill_group(krk_state* s, int g0, int S, int64_t rows, PrefillWs& w, cudaStream_t st) {
+void prefill_group(krk_state* s, int g0, int S, int64_t rows, int nblk, int blk_rows, int kmax, PrefillWs& w,
+                   cudaStream_t st) {
     const krk_model* m = s->m;
     auto timed = [&](krk_state* sp, int cls, auto&& f) { timed_on(sp, st, cls, 0, f); };
     const int T = (int)round_up(rows, 64);
@@ -702,8 +706,8 @@ void prefill_group(krk_state* s, int g0, int S, int64_t rows, PrefillWs& w, cuda
             const int64_t c_sb = (int64_t)s->ctx * HID;
             timed(s, KRK_PROF_OTHER, [&] { kk(krk::rope_kv_prefill(w.qkv, QKV, kc, vc, c_sb, HD, HID, w.cu, w.start, S, NH, HD, R, THETA, s->rope, st),
                "rope/kv"); });
-            timed(s, KRK_PROF_ATTN_PREFILL, [&] { kk(krk::attn_prefill(w.qkv, QKV, kc, vc, c_sb, HD, HID, w.cu, w.start, w.row_seq, S, NH, HD, R, s->ctx,
-                                 w.ao_t, 1, T, st),
+            timed(s, KRK_PROF_ATTN_PREFILL, [&] { kk(krk::attn_prefill(w.qkv, QKV, kc, vc, c_sb, HD, HID, w.cu, w.start, w.blk, nblk, blk_rows, NH, HD,
+                                 kmax, w.ao_t, 1, T, st),
                "attention"); });
             timed(s, KRK_PROF_GEMM, [&] { kk(krk::gemm(w.ao_t, T, L.wo_t, HID, w.x_t, T, T, HID, HID, krk::EPI_RESIDUAL, true, st), "wo"); });
             timed(s, KRK_PROF_NORM, [&] { kk(krk::rmsnorm_fm(w.x_t, T, L.ln2, RMS_EPS, HID, R, w.hn_t, T, st), "ln2"); });
@@ -746,6 +750,8 @@ int run_prefill(krk_state* s, const uint32_t* tokens, const int32_t* lens, bool 
         int g0, S;
         int64_t rows, off;
         std::vector<int32_t> cu, start, last, dst, row_seq;  // alive until the final sync
+        std::vector<int2> blk;
+        int blk_rows, kmax;
     };
     std::vector<Group> groups;
     {
@@ -767,6 +773,11 @@ int run_prefill(krk_state* s, const uint32_t* tokens, const int32_t* lens, bool 
                 g.dst[i] = g0 + i;
                 for (int r = g.cu[i]; r < g.cu[i + 1]; ++r) g.row_seq[r] = i;
             }
+            g.kmax = 1;
+            for (int i = 0; i < g.S; ++i) g.kmax = std::max(g.kmax, g.start[i] + lens[g0 + i]);
+            g.blk_rows = krk::attn_prefill_rows(g.kmax, HD);
+            for (int i = 0; i < g.S; ++i)
+                for (int r = 0; r < lens[g0 + i]; r += g.blk_rows) g.blk.push_back(make_int2(i, r));
             groups.push_back(std::move(g));
             off += rows;
             g0 = g1;
@@ -799,8 +810,9 @@ int run_prefill(krk_state* s, const uint32_t* tokens, const int32_t* lens, bool 
         kk(cudaMemcpyAsync(w.last, g.last.data(), g.S * 4, cudaMemcpyHostToDevice, gs), "h2d last");
         kk(cudaMemcpyAsync(w.dst, g.dst.data(), g.S * 4, cudaMemcpyHostToDevice, gs), "h2d dst");
         kk(cudaMemcpyAsync(w.row_seq, g.row_seq.data(), g.rows * 4, cudaMemcpyHostToDevice, gs), "h2d row_seq");
+        kk(cudaMemcpyAsync(w.blk, g.blk.data(), g.blk.size() * sizeof(int2), cudaMemcpyHostToDevice, gs), "h2d blocks");
         if (i == 0) total_begin(s);
-        prefill_group(s, g.g0, g.S, g.rows, w, gs);
+        prefill_group(s, g.g0, g.S, g.rows, (int)g.blk.size(), g.blk_rows, g.kmax, w, gs);
         if (mark)
             timed_on(s, gs, KRK_PROF_OTHER, 0, [&] {
                 kk(krk::mark_seen(w.tok, w.row_seq, (int)g.rows, s->seen_d + (size_t)g.g0 * SEEN_WORDS, SEEN_WORDS,

@@ -627,42 +627,83 @@ __global__ void rope_kv_prefill_kernel(float* __restrict__ qkv, int64_t q_rs, fl
     vc[cb + i + half] = vr[i + half];
 }
 
-// Causal attention for packed prefill rows (src/model.rs:519-548): one warp per
-// (row, head).  Scores are full reference dots (lane per key); after the max
-// and the sum of exponentials, each lane owns output dims d = lane + 32i and
-// accumulates w_j * v_j[d] over j in order.
+// Causal attention for packed prefill rows (src/model.rs:519-548), a CTA per
+// block of ROWS consecutive query rows of one sequence and one head, a warp per
+// row.  The rows of a block share their sequence's K and V rows, so the CTA
+// stages them in shared memory a tile of PF_KT keys at a time (cp.async, K
+// tiles for the scores, then V tiles for the output) and every warp reads
+// them from there.  Per row the arithmetic is the reference's: full reference
+// dots (lane per key), the max and the sum of exponentials over all keys,
+// then out[d] = sum_j (e_j / l) * v_j[d] in key order, lane d owning dims
+// d + 32i.  Scores are kept per row in shared memory ([ROWS][kmax]).
+constexpr int PF_KT = 64;
+constexpr int PF_MAX_SMEM = 227 * 1024;
+
 template <int DH>
-__global__ void attn_prefill_kernel(const float* __restrict__ qkv, int64_t q_rs, const float* __restrict__ kc,
-                                    const float* __restrict__ vc, int64_t c_sb, int64_t c_sh, int64_t c_st,
-                                    const int32_t* __restrict__ cu, const int32_t* __restrict__ start,
-                                    const int32_t* __restrict__ row_seq, int H, int total_rows, int ctx,
-                                    float* __restrict__ out, int64_t o_rs, int64_t o_cs) {
-    constexpr int ND = (DH + 31) / 32;
+struct PfLayout {
+    static constexpr int KLD = ((DH / 4) & 1) ? DH : DH + 4;  // odd float4 row stride: conflict-free
+};
+
+template <int DH, int ROWS>
+size_t pf_smem_bytes(int kmax) {
+    return sizeof(float) * ((size_t)PF_KT * PfLayout<DH>::KLD + (size_t)ROWS * DH + (size_t)ROWS * kmax);
+}
+
+template <int DH, int ROWS>
+__global__ void __launch_bounds__(ROWS * 32) attn_prefill_kernel(
+    const float* __restrict__ qkv, int64_t q_rs, const float* __restrict__ kc, const float* __restrict__ vc,
+    int64_t c_sb, int64_t c_sh, int64_t c_st, const int32_t* __restrict__ cu, const int32_t* __restrict__ start,
+    const int2* __restrict__ blocks, int kmax, float* __restrict__ out, int64_t o_rs, int64_t o_cs) {
+    constexpr int ND = (DH + 31) / 32, KLD = PfLayout<DH>::KLD, DH4 = DH / 4, NT = ROWS * 32;
     extern __shared__ __align__(16) float sm[];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-    float* qsh = sm + warp * DH;
-    float* sc = sm + nw * DH + (size_t)warp * ctx;
-    const int row = blockIdx.x * nw + warp, h = blockIdx.y;
-    if (row >= total_rows) return;
-    const int sq = row_seq[row];
-    const int qpos = start[sq] + (row - cu[sq]);
-    const int nk = qpos + 1;
-    const float* qr = qkv + (size_t)row * q_rs + (size_t)h * DH;
-    for (int d = lane; d < DH; d += 32) qsh[d] = qr[d];
+    float* kt = sm;                   // [PF_KT][KLD]: the staged K or V tile
+    float* qsh = kt + PF_KT * KLD;    // [ROWS][DH]
+    float* sc = qsh + ROWS * DH;      // [ROWS][kmax]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, h = blockIdx.y;
+    const int2 blk = blocks[blockIdx.x];
+    const int sq = blk.x, r0 = blk.y;
+    const int len = cu[sq + 1] - cu[sq];
+    const int r = r0 + warp;  // this warp's row within its sequence
+    const bool valid = r < len;
+    const int nk = valid ? start[sq] + r + 1 : 0;
+    const int nk_blk = start[sq] + min(r0 + ROWS, len);  // keys some row of the block needs
+    const size_t row = (size_t)(cu[sq] + (valid ? r : 0));
+    float* qw = qsh + warp * DH;
+    float* scw = sc + (size_t)warp * kmax;
+    if (valid)
+        for (int d = lane; d < DH; d += 32) qw[d] = qkv[row * q_rs + (size_t)h * DH + d];
     __syncwarp();
     const float scale = 1.0f / sqrtf((float)DH);
     const size_t cb = (size_t)sq * c_sb + (size_t)h * c_sh;
+
+    auto stage = [&](const float* src, int t0, int nt) {
+        __syncthreads();  // every warp is done with the previous tile
+        for (int i = threadIdx.x; i < nt * DH4; i += NT) {
+            const int rr = i / DH4, c4 = i % DH4;
+            cp_async16(kt + rr * KLD + c4 * 4, src + cb + (size_t)(t0 + rr) * c_st + c4 * 4);
+        }
+        cp_async_commit();
+        cp_async_wait<0>();
+        __syncthreads();
+    };
+
+    // scores, lane j % 32 for key j as in the row-per-warp form
     float mx = -INFINITY;
-    for (int j = lane; j < nk; j += 32) {
-        const float sv = dot_ref(qsh, kc + cb + (size_t)j * c_st, DH) * scale;
-        sc[j] = sv;
-        mx = fmaxf(mx, sv);
+    for (int t0 = 0; t0 < nk_blk; t0 += PF_KT) {
+        const int nt = min(PF_KT, nk_blk - t0);
+        stage(kc, t0, nt);
+        const int jend = min(t0 + nt, nk);
+        for (int j = t0 + lane; j < jend; j += 32) {
+            const float sv = dot_ref(qw, kt + (j - t0) * KLD, DH) * scale;
+            scw[j] = sv;
+            mx = fmaxf(mx, sv);
+        }
     }
     mx = warp_max(mx);
     float ls = 0.0f;
     for (int j = lane; j < nk; j += 32) {
-        const float e = expf(sc[j] - mx);
-        sc[j] = e;
+        const float e = expf(scw[j] - mx);
+        scw[j] = e;
         ls += e;
     }
     ls = warp_sum(ls);
@@ -671,19 +712,25 @@ __global__ void attn_prefill_kernel(const float* __restrict__ qkv, int64_t q_rs,
     float o[ND];
 #pragma unroll
     for (int i = 0; i < ND; ++i) o[i] = 0.0f;
-    for (int j = 0; j < nk; ++j) {
-        const float w = sc[j] * inv;
-        const float* vr = vc + cb + (size_t)j * c_st;
+    for (int t0 = 0; t0 < nk_blk; t0 += PF_KT) {
+        const int nt = min(PF_KT, nk_blk - t0);
+        stage(vc, t0, nt);
+        const int jend = min(t0 + nt, nk);
+        for (int j = t0; j < jend; ++j) {
+            const float w = scw[j] * inv;
+            const float* vr = kt + (j - t0) * KLD;
 #pragma unroll
-        for (int i = 0; i < ND; ++i) {
-            const int d = lane + 32 * i;
-            if (d < DH) o[i] = o[i] + w * vr[d];
+            for (int i = 0; i < ND; ++i) {
+                const int d = lane + 32 * i;
+                if (d < DH) o[i] = o[i] + w * vr[d];
+            }
         }
     }
+    if (!valid) return;
 #pragma unroll
     for (int i = 0; i < ND; ++i) {
         const int d = lane + 32 * i;
-        if (d < DH) out[(size_t)row * o_rs + (size_t)(h * DH + d) * o_cs] = o[i];
+        if (d < DH) out[row * o_rs + (size_t)(h * DH + d) * o_cs] = o[i];
     }
 }
 
@@ -793,31 +840,34 @@ cudaError_t rope_kv_prefill(float* qkv, int64_t q_rs, float* kc, float* vc, int6
     return cudaGetLastError();
 }
 
+int attn_prefill_rows(int kmax, int dh) {
+    const size_t need = dh == 76 ? pf_smem_bytes<76, PF_ROWS>(kmax) : pf_smem_bytes<64, PF_ROWS>(kmax);
+    return need <= PF_MAX_SMEM ? PF_ROWS : 1;
+}
+
 cudaError_t attn_prefill(const float* qkv, int64_t q_rs, const float* kc, const float* vc, int64_t c_sb,
                          int64_t c_sh, int64_t c_st, const int32_t* cu_seqlens, const int32_t* start,
-                         const int32_t* row_seq, int S, int H, int dh, int total_rows, int ctx, float* out,
+                         const int2* blocks, int nblocks, int rows_per_block, int H, int dh, int kmax, float* out,
                          int64_t o_rs, int64_t o_cs, cudaStream_t s) {
-    (void)S;
-    if (H <= 0 || total_rows <= 0 || ctx <= 0 || (dh != 64 && dh != 76) || (q_rs & 3) || (c_st & 3) ||
-        (c_sh & 3) || (c_sb & 3) || (((uintptr_t)qkv | (uintptr_t)kc | (uintptr_t)vc) & 15))
+    if (H <= 0 || nblocks <= 0 || kmax <= 0 || (dh != 64 && dh != 76) || (q_rs & 3) || (c_st & 3) ||
+        (c_sh & 3) || (c_sb & 3) || (((uintptr_t)qkv | (uintptr_t)kc | (uintptr_t)vc) & 15) ||
+        (rows_per_block != PF_ROWS && rows_per_block != 1))
         return cudaErrorInvalidValue;
-    int nw = 8;
-    while (nw > 1 && (size_t)nw * (dh + ctx) * sizeof(float) > 200 * 1024) nw >>= 1;
-    const size_t smem = (size_t)nw * (dh + ctx) * sizeof(float);
-    if (smem > 227 * 1024) return cudaErrorInvalidValue;
-    dim3 grid((total_rows + nw - 1) / nw, H);
+    const bool wide = rows_per_block == PF_ROWS;
+    const size_t smem = dh == 76 ? (wide ? pf_smem_bytes<76, PF_ROWS>(kmax) : pf_smem_bytes<76, 1>(kmax))
+                                 : (wide ? pf_smem_bytes<64, PF_ROWS>(kmax) : pf_smem_bytes<64, 1>(kmax));
+    if (smem > PF_MAX_SMEM) return cudaErrorInvalidValue;
+    const void* fns[4] = {(const void*)attn_prefill_kernel<64, 1>, (const void*)attn_prefill_kernel<64, PF_ROWS>,
+                          (const void*)attn_prefill_kernel<76, 1>, (const void*)attn_prefill_kernel<76, PF_ROWS>};
+    const int v = (dh == 76 ? 2 : 0) + (wide ? 1 : 0);
+    static DeviceOnce once[4];
     cudaError_t e;
-    if (dh == 76) {
-        static DeviceOnce once;
-        if ((e = once.set_smem((const void*)attn_prefill_kernel<76>, 227 * 1024)) != cudaSuccess) return e;
-        attn_prefill_kernel<76><<<grid, nw * 32, smem, s>>>(qkv, q_rs, kc, vc, c_sb, c_sh, c_st, cu_seqlens,
-                                                            start, row_seq, H, total_rows, ctx, out, o_rs, o_cs);
-    } else {
-        static DeviceOnce once;
-        if ((e = once.set_smem((const void*)attn_prefill_kernel<64>, 227 * 1024)) != cudaSuccess) return e;
-        attn_prefill_kernel<64><<<grid, nw * 32, smem, s>>>(qkv, q_rs, kc, vc, c_sb, c_sh, c_st, cu_seqlens,
-                                                            start, row_seq, H, total_rows, ctx, out, o_rs, o_cs);
-    }
+    if ((e = once[v].set_smem(fns[v], PF_MAX_SMEM)) != cudaSuccess) return e;
+    dim3 grid(nblocks, H);
+    void* params[] = {(void*)&qkv, (void*)&q_rs, (void*)&kc, (void*)&vc, (void*)&c_sb, (void*)&c_sh,
+                      (void*)&c_st, (void*)&cu_seqlens, (void*)&start, (void*)&blocks, (void*)&kmax,
+                      (void*)&out, (void*)&o_rs, (void*)&o_cs};
+    if ((e = cudaLaunchKernel(fns[v], grid, dim3(rows_per_block * 32), params, smem, s)) != cudaSuccess) return e;
     add_launches(1);
     return cudaGetLastError();
 }

@@ -146,10 +146,16 @@ cudaError_t wait_probe(const float* src, int polls, bool copy, int* err, cudaStr
 cudaError_t rope_kv_prefill(float* qkv, int64_t q_rs, float* kc, float* vc, int64_t c_sb, int64_t c_sh,
                             int64_t c_st, const int32_t* cu_seqlens, const int32_t* start, int S, int H, int dh,
                             int total_rows, float theta, const float2* rope, cudaStream_t s);
-// Causal attention of packed query rows over their sequence's cache.
+// Causal attention of packed query rows over their sequence's cache, by
+// blocks of rows_per_block consecutive rows of one sequence: blocks[i] =
+// (sequence, first row within it); kmax >= start[s] + rows of s for every s.
+// rows_per_block = attn_prefill_rows(kmax, dh): PF_ROWS, or 1 when the
+// scores of PF_ROWS rows over kmax keys do not fit in shared memory.
+constexpr int PF_ROWS = 8;
+int attn_prefill_rows(int kmax, int dh);
 cudaError_t attn_prefill(const float* qkv, int64_t q_rs, const float* kc, const float* vc, int64_t c_sb,
                          int64_t c_sh, int64_t c_st, const int32_t* cu_seqlens, const int32_t* start,
-                         const int32_t* row_seq, int S, int H, int dh, int total_rows, int ctx, float* out,
+                         const int2* blocks, int nblocks, int rows_per_block, int H, int dh, int kmax, float* out,
                          int64_t o_rs, int64_t o_cs, cudaStream_t s);
 
 // ---------------------------------------------------------------- sampling
