@@ -200,9 +200,10 @@ KRK_API int krk_state_profile(krk_state* state, int enable);
 KRK_API int krk_state_profile_read(const krk_state* state, int cls, double* total_ms, int64_t* launches);
 /* Decode sequences processed by the timed launches of a class (the sum over
  * its decode launches of the sequences each covered; prefill launches add 0).
- * A decode batch of 256+ sequences runs as two halves on two streams, each
- * launch timed on its own stream, so per-class times are kernel times that may
- * overlap and can add up to more than KRK_PROF_DEVICE_TOTAL. */
+ * A decode batch of 256+ sequences runs in parts on up to three streams, and
+ * a large prefill in groups on up to three streams, each launch timed on its
+ * own stream, so per-class times are kernel times that may overlap and can add
+ * up to more than KRK_PROF_DEVICE_TOTAL. */
 KRK_API int krk_state_profile_units(const krk_state* state, int cls, int64_t* units);
 
 /* ------------------------------------------------------ per-kernel entry points
