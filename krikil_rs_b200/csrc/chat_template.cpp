@@ -246,6 +246,20 @@ std::vector<Tok> lex_expr(const std::string& src) {
     return out;
 }
 
+// Nesting limit of expressions and blocks: the parser recurses per level, so a
+// hostile template must not be able to exhaust the stack.
+constexpr int MAX_NEST = 100;
+struct NestGuard {
+    int& d;
+    NestGuard(int& depth, const char* what) : d(depth) {
+        if (++d > MAX_NEST) {
+            --d;
+            throw SyntaxError(std::string(what) + " nested too deeply");
+        }
+    }
+    ~NestGuard() { --d; }
+};
+
 // ----------------------------------------------------------------- the tree
 struct Expr;
 using ExprP = std::shared_ptr<Expr>;
@@ -299,6 +313,7 @@ class ExprParser {
    private:
     std::vector<Tok> t_;
     size_t p_ = 0;
+    int depth_ = 0;
 
     bool is_op(const char* o) const { return t_[p_].k == Tok::Op && t_[p_].s == o; }
     bool is_name(const char* w) const { return t_[p_].k == Tok::Name && t_[p_].s == w; }
@@ -324,6 +339,7 @@ class ExprParser {
     }
 
     ExprP expr() {  // a if cond else b
+        NestGuard g(depth_, "expression");
         ExprP a = expr_no_cond();
         if (accept_name("if")) {
             ExprP c = or_expr();
@@ -346,7 +362,10 @@ class ExprParser {
         return a;
     }
     ExprP not_expr() {
-        if (accept_name("not")) return mk(Expr::Unary, "not", {not_expr()});
+        if (accept_name("not")) {
+            NestGuard g(depth_, "expression");
+            return mk(Expr::Unary, "not", {not_expr()});
+        }
         return compare();
     }
     ExprP compare() {
@@ -401,8 +420,14 @@ class ExprParser {
         }
     }
     ExprP unary() {
-        if (accept_op("-")) return mk(Expr::Unary, "-", {unary()});
-        if (accept_op("+")) return unary();
+        if (accept_op("-")) {
+            NestGuard g(depth_, "expression");
+            return mk(Expr::Unary, "-", {unary()});
+        }
+        if (accept_op("+")) {
+            NestGuard g(depth_, "expression");
+            return unary();
+        }
         return postfix(primary());
     }
     std::vector<ExprP> call_args() {  // after "("
@@ -596,6 +621,7 @@ class TemplateParser {
    private:
     std::vector<Piece> ps_;
     size_t i_ = 0;
+    int depth_ = 0;
     std::vector<Tok> rest_;  // tokens after the keyword of the statement that ended the last body
 
     static std::vector<Tok> tokens_after_keyword(const std::string& stmt, std::string& kw) {
@@ -608,6 +634,7 @@ class TemplateParser {
     // Parses nodes until one of the stop keywords; `stop` receives it ("" at
     // the end of input) and rest_ the tokens after it.
     Body body(const std::vector<std::string>& stops, std::string& stop) {
+        NestGuard g(depth_, "block");
         Body out;
         while (i_ < ps_.size()) {
             const Piece& pc = ps_[i_++];

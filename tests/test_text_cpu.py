@@ -184,6 +184,12 @@ def test_template_minijinja_printing_and_errors(tmp_path):
         with pytest.raises(KrikilError) as e:
             ChatTemplateEngine(src).render([], False)
         assert e.value.message.startswith("Failed to render Jinja chat template"), src
+    for src in ("{{ " + "(" * 5000 + "1" + ")" * 5000 + " }}", "{% if x %}" * 3000 + "{% endif %}" * 3000,
+                "{{ " + "-" * 5000 + "1 }}", "{{ " + "not " * 5000 + "x }}", "{{ " + "[" * 5000 + "]" * 5000 + " }}"):
+        with pytest.raises(KrikilError) as e:  # deep nesting is refused, not a stack overflow
+            ChatTemplateEngine(src).render([], False)
+        assert "nested too deeply" in e.value.message
+    assert ChatTemplateEngine("{{ " + "(" * 50 + "1" + ")" * 50 + " }}").render([], False) == "1"
     with pytest.raises(KrikilError) as e:
         ChatTemplateEngine.from_file(tmp_path / "none.jinja")
     assert "Failed to read chat template from" in e.value.message
