@@ -134,6 +134,51 @@ def test_load_errors(tmp_path):
     assert "invalid JSON" in e.value.message
 
 
+def test_unsupported_tokenizer_files_are_refused(tmp_path):
+    """Only what the Pebble tokenizer uses is implemented; anything else fails
+    at load with a message naming it rather than tokenizing differently."""
+    import copy
+    base = _load("tokenizer_small.json")
+    cases = [("normalizer", {"type": "NFC"}, "normalizer"),
+             ("pre_tokenizer", {"type": "Whitespace"}, "pre_tokenizer"),
+             ("decoder", {"type": "WordPiece"}, "decoder"),
+             ("model.dropout", 0.1, "dropout"),
+             ("model.byte_fallback", True, "byte_fallback"),
+             ("model.unk_token", "<unk>", "unk_token"),
+             ("model.continuing_subword_prefix", "##", "continuing_subword_prefix")]
+    for key, val, needle in cases:
+        d = copy.deepcopy(base)
+        if key.startswith("model."):
+            d["model"][key[6:]] = val
+        else:
+            d[key] = val
+        f = tmp_path / "t.json"
+        f.write_text(json.dumps(d))
+        with pytest.raises(KrikilError) as e:
+            PebbleTokenizer.from_file(f)
+        assert e.value.status == _lib.IO and needle in e.value.message, (key, e.value.message)
+    d = copy.deepcopy(base)
+    d["added_tokens"][0]["single_word"] = True
+    (tmp_path / "t.json").write_text(json.dumps(d))
+    with pytest.raises(KrikilError) as e:
+        PebbleTokenizer.from_file(tmp_path / "t.json")
+    assert "single_word" in e.value.message
+    d = copy.deepcopy(base)
+    d["model"]["merges"] = d["model"]["merges"] + [["zzq", "qqz"]]
+    (tmp_path / "t.json").write_text(json.dumps(d))
+    with pytest.raises(KrikilError) as e:
+        PebbleTokenizer.from_file(tmp_path / "t.json")
+    assert "merge token missing from vocab" in e.value.message
+    # merges written as "a b" strings (the older file format) load and encode the same
+    d = copy.deepcopy(base)
+    d["model"]["merges"] = [" ".join(m) for m in d["model"]["merges"]]
+    (tmp_path / "t.json").write_text(json.dumps(d))
+    a = PebbleTokenizer.from_file(tmp_path / "t.json")
+    b = PebbleTokenizer.from_file(os.path.join(GOLDEN, "tokenizer_small.json"))
+    for text in ("the cat sat on the mat", "they're going home!", "Москва 1234"):
+        assert a.encode(text) == b.encode(text)
+
+
 def test_resolve_path(tmp_path, monkeypatch):
     """src/tokenizer.rs:54-79: explicit path, the model's sibling, ./tokenizer.json."""
     model = tmp_path / "m" / "model.safetensors"
