@@ -179,6 +179,18 @@ def test_unsupported_tokenizer_files_are_refused(tmp_path):
         assert a.encode(text) == b.encode(text)
 
 
+@pytest.mark.parametrize("text", ['{"a": "x', '{"a": "\\q"}', '{"a": "\\ud800"}', '{"a": 1,}', '[1 2]',
+                                  '{"a": tru}', '{} {}', '{"a": "\x01"}', '[' * 600 + ']' * 600, '-', '{"a": 1e}'])
+def test_malformed_json_is_refused(tmp_path, text):
+    """The tokenizer file reader rejects malformed JSON (and nesting beyond 512
+    levels) with a positioned message instead of reading past it."""
+    f = tmp_path / "t.json"
+    f.write_text(text)
+    with pytest.raises(KrikilError) as e:
+        PebbleTokenizer.from_file(f)
+    assert e.value.status == _lib.IO and "invalid JSON" in e.value.message and "at byte" in e.value.message
+
+
 def test_resolve_path(tmp_path, monkeypatch):
     """src/tokenizer.rs:54-79: explicit path, the model's sibling, ./tokenizer.json."""
     model = tmp_path / "m" / "model.safetensors"
