@@ -213,6 +213,10 @@ struct krk_state {
     uint32_t* hist_d = nullptr;
     cudaEvent_t ev_fork = nullptr, ev_join = nullptr;  // ordering of the decode streams
     cudaEvent_t ev_join3 = nullptr, ev_join4 = nullptr;
+    // CUDA graphs of one decode step for batches of one 64-row tile, one per
+    // count of attention key blocks (index: blocks - 1); captured on first use.
+    std::vector<cudaGraphExec_t> step_graphs;
+    std::vector<uint64_t> step_graph_kernels;
 };
 
 namespace {
@@ -663,6 +667,56 @@ void decode_forward(krk_state* s, const uint8_t* active, int max_keys) {
     }
 }
 
+// A decode step of a batch of one 64-row tile is ~260 small launches whose
+// launch gaps, not their work, set the time per token; such steps replay a
+// CUDA graph of decode_forward instead, one graph per count of 64-key
+// attention blocks (the attention grid's depth), captured the first time that
+// count comes up.  The graph's attention reads up to blocks * 64 rows (fewer
+// than ctx): rows past a sequence's position are masked as always.  Not used
+// while per-kernel profiling records events around each launch, nor for split
+// batches.
+constexpr int GRAPH_MAX_MP = 64;
+
+void decode_step(krk_state* s, int max_keys) {
+    Part parts[4];
+    if ((s->prof.on && s->prof.per_kernel) || s->Mp > GRAPH_MAX_MP || decode_parts(s, parts) != 1) {
+        decode_forward(s, s->active_d, max_keys);
+        return;
+    }
+    const int keys_cap = std::min(std::max(max_keys, 1), s->ctx);
+    const int z = (keys_cap + s->attn_split - 1) / s->attn_split;
+    const int keys = std::min(z * s->attn_split, s->ctx);
+    if ((int)s->step_graphs.size() < z) {
+        s->step_graphs.resize(z, nullptr);
+        s->step_graph_kernels.resize(z, 0);
+    }
+    cudaStream_t st = s->m->stream;
+    cudaGraphExec_t& ex = s->step_graphs[z - 1];
+    if (!ex) {
+        // capture: the launchers count their launches as they are recorded,
+        // which stands for this first replay
+        const uint64_t n0 = krk::launch_count();
+        cudaGraph_t g = nullptr;
+        kk(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal), "graph capture");
+        try {
+            decode_forward(s, s->active_d, keys);
+        } catch (...) {
+            cudaStreamEndCapture(st, &g);
+            if (g) cudaGraphDestroy(g);
+            throw;
+        }
+        kk(cudaStreamEndCapture(st, &g), "graph capture");
+        const cudaError_t e = cudaGraphInstantiate(&ex, g, 0);
+        cudaGraphDestroy(g);
+        if (e != cudaSuccess) ex = nullptr;
+        kk(e, "graph instantiate");
+        s->step_graph_kernels[z - 1] = krk::launch_count() - n0;
+    } else {
+        krk::add_launches(s->step_graph_kernels[z - 1]);
+    }
+    kk(cudaGraphLaunch(ex, st), "graph launch");
+}
+
 // Prefill of sequences [g0, g0+S) whose packed tokens are already in pre.tok etc.
 void prefill_group(krk_state* s, int g0, int S, int64_t rows, int nblk, int blk_rows, int kmax, PrefillWs& w,
                    cudaStream_t st) {
@@ -1010,6 +1064,8 @@ int krk_state_free(krk_state* s) {
         if (s->ev_join) cudaEventDestroy(s->ev_join);
         if (s->ev_join3) cudaEventDestroy(s->ev_join3);
         if (s->ev_join4) cudaEventDestroy(s->ev_join4);
+        for (cudaGraphExec_t g : s->step_graphs)
+            if (g) cudaGraphExecDestroy(g);
         for (auto& w : s->pre) w.arena.release();
         s->hist_arena.release();
         s->arena.release();
@@ -1185,7 +1241,7 @@ static int generate_impl(const krk_model* m, krk_state* s, const uint32_t* promp
         // step i runs every active sequence at position pos_h[b] + i at most
         const int64_t pos0 = *std::max_element(s->pos_h.begin(), s->pos_h.end());
         for (int i = 0; i < max_steps; ++i) {
-            decode_forward(s, s->active_d, (int)(pos0 + i + 1));
+            decode_step(s, (int)(pos0 + i + 1));
             timed(s, KRK_PROF_OTHER, [&] { kk(krk::sample(ga, st), "sample"); });
         }
         total_end(s);
