@@ -137,7 +137,11 @@ KRK_API int krk_step(const krk_model* model, krk_state* state, const uint32_t* t
  * if stop_at_eos -- when it picks KRK_EOS_TOKEN (not emitted).  With
  * stop_at_eos = 0 every sequence emits min(max_new_tokens, max_ctx - len + 1)
  * tokens.  tokens_out (host, [batch][max_new_tokens]) and n_out (host,
- * [batch]) receive the generated ids and their counts. */
+ * [batch]) receive the generated ids and their counts.  For states of at most
+ * 64 sequences each decode step replays a CUDA graph held by the state (one
+ * per count of 64-key attention blocks, captured on the model stream the first
+ * time the count comes up) unless per-kernel profiling is on; krk_generate_sample
+ * does the same. */
 KRK_API int krk_generate_greedy(const krk_model* model, krk_state* state, const uint32_t* prompts,
                                 const int32_t* lens, int max_new_tokens, float repetition_penalty, int stop_at_eos,
                                 uint32_t* tokens_out, int32_t* n_out);
