@@ -39,6 +39,7 @@ namespace {
 constexpr int NORM_COLS = 8;
 constexpr int NORM_MAXK = 1216;
 constexpr int NORM_CHUNKS = 8;
+constexpr int NORM_WS_MAX_COLS = 128;  // up to this many columns the weights are staged
 
 // cp.async.wait_group with a run-time count n in [0, NORM_CHUNKS).
 KRK_DEV void cp_async_wait_upto(int n) {
@@ -54,11 +55,16 @@ KRK_DEV void cp_async_wait_upto(int n) {
     }
 }
 
+// WS (few columns, where the kernel's latency is the whole cost): the weights
+// are staged in shared memory while the column block is in flight, instead of
+// one global read per written element.
+template <bool WS>
 __global__ void __launch_bounds__(256) rmsnorm_fm_kernel(const float* __restrict__ x, int ldx,
                                                          const float* __restrict__ w, float eps, int K, int M,
                                                          float* __restrict__ out, int ldo) {
-    extern __shared__ __align__(16) float blk[];  // [K][NORM_COLS]
+    extern __shared__ __align__(16) float blk[];  // [K][NORM_COLS], then (WS) w [K]
     __shared__ float scale_s[NORM_COLS];
+    float* ws = blk + (size_t)K * NORM_COLS;
     const int tid = threadIdx.x;
     const int m0 = blockIdx.x * NORM_COLS;
     const int ncols = min(NORM_COLS, M - m0);
@@ -79,6 +85,8 @@ __global__ void __launch_bounds__(256) rmsnorm_fm_kernel(const float* __restrict
             blk[i] = c < ncols ? x[(size_t)k * ldx + m0 + c] : 0.0f;
         }
     }
+    if (WS)
+        for (int k = tid; k < K; k += 256) ws[k] = w[k];
     float ss = 0.0f;
     for (int c = 0; c < NORM_CHUNKS; ++c) {
         if (full) cp_async_wait_upto(NORM_CHUNKS - 1 - c);
@@ -100,8 +108,14 @@ __global__ void __launch_bounds__(256) rmsnorm_fm_kernel(const float* __restrict
     const int c = tid % NORM_COLS;
     if (c < ncols) {
         const float sc = scale_s[c];
-        for (int k = tid / NORM_COLS; k < K; k += 256 / NORM_COLS)
-            out[(size_t)k * ldo + m0 + c] = blk[k * NORM_COLS + c] * sc * w[k];
+        if (WS) {
+#pragma unroll 4
+            for (int k = tid / NORM_COLS; k < K; k += 256 / NORM_COLS)
+                out[(size_t)k * ldo + m0 + c] = blk[k * NORM_COLS + c] * sc * ws[k];
+        } else {
+            for (int k = tid / NORM_COLS; k < K; k += 256 / NORM_COLS)
+                out[(size_t)k * ldo + m0 + c] = blk[k * NORM_COLS + c] * sc * w[k];
+        }
     }
 }
 
@@ -238,11 +252,14 @@ __global__ void pointwise_kernel(int op, const float* __restrict__ x, float* __r
 cudaError_t rmsnorm_fm(const float* x, int ldx, const float* w, float eps, int K, int M, float* out, int ldo,
                        cudaStream_t s) {
     if (K <= 0 || M <= 0 || K > NORM_MAXK || ldx < M || ldo < M) return cudaErrorInvalidValue;
-    static DeviceOnce once;
-    size_t smem = (size_t)K * NORM_COLS * sizeof(float);
-    cudaError_t e = once.set_smem((const void*)rmsnorm_fm_kernel, (size_t)NORM_MAXK * NORM_COLS * sizeof(float));
+    const bool ws = M <= NORM_WS_MAX_COLS;
+    static DeviceOnce once[2];
+    const size_t smem = (size_t)K * (NORM_COLS + (ws ? 1 : 0)) * sizeof(float);
+    const void* fn = ws ? (const void*)rmsnorm_fm_kernel<true> : (const void*)rmsnorm_fm_kernel<false>;
+    cudaError_t e = once[ws ? 1 : 0].set_smem(fn, (size_t)NORM_MAXK * (NORM_COLS + 1) * sizeof(float));
     if (e != cudaSuccess) return e;
-    rmsnorm_fm_kernel<<<(M + NORM_COLS - 1) / NORM_COLS, 256, smem, s>>>(x, ldx, w, eps, K, M, out, ldo);
+    if (ws) rmsnorm_fm_kernel<true><<<(M + NORM_COLS - 1) / NORM_COLS, 256, smem, s>>>(x, ldx, w, eps, K, M, out, ldo);
+    else rmsnorm_fm_kernel<false><<<(M + NORM_COLS - 1) / NORM_COLS, 256, smem, s>>>(x, ldx, w, eps, K, M, out, ldo);
     add_launches(1);
     return cudaGetLastError();
 }
