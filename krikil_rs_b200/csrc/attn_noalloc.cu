@@ -16,6 +16,14 @@
 // Nothing in it has to start at zero: every partial that the combine step reads
 // is written earlier in the same call, and the array keeps whatever the last
 // call left in it.
+//
+// The call runs on the device that owns `stream` (the current device for the
+// default stream) and leaves the caller's current device as it was.  The
+// array's device address is looked up on the first call on each device (that
+// first call should come before any stream capture) and kept for later calls
+// in the same CUDA context of that device; after a device reset the next call
+// looks it up again in the new context.
+#include <cuda.h>  // driver types only (CUcontext, CUresult); the entry points come from the runtime
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -34,28 +42,77 @@ static __device__ __align__(256) float g_attn_scratch[KRK_ATTN_NOALLOC_MAX_FLOAT
 
 constexpr int kMaxDevices = 64;
 std::mutex g_mu;
-float* g_scratch_ptr[kMaxDevices] = {};
+struct Cached {
+    unsigned long long ctx_id = 0;  // 0: not looked up yet
+    float* ptr = nullptr;
+};
+Cached g_scratch[kMaxDevices];
 
-// Device address of g_attn_scratch on the current device.  The array's name in
-// host code is only a host-side handle, so the address is looked up once per
-// device with that device current, and cached.
-int scratch_for_current_device(float** out) {
-    int dev = -1;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return krk::report_error(KRK_CUDA, std::string("cudaGetDevice: ") + cudaGetErrorString(e));
+// Unique id of the calling thread's current CUDA context (the device's primary
+// context once the runtime has used it); 0 if it cannot be read.  Context ids
+// are never reused within a process, so a reset device shows a new id.
+unsigned long long current_context_id() {
+    using GetCurrent = CUresult (*)(CUcontext*);
+    using GetId = CUresult (*)(CUcontext, unsigned long long*);
+    static GetCurrent get_current = nullptr;
+    static GetId get_id = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &f, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_current = reinterpret_cast<GetCurrent>(f);
+        f = nullptr;
+        if (cudaGetDriverEntryPointByVersion("cuCtxGetId", &f, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_id = reinterpret_cast<GetId>(f);
+    });
+    CUcontext ctx = nullptr;
+    unsigned long long id = 0;
+    if (!get_current || !get_id || get_current(&ctx) != CUDA_SUCCESS || !ctx || get_id(ctx, &id) != CUDA_SUCCESS)
+        return 0;
+    return id;
+}
+
+// Device address of g_attn_scratch on the current device `dev`.  The array's
+// name in host code is only a host-side handle, so the address is looked up
+// with that device current, and cached per device and context.
+int scratch_for_device(int dev, float** out) {
     if (dev < 0 || dev >= kMaxDevices) return krk::report_error(KRK_INVALID, "device ordinal out of range");
+    // binds the device's primary context to this thread (initialising it if
+    // needed), so that its id can be read; allocates nothing
+    cudaError_t e = cudaSetDevice(dev);
+    if (e != cudaSuccess) return krk::report_error(KRK_CUDA, std::string("cudaSetDevice: ") + cudaGetErrorString(e));
+    const unsigned long long id = current_context_id();
     std::lock_guard<std::mutex> lock(g_mu);
-    if (!g_scratch_ptr[dev]) {
+    Cached& c = g_scratch[dev];
+    if (id == 0 || c.ctx_id != id || !c.ptr) {
         void* p = nullptr;
         e = cudaGetSymbolAddress(&p, g_attn_scratch);
         if (e != cudaSuccess || !p)
             return krk::report_error(KRK_CUDA,
                                      std::string("cudaGetSymbolAddress(attention scratch): ") + cudaGetErrorString(e));
-        g_scratch_ptr[dev] = static_cast<float*>(p);
+        c.ptr = static_cast<float*>(p);
+        c.ctx_id = id;  // id 0 (unreadable): looked up again on every call
     }
-    *out = g_scratch_ptr[dev];
+    *out = c.ptr;
     return KRK_OK;
 }
+
+// Makes `dev` current for the scope and restores the caller's device after.
+struct OnDevice {
+    int prev = -1;
+    cudaError_t err = cudaSuccess;
+    explicit OnDevice(int dev) {
+        err = cudaGetDevice(&prev);
+        if (err == cudaSuccess && prev != dev) err = cudaSetDevice(dev);
+    }
+    ~OnDevice() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
 
 }  // namespace
 
@@ -73,8 +130,15 @@ extern "C" int krk_k_rope_kv_attn_decode_noalloc(const float* q, const float* k,
                              std::to_string((size_t)KRK_ATTN_NOALLOC_MAX_FLOATS) +
                              "; use a larger split, fewer sequences per call, or krk_k_rope_kv_attn_decode with a "
                              "caller-provided buffer");
+    int dev = -1;
+    cudaError_t se = cudaStreamGetDevice((cudaStream_t)stream, &dev);
+    if (se != cudaSuccess)
+        return krk::report_error(KRK_INVALID, std::string("stream's device: ") + cudaGetErrorString(se));
+    OnDevice on(dev);
+    if (on.err != cudaSuccess)
+        return krk::report_error(KRK_CUDA, std::string("cudaSetDevice: ") + cudaGetErrorString(on.err));
     float* scratch = nullptr;
-    int rc = scratch_for_current_device(&scratch);
+    int rc = scratch_for_device(dev, &scratch);
     if (rc != KRK_OK) return rc;
     krk::AttnDecodeArgs a{};
     a.q = q; a.k = k; a.v = v; a.in_sb = (int64_t)H * dh; a.in_sh = dh;

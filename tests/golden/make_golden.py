@@ -28,4 +28,6 @@ def main(ref_dir: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit(f"usage: python {os.path.basename(__file__)} <krikil-rs checkout>")
+    main(sys.argv[1])

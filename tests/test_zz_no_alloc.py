@@ -52,8 +52,12 @@ def _no_alloc(q, k, v, kc, vc, pos, b, h, dh, ctx, split, stream):
     return out
 
 
-def test_no_alloc_matches_buffered_entry_point_twice():
-    b, h, dh, ctx, split = 64, 8, 64, 2048, 256  # the [64,8,2048,64] decode benchmark shape
+@pytest.mark.parametrize("b,h,dh,ctx,split", [
+    (64, 8, 64, 2048, 256),  # the [64,8,2048,64] decode benchmark shape: generic split kernel, narrow merge
+    (16, 8, 64, 2048, 64),   # warp-per-16-keys split kernel and the wide merge (32 splits per sequence)
+], ids=["split256", "split64-wide-merge"])
+def test_no_alloc_matches_buffered_entry_point_twice(b, h, dh, ctx, split):
+    assert lib.krk_attn_work_floats(b, h, dh, ctx, split) <= (1 << 20)
     q, k, v, pos, kc, vc = synth.attn_decode_inputs(b, h, dh, ctx, seed=0)
     stream = torch.cuda.current_stream().cuda_stream
     kc_a, vc_a, kc_b, vc_b = _t(kc), _t(vc), _t(kc), _t(vc)
@@ -69,6 +73,23 @@ def test_no_alloc_matches_buffered_entry_point_twice():
         np.testing.assert_allclose(got.cpu().numpy(), ref.cpu().numpy(), atol=ATOL, rtol=RTOL,
                                    err_msg=f"call {call}")
         assert torch.equal(kc_a, kc_b) and torch.equal(vc_a, vc_b)
+
+
+def test_no_alloc_runs_on_the_streams_device_and_keeps_the_callers_device():
+    """A stream of device 0 passed while device 0 is current: the call succeeds
+    and the current device is unchanged afterwards (with one GPU the stream's
+    device is always the current one; the lookup path is the same)."""
+    b, h, dh, ctx, split = 4, 8, 64, 512, 64
+    q, k, v, pos, kc, vc = synth.attn_decode_inputs(b, h, dh, ctx, seed=3)
+    s = torch.cuda.Stream(device=DEV)
+    gq, gk, gv, gp, gkc, gvc = (_t(a) for a in (q, k, v, pos, kc, vc))
+    before = torch.cuda.current_device()
+    got = _no_alloc(gq, gk, gv, gkc, gvc, gp, b, h, dh, ctx, split, s.cuda_stream)
+    s.synchronize()
+    assert torch.cuda.current_device() == before
+    ref = _with_buffer(gq, gk, gv, _t(kc), _t(vc), gp, b, h, dh, ctx, split, s.cuda_stream)
+    s.synchronize()
+    np.testing.assert_allclose(got.cpu().numpy(), ref.cpu().numpy(), atol=ATOL, rtol=RTOL)
 
 
 def test_no_alloc_rejects_sizes_beyond_its_scratch():
