@@ -1,22 +1,30 @@
 #!/usr/bin/env python
 """Benchmark: batched greedy decode of the Pebble-25M architecture on B200.
 
-Workload (one "step"): krk_generate_greedy over `--seqs` independent sequences
-per GPU -- prompts of 128 token ids ~U[0,2048) (numpy seed 1), 256 new tokens
-each with EOS ignored, context 2048 -- on random-init seed-0 weights (the real
-checkpoint is not distributed).  Throughput = generated tokens / time, summed
-over all ranks.  With N GPUs each rank runs its own disjoint slice of
-N*seqs sequences (no collectives on the data path; weak scaling).
+Workload (one "step"): krk_generate_greedy over the rank's sequences --
+prompts of 128 token ids ~U[0,2048) (numpy seed 1), 256 new tokens each with
+EOS ignored, context 2048 -- on random-init seed-0 weights (the real
+checkpoint is not distributed).  By default 1024 sequences in total are split
+evenly over the N GPUs (strong scaling: 128 per GPU at N=8); `--seqs S` runs S
+sequences per GPU instead (weak scaling).  No collectives on the data path;
+throughput = generated tokens of all ranks / max over ranks of the time.
 
-  value  device time of the generate calls (inputs already on the device)
-  e2e    the same calls timed end to end on the device clock, including the
+  value  device time of the generate calls from the state reset to the last
+         pick (the prompts and the call's tables are already on the device);
+         the timed loop runs with whole-call events only (no per-kernel events)
+  e2e    the same calls timed end to end on the model stream, including the
          pinned-host -> device prompt copy and the device -> host token read
+  roofline  the decode SSD update's per-launch rate in a separate profiled
+         call after the timed region (same configuration, per-kernel events)
+  c1     batch 1, a 32-token prompt, 64 greedy tokens through the same call
+         (the reference's own use case), with the oracle's batch-1 rate
   kernels  per-kernel HBM throughput of the fused layer kernels at their
          benchmark shapes (gated norm [16384,512], RoPE+KV+attention
          [64,8,2048,64], conv+SSD step [256,16,64,128], conv+SSD scan T=2048)
 
 `--impl reference` times the CPU restatement of the reference path (the Rust
-crate cannot be built on these machines) on the host cores.
+crate cannot be built on these machines) on the host cores; it loads only the
+oracle's library and numpy, never the CUDA library.
 """
 from __future__ import annotations
 
@@ -49,7 +57,9 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--seqs", type=int, default=1024, help="sequences per GPU")
+    ap.add_argument("--total-seqs", type=int, default=1024,
+                    help="sequences split evenly over the GPUs (strong scaling, the default)")
+    ap.add_argument("--seqs", type=int, default=0, help="sequences per GPU instead (weak scaling)")
     ap.add_argument("--prompt-len", type=int, default=128)
     ap.add_argument("--new-tokens", type=int, default=256)
     ap.add_argument("--ctx", type=int, default=2048)
@@ -59,7 +69,19 @@ def parse_args():
     ap.add_argument("--kernels-only", action="store_true", help="only the per-kernel table")
     ap.add_argument("--scan-t", type=int, default=2048, help="tokens of the conv+SSD scan case")
     ap.add_argument("--decode-streams", type=int, default=3, help="parts of the decode batch on their own streams")
-    return ap.parse_args()
+    ap.add_argument("--no-c1", action="store_true", help="skip the batch-1 (C1) line")
+    ap.add_argument("--no-step-graphs", action="store_true",
+                    help="launch each decode step kernel by kernel instead of replaying its CUDA graph")
+    args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if args.seqs > 0:
+        args.scaling, args.seqs_per_gpu = "weak", args.seqs
+    else:
+        if args.total_seqs % world:
+            ap.error(f"--total-seqs {args.total_seqs} does not split evenly over {world} GPUs")
+        args.scaling, args.seqs_per_gpu = "strong", args.total_seqs // world
+    args.world = world
+    return args
 
 
 # ----------------------------------------------------------------- peaks / clocks
@@ -160,26 +182,37 @@ def single_stream_summary(prof, seqs, plen, steps, tokens, peak, fp32_nominal):
 
 
 # ----------------------------------------------------------------- CPU baseline
-def cpu_baseline(args, budget_s: float):
-    """The oracle (CPU restatement of the reference path) on this host's cores:
-    whole sequences (prompt + new tokens, batch 1 as the reference runs) until
-    the time budget is used."""
+def _oracle_model():
+    """The oracle (CPU restatement of the reference path) on the seed-0 weights.
+    Imports only oracle/ and the numpy helpers of krikil_rs_b200.synth; the
+    package's CUDA library is loaded lazily and is never touched here."""
     import oracle as O
     from krikil_rs_b200 import synth
     threads = os.cpu_count() or 1
     O.lib.orc_set_num_threads(threads)
-    model = O.OracleModel(synth.make_weights(0))
-    prompts = synth.decode_prompts(max(args.seqs, 64), args.prompt_len, seed=1)
-    new = args.new_tokens
+    return O, O.OracleModel(synth.make_weights(0)), threads
+
+
+def cpu_baseline(args, budget_s: float, prompt_len=None, new_tokens=None, seed=1, start=0, _cache={}):
+    """The oracle on this host's cores: whole sequences (prompt + new tokens,
+    batch 1 as the reference runs), sequences start, start+1, ... of the
+    workload's prompts, until the time budget is used (at least one)."""
+    from krikil_rs_b200 import synth
+    if "m" not in _cache:
+        _cache["m"] = _oracle_model()
+    O, model, threads = _cache["m"]
+    plen = prompt_len or args.prompt_len
+    new = new_tokens or args.new_tokens
+    prompts = synth.decode_prompts(max(args.seqs_per_gpu, 64) + start, plen, seed=seed)
     t0 = time.perf_counter()
     toks, nseq = 0, 0
-    while nseq == 0 or (time.perf_counter() - t0 < budget_s and nseq < len(prompts)):
-        out, _ = O.generate_greedy(model, O.OracleState(args.ctx), prompts[nseq].tolist(), new, eos=None)
+    while nseq == 0 or (time.perf_counter() - t0 < budget_s and start + nseq < len(prompts)):
+        out, _ = O.generate_greedy(model, O.OracleState(args.ctx), prompts[start + nseq].tolist(), new, eos=None)
         toks += len(out)
         nseq += 1
     dt = time.perf_counter() - t0
-    return {"value": toks / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
-            "sample": f"{nseq} sequence(s) x ({args.prompt_len}-token prompt + {new} greedy tokens), batch 1, "
+    return {"value": toks / dt, "unit": "tokens/s", "cores": threads, "kind": "port", "tokens": toks, "s": dt,
+            "sample": f"{nseq} sequence(s) x ({plen}-token prompt + {new} greedy tokens), batch 1, "
                       f"oracle C restatement (-O3 AVX2/FMA, OpenMP {threads} threads), {dt:.1f} s"}
 
 
@@ -188,30 +221,39 @@ def run_reference(args):
     if rank != 0:
         return
     os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count() or 1))
-    budget = max(3.0, min(20.0, args.cpu_seconds))
-    for _ in range(args.warmup):
-        cpu_baseline(args, 0.0)
-    vals = [cpu_baseline(args, budget) for _ in range(args.steps)]
-    v = statistics.median(x["value"] for x in vals)
-    cb = dict(vals[0])
+    # each step is a bounded sample of the workload (whole sequences), sized so
+    # the whole run stays within a few minutes
+    budget = max(2.0, min(args.cpu_seconds, 120.0 / max(args.steps, 1)))
+    for i in range(args.warmup):
+        cpu_baseline(args, 0.0, start=i)
+    vals = [cpu_baseline(args, budget, start=args.warmup + 8 * i) for i in range(args.steps)]
+    toks = sum(x["tokens"] for x in vals)
+    secs = sum(x["s"] for x in vals)
+    v = toks / secs
+    cb = {k: vals[0][k] for k in ("unit", "cores", "kind")}
     cb["value"] = v
-    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+    cb["sample"] = (f"{args.steps} step(s), each whole sequences at batch 1 for about {budget:.0f} s "
+                    f"({toks} generated tokens in {secs:.1f} s); " + vals[0]["sample"].split(", ", 1)[1])
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": secs * 1e3 / args.steps,
+            "higher_is_better": True, "scaling": args.scaling,
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded prompts, random-init weights)",
             "config": workload_config(args),
             "cpu_baseline": cb,
             "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "note": "the reference Rust crate cannot be built here (no cargo); its path is timed through the "
-                    "oracle's C restatement on the host cores"}
+                    "oracle's C restatement on the host cores (rank 0 only)"}
     print(json.dumps(line), flush=True)
 
 
 def workload_config(args):
     return {"workload": "batched greedy decode of Pebble-25M (config.json dims), random-init seed 0",
-            "seqs_per_gpu": args.seqs, "prompt_len": args.prompt_len, "new_tokens": args.new_tokens,
+            "seqs_total": args.seqs_per_gpu * args.world, "seqs_per_gpu": args.seqs_per_gpu,
+            "prompt_len": args.prompt_len, "new_tokens": args.new_tokens,
             "ctx": args.ctx, "eos": "ignored", "prompts": "U[0,2048) numpy seed 1",
-            "l2": "inputs larger than L2 (SSD state 3.8 GB + KV cache per GPU)",
-            "decode_parts": getattr(args, "decode_streams", 3)}
+            "l2": "inputs larger than L2 (SSD state + KV cache per GPU: 3.8 GB at 1024 sequences)",
+            "decode_parts": args.decode_streams, "step_graphs": not args.no_step_graphs,
+            "parallelism": f"replicas x{args.world} (no collectives)"}
 
 
 # ----------------------------------------------------------------- per-kernel table
@@ -272,7 +314,7 @@ def kernel_table(torch, peak, scan_t=2048):
     out = torch.empty_like(q)
     nb = int(sum((int(p) + 1) * 8 * 64 * 4 * 2 for p in pos) + 64 * 8 * 64 * 4 * 6)
     ms = {sp: timeit(lambda: K.rope_kv_attn_decode(q, k, v, kc, vc, posd, split=sp, work=work, out=out))
-          for sp in (64, 128, 256)}
+          for sp in (0, 64, 128, 256)}  # 0: the cluster kernel (one launch, no scratch)
     best = min(ms, key=ms.get)
     put("rope_kv_attn_decode[64,8,2048,64]", nb, ms[best],
         {"split": best, "ms_by_split": {str(k): round(v, 4) for k, v in ms.items()}})
@@ -305,12 +347,55 @@ def kernel_table(torch, peak, scan_t=2048):
 
 
 # ----------------------------------------------------------------- our arm
+def c1_line(args, model, peak):
+    """BASELINE config 1 on the device: batch 1, a 32-token prompt (ids
+    ~U[0,2048), seed 0), 64 greedy tokens, context 2048, through the same
+    generate call; the oracle's batch-1 rate on this host beside it."""
+    import torch
+    from krikil_rs_b200 import PebbleState
+    from krikil_rs_b200._lib import check, lib
+    plen, new, reps = 32, 64, 20
+    prompt = np.random.default_rng(0).integers(0, VOC, plen).astype(np.uint32)
+    st = PebbleState(model, args.ctx, batch=1)
+    toks_h = torch.from_numpy(prompt.view(np.int32).copy()).pin_memory()
+    lens_h = torch.full((1,), plen, dtype=torch.int32).pin_memory()
+    out_h = torch.zeros((1, new), dtype=torch.int32).pin_memory()
+    n_h = torch.zeros((1,), dtype=torch.int32).pin_memory()
+
+    def gen():
+        check(lib.krk_generate_greedy(model._h, st._h, toks_h.data_ptr(), lens_h.data_ptr(), new, 1.0, 0,
+                                      out_h.data_ptr(), n_h.data_ptr()))
+    for _ in range(3):
+        gen()
+    stream = torch.cuda.ExternalStream(model.stream)
+    st.profile(True, per_kernel=False)
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    ntok = 0
+    for _ in range(reps):
+        gen()
+        ntok += int(n_h.sum())
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = ev0.elapsed_time(ev1)
+    dev_ms = st.profile_read()["device_total"][0]
+    st.profile(False)
+    st.close()
+    line = {"workload": "C1: batch 1, 32-token prompt, 64 greedy tokens, ctx 2048 (prefill inside the call)",
+            "calls": reps, "tokens_per_s": ntok / (dev_ms * 1e-3), "e2e_tokens_per_s": ntok / (e2e_ms * 1e-3),
+            "ms_per_call": e2e_ms / reps}
+    if not args.no_cpu_baseline:
+        cb = cpu_baseline(args, 5.0, prompt_len=plen, new_tokens=new, seed=0)
+        line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
+    return line
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
+    world, rank = args.world, int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
@@ -322,10 +407,11 @@ def run_ours(args):
     peak, peak_kind = measured_peaks()
     path = synth.weights_file(0)
     model = PebbleModel.load_safetensors(path, device=local)
-    seqs, plen, new = args.seqs, args.prompt_len, args.new_tokens
+    seqs, plen, new = args.seqs_per_gpu, args.prompt_len, args.new_tokens
     prompts = replicas.shard(synth.decode_prompts(world * seqs, plen, seed=1), world, rank)
     state = PebbleState(model, args.ctx, batch=seqs)
     state.set_decode_streams(args.decode_streams)
+    state.set_step_graphs(not args.no_step_graphs)
 
     # pinned host buffers for the end-to-end calls
     toks_h = torch.from_numpy(np.ascontiguousarray(prompts.reshape(-1).view(np.int32))).pin_memory()
@@ -340,7 +426,8 @@ def run_ours(args):
     for _ in range(args.warmup):
         generate()
     stream = torch.cuda.ExternalStream(model.stream)
-    state.profile(True)
+    # the timed loop: whole-call device brackets only (no per-kernel events)
+    state.profile(True, per_kernel=False)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -358,17 +445,8 @@ def run_ours(args):
     launches = launch_count() - l0
     clk = clocks.stop()
     e2e_ms = ev0.elapsed_time(ev1)
-    prof = state.profile_read()
+    dev_ms = state.profile_read()["device_total"][0]
     state.profile(False)
-    # One more call on a single stream (outside the timed region): the same
-    # kernels without the batch's other parts beside them, for per-kernel rates.
-    state.set_decode_streams(1)
-    state.profile(True)
-    generate()
-    prof1 = state.profile_read()
-    state.profile(False)
-    state.set_decode_streams(args.decode_streams)
-    dev_ms = prof["device_total"][0]
     (e2e_ms, dev_ms), total_tokens = replicas.reduce_timings(dist, "cuda", [e2e_ms, dev_ms], gen_tokens)
     if world > 1:
         dist.barrier()
@@ -380,6 +458,20 @@ def run_ours(args):
             dist.destroy_process_group()
         return
 
+    # After the timed region: one call with per-kernel events in the same
+    # configuration (the kernels' rates beside the other decode parts), and one
+    # with the decode on a single stream (each kernel without the others).
+    state.profile(True)
+    generate()
+    prof = state.profile_read()
+    state.profile(False)
+    state.set_decode_streams(1)
+    state.profile(True)
+    generate()
+    prof1 = state.profile_read()
+    state.profile(False)
+    state.set_decode_streams(args.decode_streams)
+
     steps_per_gen = min(new, args.ctx - plen)
     # Per-class times are kernel times on their own stream; a decode batch of
     # 256+ sequences runs as concurrent parts, so these are per-launch rates
@@ -389,13 +481,17 @@ def run_ours(args):
     ssd_bytes = ssd_step_bytes_per_launch(1) * ssd_seqs
     ssd_gbs = ssd_bytes / (ssd_ms * 1e-3) / 1e9
     gemm_ms, gemm_n, _ = prof["gemm"]
-    gemm_flops = gemm_flops_per_generate(seqs, plen, steps_per_gen) * args.steps
+    gemm_flops = gemm_flops_per_generate(seqs, plen, steps_per_gen)
     attn_ms, attn_n, _ = prof["attn_decode"]
-    attn_bytes = attn_decode_bytes(seqs, plen, steps_per_gen) * args.steps
+    attn_bytes = attn_decode_bytes(seqs, plen, steps_per_gen)
     kernel_ms = sum(v[0] for k, v in prof.items() if k != "device_total")
     share = {k: round(v[0] / kernel_ms, 4) for k, v in prof.items() if k != "device_total"}
     fp32_tflops_nominal = 148 * 128 * 2 * 1.965e9 / 1e12  # 148 SMs x 128 FP32 lanes x FMA x 1965 MHz
     gemm_tflops = gemm_flops / (gemm_ms * 1e-3) / 1e12 if gemm_ms else 0.0
+    # whole-call HBM floor: SSD state read + write per sequence, layer and step
+    # (prefill scan and decode) and the decode attention's K/V reads
+    call_bytes = ssd_step_bytes_per_launch(seqs) * MAMBA_LAYERS * steps_per_gen + attn_bytes
+    call_ms = dev_ms / args.steps
 
     line = {
         "metric": METRIC,
@@ -404,13 +500,13 @@ def run_ours(args):
         "n_gpus": world,
         "steps": args.steps,
         "warmup": args.warmup,
-        "ms_per_step": dev_ms / args.steps,
+        "ms_per_step": call_ms,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": args.scaling,
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic (seeded prompts, random-init weights)",
-        "config": dict(workload_config(args), parallelism=f"replicas x{world} (no collectives)"),
+        "config": workload_config(args),
         "e2e": {"value": total_tokens / (e2e_ms * 1e-3), "unit": "tokens/s",
                 "h2d_bytes_per_step": int(toks_h.numel() * 4 + lens_h.numel() * 4),
                 "d2h_bytes_per_step": int(out_h.numel() * 4 + n_h.numel() * 4 + seqs * 4 + 4),
@@ -422,10 +518,17 @@ def run_ours(args):
                      "traffic": int(SSD_TRAFFIC_PER_SEQ * ssd_seqs / max(ssd_n, 1)),
                      "traffic_source": "ncu dram__bytes_read+write, 256-sequence launches, scaled",
                      "peak_kind": peak_kind,
-                     "note": "live per-launch rate while the other decode parts' kernels share the GPU; "
+                     "measured": "CUDA events around each launch on its stream, in one profiled call after the "
+                                 "timed region with the timed configuration",
+                     "note": "per-launch rate while the other decode parts' kernels share the GPU; "
                              "see single_stream for the same kernel without them",
                      "algorithmic_bytes_per_launch": int(ssd_bytes / max(ssd_n, 1)),
                      "launches": ssd_n, "avg_launch_us": round(ssd_ms * 1e3 / max(ssd_n, 1), 2)},
+        "roofline_call": {"what": "whole generate call against its HBM floor (SSD state r+w of every decode "
+                                  "step, decode K/V reads)",
+                          "bytes": int(call_bytes), "ms": round(call_ms, 2),
+                          "achieved": round(call_bytes / (call_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                          "frac": round(call_bytes / (call_ms * 1e-3) / 1e9 / peak, 3)},
         "roofline_gemm": {"kernel": "gemm_lane8 (fp32 SIMT projections)", "bound": "fp32",
                           "achieved": round(gemm_tflops, 2), "unit": "TFLOP/s",
                           "peak_nominal": round(fp32_tflops_nominal, 1),
@@ -434,18 +537,24 @@ def run_ours(args):
         "roofline_attn": {"kernel": "attn_decode", "bound": "hbm",
                           "achieved": round(attn_bytes / (attn_ms * 1e-3) / 1e9, 1) if attn_ms else None,
                           "unit": "GB/s", "launches": attn_n},
-        "single_stream": single_stream_summary(prof1, seqs, plen, steps_per_gen, seqs * min(new, args.ctx - plen + 1), peak,
-                                               fp32_tflops_nominal),
+        "single_stream": single_stream_summary(prof1, seqs, plen, steps_per_gen,
+                                               seqs * min(new, args.ctx - plen + 1), peak, fp32_tflops_nominal),
         "time_share": share,
-        "kernel_ms_over_device_ms": round(kernel_ms / dev_ms, 3),
+        "kernel_ms_over_device_ms": round(kernel_ms / prof["device_total"][0], 3),
         "gpu_launches": launches,
         "clocks": clk,
     }
-    if not args.no_kernels:
-        line["kernels"] = kernel_table(torch, peak, args.scan_t)
-    if not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(args, args.cpu_seconds)
+    if world == 1:
+        if not args.no_c1:
+            line["c1"] = c1_line(args, model, peak)
+        if not args.no_kernels:
+            line["kernels"] = kernel_table(torch, peak, args.scan_t)
+        if not args.no_cpu_baseline:
+            line["cpu_baseline"] = {k: v for k, v in cpu_baseline(args, args.cpu_seconds).items()
+                                    if k not in ("tokens", "s")}
     print(json.dumps(line), flush=True)
+    state.close()
+    model.close()
     if world > 1:
         dist.destroy_process_group()
 

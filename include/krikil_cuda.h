@@ -137,11 +137,10 @@ KRK_API int krk_step(const krk_model* model, krk_state* state, const uint32_t* t
  * if stop_at_eos -- when it picks KRK_EOS_TOKEN (not emitted).  With
  * stop_at_eos = 0 every sequence emits min(max_new_tokens, max_ctx - len + 1)
  * tokens.  tokens_out (host, [batch][max_new_tokens]) and n_out (host,
- * [batch]) receive the generated ids and their counts.  For states of at most
- * 64 sequences each decode step replays a CUDA graph held by the state (one
- * per count of 64-key attention blocks, captured on the model stream the first
- * time the count comes up) unless per-kernel profiling is on; krk_generate_sample
- * does the same. */
+ * [batch]) receive the generated ids and their counts.  Each decode step
+ * replays a CUDA graph held by the state (see krk_state_set_step_graphs)
+ * unless per-kernel profiling is on; krk_generate_sample does the same.  The
+ * call synchronises with the device once, at its end. */
 KRK_API int krk_generate_greedy(const krk_model* model, krk_state* state, const uint32_t* prompts,
                                 const int32_t* lens, int max_new_tokens, float repetition_penalty, int stop_at_eos,
                                 uint32_t* tokens_out, int32_t* n_out);
@@ -196,6 +195,16 @@ enum {
  * of whole sequences at once on the same streams.  n = 1 runs decode and
  * prefill on the model stream alone.  Results are identical for every n. */
 KRK_API int krk_state_set_decode_streams(krk_state* state, int n);
+
+/* Decode scheduling (no reference counterpart): with enable != 0 (the
+ * default) the generation loops replay each decode step as a CUDA graph held
+ * by the state -- one per count of 64-key attention blocks, captured on the
+ * model's streams the first time the count comes up -- instead of launching
+ * its kernels one by one; 0 launches them one by one and drops the graphs.
+ * Results are identical either way.  Per-kernel profiling also launches them
+ * one by one.  Generation calls of states that share a model must not run
+ * concurrently (the capture runs on the model's streams). */
+KRK_API int krk_state_set_step_graphs(krk_state* state, int enable);
 
 /* enable: 0 off, 1 every kernel class and the whole-call total, 2 the
  * whole-call total only (two events per call: no per-kernel event records and
@@ -279,9 +288,15 @@ KRK_API int krk_k_conv_ssd_scan(const float* x, const float* bm, const float* cm
 /* Decode RoPE (src/math.rs:234-260) + KV-cache append (src/model.rs:730-733)
  * + single-query softmax attention (src/model.rs:736-760) on a [B][H][ctx][dh]
  * cache: q,k,v [B][H][dh] (dh = 64 or 76), pos [B] (int32, < ctx), kc/vc
- * updated at slot pos[b], out [B][H][dh].  Keys are processed in splits of
- * `split` (multiple of 64; 0 picks 256); when a sequence needs more than one
- * split, `work` must hold krk_attn_work_floats() floats of device scratch. */
+ * updated at slot pos[b], out [B][H][dh].
+ *   split = 0: eight CTAs per (sequence, head) form a thread-block cluster and
+ *     share the keys 0..pos evenly; CTA 0 merges their softmax partials through
+ *     distributed shared memory.  One launch, no scratch: `work` may be NULL and
+ *     krk_attn_work_floats() is 0.
+ *   split > 0 (multiple of 64): keys in splits of `split` keys, one CTA each,
+ *     and a second launch merging the splits; when a sequence needs more than
+ *     one split, `work` must hold krk_attn_work_floats() floats of device
+ *     scratch. */
 KRK_API size_t krk_attn_work_floats(int B, int H, int dh, int ctx, int split);
 KRK_API int krk_k_rope_kv_attn_decode(const float* q, const float* k, const float* v, float* kc, float* vc,
                                       const int32_t* pos, float* out, float* work, int B, int H, int dh, int ctx,
@@ -294,14 +309,18 @@ KRK_API int krk_k_rope_kv_attn_decode(const float* q, const float* k, const floa
  * allocator or a fixed budget: the split partials go to a fixed array inside
  * the library's device image, KRK_ATTN_NOALLOC_MAX_FLOATS floats (4 MiB) held by
  * every GPU that loads the library until the process exits.  Same arguments and
- * results as krk_k_rope_kv_attn_decode without `work`; when the cache needs
- * more than one split and krk_attn_work_floats() exceeds the maximum, the call
+ * results as krk_k_rope_kv_attn_decode without `work`, with `split` > 0 (0 picks
+ * 256 here); when the cache needs more than one split and
+ * krk_attn_work_floats() for that split exceeds the maximum, the call
  * fails with KRK_INVALID before launching anything.  It calls no allocator.  The
- * first call on a device looks up the array's device address (once per device,
- * with that device current), so make it before any stream capture.  All calls on
- * a GPU share the array: calls that overlap on the GPU race and must be
- * serialised by the caller.  No part of the array needs clearing between calls
- * (each call writes every partial it reads). */
+ * call runs on the device that owns `stream` (the current device for the
+ * default stream) and restores the caller's current device.  The first call on
+ * a device looks up the array's device address (once per device and CUDA
+ * context, with that device current; after a device reset the next call looks
+ * it up again), so make it before any stream capture.  All calls on a GPU share
+ * the array: calls that overlap on the GPU race and must be serialised by the
+ * caller.  No part of the array needs clearing between calls (each call writes
+ * every partial it reads). */
 #define KRK_ATTN_NOALLOC_MAX_FLOATS (1 << 20)
 KRK_API int krk_k_rope_kv_attn_decode_noalloc(const float* q, const float* k, const float* v, float* kc, float* vc,
                                               const int32_t* pos, float* out, int B, int H, int dh, int ctx,

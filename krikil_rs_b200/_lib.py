@@ -46,6 +46,7 @@ _SIGS = {
     "krk_state_profile_read": (_i32, [_vp, _i32, C.POINTER(C.c_double), C.POINTER(_i64)]),
     "krk_state_profile_units": (_i32, [_vp, _i32, C.POINTER(_i64)]),
     "krk_state_set_decode_streams": (_i32, [_vp, _i32]),
+    "krk_state_set_step_graphs": (_i32, [_vp, _i32]),
     "krk_generate_sample": (_i32, [_vp, _vp, _vp, _vp, _i32, _f32, _f32, _i32, _f32, _vp, _i32, _vp, _vp]),
     "krk_k_sample": (_i32, [_fp, _i64, _i32, _i32, _vp, _f32, _f32, _i32, _f32, _vp, _vp, _vp]),
     "krk_rng_seed_state": (_i32, [C.c_uint64, _vp]),

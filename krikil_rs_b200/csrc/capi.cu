@@ -110,6 +110,38 @@ struct Budget {
     void add(size_t count) { bytes = round_up((int64_t)bytes, 256) + count * sizeof(T); }
 };
 
+// Pinned host memory for a call's small host<->device traffic (prefill group
+// tables, generation limits, seeds, positions, the generated tokens): copies
+// from and to it are truly asynchronous, so a call issues all its work and
+// synchronises once at its end.  Every API call of a state ends with a
+// stream synchronisation, so the next call may reuse the buffer; ensure() is
+// only called at the start of a call, when no copy from it is pending.
+struct HostStage {
+    char* base = nullptr;
+    size_t cap = 0, used = 0;
+    void ensure(size_t bytes) {
+        used = 0;
+        if (bytes <= cap) return;
+        release();
+        ck(cudaHostAlloc((void**)&base, bytes, cudaHostAllocDefault), "cudaHostAlloc");
+        cap = bytes;
+    }
+    template <typename T>
+    T* take(size_t count) {
+        size_t off = round_up((int64_t)used, 256);
+        size_t bytes = count * sizeof(T);
+        if (off + bytes > cap) throw KrkError{KRK_CHECK_FAILED, "internal host staging overflow"};
+        used = off + bytes;
+        return reinterpret_cast<T*>(base + off);
+    }
+    void release() {
+        if (base) cudaFreeHost(base);
+        base = nullptr;
+        cap = used = 0;
+    }
+    ~HostStage() { release(); }
+};
+
 struct LayerW {
     // Mamba (src/model.rs:86-96)
     float *ln = nullptr, *in_t = nullptr, *conv_w = nullptr, *conv_b = nullptr, *dt_bias = nullptr,
@@ -179,9 +211,6 @@ struct PrefillWs {
     int cap_seqs = 0;
     Arena arena;
     float *x_t, *hn_t, *zx, *xbc, *y_t, *yn_t, *qkv, *ao_t, *mlp_t;
-    uint32_t* tok;
-    int32_t *row_seq, *cu, *start, *last, *dst;
-    int2* blk;  // prefill attention blocks: (sequence, first row)
 };
 
 }  // namespace
@@ -196,8 +225,6 @@ struct krk_state {
     uint8_t* active_d = nullptr;
     uint32_t* seen_d = nullptr;
     uint32_t* tok_d = nullptr;
-    int32_t* tlimit_d = nullptr;
-    int32_t* slimit_d = nullptr;
     int32_t* step_d = nullptr;
     int32_t* err_d = nullptr;  // set by a decode attention kernel whose K/V copy wait timed out
     uint32_t* rng_d = nullptr;  // [B][10] sampler random state (stochastic generation)
@@ -207,6 +234,10 @@ struct krk_state {
     int decode_streams = 3;  // decode batches of 256+ in up to this many parts on their own streams
     std::vector<int64_t> pos_h;
     PrefillWs pre[PREFILL_STREAMS];  // one workspace per prefill stream
+    HostStage stage;                 // pinned per-call host tables (see HostStage)
+    Arena meta_arena;                // their device copy: one H2D copy per call, same layout
+    Arena prompt_arena;              // the call's packed prompt tokens on the device
+    size_t prompt_cap = 0;
     Prof prof;
     Arena hist_arena;
     int64_t hist_cap = 0;
@@ -217,6 +248,7 @@ struct krk_state {
     // count of attention key blocks (index: blocks - 1); captured on first use.
     std::vector<cudaGraphExec_t> step_graphs;
     std::vector<uint64_t> step_graph_kernels;
+    bool step_graphs_on = true;
 };
 
 namespace {
@@ -363,7 +395,7 @@ void create_state(krk_state* s, const krk_model* m, int B, int ctx) {
         }
     }
     b.add<int32_t>(B); b.add<uint8_t>(B); b.add<uint32_t>((size_t)B * SEEN_WORDS); b.add<uint32_t>(Mp);
-    b.add<int32_t>(B); b.add<int32_t>(B); b.add<int32_t>(1); b.add<int32_t>(1); b.add<uint32_t>((size_t)B * 10);
+    b.add<int32_t>(1); b.add<int32_t>(1); b.add<uint32_t>((size_t)B * 10);
     b.add<float>(HID * Mp); b.add<float>(HID * Mp); b.add<float>(Mp * DIP_PAD); b.add<float>(DI * Mp);
     b.add<float>(DI * Mp); b.add<float>(Mp * QKV); b.add<float>(HID * Mp); b.add<float>(INTER * Mp);
     b.add<float>(Mp * VOC); b.add<float>(work); b.add<float2>((size_t)ctx * (HD / 2));
@@ -381,8 +413,6 @@ void create_state(krk_state* s, const krk_model* m, int B, int ctx) {
     s->active_d = s->arena.take<uint8_t>(B);
     s->seen_d = s->arena.take<uint32_t>((size_t)B * SEEN_WORDS);
     s->tok_d = s->arena.take<uint32_t>(Mp);
-    s->tlimit_d = s->arena.take<int32_t>(B);
-    s->slimit_d = s->arena.take<int32_t>(B);
     s->step_d = s->arena.take<int32_t>(1);
     s->err_d = s->arena.take<int32_t>(1);
     s->rng_d = s->arena.take<uint32_t>((size_t)B * 10);
@@ -431,9 +461,6 @@ void ensure_prefill_ws(krk_state* s, int k, int64_t tokens, int seqs) {
     b.add<float>(HID * T); b.add<float>(HID * T); b.add<float>(T * DIP_PAD); b.add<float>(T * DXBC);
     b.add<float>(DI * T); b.add<float>(DI * T); b.add<float>(T * QKV); b.add<float>(HID * T);
     b.add<float>(INTER * T);
-    b.add<uint32_t>(T); b.add<int32_t>(T); b.add<int32_t>(S + 1); b.add<int32_t>(S); b.add<int32_t>(S);
-    b.add<int32_t>(S);
-    b.add<int2>(T + S);
     sync_model_streams(s->m);  // the old workspace may still be in use on any stream
     w.arena.reserve(b.bytes);
     w.x_t = w.arena.take<float>(HID * T);
@@ -445,13 +472,6 @@ void ensure_prefill_ws(krk_state* s, int k, int64_t tokens, int seqs) {
     w.qkv = w.arena.take<float>(T * QKV);
     w.ao_t = w.arena.take<float>(HID * T);
     w.mlp_t = w.arena.take<float>(INTER * T);
-    w.tok = w.arena.take<uint32_t>(T);
-    w.row_seq = w.arena.take<int32_t>(T);
-    w.cu = w.arena.take<int32_t>(S + 1);
-    w.start = w.arena.take<int32_t>(S);
-    w.last = w.arena.take<int32_t>(S);
-    w.dst = w.arena.take<int32_t>(S);
-    w.blk = w.arena.take<int2>(T + S);
     ck(cudaMemsetAsync(w.arena.base, 0, w.arena.cap, s->m->stream), "prefill ws memset");
     w.cap_tokens = T;
     w.cap_seqs = S;
@@ -667,19 +687,18 @@ void decode_forward(krk_state* s, const uint8_t* active, int max_keys) {
     }
 }
 
-// A decode step of a batch of one 64-row tile is ~260 small launches whose
-// launch gaps, not their work, set the time per token; such steps replay a
-// CUDA graph of decode_forward instead, one graph per count of 64-key
-// attention blocks (the attention grid's depth), captured the first time that
-// count comes up.  The graph's attention reads up to blocks * 64 rows (fewer
-// than ctx): rows past a sequence's position are masked as always.  Not used
-// while per-kernel profiling records events around each launch, nor for split
-// batches.
-constexpr int GRAPH_MAX_MP = 64;
-
+// A decode step is ~90 launches per part (~260 for one 64-row tile with the
+// sampling, ~800 for three parts); for small batches their launch gaps, not
+// their work, set the time per token, and for large ones the host's launch
+// time approaches the device's.  The generation loop therefore replays a CUDA
+// graph of decode_forward -- the parts' streams, forks and joins included --
+// one graph per count of 64-key attention blocks (the attention grid's depth),
+// captured the first time that count comes up.  The graph's attention reads up
+// to blocks * 64 rows (fewer than ctx): rows past a sequence's position are
+// masked as always.  Not used while per-kernel profiling records events around
+// each launch, nor when the state's step graphs are switched off.
 void decode_step(krk_state* s, int max_keys) {
-    Part parts[4];
-    if ((s->prof.on && s->prof.per_kernel) || s->Mp > GRAPH_MAX_MP || decode_parts(s, parts) != 1) {
+    if ((s->prof.on && s->prof.per_kernel) || !s->step_graphs_on) {
         decode_forward(s, s->active_d, max_keys);
         return;
     }
@@ -717,9 +736,16 @@ void decode_step(krk_state* s, int max_keys) {
     kk(cudaGraphLaunch(ex, st), "graph launch");
 }
 
-// Prefill of sequences [g0, g0+S) whose packed tokens are already in pre.tok etc.
+// Device pointers to one prefill group's tables (in the call's metadata copy).
+struct GroupDev {
+    const uint32_t* tok;  // the group's packed prompt tokens
+    const int32_t *cu, *start, *last, *dst, *row_seq;
+    const int2* blk;
+};
+
+// Prefill of sequences [g0, g0+S) whose packed tokens and tables are on the device.
 void prefill_group(krk_state* s, int g0, int S, int64_t rows, int nblk, int blk_rows, int kmax, PrefillWs& w,
-                   cudaStream_t st) {
+                   const GroupDev& gd, cudaStream_t st) {
     const krk_model* m = s->m;
     auto timed = [&](krk_state* sp, int cls, auto&& f) { timed_on(sp, st, cls, 0, f); };
     const int T = (int)round_up(rows, 64);
@@ -729,7 +755,7 @@ void prefill_group(krk_state* s, int g0, int S, int64_t rows, int nblk, int blk_
     zero_pad_cols(w.y_t, T, R, DI, st);
     zero_pad_cols(w.yn_t, T, R, DI, st);
     zero_pad_cols(w.ao_t, T, R, HID, st);
-    timed(s, KRK_PROF_OTHER, [&] { kk(krk::embed_fm(w.tok, m->wte, VOC, HID, R, w.x_t, T, st), "embed"); });
+    timed(s, KRK_PROF_OTHER, [&] { kk(krk::embed_fm(gd.tok, m->wte, VOC, HID, R, w.x_t, T, st), "embed"); });
     for (int l = 0; l < NL; ++l) {
         const LayerW& L = m->L[l];
         if (is_mamba(l)) {  // src/model.rs:370-464
@@ -737,7 +763,7 @@ void prefill_group(krk_state* s, int g0, int S, int64_t rows, int nblk, int blk_
             timed(s, KRK_PROF_GEMM, [&] { kk(krk::gemm(w.hn_t, T, L.in_t, DIP_PAD, w.zx, DIP_PAD, T, DIP_PAD, HID, krk::EPI_STORE, false, st),
                "in_proj"); });
             timed(s, KRK_PROF_CONV, [&] { kk(krk::conv_prefill4(w.zx + OFF_X, DIP_PAD, w.xbc, DXBC, s->conv[l] + (size_t)g0 * DXBC * 4, L.conv_w,
-                                  L.conv_b, w.cu, S, DXBC, st),
+                                  L.conv_b, gd.cu, S, DXBC, st),
                "conv"); });
             krk::SsdScanArgs a{};
             a.x = w.xbc; a.x_rs = DXBC;
@@ -747,7 +773,7 @@ void prefill_group(krk_state* s, int g0, int S, int64_t rows, int nblk, int blk_
             a.ssm = s->ssm[l] + (size_t)g0 * MH * MP * DS;
             a.dt_bias = L.dt_bias; a.a_neg = L.a_neg; a.dsk = L.dsk;
             a.y = w.y_t; a.y_rs = 1; a.y_cs = T;
-            a.cu_seqlens = w.cu;
+            a.cu_seqlens = gd.cu;
             a.S = S; a.H = MH; a.P = MP; a.N = DS;
             timed(s, KRK_PROF_SSD_SCAN, [&] { kk(krk::ssd_scan(a, false, st), "ssd scan"); });
             timed(s, KRK_PROF_NORM, [&] { kk(krk::rmsnorm_fm(w.y_t, T, L.norm_w, MNORM_EPS, DI, R, w.yn_t, T, st), "gated norm"); });
@@ -758,9 +784,9 @@ void prefill_group(krk_state* s, int g0, int S, int64_t rows, int nblk, int blk_
             float* kc = s->kc[l] + (size_t)g0 * s->ctx * HID;
             float* vc = s->vc[l] + (size_t)g0 * s->ctx * HID;
             const int64_t c_sb = (int64_t)s->ctx * HID;
-            timed(s, KRK_PROF_OTHER, [&] { kk(krk::rope_kv_prefill(w.qkv, QKV, kc, vc, c_sb, HD, HID, w.cu, w.start, S, NH, HD, R, THETA, s->rope, st),
+            timed(s, KRK_PROF_OTHER, [&] { kk(krk::rope_kv_prefill(w.qkv, QKV, kc, vc, c_sb, HD, HID, gd.cu, gd.start, S, NH, HD, R, THETA, s->rope, st),
                "rope/kv"); });
-            timed(s, KRK_PROF_ATTN_PREFILL, [&] { kk(krk::attn_prefill(w.qkv, QKV, kc, vc, c_sb, HD, HID, w.cu, w.start, w.blk, nblk, blk_rows, NH, HD,
+            timed(s, KRK_PROF_ATTN_PREFILL, [&] { kk(krk::attn_prefill(w.qkv, QKV, kc, vc, c_sb, HD, HID, gd.cu, gd.start, gd.blk, nblk, blk_rows, NH, HD,
                                  kmax, w.ao_t, 1, T, st),
                "attention"); });
             timed(s, KRK_PROF_GEMM, [&] { kk(krk::gemm(w.ao_t, T, L.wo_t, HID, w.x_t, T, T, HID, HID, krk::EPI_RESIDUAL, true, st), "wo"); });
@@ -770,13 +796,36 @@ void prefill_group(krk_state* s, int g0, int S, int64_t rows, int nblk, int blk_
         }
     }
     // last token of each sequence -> decode residual buffer column g0 + s
-    timed(s, KRK_PROF_OTHER, [&] { kk(krk::gather_cols(w.x_t, T, w.last, s->h_t, (int)s->Mp, w.dst, HID, S, st), "gather last"); });
+    timed(s, KRK_PROF_OTHER, [&] { kk(krk::gather_cols(w.x_t, T, gd.last, s->h_t, (int)s->Mp, gd.dst, HID, S, st), "gather last"); });
 }
 
-// Validates and runs a batched prefill; on return the decode buffers hold the
-// logits of each sequence's last token.  mark: record prompt tokens in the
-// repetition-penalty bitmaps.
-int run_prefill(krk_state* s, const uint32_t* tokens, const int32_t* lens, bool mark) {
+// A validated batched prefill split into groups of whole sequences of up to
+// PREFILL_GROUP_TOKENS tokens.  The groups are independent (disjoint
+// sequences, states and cache rows), so up to PREFILL_STREAMS of them run at
+// once, group i on stream i % PREFILL_STREAMS with that stream's workspace:
+// one group's projections overlap another's scan, attention and norms.
+// Stream order makes a workspace's reuse safe.  The group tables are built in
+// the state's pinned stage and reach the device with the call's one metadata
+// copy.
+struct PrefillPlan {
+    struct Group {
+        int g0 = 0, S = 0;
+        int64_t rows = 0, off = 0;  // packed rows and their offset in the prompt array
+        int blk_rows = 1, kmax = 1, nblk = 0;
+        int32_t *cu = nullptr, *start = nullptr, *last = nullptr, *dst = nullptr, *row_seq = nullptr;
+        int2* blk = nullptr;  // prefill attention blocks: (sequence, first row)
+    };
+    std::vector<Group> groups;
+    int64_t total = 0;
+    int32_t* pos_after = nullptr;  // [B] positions after the prefill (stage)
+};
+
+inline int64_t start_pos(const krk_state* s, int b, bool from_zero) { return from_zero ? 0 : s->pos_h[b]; }
+
+// The reference's checks in its order (src/model.rs:317-335): empty, context,
+// token.  from_zero: against positions 0 (the prefill follows a reset).
+int check_prefill(const krk_state* s, const uint32_t* tokens, const int32_t* lens, bool from_zero,
+                  int64_t* total_out) {
     const int B = s->B;
     if (!lens) return fail(KRK_INVALID, "null lens");
     int64_t total = 0;
@@ -785,58 +834,99 @@ int run_prefill(krk_state* s, const uint32_t* tokens, const int32_t* lens, bool 
         total += lens[b];
     }
     if (!tokens) return fail(KRK_INVALID, "null tokens");
-    for (int b = 0; b < B; ++b)
-        if (s->pos_h[b] + lens[b] > s->ctx)
-            return fail(KRK_CONTEXT_OVERFLOW, "Sequence length " + std::to_string(s->pos_h[b] + lens[b]) +
-                                                  " exceeds context limit " + std::to_string(s->ctx));
+    for (int b = 0; b < B; ++b) {
+        const int64_t end = start_pos(s, b, from_zero) + lens[b];
+        if (end > s->ctx)
+            return fail(KRK_CONTEXT_OVERFLOW, "Sequence length " + std::to_string(end) + " exceeds context limit " +
+                                                  std::to_string(s->ctx));
+    }
     for (int64_t i = 0; i < total; ++i)
         if (tokens[i] >= (uint32_t)VOC)
             return fail(KRK_BAD_TOKEN,
                         "Token ID " + std::to_string(tokens[i]) + " exceeds vocab size " + std::to_string(VOC));
-    const krk_model* m = s->m;
-    cudaStream_t st = m->stream;
-    // Groups of whole sequences up to PREFILL_GROUP_TOKENS tokens.  They are
-    // independent (disjoint sequences, states and cache rows), so up to
-    // PREFILL_STREAMS of them run at once, group i on stream i % PREFILL_STREAMS
-    // with that stream's workspace: one group's projections overlap another's
-    // scan, attention and norms.  Stream order makes a workspace's reuse safe.
-    struct Group {
-        int g0, S;
-        int64_t rows, off;
-        std::vector<int32_t> cu, start, last, dst, row_seq;  // alive until the final sync
-        std::vector<int2> blk;
-        int blk_rows, kmax;
-    };
-    std::vector<Group> groups;
-    {
-        int64_t off = 0;
-        int g0 = 0;
-        while (g0 < B) {
-            int g1 = g0;
-            int64_t rows = 0;
-            while (g1 < B && (g1 == g0 || rows + lens[g1] <= PREFILL_GROUP_TOKENS)) rows += lens[g1++];
-            Group g;
-            g.g0 = g0; g.S = g1 - g0; g.rows = rows; g.off = off;
-            g.cu.resize(g.S + 1); g.start.resize(g.S); g.last.resize(g.S); g.dst.resize(g.S);
-            g.row_seq.resize(rows);
-            g.cu[0] = 0;
-            for (int i = 0; i < g.S; ++i) {
-                g.cu[i + 1] = g.cu[i] + lens[g0 + i];
-                g.start[i] = (int32_t)s->pos_h[g0 + i];
-                g.last[i] = g.cu[i + 1] - 1;
-                g.dst[i] = g0 + i;
-                for (int r = g.cu[i]; r < g.cu[i + 1]; ++r) g.row_seq[r] = i;
-            }
-            g.kmax = 1;
-            for (int i = 0; i < g.S; ++i) g.kmax = std::max(g.kmax, g.start[i] + lens[g0 + i]);
-            g.blk_rows = krk::attn_prefill_rows(g.kmax, HD);
-            for (int i = 0; i < g.S; ++i)
-                for (int r = 0; r < lens[g0 + i]; r += g.blk_rows) g.blk.push_back(make_int2(i, r));
-            groups.push_back(std::move(g));
-            off += rows;
-            g0 = g1;
+    *total_out = total;
+    return KRK_OK;
+}
+
+// Forms the groups and adds their host tables to the call's stage budget.
+void plan_prefill(const krk_state* s, const int32_t* lens, bool from_zero, PrefillPlan& p, Budget& bud) {
+    const int B = s->B;
+    int64_t off = 0;
+    int g0 = 0;
+    while (g0 < B) {
+        int g1 = g0;
+        int64_t rows = 0;
+        while (g1 < B && (g1 == g0 || rows + lens[g1] <= PREFILL_GROUP_TOKENS)) rows += lens[g1++];
+        PrefillPlan::Group g;
+        g.g0 = g0; g.S = g1 - g0; g.rows = rows; g.off = off;
+        for (int i = g0; i < g1; ++i) g.kmax = std::max<int>(g.kmax, (int)(start_pos(s, i, from_zero) + lens[i]));
+        g.blk_rows = krk::attn_prefill_rows(g.kmax, HD);
+        for (int i = g0; i < g1; ++i) g.nblk += (lens[i] + g.blk_rows - 1) / g.blk_rows;
+        bud.add<int32_t>(g.S + 1); bud.add<int32_t>(g.S); bud.add<int32_t>(g.S); bud.add<int32_t>(g.S);
+        bud.add<int32_t>(rows); bud.add<int2>(g.nblk);
+        p.groups.push_back(g);
+        p.total += rows;
+        off += rows;
+        g0 = g1;
+    }
+    bud.add<int32_t>(B);
+}
+
+// Writes the group tables into the stage (after stage.ensure of the budget).
+void fill_prefill(krk_state* s, const int32_t* lens, bool from_zero, PrefillPlan& p) {
+    HostStage& hs = s->stage;
+    for (auto& g : p.groups) {
+        g.cu = hs.take<int32_t>(g.S + 1); g.start = hs.take<int32_t>(g.S); g.last = hs.take<int32_t>(g.S);
+        g.dst = hs.take<int32_t>(g.S); g.row_seq = hs.take<int32_t>(g.rows); g.blk = hs.take<int2>(g.nblk);
+        g.cu[0] = 0;
+        int nb = 0;
+        for (int i = 0; i < g.S; ++i) {
+            const int b = g.g0 + i;
+            g.cu[i + 1] = g.cu[i] + lens[b];
+            g.start[i] = (int32_t)start_pos(s, b, from_zero);
+            g.last[i] = g.cu[i + 1] - 1;
+            g.dst[i] = b;
+            for (int r = g.cu[i]; r < g.cu[i + 1]; ++r) g.row_seq[r] = i;
+            for (int r = 0; r < lens[b]; r += g.blk_rows) g.blk[nb++] = make_int2(i, r);
         }
     }
+    p.pos_after = hs.take<int32_t>(s->B);
+    for (int b = 0; b < s->B; ++b) p.pos_after[b] = (int32_t)(start_pos(s, b, from_zero) + lens[b]);
+}
+
+// Device address of a pointer into the stage's first `meta_bytes` (the part
+// upload_call copied to the device).
+template <typename T>
+T* meta_dev(const krk_state* s, const T* host) {
+    return reinterpret_cast<T*>(s->meta_arena.base + (reinterpret_cast<const char*>(host) - s->stage.base));
+}
+
+// Copies the stage's first meta_bytes and the packed prompt tokens to the
+// device on the model stream (two asynchronous copies).  Grows the device
+// buffers when needed (after the model's streams are idle).
+void upload_call(krk_state* s, const uint32_t* tokens, int64_t ntok, size_t meta_bytes) {
+    cudaStream_t st = s->m->stream;
+    if (meta_bytes > s->meta_arena.cap || (size_t)ntok * 4 > s->prompt_cap) {
+        sync_model_streams(s->m);
+        if (meta_bytes > s->meta_arena.cap) s->meta_arena.reserve(std::max(meta_bytes, s->stage.cap));
+        if ((size_t)ntok * 4 > s->prompt_cap) {
+            s->prompt_arena.reserve((size_t)ntok * 4);
+            s->prompt_cap = (size_t)ntok * 4;
+        }
+    }
+    if (meta_bytes) kk(cudaMemcpyAsync(s->meta_arena.base, s->stage.base, meta_bytes, cudaMemcpyHostToDevice, st),
+                       "h2d tables");
+    if (ntok) kk(cudaMemcpyAsync(s->prompt_arena.base, tokens, (size_t)ntok * 4, cudaMemcpyHostToDevice, st),
+                 "h2d tokens");
+}
+
+// Launches a planned, uploaded prefill; afterwards (in stream order) the decode
+// buffers hold the logits of each sequence's last token.  mark: record prompt
+// tokens in the repetition-penalty bitmaps.  No host synchronisation.
+void launch_prefill(krk_state* s, const PrefillPlan& p, bool mark) {
+    const krk_model* m = s->m;
+    cudaStream_t st = m->stream;
+    const auto& groups = p.groups;
     // decode_streams == 1 keeps the prefill on the model stream too
     const int ns = s->decode_streams == 1 ? 1 : std::min<int>(PREFILL_STREAMS, (int)groups.size());
     cudaStream_t streams[PREFILL_STREAMS] = {m->stream, m->stream2, m->stream3};
@@ -853,23 +943,17 @@ int run_prefill(krk_state* s, const uint32_t* tokens, const int32_t* lens, bool 
         kk(cudaEventRecord(s->ev_fork, st), "fork");
         for (int k = 1; k < ns; ++k) kk(cudaStreamWaitEvent(streams[k], s->ev_fork, 0), "fork");
     }
+    const uint32_t* tok_d = reinterpret_cast<const uint32_t*>(s->prompt_arena.base);
     for (size_t i = 0; i < groups.size(); ++i) {
-        const Group& g = groups[i];
+        const PrefillPlan::Group& g = groups[i];
         const int k = (int)(i % ns);
         cudaStream_t gs = streams[k];
-        PrefillWs& w = s->pre[k];
-        kk(cudaMemcpyAsync(w.tok, tokens + g.off, g.rows * 4, cudaMemcpyHostToDevice, gs), "h2d tokens");
-        kk(cudaMemcpyAsync(w.cu, g.cu.data(), (g.S + 1) * 4, cudaMemcpyHostToDevice, gs), "h2d cu");
-        kk(cudaMemcpyAsync(w.start, g.start.data(), g.S * 4, cudaMemcpyHostToDevice, gs), "h2d start");
-        kk(cudaMemcpyAsync(w.last, g.last.data(), g.S * 4, cudaMemcpyHostToDevice, gs), "h2d last");
-        kk(cudaMemcpyAsync(w.dst, g.dst.data(), g.S * 4, cudaMemcpyHostToDevice, gs), "h2d dst");
-        kk(cudaMemcpyAsync(w.row_seq, g.row_seq.data(), g.rows * 4, cudaMemcpyHostToDevice, gs), "h2d row_seq");
-        kk(cudaMemcpyAsync(w.blk, g.blk.data(), g.blk.size() * sizeof(int2), cudaMemcpyHostToDevice, gs), "h2d blocks");
-        if (i == 0) total_begin(s);
-        prefill_group(s, g.g0, g.S, g.rows, (int)g.blk.size(), g.blk_rows, g.kmax, w, gs);
+        GroupDev gd{tok_d + g.off, meta_dev(s, g.cu), meta_dev(s, g.start), meta_dev(s, g.last), meta_dev(s, g.dst),
+                    meta_dev(s, g.row_seq), meta_dev(s, g.blk)};
+        prefill_group(s, g.g0, g.S, g.rows, g.nblk, g.blk_rows, g.kmax, s->pre[k], gd, gs);
         if (mark)
             timed_on(s, gs, KRK_PROF_OTHER, 0, [&] {
-                kk(krk::mark_seen(w.tok, w.row_seq, (int)g.rows, s->seen_d + (size_t)g.g0 * SEEN_WORDS, SEEN_WORDS,
+                kk(krk::mark_seen(gd.tok, gd.row_seq, (int)g.rows, s->seen_d + (size_t)g.g0 * SEEN_WORDS, SEEN_WORDS,
                                   gs),
                    "mark seen");
             });
@@ -879,13 +963,9 @@ int run_prefill(krk_state* s, const uint32_t* tokens, const int32_t* lens, bool 
         kk(cudaEventRecord(joins[k], streams[k]), "join");
         kk(cudaStreamWaitEvent(st, joins[k], 0), "join");
     }
-    kk(cudaStreamSynchronize(st), "prefill groups");  // the groups' host vectors go out of scope below
     lm_head(s);
-    for (int b = 0; b < B; ++b) s->pos_h[b] += lens[b];
-    std::vector<int32_t> p32(s->pos_h.begin(), s->pos_h.end());
-    kk(cudaMemcpyAsync(s->pos_d, p32.data(), B * 4, cudaMemcpyHostToDevice, st), "h2d pos");
-    kk(cudaStreamSynchronize(st), "prefill");
-    return KRK_OK;
+    for (int b = 0; b < s->B; ++b) s->pos_h[b] = p.pos_after[b];
+    kk(cudaMemcpyAsync(s->pos_d, meta_dev(s, p.pos_after), (size_t)s->B * 4, cudaMemcpyDeviceToDevice, st), "pos");
 }
 
 int copy_logits(krk_state* s, float* logits_out) {
@@ -916,8 +996,9 @@ int cuda_status(cudaError_t e, const char* what) {
     return fail(e == cudaErrorInvalidValue ? KRK_INVALID : KRK_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
 }
 
-int reset_state(krk_state* s, const uint8_t* mask) {
-    DeviceGuard g(s->m->device);
+// state.reset() for every sequence (mask null) or the masked ones
+// (src/model.rs:220-229).  Stream-ordered; sync: wait for it on the host.
+void reset_state(krk_state* s, const uint8_t* mask, bool sync) {
     cudaStream_t st = s->m->stream;
     if (!mask) {  // every sequence: one memset per array
         for (int l = 0; l < NL; ++l) {
@@ -928,23 +1009,24 @@ int reset_state(krk_state* s, const uint8_t* mask) {
         kk(cudaMemsetAsync(s->seen_d, 0, (size_t)s->B * SEEN_WORDS * 4, st), "reset seen");
         kk(cudaMemsetAsync(s->pos_d, 0, (size_t)s->B * 4, st), "reset pos");
         std::fill(s->pos_h.begin(), s->pos_h.end(), 0);
-        kk(cudaStreamSynchronize(st), "reset");
-        return KRK_OK;
-    }
-    for (int b = 0; b < s->B; ++b) {
-        if (mask && !mask[b]) continue;
-        s->pos_h[b] = 0;
-        for (int l = 0; l < NL; ++l) {
-            if (!is_mamba(l)) continue;  // attention reset only rewinds the length
-            kk(cudaMemsetAsync(s->conv[l] + (size_t)b * DXBC * 4, 0, (size_t)DXBC * 4 * 4, st), "reset conv");
-            kk(cudaMemsetAsync(s->ssm[l] + (size_t)b * MH * MP * DS, 0, (size_t)MH * MP * DS * 4, st), "reset ssm");
+    } else {
+        for (int b = 0; b < s->B; ++b) {
+            if (!mask[b]) continue;
+            s->pos_h[b] = 0;
+            for (int l = 0; l < NL; ++l) {
+                if (!is_mamba(l)) continue;  // attention reset only rewinds the length
+                kk(cudaMemsetAsync(s->conv[l] + (size_t)b * DXBC * 4, 0, (size_t)DXBC * 4 * 4, st), "reset conv");
+                kk(cudaMemsetAsync(s->ssm[l] + (size_t)b * MH * MP * DS, 0, (size_t)MH * MP * DS * 4, st),
+                   "reset ssm");
+            }
+            kk(cudaMemsetAsync(s->seen_d + (size_t)b * SEEN_WORDS, 0, SEEN_WORDS * 4, st), "reset seen");
         }
-        kk(cudaMemsetAsync(s->seen_d + (size_t)b * SEEN_WORDS, 0, SEEN_WORDS * 4, st), "reset seen");
+        s->stage.ensure(round_up((int64_t)s->B * 4, 256));
+        int32_t* p32 = s->stage.take<int32_t>(s->B);
+        for (int b = 0; b < s->B; ++b) p32[b] = (int32_t)s->pos_h[b];
+        kk(cudaMemcpyAsync(s->pos_d, p32, s->B * 4, cudaMemcpyHostToDevice, st), "h2d pos");
     }
-    std::vector<int32_t> p32(s->pos_h.begin(), s->pos_h.end());
-    kk(cudaMemcpyAsync(s->pos_d, p32.data(), s->B * 4, cudaMemcpyHostToDevice, st), "h2d pos");
-    kk(cudaStreamSynchronize(st), "reset");
-    return KRK_OK;
+    if (sync || mask) kk(cudaStreamSynchronize(st), "reset");  // a masked reset's table is in the stage
 }
 
 }  // namespace
@@ -1077,7 +1159,9 @@ int krk_state_free(krk_state* s) {
 int krk_state_reset(krk_state* s, const uint8_t* mask) {
     return guarded([&]() -> int {
         if (!s) return fail(KRK_INVALID, "null state");
-        return reset_state(s, mask);
+        DeviceGuard g(s->m->device);
+        reset_state(s, mask, true);
+        return KRK_OK;
     });
 }
 
@@ -1102,9 +1186,18 @@ int krk_state_positions(const krk_state* s, int64_t* pos_out) {
 int krk_prefill(const krk_model* m, krk_state* s, const uint32_t* tokens, const int32_t* lens, float* logits_out) {
     return guarded([&]() -> int {
         if (!m || !s || s->m != m) return fail(KRK_INVALID, "null handle or state of another model");
-        DeviceGuard g(m->device);
-        int rc = run_prefill(s, tokens, lens, false);
+        int64_t total = 0;
+        int rc = check_prefill(s, tokens, lens, false, &total);
         if (rc) return rc;
+        DeviceGuard g(m->device);
+        PrefillPlan plan;
+        Budget bud;
+        plan_prefill(s, lens, false, plan, bud);
+        s->stage.ensure(bud.bytes);
+        fill_prefill(s, lens, false, plan);
+        upload_call(s, tokens, total, s->stage.used);
+        total_begin(s);
+        launch_prefill(s, plan, false);
         total_end(s);
         rc = copy_logits(s, logits_out);
         kk(cudaStreamSynchronize(m->stream), "prefill");
@@ -1194,46 +1287,72 @@ static int generate_impl(const krk_model* m, krk_state* s, const uint32_t* promp
         DeviceGuard g(m->device);
         cudaStream_t st = m->stream;
         const int B = s->B;
-        // state.reset() (src/generate.rs:65)
-        int rc = reset_state(s, nullptr);
-        if (rc) return rc;
-        rc = run_prefill(s, prompts, lens, true);
-        if (rc) return rc;
+        // state.reset() (src/generate.rs:65), then forward_prefill's checks
+        // against the reset positions; a failing prefill leaves the state reset.
+        int64_t total = 0;
+        int rc = check_prefill(s, prompts, lens, true, &total);
+        if (rc) {
+            reset_state(s, nullptr, true);
+            return rc;
+        }
         // src/generate.rs:86-114 per sequence: a pick is pushed unless it is EOS;
         // after a push the loop stops if current_pos >= context_limit, else it
         // runs forward_step -- also after the max_new_tokens-th push.  So a
         // sequence pushes at most tlimit = min(max_new, ctx - len + 1) tokens
         // and runs at most slimit = min(max_new, ctx - len) decode steps.
-        std::vector<int32_t> tlimit(B), slimit(B);
         int max_picks = 0, max_steps = 0;
         for (int b = 0; b < B; ++b) {
-            tlimit[b] = (int32_t)std::min<int64_t>(max_new_tokens, (int64_t)s->ctx - lens[b] + 1);
-            slimit[b] = (int32_t)std::min<int64_t>(max_new_tokens, (int64_t)s->ctx - lens[b]);
-            max_picks = std::max(max_picks, tlimit[b]);
-            max_steps = std::max(max_steps, slimit[b]);
+            max_picks = std::max<int>(max_picks, (int)std::min<int64_t>(max_new_tokens, (int64_t)s->ctx - lens[b] + 1));
+            max_steps = std::max<int>(max_steps, (int)std::min<int64_t>(max_new_tokens, (int64_t)s->ctx - lens[b]));
         }
         if ((int64_t)max_picks * B > s->hist_cap) {
             s->hist_arena.reserve((size_t)max_picks * B * 4 + 256);
             s->hist_d = s->hist_arena.take<uint32_t>((size_t)max_picks * B);
             s->hist_cap = (int64_t)max_picks * B;
         }
-        kk(cudaMemcpyAsync(s->tlimit_d, tlimit.data(), B * 4, cudaMemcpyHostToDevice, st), "h2d limit");
-        kk(cudaMemcpyAsync(s->slimit_d, slimit.data(), B * 4, cudaMemcpyHostToDevice, st), "h2d limit");
+        // Host tables of the call in the pinned stage: the prefill groups, the
+        // limits and seeds (copied to the device together), then room for the
+        // results read back at the end.
+        PrefillPlan plan;
+        Budget bud;
+        plan_prefill(s, lens, true, plan, bud);
+        bud.add<int32_t>(B); bud.add<int32_t>(B);
+        if (stochastic) bud.add<uint32_t>((size_t)B * 10);
+        bud.add<uint32_t>((size_t)max_picks * B); bud.add<int32_t>(B); bud.add<int32_t>(1);
+        s->stage.ensure(bud.bytes);
+        fill_prefill(s, lens, true, plan);
+        int32_t* tlimit = s->stage.take<int32_t>(B);
+        int32_t* slimit = s->stage.take<int32_t>(B);
+        for (int b = 0; b < B; ++b) {
+            tlimit[b] = (int32_t)std::min<int64_t>(max_new_tokens, (int64_t)s->ctx - lens[b] + 1);
+            slimit[b] = (int32_t)std::min<int64_t>(max_new_tokens, (int64_t)s->ctx - lens[b]);
+        }
+        uint32_t* rng = nullptr;
+        if (stochastic) {  // Sampler::new with config.seed (src/sampler.rs:34-40), one per sequence
+            rng = s->stage.take<uint32_t>((size_t)B * 10);
+            for (int b = 0; b < B; ++b) krk::rng_seed_state(cfg.seeds[b], rng + (size_t)b * 10);
+        }
+        const size_t meta_bytes = s->stage.used;
+        uint32_t* hist = s->stage.take<uint32_t>((size_t)max_picks * B);
+        int32_t* pos = s->stage.take<int32_t>(B);
+        int32_t* err_h = s->stage.take<int32_t>(1);
+        upload_call(s, prompts, total, meta_bytes);
+        // device time from here on: the inputs are on the device
+        total_begin(s);
+        reset_state(s, nullptr, false);
+        launch_prefill(s, plan, true);
         kk(cudaMemsetAsync(s->active_d, 1, B, st), "active");
         kk(cudaMemsetAsync(s->step_d, 0, 4, st), "step");
         kk(cudaMemsetAsync(s->hist_d, 0xff, (size_t)max_picks * B * 4, st), "hist");
-        std::vector<uint32_t> rng;
-        if (stochastic) {  // Sampler::new with config.seed (src/sampler.rs:34-40), one per sequence
-            rng.resize((size_t)B * 10);
-            for (int b = 0; b < B; ++b) krk::rng_seed_state(cfg.seeds[b], rng.data() + (size_t)b * 10);
-            kk(cudaMemcpyAsync(s->rng_d, rng.data(), rng.size() * 4, cudaMemcpyHostToDevice, st), "h2d rng");
-        }
+        if (stochastic)
+            kk(cudaMemcpyAsync(s->rng_d, meta_dev(s, rng), (size_t)B * 40, cudaMemcpyDeviceToDevice, st), "rng");
         krk::GreedyArgs ga{};
         ga.temperature = cfg.temperature; ga.top_p = cfg.top_p; ga.top_k = cfg.top_k; ga.rng = s->rng_d;
         ga.logits = s->logits; ga.ld = VOC; ga.vocab = VOC; ga.B = B;
         ga.seen = s->seen_d; ga.penalty = repetition_penalty;
         ga.tok = s->tok_d; ga.active = s->active_d; ga.hist = s->hist_d; ga.step = s->step_d;
-        ga.tlimit = s->tlimit_d; ga.slimit = s->slimit_d; ga.stop_eos = stop_at_eos; ga.eos = KRK_EOS_TOKEN;
+        ga.tlimit = meta_dev(s, tlimit); ga.slimit = meta_dev(s, slimit);
+        ga.stop_eos = stop_at_eos; ga.eos = KRK_EOS_TOKEN;
         ga.pos = nullptr;
         // first pick from the prefill logits (src/generate.rs:81-82)
         timed(s, KRK_PROF_OTHER, [&] { kk(krk::sample(ga, st), "sample"); });
@@ -1245,15 +1364,12 @@ static int generate_impl(const krk_model* m, krk_state* s, const uint32_t* promp
             timed(s, KRK_PROF_OTHER, [&] { kk(krk::sample(ga, st), "sample"); });
         }
         total_end(s);
-        std::vector<uint32_t> hist((size_t)max_picks * B);
-        std::vector<int32_t> pos(B);
-        kk(cudaMemcpyAsync(hist.data(), s->hist_d, hist.size() * 4, cudaMemcpyDeviceToHost, st), "d2h tokens");
-        kk(cudaMemcpyAsync(pos.data(), s->pos_d, B * 4, cudaMemcpyDeviceToHost, st), "d2h pos");
-        int32_t err_h = 0;
-        kk(cudaMemcpyAsync(&err_h, s->err_d, 4, cudaMemcpyDeviceToHost, st), "d2h status");
-        kk(cudaStreamSynchronize(st), "generate");
+        kk(cudaMemcpyAsync(hist, s->hist_d, (size_t)max_picks * B * 4, cudaMemcpyDeviceToHost, st), "d2h tokens");
+        kk(cudaMemcpyAsync(pos, s->pos_d, B * 4, cudaMemcpyDeviceToHost, st), "d2h pos");
+        kk(cudaMemcpyAsync(err_h, s->err_d, 4, cudaMemcpyDeviceToHost, st), "d2h status");
+        kk(cudaStreamSynchronize(st), "generate");  // the call's one host synchronisation
         prof_collect_if_large(s);
-        if (err_h) return device_wait_error(s);
+        if (*err_h) return device_wait_error(s);
         for (int b = 0; b < B; ++b) {
             int n = 0;
             for (int i = 0; i < tlimit[b]; ++i) {
@@ -1297,10 +1413,33 @@ int krk_state_export(const krk_state* s, int seq, int layer, int what, float* ou
     });
 }
 
+// Drops the state's step graphs (they hold the old part layout).
+static void drop_step_graphs(krk_state* s) {
+    if (s->step_graphs.empty()) return;
+    DeviceGuard g(s->m->device);
+    sync_model_streams(s->m);
+    for (cudaGraphExec_t& ex : s->step_graphs)
+        if (ex) cudaGraphExecDestroy(ex);
+    s->step_graphs.clear();
+    s->step_graph_kernels.clear();
+}
+
 int krk_state_set_decode_streams(krk_state* s, int n) {
     if (!s || n < 1 || n > 4) return fail(KRK_INVALID, "decode streams must be 1 to 4");
-    s->decode_streams = n;
-    return KRK_OK;
+    return guarded([&]() -> int {
+        if (n != s->decode_streams) drop_step_graphs(s);
+        s->decode_streams = n;
+        return KRK_OK;
+    });
+}
+
+int krk_state_set_step_graphs(krk_state* s, int enable) {
+    if (!s) return fail(KRK_INVALID, "null state");
+    return guarded([&]() -> int {
+        if (!enable) drop_step_graphs(s);
+        s->step_graphs_on = enable != 0;
+        return KRK_OK;
+    });
 }
 
 int krk_state_profile(krk_state* s, int enable) {
@@ -1432,7 +1571,7 @@ int krk_k_conv_ssd_scan(const float* x, const float* bm, const float* cm, const 
 }
 
 size_t krk_attn_work_floats(int B, int H, int dh, int ctx, int split) {
-    if (split <= 0) split = 256;
+    if (split <= 0) return 0;  // 0: the cluster kernel, which needs no scratch
     if (B <= 0 || H <= 0 || dh <= 0 || ctx <= 0) return 0;
     return krk::attn_decode_work_floats(B, H, dh, ctx, split);
 }
@@ -1446,7 +1585,8 @@ int krk_k_rope_kv_attn_decode(const float* q, const float* k, const float* v, fl
     a.pos = pos; a.active = nullptr;
     a.out = out; a.o_sb = (int64_t)H * dh; a.o_sh = dh; a.o_sd = 1;
     a.work = work;
-    a.B = B; a.H = H; a.dh = dh; a.ctx = ctx; a.split = split <= 0 ? 256 : split; a.theta = theta;
+    if (split < 0) return fail(KRK_INVALID, "split must be 0 (cluster kernel) or a positive multiple of 64");
+    a.B = B; a.H = H; a.dh = dh; a.ctx = ctx; a.split = split; a.theta = theta;
     a.rope = nullptr;
     return cuda_status(krk::attn_decode(a, (cudaStream_t)stream), "rope_kv_attn_decode");
 }

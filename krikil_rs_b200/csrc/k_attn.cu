@@ -1,6 +1,8 @@
 // Attention kernels: RoPE + KV-cache append + single-query softmax attention
 // for decode (split over the cache like flash-decoding), and RoPE/append plus
 // causal attention for prefill (fp32).
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -500,6 +502,182 @@ __global__ void wait_probe_kernel(const float* src, int polls, int copy, int* er
     if (threadIdx.x == 0 && !ok && err) atomicOr(err, 1);
 }
 
+// Decode attention without split scratch: the AC_CTAS CTAs of one (sequence,
+// head) form a thread-block cluster.  CTA r of the cluster takes the r-th of
+// AC_CTAS equal ranges of the keys 0..pos (whole 16-key groups), so the
+// cluster's CTAs finish together whatever the position.  A CTA works as
+// attn_decode_kernel does on one split -- 64-key K tiles staged with cp.async
+// for the scores, the softmax partial of its range, then 64-key V tiles for
+// the weighted sum -- and keeps its partial (max, sum, unnormalised output) in
+// shared memory.  After a cluster barrier CTA 0 merges the AC_CTAS partials
+// through distributed shared memory and writes the output; a second cluster
+// barrier keeps every CTA's shared memory alive until then.  No thread leaves
+// early: every thread of every CTA reaches both cluster barriers, and the CTA
+// barriers inside a range's work are taken by the whole CTA or skipped by the
+// whole CTA (an empty range is CTA-uniform).
+constexpr int AC_CTAS = 8;
+
+// keys per CTA at most for a cache of ctx slots (a multiple of 16)
+inline int ac_per_max(int ctx) { return ((ctx + AC_CTAS - 1) / AC_CTAS + 15) / 16 * 16; }
+
+template <int DH>
+size_t ac_smem_bytes(int ctx) {
+    return sizeof(float) * (3 * DH + AD_RED + ac_per_max(ctx) + AD_TILE * AdLayout<DH>::KLD + 64 + DH + 4);
+}
+
+template <int DH>
+__global__ void __cluster_dims__(1, 1, AC_CTAS) __launch_bounds__(AD_THREADS)
+    attn_decode_cluster_kernel(AttnDecodeArgs a, int per_max) {
+    using L = AdLayout<DH>;
+    namespace cg = cooperative_groups;
+    constexpr int HALF = DH / 2;
+    extern __shared__ __align__(16) float sm[];
+    float* qs = sm;
+    float* kn = qs + DH;
+    float* vn = kn + DH;
+    float* red = vn + DH;
+    float* sc = red + AD_RED;
+    float* tile = sc + per_max;
+    float* scratch = tile + AD_TILE * L::KLD;
+    float* cpart = scratch + 64;  // [DH + 2]: the CTA's unnormalised output, max, sum
+    cg::cluster_group cluster = cg::this_cluster();
+    const int rank = (int)cluster.block_rank();
+    const int b = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
+
+    const bool live = !a.active || a.active[b];
+    const int pos = live ? a.pos[b] : -1;
+    const bool ok = live && pos >= 0 && pos < a.ctx;  // the host rejects bad positions before launch
+    const int nkeys = ok ? pos + 1 : 0;
+    const int per = ((nkeys + AC_CTAS - 1) / AC_CTAS + 15) / 16 * 16;  // <= per_max
+    const int j0 = min(nkeys, rank * per), j1 = min(nkeys, j0 + per);
+
+    if (j1 > j0) {  // uniform over the CTA
+        const size_t in_off = (size_t)b * a.in_sb + (size_t)h * a.in_sh;
+        if (tid < DH) {
+            qs[tid] = a.q[in_off + tid];
+            kn[tid] = a.k[in_off + tid];
+            vn[tid] = a.v[in_off + tid];
+        }
+        __syncthreads();
+        if (tid < HALF) {  // src/model.rs:721-728
+            float c, s;
+            if (a.rope) {
+                const float2 cs = a.rope[(size_t)pos * HALF + tid];
+                c = cs.x;
+                s = cs.y;
+            } else {
+                rope_cs(a.freq, tid, pos, c, s);
+            }
+            rope_pair(qs[tid], qs[tid + HALF], c, s);
+            rope_pair(kn[tid], kn[tid + HALF], c, s);
+        }
+        __syncthreads();
+        const size_t cbase = (size_t)b * a.c_sb + (size_t)h * a.c_sh;
+        if (j1 == nkeys && tid < DH) {  // KV append (src/model.rs:730-733), by the CTA holding slot pos
+            a.kc[cbase + (size_t)pos * a.c_st + tid] = kn[tid];
+            a.vc[cbase + (size_t)pos * a.c_st + tid] = vn[tid];
+        }
+        // scores (src/model.rs:742-748): dot(q_h, k_j) * (1/sqrt(dh))
+        const float scale = 1.0f / sqrtf((float)DH);
+        float mx = -INFINITY;
+        for (int t0 = j0; t0 < j1; t0 += AD_TILE) {
+            const int nk = min(AD_TILE, j1 - t0);
+            for (int i = tid; i < nk * L::DH4; i += AD_THREADS) {
+                const int r = i / L::DH4, c4 = i % L::DH4;
+                float* dst = tile + r * L::KLD + c4 * 4;
+                const int j = t0 + r;
+                if (j == pos) *reinterpret_cast<float4*>(dst) = *reinterpret_cast<const float4*>(kn + c4 * 4);
+                else cp_async16(dst, a.kc + cbase + (size_t)j * a.c_st + c4 * 4);
+            }
+            cp_async_commit();
+            cp_async_wait<0>();
+            __syncthreads();
+            if (tid < nk) {
+                const float sv = dot_ref(qs, tile + tid * L::KLD, DH) * scale;
+                sc[t0 - j0 + tid] = sv;
+                mx = fmaxf(mx, sv);
+            }
+            __syncthreads();
+        }
+        // softmax partial over this range (src/math.rs:213-232)
+        const float m = block_reduce(mx, scratch, true);
+        const int n = j1 - j0;
+        float lsum = 0.0f;
+        for (int j = tid; j < n; j += AD_THREADS) {
+            const float e = expf(sc[j] - m);
+            sc[j] = e;
+            lsum += e;
+        }
+        const float l = block_reduce(lsum, scratch, false);
+        __syncthreads();
+        // out += w_j * v_j (src/model.rs:752-759)
+        const int g = tid / L::DH4, d4 = tid % L::DH4;
+        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int t0 = j0; t0 < j1; t0 += AD_TILE) {
+            const int nk = min(AD_TILE, j1 - t0);
+            for (int i = tid; i < nk * L::DH4; i += AD_THREADS) {
+                const int r = i / L::DH4, c4 = i % L::DH4;
+                float* dst = tile + r * L::KLD + c4 * 4;
+                const int j = t0 + r;
+                if (j == pos) *reinterpret_cast<float4*>(dst) = *reinterpret_cast<const float4*>(vn + c4 * 4);
+                else cp_async16(dst, a.vc + cbase + (size_t)j * a.c_st + c4 * 4);
+            }
+            cp_async_commit();
+            cp_async_wait<0>();
+            __syncthreads();
+            if (g < L::G) {
+                for (int r = g; r < nk; r += L::G) {
+                    const float w = sc[t0 - j0 + r];
+                    const float4 vv = *reinterpret_cast<const float4*>(tile + r * L::KLD + d4 * 4);
+                    o.x = o.x + w * vv.x;
+                    o.y = o.y + w * vv.y;
+                    o.z = o.z + w * vv.z;
+                    o.w = o.w + w * vv.w;
+                }
+            }
+            __syncthreads();
+        }
+        if (g < L::G) *reinterpret_cast<float4*>(red + g * DH + d4 * 4) = o;
+        __syncthreads();
+        if (tid < DH) {
+            float acc = red[tid];
+            for (int gg = 1; gg < L::G; ++gg) acc = acc + red[gg * DH + tid];
+            cpart[tid] = acc;
+        }
+        if (tid == 0) {
+            cpart[DH] = m;
+            cpart[DH + 1] = l;
+        }
+    } else {
+        if (tid < DH) cpart[tid] = 0.0f;
+        if (tid == 0) {
+            cpart[DH] = -INFINITY;
+            cpart[DH + 1] = 0.0f;
+        }
+    }
+    cluster.sync();  // every CTA partial written and visible across the cluster
+    if (rank == 0 && ok && tid < DH) {
+        float mp[AC_CTAS];
+        float m = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < AC_CTAS; ++c) {
+            mp[c] = cluster.map_shared_rank(cpart, c)[DH];
+            m = fmaxf(m, mp[c]);
+        }
+        float acc = 0.0f, l = 0.0f;
+#pragma unroll
+        for (int c = 0; c < AC_CTAS; ++c) {
+            if (mp[c] == -INFINITY) continue;  // an empty range
+            const float* pc = cluster.map_shared_rank(cpart, c);
+            const float f = expf(mp[c] - m);
+            acc = acc + pc[tid] * f;
+            l = l + pc[DH + 1] * f;
+        }
+        a.out[(size_t)b * a.o_sb + (size_t)h * a.o_sh + (size_t)tid * a.o_sd] = acc * (1.0f / l);
+    }
+    cluster.sync();  // CTA 0 has read every partial: shared memory may go
+}
+
 // Merges the per-split (max, sum, unnormalised out) partials of one (b, h).
 // Launched as a programmatic dependent of the split kernel: it reads the
 // positions while that kernel drains, then waits for its partials.
@@ -751,6 +929,29 @@ size_t attn_decode_work_floats(int B, int H, int dh, int ctx, int split) {
 cudaError_t attn_decode(const AttnDecodeArgs& args, cudaStream_t s) {
     AttnDecodeArgs a = args;
     if (!a.rope) a.freq = rope_freqs(a.dh, a.theta);
+    if (a.split == 0) {  // clusters of AC_CTAS CTAs per (sequence, head), merged in distributed shared memory
+        if (a.B <= 0 || a.H <= 0 || a.H > 65535 || a.ctx <= 0 || (a.dh != 64 && a.dh != 76) || (a.c_sb & 3) ||
+            (a.c_sh & 3) || (a.c_st & 3) || (((uintptr_t)a.kc | (uintptr_t)a.vc) & 15))
+            return cudaErrorInvalidValue;
+        const dim3 grid(a.B, a.H, AC_CTAS);
+        const int per_max = ac_per_max(a.ctx);
+        cudaError_t e;
+        if (a.dh == 76) {
+            static DeviceOnce once;
+            const size_t smem = ac_smem_bytes<76>(a.ctx);
+            if (smem > 227 * 1024) return cudaErrorInvalidValue;
+            if ((e = once.set_smem((const void*)attn_decode_cluster_kernel<76>, 227 * 1024)) != cudaSuccess) return e;
+            attn_decode_cluster_kernel<76><<<grid, AD_THREADS, smem, s>>>(a, per_max);
+        } else {
+            static DeviceOnce once;
+            const size_t smem = ac_smem_bytes<64>(a.ctx);
+            if (smem > 227 * 1024) return cudaErrorInvalidValue;
+            if ((e = once.set_smem((const void*)attn_decode_cluster_kernel<64>, 227 * 1024)) != cudaSuccess) return e;
+            attn_decode_cluster_kernel<64><<<grid, AD_THREADS, smem, s>>>(a, per_max);
+        }
+        add_launches(1);
+        return cudaGetLastError();
+    }
     if (a.B <= 0 || a.H <= 0 || a.ctx <= 0 || a.split <= 0 || a.split % 64 || (a.dh != 64 && a.dh != 76) ||
         (a.c_sb & 3) || (a.c_sh & 3) || (a.c_st & 3) || (((uintptr_t)a.kc | (uintptr_t)a.vc) & 15))
         return cudaErrorInvalidValue;

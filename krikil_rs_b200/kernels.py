@@ -117,7 +117,9 @@ def wait_probe(src16, status, polls: int, copy: bool) -> None:
 
 
 def rope_kv_attn_decode(q, k, v, kc, vc, pos, split: int = 0, theta: float = 10000.0, work=None, out=None):
-    """q,k,v [B,H,dh]; kc,vc [B,H,ctx,dh] (updated at pos); pos int32 [B]."""
+    """q,k,v [B,H,dh]; kc,vc [B,H,ctx,dh] (updated at pos); pos int32 [B].
+    split 0: the cluster kernel (no scratch); split > 0: splits of that many
+    keys merged through `work` (allocated here when not given)."""
     _f32(q, k, v, kc, vc, work, out)
     b, h, dh = q.shape
     ctx = kc.shape[2]

@@ -193,6 +193,11 @@ class PebbleState:
         own streams (3 by default, at most 4); 1: decode and prefill on one stream."""
         check(lib.krk_state_set_decode_streams(self._h, int(n)))
 
+    def set_step_graphs(self, enable: bool) -> None:
+        """Replay each decode step of the generation loops as a CUDA graph (the
+        default) or launch its kernels one by one; results are identical."""
+        check(lib.krk_state_set_step_graphs(self._h, int(bool(enable))))
+
     def profile(self, enable: bool = True, per_kernel: bool = True) -> None:
         """Turn CUDA-event timing of later calls on/off (resets totals): per kernel
         class and whole calls, or (per_kernel=False) whole calls only."""

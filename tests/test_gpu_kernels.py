@@ -205,9 +205,11 @@ def test_conv_ssd_scan_split_invariance_full_size():
 
 
 # ------------------------------------------------------------- attention
-@pytest.mark.parametrize("split", [64, 128, 256, 2048])
+@pytest.mark.parametrize("split", [0, 64, 128, 256, 2048])
 def test_rope_kv_attn_decode_full_size(split):
-    """Config: q,k,v [64,8,1,64], positions ~U[0,2048), cache [64,8,2048,64]."""
+    """Config: q,k,v [64,8,1,64], positions ~U[0,2048), cache [64,8,2048,64].
+    split 0 is the cluster kernel (eight CTAs per sequence and head merged in
+    distributed shared memory, no scratch)."""
     q, k, v, pos, kc, vc = synth.attn_decode_inputs()
     g_kc, g_vc = cu(kc), cu(vc)
     out = K.rope_kv_attn_decode(cu(q), cu(k), cu(v), g_kc, g_vc, cu(pos), split=split)
@@ -221,12 +223,16 @@ def test_rope_kv_attn_decode_full_size(split):
         np.testing.assert_array_equal(gk[b, :, : pos[b]], kc[b, :, : pos[b]])  # history untouched
 
 
-@pytest.mark.parametrize("split", [64, 128])
+@pytest.mark.parametrize("split", [0, 64, 128])
 @pytest.mark.parametrize("dh,ctx,posv", [(76, 16, [0, 15, 7]), (64, 300, [0, 63, 64, 299]), (76, 700, [699, 1, 256]),
                                          (64, 200, [15, 16, 17, 47, 48, 127, 128, 199]),
-                                         (76, 200, [15, 16, 31, 32, 63, 64, 65, 191])])
+                                         (76, 200, [15, 16, 31, 32, 63, 64, 65, 191]),
+                                         (64, 2048, [0, 1, 127, 128, 129, 1000, 2046, 2047]),
+                                         (76, 1100, [1099, 511, 512, 513, 1024, 8, 136, 1087])])
 def test_rope_kv_attn_decode_edges(dh, ctx, posv, split):
-    """First slot, last slot, 16-key warp and split boundaries, head dim 76 (19 float4s)."""
+    """First slot, last slot, 16-key warp and split boundaries, head dim 76 (19
+    float4s); for the cluster kernel (split 0) positions at the boundaries of
+    its per-CTA ranges (multiples of 8 x 16 keys) and of its 16-key groups."""
     rng = np.random.default_rng(dh + ctx)
     bsz, nh = len(posv), 8
     q = rng.standard_normal((bsz, nh, dh)).astype(np.float32)

@@ -172,6 +172,31 @@ def test_c5_subset_token_streams(models):
         assert got[b] == ref, b
 
 
+def test_c5_benchmark_call_streams_match_oracle():
+    """The decode benchmark's own call: 1024 sequences, prompts of 128 ids
+    ~U[0,2048) (seed 1), 256 greedy tokens each with EOS ignored, context 2048,
+    the decode in its default three parts (rows 0-383, 384-703, 704-1023) on
+    seed-0 weights.  32 of the 1024 streams -- both ends of every part and
+    spread over the batch -- equal the oracle's token for token."""
+    path = synth.weights_file(0)
+    gpu = PebbleModel.load_safetensors(path)
+    orc = O.OracleModel(synth.load_safetensors(path))
+    prompts = synth.decode_prompts(1024, 128, seed=1)
+    st = PebbleState(gpu, 2048, batch=1024)
+    got = gpu.generate_greedy([p.tolist() for p in prompts], st, 256, stop_at_eos=False)
+    assert all(len(g) == 256 for g in got)
+    picks = sorted(set(np.linspace(0, 1023, 22).astype(int).tolist()) |
+                   {1, 127, 128, 383, 384, 385, 703, 704, 705, 1022})
+    assert len(picks) == 32
+    for b in picks:
+        ref, _ = O.generate_greedy(orc, O.OracleState(2048), prompts[b].tolist(), 256, eos=None)
+        if got[b] != ref:
+            i = next(i for i, (x, y) in enumerate(zip(got[b], ref)) if x != y)
+            pytest.fail(f"sequence {b}: first difference at token {i}: gpu {got[b][i]} oracle {ref[i]}")
+    st.close()
+    gpu.close()
+
+
 def test_large_batch_halves_match_single_sequences(models):
     """A batch of 256+ sequences decodes as two halves on two streams; every
     sequence's logits equal (bitwise) those of the same sequence run alone, on
@@ -290,6 +315,30 @@ def test_small_batch_step_graphs(models):
         if profiled:
             st.profile(True)
         outs.append(gpu.generate_sample(prompts, st, 70, 0.8, 0.9, 20, 1.1, list(range(40)), stop_at_eos=False))
+    assert outs[0] == outs[1]
+
+
+@pytest.mark.parametrize("bsz,parts", [(128, 3), (384, 3), (520, 2)])
+def test_step_graphs_of_batches_in_parts(models, bsz, parts):
+    """Decode steps of larger batches -- one stream at 128 sequences, three or
+    two parts on their own streams with forks and joins at 384 and 520 -- also
+    replay CUDA graphs: ragged prompts crossing several attention key-block
+    counts give exactly the tokens of the same call launched kernel by kernel,
+    and a graph captured for one part layout is dropped when the layout
+    changes."""
+    gpu, _ = models
+    rng = np.random.default_rng(bsz)
+    prompts = [rng.integers(0, 2048, int(n)).astype(np.uint32).tolist() for n in rng.integers(1, 140, bsz)]
+    outs = []
+    for graphs in (True, False):
+        st = PebbleState(gpu, 256, batch=bsz)
+        st.set_decode_streams(parts)
+        st.set_step_graphs(graphs)
+        outs.append(gpu.generate_greedy(prompts, st, 40, repetition_penalty=1.1, stop_at_eos=False))
+        if graphs:  # a new part layout: the captured graphs go, the results stay the same
+            st.set_decode_streams(1)
+            assert gpu.generate_greedy(prompts, st, 40, repetition_penalty=1.1, stop_at_eos=False) == outs[0]
+        st.close()
     assert outs[0] == outs[1]
 
 
