@@ -168,6 +168,25 @@ KRK_API int krk_state_export(const krk_state* state, int seq, int layer, int wha
  * kernel node). */
 KRK_API int krk_launch_count(uint64_t* count);
 
+/* Checked builds (no reference counterpart; the reference's bounds checks are
+ * Rust's own).  `make CHECKED=1` builds lib/libkrikil_cuda_checked.so, whose
+ * kernels test the preconditions on device data the host cannot see before a
+ * launch (token ids, positions, table entries read on the device); a kernel
+ * that finds one violated sets a KRK_CHECK_* bit of a device status word and
+ * skips the access (no trap, no assert), and krk_prefill / krk_step /
+ * krk_generate_* then fail with KRK_CHECK_FAILED naming the checks.
+ * krk_checked_build: 1 for a checked build, else 0.  krk_check_status: the
+ * bits set on the current device since they were last cleared (always 0 in
+ * other builds); call it after the checked work has finished (the model calls
+ * synchronise before they return; for a per-kernel entry point synchronise its
+ * stream first); clear != 0 resets them. */
+#define KRK_CHECK_TOKEN 1u    /* a token id >= vocab reached a kernel */
+#define KRK_CHECK_POSITION 2u /* a position outside [0, ctx) or past the launch's key bound */
+#define KRK_CHECK_TABLE 4u    /* a prefill table entry outside its sequence or key bound */
+#define KRK_CHECK_COLUMN 8u   /* a gather column outside its matrix */
+KRK_API int krk_checked_build(void);
+KRK_API int krk_check_status(uint32_t* bits, int clear);
+
 /* Measurement hook (no reference counterpart; the reference only times whole
  * calls, src/generate.rs:76-78, :116-122): with profiling on, every later
  * prefill / step / generate call on this state brackets each kernel launch

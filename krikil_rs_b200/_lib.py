@@ -9,10 +9,14 @@ import ctypes as C
 import os
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "lib", "libkrikil_cuda.so")
+# KRIKIL_CHECKED=1 loads the checked build (make CHECKED=1), whose kernels
+# report violated preconditions on device data (krk_check_status).
+CHECKED = os.environ.get("KRIKIL_CHECKED", "0") == "1"
+LIB_PATH = os.path.join(_HERE, "lib", "libkrikil_cuda_checked.so" if CHECKED else "libkrikil_cuda.so")
 
 if not os.path.exists(LIB_PATH):
-    raise ImportError(f"{LIB_PATH} is missing: build it with `make -C {_HERE}` (or __graft_entry__.build())")
+    raise ImportError(f"{LIB_PATH} is missing: build it with `make -C {_HERE}{' CHECKED=1' if CHECKED else ''}` "
+                      "(or __graft_entry__.build())")
 
 lib = C.CDLL(LIB_PATH)
 
@@ -42,6 +46,8 @@ _SIGS = {
     "krk_generate_greedy": (_i32, [_vp, _vp, _vp, _vp, _i32, _f32, _i32, _vp, _vp]),
     "krk_state_export": (_i32, [_vp, _i32, _i32, _i32, _vp, _i64]),
     "krk_launch_count": (_i32, [C.POINTER(C.c_uint64)]),
+    "krk_checked_build": (_i32, []),
+    "krk_check_status": (_i32, [C.POINTER(C.c_uint32), _i32]),
     "krk_state_profile": (_i32, [_vp, _i32]),
     "krk_state_profile_read": (_i32, [_vp, _i32, C.POINTER(C.c_double), C.POINTER(_i64)]),
     "krk_state_profile_units": (_i32, [_vp, _i32, C.POINTER(_i64)]),
@@ -86,6 +92,7 @@ for _name, (_res, _args) in _SIGS.items():
 EXPORTED = tuple(_SIGS)
 
 OK, BAD_TOKEN, CONTEXT_OVERFLOW, EMPTY, IO, NOT_FOUND, INVALID, CUDA, CHECK_FAILED = range(9)
+CHECK_TOKEN, CHECK_POSITION, CHECK_TABLE, CHECK_COLUMN = 1, 2, 4, 8  # krk_check_status bits
 
 # krk_state_profile_read classes
 PROF_CLASSES = ("device_total", "gemm", "ssd_step", "attn_decode", "norm", "conv", "ssd_scan", "attn_prefill",

@@ -1034,7 +1034,40 @@ void reset_state(krk_state* s, const uint8_t* mask, bool sync) {
 namespace krk {
 // Sets the calling thread's krk_last_error() message (for other translation units).
 int report_error(int status, const std::string& msg) { return fail(status, msg); }
+
+// The device check words of a checked build, one reader per translation unit
+// with kernels (registered while the library loads).
+static std::vector<unsigned (*)(bool)>& check_readers() {
+    static std::vector<unsigned (*)(bool)> v;
+    return v;
+}
+void register_check_word(unsigned (*read)(bool clear)) { check_readers().push_back(read); }
+static unsigned read_checks(bool clear) {
+    unsigned bits = 0;
+    for (auto f : check_readers()) bits |= f(clear);
+    return bits;
+}
 }  // namespace krk
+
+namespace {
+// In a checked build, a call that launched kernels ends by reading (and
+// clearing) the device check words of its device: a set bit means a kernel
+// found a precondition on device data violated and skipped the access.
+int checked_result(int rc) {
+#ifdef KRIKIL_CHECKED
+    const unsigned bits = krk::read_checks(true);
+    if (bits) {
+        std::string what;
+        const char* names[] = {"token id >= vocab", "position outside the cache or the key bound",
+                               "prefill table entry out of range", "gather column out of range"};
+        for (int i = 0; i < 4; ++i)
+            if (bits & (1u << i)) what += std::string(what.empty() ? "" : "; ") + names[i];
+        return fail(KRK_CHECK_FAILED, "device check failed: " + what + "; outputs of this call are not valid");
+    }
+#endif
+    return rc;
+}
+}  // namespace
 
 // =================================================================== C ABI
 extern "C" {
@@ -1202,7 +1235,7 @@ int krk_prefill(const krk_model* m, krk_state* s, const uint32_t* tokens, const 
         rc = copy_logits(s, logits_out);
         kk(cudaStreamSynchronize(m->stream), "prefill");
         prof_collect_if_large(s);
-        return rc;
+        return checked_result(rc);
     });
 }
 
@@ -1240,7 +1273,7 @@ int krk_step(const krk_model* m, krk_state* s, const uint32_t* tokens, float* lo
         kk(cudaStreamSynchronize(st), "step");
         prof_collect_if_large(s);
         if (err_h) return device_wait_error(s);
-        return rc;
+        return checked_result(rc);
     });
 }
 
@@ -1380,7 +1413,7 @@ static int generate_impl(const krk_model* m, krk_state* s, const uint32_t* promp
             n_out[b] = n;
             s->pos_h[b] = pos[b];
         }
-        return KRK_OK;
+        return checked_result(KRK_OK);
     });
 }
 
@@ -1490,6 +1523,20 @@ int krk_state_profile_units(const krk_state* s, int cls, int64_t* units) {
         *units = s->prof.units[cls];
         return KRK_OK;
     });
+}
+
+int krk_checked_build(void) {
+#ifdef KRIKIL_CHECKED
+    return 1;
+#else
+    return 0;
+#endif
+}
+
+int krk_check_status(uint32_t* bits, int clear) {
+    if (!bits) return fail(KRK_INVALID, "null argument");
+    *bits = krk::read_checks(clear != 0);
+    return KRK_OK;
 }
 
 int krk_launch_count(uint64_t* count) {

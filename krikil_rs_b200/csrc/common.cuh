@@ -99,4 +99,47 @@ KRK_DEV bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int limit) {
     return false;
 }
 
+// ---- checked builds ---------------------------------------------------------
+// Compiled with -DKRIKIL_CHECKED (make CHECKED=1), kernels test the
+// preconditions on device data that the host cannot see before a launch --
+// token ids, sequence positions, table entries read on the device -- and where
+// one fails they set a bit of their translation unit's device status word and
+// skip the access instead of making it; krk_check_status() reads the words,
+// and the model API's calls turn a set bit into KRK_CHECK_FAILED.  No trap and
+// no assert: the kernel carries on or returns, and the context stays usable.
+// In other builds the checks compile to nothing (the guards every build has
+// stay as they are).
+enum CheckBits : unsigned {
+    CHK_TOKEN = 1u,     // a token id >= vocab reached a kernel
+    CHK_POSITION = 2u,  // a sequence position outside [0, ctx), or past the launch's key bound
+    CHK_TABLE = 4u,     // a prefill table entry outside its sequence or its key bound
+    CHK_COLUMN = 8u,    // a gather column outside its matrix
+};
+#ifdef KRIKIL_CHECKED
+constexpr bool kChecked = true;
+#else
+constexpr bool kChecked = false;
+#endif
+// Registers a translation unit's reader of its status word (defined in capi.cu).
+void register_check_word(unsigned (*read)(bool clear));
+
+namespace {
+#ifdef KRIKIL_CHECKED
+__device__ unsigned g_check_word;  // one per translation unit (each is its own device module)
+KRK_DEV void check_fail(unsigned bit) { atomicOr(&g_check_word, bit); }
+unsigned read_check_word(bool clear) {
+    unsigned v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_check_word, sizeof v) != cudaSuccess) return 0;
+    if (clear && v) {
+        const unsigned z = 0;
+        cudaMemcpyToSymbol(g_check_word, &z, sizeof z);
+    }
+    return v;
+}
+const bool g_check_word_registered = (register_check_word(&read_check_word), true);
+#else
+KRK_DEV void check_fail(unsigned) {}
+#endif
+}  // namespace
+
 }  // namespace krk

@@ -89,7 +89,10 @@ __global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(AttnDecodeArgs 
     const int b = blockIdx.x, h = blockIdx.y, sp = blockIdx.z, tid = threadIdx.x;
     if (a.active && !a.active[b]) return;
     const int pos = a.pos[b];
-    if (pos < 0 || pos >= a.ctx) return;  // the host rejects these before launch
+    if (pos < 0 || pos >= a.ctx) {  // the host rejects these before launch
+        if (tid == 0) check_fail(CHK_POSITION);
+        return;
+    }
     const int nkeys = pos + 1;
     const int j0 = sp * a.split;
     if (j0 >= nkeys) return;
@@ -297,6 +300,13 @@ __global__ void __launch_bounds__(NW * 32) attn_decode_warp_kernel(AttnDecodeArg
     const bool live = !a.active || a.active[b];
     const int pos = a.pos[b];
     if (!live || pos < 0 || pos >= a.ctx) {  // the host rejects bad positions before launch
+        if (live && threadIdx.x == 0) check_fail(CHK_POSITION);
+        drain();
+        return;
+    }
+    // the copies above covered the rows below the batch's key bound only
+    if (kChecked && BULK && a.max_keys > 0 && pos + 1 > a.max_keys) {
+        if (threadIdx.x == 0) check_fail(CHK_POSITION);
         drain();
         return;
     }
@@ -547,6 +557,7 @@ __global__ void __cluster_dims__(1, 1, AC_CTAS) __launch_bounds__(AD_THREADS)
     const bool live = !a.active || a.active[b];
     const int pos = live ? a.pos[b] : -1;
     const bool ok = live && pos >= 0 && pos < a.ctx;  // the host rejects bad positions before launch
+    if (live && !ok && rank == 0 && tid == 0) check_fail(CHK_POSITION);
     const int nkeys = ok ? pos + 1 : 0;
     const int per = ((nkeys + AC_CTAS - 1) / AC_CTAS + 15) / 16 * 16;  // <= per_max
     const int j0 = min(nkeys, rank * per), j1 = min(nkeys, j0 + per);
@@ -685,7 +696,10 @@ __global__ void attn_combine_kernel(AttnDecodeArgs a, int max_splits) {
     const int b = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
     if (a.active && !a.active[b]) return;
     const int pos = a.pos[b];
-    if (pos < 0 || pos >= a.ctx) return;
+    if (pos < 0 || pos >= a.ctx) {
+        if (threadIdx.x == 0) check_fail(CHK_POSITION);
+        return;
+    }
     const int nsplit = (pos + a.split) / a.split;
     if (nsplit <= 1 || d >= a.dh) return;
     pdl_wait();
@@ -720,7 +734,10 @@ __global__ void __launch_bounds__(ACW_THREADS) attn_combine_wide_kernel(AttnDeco
     const int b = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
     if (a.active && !a.active[b]) return;
     const int pos = a.pos[b];
-    if (pos < 0 || pos >= a.ctx) return;
+    if (pos < 0 || pos >= a.ctx) {
+        if (threadIdx.x == 0) check_fail(CHK_POSITION);
+        return;
+    }
     const int nsplit = (pos + a.split) / a.split;
     if (nsplit <= 1) return;
     pdl_wait();
@@ -845,6 +862,10 @@ __global__ void __launch_bounds__(ROWS * 32) attn_prefill_kernel(
     const bool valid = r < len;
     const int nk = valid ? start[sq] + r + 1 : 0;
     const int nk_blk = start[sq] + min(r0 + ROWS, len);  // keys some row of the block needs
+    if (kChecked && (r0 < 0 || r0 >= len || start[sq] < 0 || nk_blk > kmax)) {  // uniform over the CTA
+        if (threadIdx.x == 0) check_fail(CHK_TABLE);
+        return;
+    }
     const size_t row = (size_t)(cu[sq] + (valid ? r : 0));
     float* qw = qsh + warp * DH;
     float* scw = sc + (size_t)warp * kmax;

@@ -230,6 +230,7 @@ __global__ void __launch_bounds__(256) embed_fm_kernel(const uint32_t* __restric
     for (int i = 0; i < 4; ++i) {
         int m = m0 + ty + 8 * i, k = k0 + tx;
         uint32_t t = m < M ? tok[m] : 0u;
+        if (kChecked && m < M && k == 0 && t >= (uint32_t)vocab) check_fail(CHK_TOKEN);
         tile[ty + 8 * i][tx] = (m < M && k < K && t < (uint32_t)vocab) ? wte[(size_t)t * K + k] : 0.0f;
     }
     __syncthreads();

@@ -200,7 +200,10 @@ __global__ void mark_seen_kernel(const uint32_t* __restrict__ tok, const int32_t
     const int r = blockIdx.x * blockDim.x + threadIdx.x;
     if (r >= rows) return;
     const uint32_t t = tok[r];
-    if (t >= (uint32_t)words * 32u) return;
+    if (t >= (uint32_t)words * 32u) {
+        check_fail(CHK_TOKEN);
+        return;
+    }
     atomicOr(seen + (size_t)row_seq[r] * words + (t >> 5), 1u << (t & 31));
 }
 
@@ -214,7 +217,12 @@ __global__ void gather_cols_kernel(const float* __restrict__ src, int lds, const
     const int j = blockIdx.x * blockDim.x + threadIdx.x;
     const int k = blockIdx.y;
     if (j >= n || k >= K) return;
-    dst[(size_t)k * ldd + dcol[j]] = src[(size_t)k * lds + scol[j]];
+    const int dc = dcol[j], sc = scol[j];
+    if (kChecked && (dc < 0 || dc >= ldd || sc < 0 || sc >= lds)) {
+        check_fail(CHK_COLUMN);
+        return;
+    }
+    dst[(size_t)k * ldd + dc] = src[(size_t)k * lds + sc];
 }
 
 }  // namespace

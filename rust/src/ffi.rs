@@ -50,6 +50,12 @@ pub const KRK_PROF_CLASSES: c_int = 9;
 
 pub const KRK_ATTN_NOALLOC_MAX_FLOATS: usize = 1 << 20;
 
+// krk_check_status bits (checked builds)
+pub const KRK_CHECK_TOKEN: u32 = 1;
+pub const KRK_CHECK_POSITION: u32 = 2;
+pub const KRK_CHECK_TABLE: u32 = 4;
+pub const KRK_CHECK_COLUMN: u32 = 8;
+
 #[repr(C)]
 pub struct krk_model {
     _private: [u8; 0],
@@ -90,6 +96,8 @@ extern "C" {
     pub fn krk_state_export(state: *const krk_state, seq: c_int, layer: c_int, what: c_int, out: *mut c_float,
                             n: i64) -> c_int;
     pub fn krk_launch_count(count: *mut u64) -> c_int;
+    pub fn krk_checked_build() -> c_int;
+    pub fn krk_check_status(bits: *mut u32, clear: c_int) -> c_int;
     pub fn krk_state_set_decode_streams(state: *mut krk_state, n: c_int) -> c_int;
     pub fn krk_state_set_step_graphs(state: *mut krk_state, enable: c_int) -> c_int;
     pub fn krk_state_profile(state: *mut krk_state, enable: c_int) -> c_int;

@@ -32,6 +32,19 @@ def test_library_exports_every_declared_symbol():
     assert set(_lib.EXPORTED) >= set(_declared())
 
 
+def test_checked_build_exports_the_same_symbols_and_says_so():
+    """The checked build (make CHECKED=1) exports every declared entry point and
+    reports itself as checked; the default build reports 0 and no check bits."""
+    assert lib.krk_checked_build() == (1 if _lib.CHECKED else 0)
+    bits = C.c_uint32(123)
+    assert lib.krk_check_status(C.byref(bits), 1) == _lib.OK and bits.value == 0
+    path = os.path.join(ROOT, "krikil_rs_b200", "lib", "libkrikil_cuda_checked.so")
+    chk = C.CDLL(path)
+    for name in _declared():
+        assert hasattr(chk, name), name
+    assert chk.krk_checked_build() == 1
+
+
 def test_abi_version_and_status_strings():
     assert lib.krk_abi_version() == 1
     assert lib.krk_status_string(_lib.BAD_TOKEN) == b"token id exceeds vocab size"
