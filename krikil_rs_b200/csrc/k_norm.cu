@@ -28,32 +28,18 @@ namespace {
 // Feature-major RMSNorm: out[k][m] = x[k][m] * scale(m) * w[k].
 //
 // One CTA owns 8 columns (sequences).  The [K][8] column block is staged into
-// shared memory with cp.async in NORM_CHUNKS row chunks (each its own commit
-// group), and thread m forms column m's sum of squares in exactly the
-// reference's order -- x[k][m]^2 added for k = 0..K-1 one after the other
-// (src/math.rs:45-48), a latency-bound chain, hence few columns per CTA and
-// many CTAs -- chunk by chunk as the chunks land, so the chain overlaps the
-// loads.  Then all threads write the normalised block (x * scale) * w
-// (src/math.rs:51-53).  K <= 1216.
+// shared memory with cp.async; then each column's sum of squares
+// (src/math.rs:45-48) is formed as 32 partials -- partial p adds x[k][c]^2 for
+// k = p, p + 32, ... in order -- folded by warp shuffles and then across the
+// eight warps in warp order, and all threads write the normalised block
+// (x * scale) * w (src/math.rs:51-53).  The sum is
+// the reference's up to the order of its additions (the reference adds the
+// squares one after the other), so results agree within rounding; the order
+// is fixed, so they do not depend on the batch, the part or the CTA.  K <= 1216.
 // ---------------------------------------------------------------------------
 constexpr int NORM_COLS = 8;
 constexpr int NORM_MAXK = 1216;
-constexpr int NORM_CHUNKS = 8;
 constexpr int NORM_WS_MAX_COLS = 128;  // up to this many columns the weights are staged
-
-// cp.async.wait_group with a run-time count n in [0, NORM_CHUNKS).
-KRK_DEV void cp_async_wait_upto(int n) {
-    switch (n) {
-        case 0: cp_async_wait<0>(); break;
-        case 1: cp_async_wait<1>(); break;
-        case 2: cp_async_wait<2>(); break;
-        case 3: cp_async_wait<3>(); break;
-        case 4: cp_async_wait<4>(); break;
-        case 5: cp_async_wait<5>(); break;
-        case 6: cp_async_wait<6>(); break;
-        default: cp_async_wait<7>(); break;
-    }
-}
 
 // WS (few columns, where the kernel's latency is the whole cost): the weights
 // are staged in shared memory while the column block is in flight, instead of
@@ -63,21 +49,19 @@ __global__ void __launch_bounds__(256) rmsnorm_fm_kernel(const float* __restrict
                                                          const float* __restrict__ w, float eps, int K, int M,
                                                          float* __restrict__ out, int ldo) {
     extern __shared__ __align__(16) float blk[];  // [K][NORM_COLS], then (WS) w [K]
-    __shared__ float scale_s[NORM_COLS];
+    __shared__ __align__(16) float scale_s[NORM_COLS];
+    __shared__ float part_s[8 * NORM_COLS];  // [warp][column] partial sums of squares
     float* ws = blk + (size_t)K * NORM_COLS;
     const int tid = threadIdx.x;
     const int m0 = blockIdx.x * NORM_COLS;
     const int ncols = min(NORM_COLS, M - m0);
     const bool full = (ncols == NORM_COLS) && ((ldx & 3) == 0) && ((((uintptr_t)x) & 15) == 0);
-    const int kc = (K + NORM_CHUNKS - 1) / NORM_CHUNKS;  // rows per chunk
+    // the weights travel with the block when both are 16-byte pieces
+    const bool wasync = WS && (K & 3) == 0 && (((uintptr_t)w) & 15) == 0;
     if (full) {
-        for (int c = 0; c < NORM_CHUNKS; ++c) {
-            const int k0 = c * kc, nk = max(0, min(K, k0 + kc) - k0);
-            for (int i = tid; i < nk * (NORM_COLS / 4); i += 256) {
-                const int k = k0 + i / (NORM_COLS / 4), c4 = i % (NORM_COLS / 4);
-                cp_async16(blk + k * NORM_COLS + c4 * 4, x + (size_t)k * ldx + m0 + c4 * 4);
-            }
-            cp_async_commit();
+        for (int i = tid; i < K * (NORM_COLS / 4); i += 256) {
+            const int k = i / (NORM_COLS / 4), c4 = i % (NORM_COLS / 4);
+            cp_async16(blk + k * NORM_COLS + c4 * 4, x + (size_t)k * ldx + m0 + c4 * 4);
         }
     } else {
         for (int i = tid; i < K * NORM_COLS; i += 256) {
@@ -85,36 +69,51 @@ __global__ void __launch_bounds__(256) rmsnorm_fm_kernel(const float* __restrict
             blk[i] = c < ncols ? x[(size_t)k * ldx + m0 + c] : 0.0f;
         }
     }
-    if (WS)
+    if (wasync) {
+        for (int i = tid; i < K / 4; i += 256) cp_async16(ws + 4 * i, w + 4 * i);
+    } else if (WS) {
         for (int k = tid; k < K; k += 256) ws[k] = w[k];
-    float ss = 0.0f;
-    for (int c = 0; c < NORM_CHUNKS; ++c) {
-        if (full) cp_async_wait_upto(NORM_CHUNKS - 1 - c);
-        __syncthreads();  // chunk c visible to the summing threads
+    }
+    cp_async_commit();
+    cp_async_wait<0>();
+    __syncthreads();  // the block is visible to every warp
+    {
+        // thread t sums column t % 8 over rows k = t / 8 (mod 32): each warp
+        // load is 4 whole rows (32 consecutive words, no bank conflict)
+        static_assert(NORM_COLS == 8, "8 columns per CTA");
+        const int col = tid & 7, lane = tid & 31, warp = tid >> 5;
+        float ss = 0.0f;
+        for (int k = tid >> 3; k < K; k += 32) {
+            const float v = blk[k * NORM_COLS + col];
+            ss += v * v;
+        }
+        ss += __shfl_xor_sync(0xffffffffu, ss, 8);  // the warp's 4 lanes of this column
+        ss += __shfl_xor_sync(0xffffffffu, ss, 16);
+        if (lane < NORM_COLS) part_s[warp * NORM_COLS + lane] = ss;
+        __syncthreads();
         if (tid < NORM_COLS) {
-            const int k1 = min(K, (c + 1) * kc);
-#pragma unroll 8
-            for (int k = c * kc; k < k1; ++k) {
-                const float v = blk[k * NORM_COLS + tid];
-                ss += v * v;
-            }
+            float t = part_s[tid];
+            for (int w8 = 1; w8 < 8; ++w8) t += part_s[w8 * NORM_COLS + tid];
+            scale_s[tid] = 1.0f / sqrtf(t / (float)K + eps);
         }
     }
-    if (tid < NORM_COLS) {
-        float mean = ss / (float)K;
-        scale_s[tid] = 1.0f / sqrtf(mean + eps);
-    }
     __syncthreads();
-    const int c = tid % NORM_COLS;
-    if (c < ncols) {
-        const float sc = scale_s[c];
-        if (WS) {
-#pragma unroll 4
+    const bool vec = ncols == NORM_COLS && (ldo & 3) == 0 && (((uintptr_t)out) & 15) == 0;
+    if (vec) {  // thread t writes columns 4(t%2) .. 4(t%2)+3 of rows t/2, t/2 + 128, ...
+        const int c4 = (tid & 1) * 4;
+        const float4 sc = *reinterpret_cast<const float4*>(scale_s + c4);
+        for (int k = tid >> 1; k < K; k += 128) {
+            const float4 v = *reinterpret_cast<const float4*>(blk + k * NORM_COLS + c4);
+            const float wk = WS ? ws[k] : w[k];
+            *reinterpret_cast<float4*>(out + (size_t)k * ldo + m0 + c4) =
+                make_float4(v.x * sc.x * wk, v.y * sc.y * wk, v.z * sc.z * wk, v.w * sc.w * wk);
+        }
+    } else {
+        const int c = tid % NORM_COLS;
+        if (c < ncols) {
+            const float sc = scale_s[c];
             for (int k = tid / NORM_COLS; k < K; k += 256 / NORM_COLS)
-                out[(size_t)k * ldo + m0 + c] = blk[k * NORM_COLS + c] * sc * ws[k];
-        } else {
-            for (int k = tid / NORM_COLS; k < K; k += 256 / NORM_COLS)
-                out[(size_t)k * ldo + m0 + c] = blk[k * NORM_COLS + c] * sc * w[k];
+                out[(size_t)k * ldo + m0 + c] = blk[k * NORM_COLS + c] * sc * (WS ? ws[k] : w[k]);
         }
     }
 }

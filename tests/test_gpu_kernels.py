@@ -1,6 +1,6 @@
 """Per-kernel parity of the CUDA library (through its C ABI) against the CPU
-oracle, on seeded inputs.  Tolerances are written per test; projections and the
-feature-major RMSNorm are bit-exact by construction."""
+oracle, on seeded inputs.  Tolerances are written per test; the projections
+are bit-exact by construction."""
 import numpy as np
 import pytest
 
@@ -68,15 +68,23 @@ def test_gemm_rejects_bad_shapes():
 
 
 # ------------------------------------------------------------- norms
-@pytest.mark.parametrize("kdim,m,ld", [(608, 64, 64), (1216, 37, 64), (608, 1, 64), (608, 1024, 1024)])
-def test_rmsnorm_feature_major_bit_exact(kdim, m, ld):
+@pytest.mark.parametrize("kdim,m,ld", [(608, 64, 64), (1216, 37, 64), (608, 1, 64), (608, 1024, 1024),
+                                       (100, 13, 16)])
+def test_rmsnorm_feature_major(kdim, m, ld):
+    """The sum of squares runs as 32 ordered partials and a fixed tree instead
+    of the reference's one sequential chain: the same to within a few ulps of
+    the scale (relative 2e-6 here), and identical for a column whatever its
+    batch or position in the block."""
     rng = np.random.default_rng(kdim + m)
-    x = rng.standard_normal((ld, kdim)).astype(np.float32)
+    x = (rng.standard_normal((ld, kdim)) * rng.uniform(0.1, 3.0, (ld, 1))).astype(np.float32)
     w = (1 + 0.1 * rng.standard_normal(kdim)).astype(np.float32)
     eps = 1e-6 if kdim == 608 else 1e-5
     out = np_(K.rmsnorm_fm(cu(x.T.copy()), cu(w), eps, m))
     for col in range(m):
-        np.testing.assert_array_equal(out[:, col], O.rms_norm(x[col], w, eps))
+        np.testing.assert_allclose(out[:, col], O.rms_norm(x[col], w, eps), rtol=2e-6, atol=1e-7)
+    # a column's result does not depend on the rest of its block or batch
+    alone = np_(K.rmsnorm_fm(cu(x[m - 1:m].T.copy()), cu(w), eps, 1))
+    np.testing.assert_array_equal(alone[:, 0], out[:, m - 1])
 
 
 def test_rmsnorm_rows():
