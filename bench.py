@@ -523,7 +523,8 @@ def run_ours(args):
                      "note": "per-launch rate while the other decode parts' kernels share the GPU; "
                              "see single_stream for the same kernel without them",
                      "algorithmic_bytes_per_launch": int(ssd_bytes / max(ssd_n, 1)),
-                     "launches": ssd_n, "avg_launch_us": round(ssd_ms * 1e3 / max(ssd_n, 1), 2)},
+                     "launches": ssd_n, "avg_launch_us": round(ssd_ms * 1e3 / max(ssd_n, 1), 2),
+                     "frac_single_stream": None},
         "roofline_call": {"what": "whole generate call against its HBM floor (SSD state r+w of every decode "
                                   "step, decode K/V reads)",
                           "bytes": int(call_bytes), "ms": round(call_ms, 2),
@@ -544,6 +545,7 @@ def run_ours(args):
         "gpu_launches": launches,
         "clocks": clk,
     }
+    line["roofline"]["frac_single_stream"] = line["single_stream"]["ssd_step"]["frac"]
     if world == 1:
         if not args.no_c1:
             line["c1"] = c1_line(args, model, peak)
