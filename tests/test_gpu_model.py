@@ -197,6 +197,30 @@ def test_c5_benchmark_call_streams_match_oracle():
     gpu.close()
 
 
+def test_state_reuse_across_calls_of_growing_size(models):
+    """One state serves generation calls whose prompts grow from a few tokens to
+    several hundred (the pinned host tables, their device copy and the prompt
+    buffer grow between calls) with a prefill and steps in between; every call
+    gives exactly the tokens of the same call on a fresh state."""
+    gpu, _ = models
+    rng = np.random.default_rng(21)
+    st = PebbleState(gpu, 1024, batch=6)
+    for n_lo, n_hi, new in ((1, 6, 12), (200, 500, 9), (30, 90, 20)):
+        prompts = [rng.integers(0, 2048, int(n)).astype(np.uint32).tolist() for n in rng.integers(n_lo, n_hi, 6)]
+        got = gpu.generate_greedy(prompts, st, new, repetition_penalty=1.2, stop_at_eos=False)
+        fresh = PebbleState(gpu, 1024, batch=6)
+        assert got == gpu.generate_greedy(prompts, fresh, new, repetition_penalty=1.2, stop_at_eos=False)
+        fresh.close()
+        # the plain API on the same state afterwards: continues from the generated positions
+        pos = st.positions.copy()
+        lg = gpu.step_batch([5, 6, 7, 8, 9, 10], st)
+        assert np.all(st.positions == pos + 1) and lg.shape == (6, 2048)
+    st.reset()
+    lg = gpu.prefill_batch([[1, 2, 3]] * 6, st)
+    fresh = PebbleState(gpu, 1024, batch=6)
+    np.testing.assert_array_equal(lg, gpu.prefill_batch([[1, 2, 3]] * 6, fresh))
+
+
 def test_large_batch_halves_match_single_sequences(models):
     """A batch of 256+ sequences decodes as two halves on two streams; every
     sequence's logits equal (bitwise) those of the same sequence run alone, on
