@@ -129,10 +129,13 @@ __device__ unsigned g_check_word;  // one per translation unit (each is its own 
 KRK_DEV void check_fail(unsigned bit) { atomicOr(&g_check_word, bit); }
 unsigned read_check_word(bool clear) {
     unsigned v = 0;
-    if (cudaMemcpyFromSymbol(&v, g_check_word, sizeof v) != cudaSuccess) return 0;
+    if (cudaMemcpyFromSymbol(&v, g_check_word, sizeof v) != cudaSuccess) {
+        cudaGetLastError();  // leave no error behind for an unrelated later check
+        return 0;
+    }
     if (clear && v) {
         const unsigned z = 0;
-        cudaMemcpyToSymbol(g_check_word, &z, sizeof z);
+        if (cudaMemcpyToSymbol(g_check_word, &z, sizeof z) != cudaSuccess) cudaGetLastError();
     }
     return v;
 }

@@ -19,6 +19,7 @@ cudaError_t DeviceOnce::set_smem(const void* func, size_t bytes) {
     if (__atomic_load_n(&mask, __ATOMIC_ACQUIRE) & bit) return cudaSuccess;
     e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
     if (e == cudaSuccess) __atomic_fetch_or(&mask, bit, __ATOMIC_RELEASE);
+    else cudaGetLastError();  // reported here: not again by a later launch's error check
     return e;
 }
 
