@@ -314,7 +314,7 @@ def kernel_table(torch, peak, scan_t=2048):
     out = torch.empty_like(q)
     nb = int(sum((int(p) + 1) * 8 * 64 * 4 * 2 for p in pos) + 64 * 8 * 64 * 4 * 6)
     ms = {sp: timeit(lambda: K.rope_kv_attn_decode(q, k, v, kc, vc, posd, split=sp, work=work, out=out))
-          for sp in (0, 64, 128, 256)}  # 0: the cluster kernel (one launch, no scratch)
+          for sp in (0, 64, 128, 256, 384, 512)}  # 0: the cluster kernel (one launch, no scratch)
     best = min(ms, key=ms.get)
     put("rope_kv_attn_decode[64,8,2048,64]", nb, ms[best],
         {"split": best, "ms_by_split": {str(k): round(v, 4) for k, v in ms.items()}})

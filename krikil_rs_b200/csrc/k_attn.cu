@@ -689,6 +689,8 @@ __global__ void __cluster_dims__(1, 1, AC_CTAS) __launch_bounds__(AD_THREADS)
     cluster.sync();  // CTA 0 has read every partial: shared memory may go
 }
 
+constexpr int ACW_MIN_SPLITS = 9;  // the wide merge from this many splits per sequence on
+
 // Merges the per-split (max, sum, unnormalised out) partials of one (b, h).
 // Launched as a programmatic dependent of the split kernel: it reads the
 // positions while that kernel drains, then waits for its partials.
@@ -703,15 +705,28 @@ __global__ void attn_combine_kernel(AttnDecodeArgs a, int max_splits) {
     const int nsplit = (pos + a.split) / a.split;
     if (nsplit <= 1 || d >= a.dh) return;
     pdl_wait();
+    // Fewer than ACW_MIN_SPLITS splits here: every partial this thread needs
+    // is requested at once (one round trip), then merged in split order.
     const float* wp = a.work + ((size_t)b * a.H + h) * max_splits * (a.dh + 2);
-    float m = -INFINITY;
-    for (int c = 0; c < nsplit; ++c) m = fmaxf(m, wp[c * (a.dh + 2) + a.dh]);
-    float l = 0.0f, o = 0.0f;
-    for (int c = 0; c < nsplit; ++c) {
+    float mc[ACW_MIN_SPLITS - 1], lc[ACW_MIN_SPLITS - 1], oc[ACW_MIN_SPLITS - 1];
+#pragma unroll
+    for (int c = 0; c < ACW_MIN_SPLITS - 1; ++c) {
         const float* p = wp + c * (a.dh + 2);
-        const float e = expf(p[a.dh] - m);
-        l = l + p[a.dh + 1] * e;
-        o = o + p[d] * e;
+        mc[c] = c < nsplit ? p[a.dh] : -INFINITY;
+        lc[c] = c < nsplit ? p[a.dh + 1] : 0.0f;
+        oc[c] = c < nsplit ? p[d] : 0.0f;
+    }
+    float m = -INFINITY;
+#pragma unroll
+    for (int c = 0; c < ACW_MIN_SPLITS - 1; ++c) m = fmaxf(m, mc[c]);
+    float l = 0.0f, o = 0.0f;
+#pragma unroll
+    for (int c = 0; c < ACW_MIN_SPLITS - 1; ++c) {
+        if (c < nsplit) {
+            const float e = expf(mc[c] - m);
+            l = l + lc[c] * e;
+            o = o + oc[c] * e;
+        }
     }
     a.out[(size_t)b * a.o_sb + (size_t)h * a.o_sh + (size_t)d * a.o_sd] = o * (1.0f / l);
 }
@@ -722,7 +737,6 @@ __global__ void attn_combine_kernel(AttnDecodeArgs a, int max_splits) {
 // thread per dim and group -- so it costs a few memory latencies however many
 // splits there are.  Also a programmatic dependent of the split kernel.
 constexpr int ACW_THREADS = 256;
-constexpr int ACW_MIN_SPLITS = 9;  // from this many splits per sequence on
 
 size_t acw_smem_bytes(int max_splits, int dh) {
     return sizeof(float) * (2 * (size_t)max_splits + (size_t)(ACW_THREADS / dh) * dh);

@@ -231,7 +231,7 @@ def test_rope_kv_attn_decode_full_size(split):
         np.testing.assert_array_equal(gk[b, :, : pos[b]], kc[b, :, : pos[b]])  # history untouched
 
 
-@pytest.mark.parametrize("split", [0, 64, 128])
+@pytest.mark.parametrize("split", [0, 64, 128, 256])
 @pytest.mark.parametrize("dh,ctx,posv", [(76, 16, [0, 15, 7]), (64, 300, [0, 63, 64, 299]), (76, 700, [699, 1, 256]),
                                          (64, 200, [15, 16, 17, 47, 48, 127, 128, 199]),
                                          (76, 200, [15, 16, 31, 32, 63, 64, 65, 191]),
