@@ -213,7 +213,7 @@ def test_conv_ssd_scan_split_invariance_full_size():
 
 
 # ------------------------------------------------------------- attention
-@pytest.mark.parametrize("split", [0, 64, 128, 256, 2048])
+@pytest.mark.parametrize("split", [0, 64, 128, 256, 512, 2048])
 def test_rope_kv_attn_decode_full_size(split):
     """Config: q,k,v [64,8,1,64], positions ~U[0,2048), cache [64,8,2048,64].
     split 0 is the cluster kernel (eight CTAs per sequence and head merged in
@@ -258,7 +258,8 @@ def test_rope_kv_attn_decode_edges(dh, ctx, posv, split):
     np.testing.assert_array_equal(np_(g_vc), o_vc)
 
 
-@pytest.mark.parametrize("split,ctx", [(64, 2048), (128, 700), (256, 2048), (64, 64 * 65)])
+@pytest.mark.parametrize("split,ctx", [(64, 2048), (128, 700), (256, 2048), (512, 2048), (384, 2000),
+                                       (64, 64 * 65)])
 def test_rope_kv_attn_decode_split_merge(split, ctx):
     """Split partials through the work buffer, up to 65 splits: the buffer
     starts as garbage and is reused across calls with other positions; every
