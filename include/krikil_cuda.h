@@ -99,7 +99,8 @@ KRK_API int krk_model_stream(const krk_model* model, void** stream);
 /* PebbleState::new(&config, max_ctx) (src/model.rs:204-219), for `batch`
  * independent sequences: per sequence 6 Mamba layers of conv [1472][4] and SSD
  * [19][64][128] state, 2 attention layers of K/V caches [max_ctx][608], all in
- * device memory and zeroed. */
+ * device memory and zeroed.  batch and max_ctx are at most 883,008 (a full-context
+ * prefill is one projection over that many rows, indexed with 32-bit offsets). */
 KRK_API int krk_state_create(const krk_model* model, int batch, int max_ctx, krk_state** out);
 KRK_API int krk_state_free(krk_state* state);
 /* PebbleState::reset (src/model.rs:221-229) for the sequences whose mask byte
@@ -264,7 +265,8 @@ KRK_API int krk_k_gated_rmsnorm_residual(const float* x, const float* z, const f
  * Wt: W K-major [K][ldw]; C batch-major [M][ldc] (out_fm = 0) or
  * feature-major [N][ldc] (out_fm = 1).  epilogue 0: store, 1: C += result
  * (residual), 2: store gelu(result) (src/math.rs:17-39).  M % 32 == 0,
- * N % 32 == 0, K % 32 == 0, leading dims % 4 == 0, pointers 16-byte aligned. */
+ * N % 32 == 0, K % 32 == 0, leading dims % 4 == 0, pointers 16-byte aligned,
+ * K * lda and K * ldw below 2^31 (KRK_INVALID otherwise). */
 KRK_API int krk_k_gemm(const float* At, int lda, const float* Wt, int ldw, float* C, int ldc, int M, int N, int K,
                        int epilogue, int out_fm, void* stream);
 

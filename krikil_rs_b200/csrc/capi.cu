@@ -38,6 +38,9 @@ constexpr int QKV = 3 * HID;
 constexpr float RMS_EPS = 1e-6f, MNORM_EPS = 1e-5f, THETA = 10000.0f;
 constexpr int SEEN_WORDS = VOC / 32;
 constexpr int64_t PREFILL_GROUP_TOKENS = 16384;
+// Largest multiple of 64 rows whose widest projection operand ([INTER][rows])
+// stays below 2^31 elements.
+constexpr int64_t MAX_ROWS = ((int64_t(1) << 31) - 1) / INTER / 64 * 64;
 constexpr int PREFILL_STREAMS = 3;  // prefill groups in flight at once, each on its own stream
 
 // Column offsets inside one in_proj output row: z | x | B | C | dt (src/model.rs:638-640, :656-658).
@@ -1158,6 +1161,10 @@ int krk_state_create(const krk_model* m, int batch, int max_ctx, krk_state** out
     return guarded([&]() -> int {
         if (!m || !out) return fail(KRK_INVALID, "null model or output handle");
         if (batch <= 0 || max_ctx <= 0) return fail(KRK_INVALID, "batch and max_ctx must be positive");
+        // A prefill of one full context is one projection over round_up(max_ctx, 64)
+        // rows, whose operands the GEMM indexes with 32-bit offsets.
+        if (round_up(max_ctx, 64) * INTER >= (int64_t(1) << 31) || round_up(batch, 64) * INTER >= (int64_t(1) << 31))
+            return fail(KRK_INVALID, "max_ctx and batch must be at most " + std::to_string(MAX_ROWS));
         *out = nullptr;
         DeviceGuard g(m->device);
         std::unique_ptr<krk_state> s(new krk_state());

@@ -73,19 +73,21 @@ __global__ void __launch_bounds__(NT, Tile<BM>::MIN_CTAS)
     const int nkb = K / BK;
 
     float* ring = sm + warp * (WSTAGE * T::WST);
-    // This warp's rows k0 + warp + 8i (i < 4) of the K-block into ring slot st.
-    auto load_stage = [&](int kb, int st) {
-        float* As = ring + st * T::WST;
-        float* Ws = As + WROWS * BM;
-        const int k0 = kb * BK + warp;
+    // Element offsets of this lane's copy sources (rows k = warp + 8r of the
+    // next K-block), advanced by BK rows per stage: one integer add per operand
+    // instead of a wide multiply per copy.  The host keeps A^T and W^T below
+    // 2^31 elements, so the 32-bit offsets cannot wrap.
+    constexpr int AR = 32 / (BM / 4);  // A rows covered by one pass of the 32 lanes
+    unsigned a_off = (unsigned)(warp + 8 * (lane / (BM / 4))) * lda + m0 + (lane % (BM / 4)) * 4;
+    unsigned w_off = (unsigned)(warp + 8 * (lane >> 3)) * ldw + n0 + (lane & 7) * 4;
+    // This warp's four rows of the next K-block into the ring slot at As.
+    auto load_stage = [&](float* As) {
 #pragma unroll
-        for (int j = 0; j < T::A_F4; ++j) {
-            const int idx = lane + 32 * j;
-            const int r = idx / (BM / 4), c4 = idx % (BM / 4);
-            cp_async16(As + r * BM + c4 * 4, At + (size_t)(k0 + 8 * r) * lda + m0 + c4 * 4);
-        }
-        const int r = lane >> 3, c4 = lane & 7;
-        cp_async16(Ws + r * BN + c4 * 4, Wt + (size_t)(k0 + 8 * r) * ldw + n0 + c4 * 4);
+        for (int j = 0; j < T::A_F4; ++j)
+            cp_async16(As + (lane / (BM / 4) + j * AR) * BM + (lane % (BM / 4)) * 4, At + a_off + j * (8 * AR) * lda);
+        cp_async16(As + WROWS * BM + (lane >> 3) * BN + (lane & 7) * 4, Wt + w_off);
+        a_off += BK * lda;
+        w_off += BK * ldw;
     };
 
     // Partial sums in pairs, one __ffma2_rn per pair.  Batch-major output pairs
@@ -97,9 +99,10 @@ __global__ void __launch_bounds__(NT, Tile<BM>::MIN_CTAS)
 #pragma unroll
     for (int i = 0; i < TM * 4; ++i) acc2[i] = make_float2(0.0f, 0.0f);
 
+    int wr = (WSTAGE - 1) * T::WST, rd = 0;  // ring offsets of the slot filled next and the slot read next
 #pragma unroll
     for (int s = 0; s < WSTAGE - 1; ++s) {
-        if (s < nkb) load_stage(s, s);
+        if (s < nkb) load_stage(ring + s * T::WST);
         cp_async_commit();
     }
     for (int kb = 0; kb < nkb; ++kb) {
@@ -107,11 +110,12 @@ __global__ void __launch_bounds__(NT, Tile<BM>::MIN_CTAS)
         // All lanes' copies of slot kb are visible, and every lane is done
         // reading the slot refilled next (consumed in iteration kb - 1).
         __syncwarp();
-        const int pf = kb + WSTAGE - 1;
-        if (pf < nkb) load_stage(pf, pf % WSTAGE);
+        if (kb + WSTAGE - 1 < nkb) load_stage(ring + wr);
         cp_async_commit();
-        const float* As = ring + (kb % WSTAGE) * T::WST;
+        wr = wr == (WSTAGE - 1) * T::WST ? 0 : wr + T::WST;
+        const float* As = ring + rd;
         const float* Ws = As + WROWS * BM;
+        rd = rd == (WSTAGE - 1) * T::WST ? 0 : rd + T::WST;
 #pragma unroll
         for (int i = 0; i < WROWS; ++i) {  // k = kb*32 + warp + 8i: this warp's lane of the reference dot
             float a[TM];
@@ -304,6 +308,7 @@ cudaError_t gemm_tiled(const float* At, int lda, const float* Wt, int ldw, float
     if (tile_rows == 0) tile_rows = gemm_tile_rows(M, N);
     if (M <= 0 || N <= 0 || K <= 0 || (tile_rows != 32 && tile_rows != 64) || M % tile_rows || N % BN || K % BK ||
         lda % 4 || ldw % 4 || ldc % 4 || lda < M || ldw < N || ldc < (out_fm ? M : N) ||
+        (int64_t)K * lda >= (1ll << 31) || (int64_t)K * ldw >= (1ll << 31) ||
         ((uintptr_t)At | (uintptr_t)Wt | (uintptr_t)C) % 16)
         return cudaErrorInvalidValue;
     if (tile_rows == 32) return dispatch<32>(At, lda, Wt, ldw, C, ldc, M, N, K, epilogue, out_fm, s);
@@ -315,6 +320,7 @@ cudaError_t gemm_conv(const float* At, int lda, const float* Wt, int ldw, float*
     if (tile_rows == 0) tile_rows = gemm_tile_rows(M, N);
     if (M <= 0 || N <= 0 || K <= 0 || (tile_rows != 32 && tile_rows != 64) || M % tile_rows || N % BN || K % BK ||
         lda % 4 || ldw % 4 || ldc % 4 || lda < M || ldw < N || ldc < N || !cv.state || !cv.w || !cv.bias ||
+        (int64_t)K * lda >= (1ll << 31) || (int64_t)K * ldw >= (1ll << 31) ||
         cv.lo < 0 || cv.lo % BN || cv.hi % BN || cv.hi <= cv.lo || cv.hi > N || cv.rows < 0 || cv.rows > M ||
         ((uintptr_t)At | (uintptr_t)Wt | (uintptr_t)C | (uintptr_t)cv.state | (uintptr_t)cv.w) % 16)
         return cudaErrorInvalidValue;

@@ -123,3 +123,12 @@ def test_rng_seed_state_matches_oracle():
         st = np.zeros(10, np.uint32)
         assert lib.krk_rng_seed_state(seed, st.ctypes.data) == _lib.OK
         np.testing.assert_array_equal(st, O.Rng(seed).state)
+
+
+def test_gemm_refuses_operands_past_32bit_offsets():
+    """The projection indexes A^T and W^T with 32-bit element offsets, so
+    K * lda or K * ldw of 2^31 or more is refused before anything touches a
+    device (INVALID, where a launch on this machine would report CUDA)."""
+    p = 16  # 16-byte aligned placeholder: the size check comes first
+    assert lib.krk_k_gemm_tiled(p, 67108868, p, 32, p, 32, 32, 32, 32, 0, 0, 0, None) == _lib.INVALID
+    assert lib.krk_k_gemm_tiled(p, 32, p, 67108868, p, 32, 32, 32, 32, 0, 0, 0, None) == _lib.INVALID

@@ -61,6 +61,27 @@ def test_gemm_residual_and_gelu_epilogues(tile):
     np.testing.assert_allclose(g, gref, atol=1e-6, rtol=1e-5)
 
 
+@pytest.mark.parametrize("m,n,k", [(1024, 2720, 608), (2048, 608, 2432)])
+@pytest.mark.parametrize("tile", [32, 64])
+def test_gemm_many_waves_all_epilogues(m, n, k, tile):
+    """Decode shapes with several tiles per SM (1360-5440 tiles): every output
+    of every wave equals the reference dot, in both output layouts, and the
+    residual and GELU epilogues apply to every tile."""
+    rng = np.random.default_rng(m + n + k + tile)
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    w = (0.02 * rng.standard_normal((n, k))).astype(np.float32)
+    ref = O.gemm_transb(a, w)
+    at, wt = cu(a.T.copy()), cu(w.T.copy())
+    np.testing.assert_array_equal(np_(K.gemm(at, wt, 0, False, tile_rows=tile)), ref)
+    np.testing.assert_array_equal(np_(K.gemm(at, wt, 0, True, tile_rows=tile)).T, ref)
+    res = rng.standard_normal((n, m)).astype(np.float32)
+    c = cu(res.copy())
+    K.gemm(at, wt, 1, True, c, tile_rows=tile)
+    np.testing.assert_array_equal(np_(c), res + ref.T)
+    g = np_(K.gemm(at, wt, 2, False, tile_rows=tile))
+    np.testing.assert_allclose(g, np.vectorize(O.gelu, otypes=[np.float32])(ref), atol=1e-6, rtol=1e-5)
+
+
 def test_gemm_rejects_bad_shapes():
     from krikil_rs_b200._lib import KrikilError
     with pytest.raises(KrikilError):
