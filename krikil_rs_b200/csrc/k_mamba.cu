@@ -153,38 +153,44 @@ __global__ void conv_prefill4_kernel(const float* __restrict__ xin, int64_t x_rs
 }
 
 // ---------------------------------------------------------------------------
-// Prefill scan: one CTA per (sequence, head), 256 threads; warp w keeps state
-// columns n = 16w .. 16w+15 and lane l rows p = l and l + 32 in registers for
-// the whole sequence.  All lanes of a warp read the same 16-byte pieces of the
-// token's B and C rows, so those shared-memory loads are broadcasts (one
-// wavefront each), and the y partial of a row over the warp's 16 columns is a
-// per-lane FMA chain; the eight warps' partials meet in shared memory once per
-// chunk and are added in warp order.  Tokens are staged CH at a time in shared
-// memory (x, gate, B, C, dt, dA); y of the chunk is buffered and written
-// coalesced.  The state update uses one FMA per element
+// Prefill scan: one CTA per (sequence, head), 256 threads.  Warp w owns state
+// columns n = 16w .. 16w+15; lane l keeps rows p = 4(l/2) .. +3 of the column
+// half 8(l%2) .. +7 (32 elements) in registers for the whole sequence.  Per
+// token a lane reads its 8 B and 8 C values (16-byte loads at two addresses
+// per warp), its 4 x values (one 16-byte load) and the token's (dt, dA); the y
+// partial of a row over the lane's 8 columns is an FMA chain, the two halves
+// of the warp's 16 columns meet by one shuffle, and the eight warps' partials
+// meet in shared memory once per chunk and are added in warp order.  Tokens
+// are staged SCAN_CH at a time (x, silu(z), B, C, dt, dA); y of the chunk is
+// buffered and written coalesced.  The state update uses one FMA per element
 // (s = fma(s, dA, B*xdt)), issued as packed pairs (__fmul2_rn / __ffma2_rn
 // round each component like the scalar forms), so results agree with the
 // sequential reference within rounding.
-// CONV: conv + SiLU of the head's 64 x channels on a 3-slot state is applied
-// while staging, by threads 0..63, each owning one channel's window.
+// CONV: conv + SiLU of the head's 64 x channels (src/model.rs:399-410) from
+// the chunk's raw x and the 3 raw rows before it (the conv state, then the
+// previous chunk's last rows): each output needs only its own window, so all
+// threads compute the chunk's outputs at once, each with the reference's
+// expression.
 // ---------------------------------------------------------------------------
 constexpr int SCAN_CH = 16;
 constexpr int SCAN_YLD = SCAN_CH + 1;
 constexpr int SCAN_WARPS = 8;
-constexpr size_t SCAN_SMEM = sizeof(float) * (SCAN_CH * SSD_P * 2 + SCAN_CH * SSD_N * 2 + SCAN_CH * 2 +
-                                              SSD_P * SCAN_YLD + SCAN_CH * SCAN_WARPS * SSD_P);
+constexpr size_t SCAN_SMEM = sizeof(float) * (SCAN_CH * SSD_N * 2 + SCAN_CH * SSD_P * 3 + 3 * SSD_P +
+                                              SCAN_CH * 2 + SSD_P * SCAN_YLD + SCAN_CH * SCAN_WARPS * SSD_P);
 
 template <bool CONV, bool GATE>
 __global__ void __launch_bounds__(256, 3) ssd_scan_kernel(SsdScanArgs a) {
     extern __shared__ __align__(16) float sm[];
     float* sB = sm;                       // [CH][N]
     float* sC = sB + SCAN_CH * SSD_N;     // [CH][N]
-    float* sx = sC + SCAN_CH * SSD_N;     // [CH][P]
-    float* sg = sx + SCAN_CH * SSD_P;     // [CH][P]
-    float* sdt = sg + SCAN_CH * SSD_P;    // [CH]
-    float* sda = sdt + SCAN_CH;           // [CH]
-    float* sy = sda + SCAN_CH;            // [P][CH+1]
+    float* sxr = sC + SCAN_CH * SSD_N;    // [CH][P] x as staged
+    float* sxc = sxr + SCAN_CH * SSD_P;   // [CH][P] CONV: conv + SiLU of x
+    float* sg = sxc + SCAN_CH * SSD_P;    // [CH][P] silu(z)
+    float* xh = sg + SCAN_CH * SSD_P;     // [3][P] CONV: the raw x rows before the chunk, oldest first
+    float* sdd = xh + 3 * SSD_P;          // [CH][2] (dt, dA)
+    float* sy = sdd + 2 * SCAN_CH;        // [P][CH+1]
     float* syp = sy + SSD_P * SCAN_YLD;   // [CH][warps][P]: y partials over each warp's columns
+    const float* xs = CONV ? sxc : sxr;   // x as the scan reads it
 
     const int h = blockIdx.x, sq = blockIdx.y;  // heads of a sequence adjacent: B, C shared in L2
     const int tid = threadIdx.x, w = tid >> 5, l = tid & 31;
@@ -192,31 +198,34 @@ __global__ void __launch_bounds__(256, 3) ssd_scan_kernel(SsdScanArgs a) {
     const int r1 = a.cu_seqlens ? a.cu_seqlens[sq + 1] : (sq + 1) * a.uniform_len;
     const float dtb = a.dt_bias[h], an = a.a_neg[h], dsk = a.dsk[h];
     const int c0 = h * SSD_P;
+    const int row0 = 4 * (l >> 1), col0 = 16 * w + 8 * (l & 1);
 
-    // s[r][k]: row l + 32r, columns 16w + 2k, +1
-    float* st = a.ssm + (((size_t)sq * a.H + h) * SSD_P + l) * SSD_N + 16 * w;
-    float2 s[2][8];
+    // s[r][j]: row row0 + r, columns col0 + 2j, +1
+    float* st = a.ssm + (((size_t)sq * a.H + h) * SSD_P + row0) * SSD_N + col0;
+    float2 s[4][4];
 #pragma unroll
-    for (int r = 0; r < 2; ++r)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const float4 v = *reinterpret_cast<const float4*>(st + r * 32 * SSD_N + 4 * j);
-            s[r][2 * j] = make_float2(v.x, v.y);
-            s[r][2 * j + 1] = make_float2(v.z, v.w);
-        }
-    float cw0 = 0.f, cw1 = 0.f, cw2 = 0.f, cw3 = 0.f, cb = 0.f, w0 = 0.f, w1 = 0.f, w2 = 0.f;
+    for (int r = 0; r < 4; ++r) {
+        const float4 v0 = *reinterpret_cast<const float4*>(st + r * SSD_N);
+        const float4 v1 = *reinterpret_cast<const float4*>(st + r * SSD_N + 4);
+        s[r][0] = make_float2(v0.x, v0.y); s[r][1] = make_float2(v0.z, v0.w);
+        s[r][2] = make_float2(v1.x, v1.y); s[r][3] = make_float2(v1.z, v1.w);
+    }
+    // CONV: this thread's channel (tid % 64: the same for all its outputs)
+    float cw0 = 0.f, cw1 = 0.f, cw2 = 0.f, cw3 = 0.f, cb = 0.f;
     float* cst = nullptr;
-    if (CONV && tid < SSD_P) {
-        const int c = c0 + tid;
+    if (CONV) {
+        const int c = c0 + (tid & (SSD_P - 1));
         cst = a.conv_state + ((size_t)sq * a.H * SSD_P + c) * 3;
-        w0 = cst[0]; w1 = cst[1]; w2 = cst[2];
         cw0 = a.conv_w[c * 4]; cw1 = a.conv_w[c * 4 + 1]; cw2 = a.conv_w[c * 4 + 2]; cw3 = a.conv_w[c * 4 + 3];
         cb = a.conv_b[c];
+        if (tid < SSD_P) {
+            xh[tid] = cst[0]; xh[SSD_P + tid] = cst[1]; xh[2 * SSD_P + tid] = cst[2];
+        }
     }
 
     for (int base = r0; base < r1; base += SCAN_CH) {
         const int nt = min(SCAN_CH, r1 - base);
-        __syncthreads();
+        __syncthreads();  // the previous chunk is done with every buffer
         for (int i = tid; i < nt * (SSD_N / 4); i += 256) {
             const int t = i / (SSD_N / 4), c4 = i % (SSD_N / 4);
             const size_t row = (size_t)(base + t);
@@ -228,7 +237,7 @@ __global__ void __launch_bounds__(256, 3) ssd_scan_kernel(SsdScanArgs a) {
         for (int i = tid; i < nt * (SSD_P / 4); i += 256) {
             const int t = i / (SSD_P / 4), c4 = i % (SSD_P / 4);
             const size_t row = (size_t)(base + t);
-            *reinterpret_cast<float4*>(sx + t * SSD_P + c4 * 4) =
+            *reinterpret_cast<float4*>(sxr + t * SSD_P + c4 * 4) =
                 __ldg(reinterpret_cast<const float4*>(a.x + row * a.x_rs + c0 + c4 * 4));
             if (GATE) {
                 float4 zv = __ldg(reinterpret_cast<const float4*>(a.z + row * a.z_rs + c0 + c4 * 4));
@@ -238,49 +247,55 @@ __global__ void __launch_bounds__(256, 3) ssd_scan_kernel(SsdScanArgs a) {
         }
         if (tid < nt) {
             const float dtv = softplus(a.dt[(size_t)(base + tid) * a.dt_rs + h] + dtb);
-            sdt[tid] = dtv;
-            sda[tid] = expf(dtv * an);
+            sdd[2 * tid] = dtv;
+            sdd[2 * tid + 1] = expf(dtv * an);
         }
         __syncthreads();
         if (CONV) {
-            if (tid < SSD_P) {
-                for (int t = 0; t < nt; ++t) {
-                    const float xr = sx[t * SSD_P + tid];
-                    const float val = w0 * cw0 + w1 * cw1 + w2 * cw2 + xr * cw3 + cb;
-                    w0 = w1; w1 = w2; w2 = xr;
-                    sx[t * SSD_P + tid] = silu(val);
-                }
+            const int p = tid & (SSD_P - 1);
+            auto raw = [&](int j) { return j >= 0 ? sxr[j * SSD_P + p] : xh[(j + 3) * SSD_P + p]; };
+            for (int t = tid / SSD_P; t < nt; t += 256 / SSD_P) {
+                // the window [x(t-3), x(t-2), x(t-1), x(t)] of src/model.rs:399-410
+                const float val = raw(t - 3) * cw0 + raw(t - 2) * cw1 + raw(t - 1) * cw2 + raw(t) * cw3 + cb;
+                sxc[t * SSD_P + p] = silu(val);
             }
-            __syncthreads();
+            __syncthreads();  // every window read the old halo
+            if (tid < SSD_P) {  // the raw rows before the next chunk
+                const float n0 = raw(nt - 3), n1 = raw(nt - 2), n2 = raw(nt - 1);
+                xh[p] = n0; xh[SSD_P + p] = n1; xh[2 * SSD_P + p] = n2;
+            }
         }
         for (int t = 0; t < nt; ++t) {
-            const float dA = sda[t], dtv = sdt[t];
-            const float2 dA2 = make_float2(dA, dA);
-            const float* Bt = sB + t * SSD_N + 16 * w;
-            const float* Ct = sC + t * SSD_N + 16 * w;
-            float2 xdt[2], ya[2], yb[2];
+            const float2 dd = *reinterpret_cast<const float2*>(sdd + 2 * t);
+            const float2 dA2 = make_float2(dd.y, dd.y);
+            const float4 xv = *reinterpret_cast<const float4*>(xs + t * SSD_P + row0);
+            const float xr[4] = {xv.x, xv.y, xv.z, xv.w};
+            const float4 b0 = *reinterpret_cast<const float4*>(sB + t * SSD_N + col0);
+            const float4 b1 = *reinterpret_cast<const float4*>(sB + t * SSD_N + col0 + 4);
+            const float4 q0 = *reinterpret_cast<const float4*>(sC + t * SSD_N + col0);
+            const float4 q1 = *reinterpret_cast<const float4*>(sC + t * SSD_N + col0 + 4);
+            const float2 bp[4] = {make_float2(b0.x, b0.y), make_float2(b0.z, b0.w), make_float2(b1.x, b1.y),
+                                  make_float2(b1.z, b1.w)};
+            const float2 cp[4] = {make_float2(q0.x, q0.y), make_float2(q0.z, q0.w), make_float2(q1.x, q1.y),
+                                  make_float2(q1.z, q1.w)};
+            float part[4];
 #pragma unroll
-            for (int r = 0; r < 2; ++r) {
-                const float xd = sx[t * SSD_P + l + 32 * r] * dtv;
-                xdt[r] = make_float2(xd, xd);
-                ya[r] = make_float2(0.f, 0.f);
-                yb[r] = make_float2(0.f, 0.f);
-            }
+            for (int r = 0; r < 4; ++r) {
+                const float xd = xr[r] * dd.x;
+                const float2 xdt = make_float2(xd, xd);
+                float2 ya = make_float2(0.f, 0.f);
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const float4 bv = *reinterpret_cast<const float4*>(Bt + 4 * j);
-                const float4 cv = *reinterpret_cast<const float4*>(Ct + 4 * j);
-#pragma unroll
-                for (int r = 0; r < 2; ++r) {
-                    s[r][2 * j] = __ffma2_rn(s[r][2 * j], dA2, __fmul2_rn(make_float2(bv.x, bv.y), xdt[r]));
-                    s[r][2 * j + 1] = __ffma2_rn(s[r][2 * j + 1], dA2, __fmul2_rn(make_float2(bv.z, bv.w), xdt[r]));
-                    ya[r] = __ffma2_rn(s[r][2 * j], make_float2(cv.x, cv.y), ya[r]);
-                    yb[r] = __ffma2_rn(s[r][2 * j + 1], make_float2(cv.z, cv.w), yb[r]);
+                for (int j = 0; j < 4; ++j) {
+                    s[r][j] = __ffma2_rn(s[r][j], dA2, __fmul2_rn(bp[j], xdt));
+                    ya = __ffma2_rn(s[r][j], cp[j], ya);
                 }
+                part[r] = ya.x + ya.y;
             }
 #pragma unroll
-            for (int r = 0; r < 2; ++r)
-                syp[(t * SCAN_WARPS + w) * SSD_P + l + 32 * r] = (ya[r].x + ya[r].y) + (yb[r].x + yb[r].y);
+            for (int r = 0; r < 4; ++r) part[r] += __shfl_xor_sync(0xffffffffu, part[r], 1);
+            if ((l & 1) == 0)
+                *reinterpret_cast<float4*>(syp + (t * SCAN_WARPS + w) * SSD_P + row0) =
+                    make_float4(part[0], part[1], part[2], part[3]);
         }
         __syncthreads();
         for (int i = tid; i < nt * SSD_P; i += 256) {  // y of the chunk: the warps' partials in order
@@ -289,7 +304,7 @@ __global__ void __launch_bounds__(256, 3) ssd_scan_kernel(SsdScanArgs a) {
             float y = yp[0];
 #pragma unroll
             for (int ww = 1; ww < SCAN_WARPS; ++ww) y = y + yp[ww * SSD_P];
-            float yv = y + dsk * sx[t * SSD_P + p];
+            float yv = y + dsk * xs[t * SSD_P + p];
             if (GATE) yv = yv * sg[t * SSD_P + p];
             sy[p * SCAN_YLD + t] = yv;
         }
@@ -307,13 +322,15 @@ __global__ void __launch_bounds__(256, 3) ssd_scan_kernel(SsdScanArgs a) {
         }
     }
 #pragma unroll
-    for (int r = 0; r < 2; ++r)
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-            *reinterpret_cast<float4*>(st + r * 32 * SSD_N + 4 * j) =
-                make_float4(s[r][2 * j].x, s[r][2 * j].y, s[r][2 * j + 1].x, s[r][2 * j + 1].y);
-    if (CONV && tid < SSD_P) {
-        cst[0] = w0; cst[1] = w1; cst[2] = w2;
+    for (int r = 0; r < 4; ++r) {
+        *reinterpret_cast<float4*>(st + r * SSD_N) = make_float4(s[r][0].x, s[r][0].y, s[r][1].x, s[r][1].y);
+        *reinterpret_cast<float4*>(st + r * SSD_N + 4) = make_float4(s[r][2].x, s[r][2].y, s[r][3].x, s[r][3].y);
+    }
+    if (CONV) {
+        __syncthreads();  // the last halo is written
+        if (tid < SSD_P) {
+            cst[0] = xh[tid]; cst[1] = xh[SSD_P + tid]; cst[2] = xh[2 * SSD_P + tid];
+        }
     }
 }
 
