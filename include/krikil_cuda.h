@@ -249,8 +249,11 @@ KRK_API int krk_k_rmsnorm_rows(const float* x, const float* w, float eps, int64_
                                void* stream);
 
 /* src/math.rs:41-54 on feature-major activations (column m of x[k*ldx + m],
- * k < K <= 1216, m < M): out[k*ldo+m] = x*scale(m)*w[k], the sum of squares
- * accumulated in the reference's sequential order. */
+ * k < K <= 1216, m < M): out[k*ldo+m] = x*scale(m)*w[k].  The sum of squares
+ * is formed as 32 partials (partial p over k = p, p + 32, ... in order) added
+ * in a fixed tree: within a few ulps of the reference's sequential sum, and
+ * the same for a column whatever M or its place in the batch.  x holds K full
+ * rows of ldx floats: columns M .. ldx-1 may be read (never written). */
 KRK_API int krk_k_rmsnorm_fm(const float* x, int ldx, const float* w, float eps, int K, int M, float* out, int ldo,
                              void* stream);
 
@@ -264,17 +267,23 @@ KRK_API int krk_k_gated_rmsnorm_residual(const float* x, const float* z, const f
  * with the reference dot's exact rounding.  At: A feature-major [K][lda];
  * Wt: W K-major [K][ldw]; C batch-major [M][ldc] (out_fm = 0) or
  * feature-major [N][ldc] (out_fm = 1).  epilogue 0: store, 1: C += result
- * (residual), 2: store gelu(result) (src/math.rs:17-39).  M % 32 == 0,
+ * (residual), 2: store gelu(result) (src/math.rs:17-39).  M % 16 == 0,
  * N % 32 == 0, K % 32 == 0, leading dims % 4 == 0, pointers 16-byte aligned,
  * K * lda and K * ldw below 2^31 (KRK_INVALID otherwise). */
 KRK_API int krk_k_gemm(const float* At, int lda, const float* Wt, int ldw, float* C, int ldc, int M, int N, int K,
                        int epilogue, int out_fm, void* stream);
 
-/* krk_k_gemm with an explicit CTA tile height: 64 or 32 output rows per CTA
- * (M must be a multiple of it), 0 = the automatic choice krk_k_gemm makes.
+/* krk_k_gemm with an explicit CTA tile height: 64, 32 or 16 output rows per
+ * CTA (M must be a multiple of it), 0 = the automatic choice krk_k_gemm makes.
  * Every choice gives bit-identical results. */
 KRK_API int krk_k_gemm_tiled(const float* At, int lda, const float* Wt, int ldw, float* C, int ldc, int M, int N,
                              int K, int epilogue, int out_fm, int tile_rows, void* stream);
+
+/* The tile height krk_k_gemm chooses for an M x N output on the current
+ * device (148 SMs assumed when no device answers): the smallest of 16 / 32 /
+ * 64 rows whose grid fits in one wave of one CTA per SM, else 32 when 64-row
+ * tiles fill under 1.5 waves, else 64.  Host only; launches nothing. */
+KRK_API int krk_k_gemm_tile_rows(int M, int N);
 
 /* Embedding gather (src/model.rs:330-338, :598) into feature-major
  * out[k*ldo + m] = wte[tok[m]*K + k]. */

@@ -61,6 +61,7 @@ _SIGS = {
     "krk_k_gated_rmsnorm_residual": (_i32, [_fp, _fp, _fp, _fp, _f32, _i64, _i32, _fp, _vp]),
     "krk_k_gemm": (_i32, [_fp, _i32, _fp, _i32, _fp, _i32, _i32, _i32, _i32, _i32, _i32, _vp]),
     "krk_k_gemm_tiled": (_i32, [_fp, _i32, _fp, _i32, _fp, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _vp]),
+    "krk_k_gemm_tile_rows": (_i32, [_i32, _i32]),
     "krk_k_embed": (_i32, [_vp, _fp, _i32, _i32, _i32, _fp, _i32, _vp]),
     "krk_k_pointwise": (_i32, [_i32, _fp, _fp, _i64, _vp]),
     "krk_k_conv_ssd_step": (_i32, [_fp] * 12 + [_i32] * 4 + [_vp]),

@@ -1583,6 +1583,8 @@ int krk_k_gemm_tiled(const float* At, int lda, const float* Wt, int ldw, float* 
         "gemm");
 }
 
+int krk_k_gemm_tile_rows(int M, int N) { return M > 0 && N > 0 ? krk::gemm_tile_rows(M, N) : 0; }
+
 int krk_k_embed(const uint32_t* tok, const float* wte, int vocab, int K, int M, float* out, int ldo, void* stream) {
     return cuda_status(krk::embed_fm(tok, wte, vocab, K, M, out, ldo, (cudaStream_t)stream), "embed");
 }

@@ -39,9 +39,9 @@ struct Tile {
     static constexpr int RED = 8 * BM * RLD_BM > 8 * BN * RLD_FM ? 8 * BM * RLD_BM : 8 * BN * RLD_FM;
     static constexpr int SMEM_FLOATS = RED > PIPE ? RED : PIPE;
     static constexpr size_t SMEM_BYTES = SMEM_FLOATS * sizeof(float);
-    static constexpr int A_F4 = BM / 32;              // float4 copies of A per lane per K-block
-    static constexpr int OUT_F4 = BM * BN / 4 / NT;   // output float4s per thread
-    static constexpr int MIN_CTAS = BM == 64 ? 2 : 3;
+    static constexpr int A_F4 = BM / 32;              // float4 copies of A per lane per K-block (BM = 16: half the lanes copy one)
+    static constexpr int OUT_F4 = (BM * BN / 4 + NT - 1) / NT;  // output float4s per thread (BM = 16: half the threads)
+    static constexpr int MIN_CTAS = BM == 64 ? 2 : BM == 32 ? 3 : 4;
 };
 
 KRK_DEV float4 f4add(float4 a, float4 b) { return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w); }
@@ -53,11 +53,14 @@ KRK_DEV float4 fold8(const float4* l) {
 }
 
 // Thread (lm, ln) of a warp owns rows m(r) and columns n(c), r < TM, c < 8:
-//   BM = 64: m in {lm*4 + i, 32 + lm*4 + i};  BM = 32: m = lm*4 + i
+//   BM = 64: m in {lm*4 + i, 32 + lm*4 + i};  BM = 32: m = lm*4 + i;  BM = 16: m = lm*2 + i
 //   n in {ln*4 + j, 16 + ln*4 + j}
 // so each 16-byte shared load of a warp hits distinct banks.
 template <int BM>
-KRK_DEV int row_of(int lm, int r) { return (r < 4) ? lm * 4 + r : 32 + lm * 4 + (r - 4); }
+KRK_DEV int row_of(int lm, int r) {
+    if (BM == 16) return lm * 2 + r;
+    return (r < 4) ? lm * 4 + r : 32 + lm * 4 + (r - 4);
+}
 KRK_DEV int col_of(int ln, int c) { return (c < 4) ? ln * 4 + c : 16 + ln * 4 + (c - 4); }
 
 template <int BM, int EPI, bool OUT_FM>
@@ -85,6 +88,7 @@ __global__ void __launch_bounds__(NT, Tile<BM>::MIN_CTAS)
 #pragma unroll
         for (int j = 0; j < T::A_F4; ++j)
             cp_async16(As + (lane / (BM / 4) + j * AR) * BM + (lane % (BM / 4)) * 4, At + a_off + j * (8 * AR) * lda);
+        if (BM == 16 && lane < 16) cp_async16(As + (lane >> 2) * BM + (lane & 3) * 4, At + a_off);
         cp_async16(As + WROWS * BM + (lane >> 3) * BN + (lane & 7) * 4, Wt + w_off);
         a_off += BK * lda;
         w_off += BK * ldw;
@@ -93,8 +97,9 @@ __global__ void __launch_bounds__(NT, Tile<BM>::MIN_CTAS)
     // Partial sums in pairs, one __ffma2_rn per pair.  Batch-major output pairs
     // rows: acc2[i*8 + c] = rows (2i, 2i+1) of column c; feature-major output
     // pairs columns: acc2[r*4 + j] = columns (2j, 2j+1) of row r (indices of
-    // row_of / col_of).  The two forms differ only in register allocation.
-    constexpr bool PAIR_ROWS = !OUT_FM;
+    // row_of / col_of).  The two forms differ only in register allocation;
+    // with two rows per thread (BM = 16) columns are paired in both.
+    constexpr bool PAIR_ROWS = !OUT_FM && TM >= 4;
     float2 acc2[TM * 4];
 #pragma unroll
     for (int i = 0; i < TM * 4; ++i) acc2[i] = make_float2(0.0f, 0.0f);
@@ -119,9 +124,12 @@ __global__ void __launch_bounds__(NT, Tile<BM>::MIN_CTAS)
 #pragma unroll
         for (int i = 0; i < WROWS; ++i) {  // k = kb*32 + warp + 8i: this warp's lane of the reference dot
             float a[TM];
-            {
+            if (TM == 2) {
+                const float2 a0 = *reinterpret_cast<const float2*>(As + i * BM + lm * 2);
+                a[0] = a0.x; a[TM == 2 ? 1 : 0] = a0.y;
+            } else {
                 const float4 a0 = *reinterpret_cast<const float4*>(As + i * BM + lm * 4);
-                a[0] = a0.x; a[1] = a0.y; a[2] = a0.z; a[3] = a0.w;
+                a[0] = a0.x; a[TM > 2 ? 1 : 0] = a0.y; a[TM > 2 ? 2 : 0] = a0.z; a[TM > 2 ? 3 : 0] = a0.w;
                 if (TM == 8) {
                     const float4 a1 = *reinterpret_cast<const float4*>(As + i * BM + 32 + lm * 4);
                     a[TM == 8 ? 4 : 0] = a1.x; a[TM == 8 ? 5 : 1] = a1.y;
@@ -174,7 +182,12 @@ __global__ void __launch_bounds__(NT, Tile<BM>::MIN_CTAS)
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
             float* d = base + col_of(ln, c) * T::RLD_FM;
-            *reinterpret_cast<float4*>(d + lm * 4) = make_float4(acc(0, c), acc(1, c), acc(2, c), acc(3, c));
+            if (TM == 2) {
+                *reinterpret_cast<float2*>(d + lm * 2) = make_float2(acc(0, c), acc(1, c));
+                continue;
+            }
+            *reinterpret_cast<float4*>(d + lm * 4) =
+                make_float4(acc(0, c), acc(TM > 2 ? 1 : 0, c), acc(TM > 2 ? 2 : 0, c), acc(TM > 2 ? 3 : 0, c));
             if (TM == 8)
                 *reinterpret_cast<float4*>(d + 32 + lm * 4) = make_float4(
                     acc(TM == 8 ? 4 : 0, c), acc(TM == 8 ? 5 : 1, c), acc(TM == 8 ? 6 : 2, c), acc(TM == 8 ? 7 : 3, c));
@@ -185,6 +198,7 @@ __global__ void __launch_bounds__(NT, Tile<BM>::MIN_CTAS)
 #pragma unroll
     for (int j = 0; j < T::OUT_F4; ++j) {
         const int idx = tid + j * NT;
+        if (BM * BN / 4 < NT && idx >= BM * BN / 4) break;
         const float* part;
         int wstride;
         float* out;
@@ -293,24 +307,35 @@ cudaError_t transpose_pad(const float* in, int rows, int cols, float* out, int l
     return cudaGetLastError();
 }
 
-// Tile choice: 32-row tiles (3 CTAs per SM, ~10% lower FMA rate than the
-// 64-row tile at full occupancy, measured on B200) only when 64-row tiles would
-// fill fewer than 1.5 waves of 2 CTAs per SM -- e.g. the 608-column projections
-// at batch 1024 (304 tiles on 296 slots).  Both give bit-identical results.
+// Tile choice.  When a tile height of 16, 32 or 64 rows puts the whole
+// projection in one wave (no more CTAs than SMs: the decode step of a small
+// batch, where a launch lasts one tile's K loop), the smallest such height,
+// whose warps have the shortest loop (at 64 rows: 16-row tiles for the
+// 608-column projections, 32 for wqkv and the LM head, 64 for in_proj and
+// fc1, measured as the fastest of the three each).  Otherwise 32-row tiles
+// (3 CTAs per SM, ~10% lower FMA rate than the 64-row tile at full
+// occupancy) only when 64-row tiles would fill fewer than 1.5 waves of 2 CTAs
+// per SM -- e.g. the 608-column projections at batch 1024 (304 tiles on 296
+// slots).  Every choice gives bit-identical results.
 int gemm_tile_rows(int M, int N) {
+    const int64_t cols = N / BN, sms = sm_count();
+    for (int t = 16; t <= 64; t *= 2)
+        if (M % t == 0 && (int64_t)(M / t) * cols <= sms) return t;
+    if (M % 32) return 16;
     if (M % 64) return 32;
-    const int64_t t64 = (int64_t)(M / 64) * (N / BN);
-    return 2 * t64 < 3 * (int64_t)sm_count() * 2 ? 32 : 64;
+    const int64_t t64 = (int64_t)(M / 64) * cols;
+    return 2 * t64 < 3 * sms * 2 ? 32 : 64;
 }
 
 cudaError_t gemm_tiled(const float* At, int lda, const float* Wt, int ldw, float* C, int ldc, int M, int N, int K,
                        int epilogue, bool out_fm, int tile_rows, cudaStream_t s) {
     if (tile_rows == 0) tile_rows = gemm_tile_rows(M, N);
-    if (M <= 0 || N <= 0 || K <= 0 || (tile_rows != 32 && tile_rows != 64) || M % tile_rows || N % BN || K % BK ||
-        lda % 4 || ldw % 4 || ldc % 4 || lda < M || ldw < N || ldc < (out_fm ? M : N) ||
+    if (M <= 0 || N <= 0 || K <= 0 || (tile_rows != 16 && tile_rows != 32 && tile_rows != 64) || M % tile_rows ||
+        N % BN || K % BK || lda % 4 || ldw % 4 || ldc % 4 || lda < M || ldw < N || ldc < (out_fm ? M : N) ||
         (int64_t)K * lda >= (1ll << 31) || (int64_t)K * ldw >= (1ll << 31) ||
         ((uintptr_t)At | (uintptr_t)Wt | (uintptr_t)C) % 16)
         return cudaErrorInvalidValue;
+    if (tile_rows == 16) return dispatch<16>(At, lda, Wt, ldw, C, ldc, M, N, K, epilogue, out_fm, s);
     if (tile_rows == 32) return dispatch<32>(At, lda, Wt, ldw, C, ldc, M, N, K, epilogue, out_fm, s);
     return dispatch<64>(At, lda, Wt, ldw, C, ldc, M, N, K, epilogue, out_fm, s);
 }
@@ -318,12 +343,14 @@ cudaError_t gemm_tiled(const float* At, int lda, const float* Wt, int ldw, float
 cudaError_t gemm_conv(const float* At, int lda, const float* Wt, int ldw, float* C, int ldc, int M, int N, int K,
                       int tile_rows, const GemmConv& cv, cudaStream_t s) {
     if (tile_rows == 0) tile_rows = gemm_tile_rows(M, N);
-    if (M <= 0 || N <= 0 || K <= 0 || (tile_rows != 32 && tile_rows != 64) || M % tile_rows || N % BN || K % BK ||
-        lda % 4 || ldw % 4 || ldc % 4 || lda < M || ldw < N || ldc < N || !cv.state || !cv.w || !cv.bias ||
+    if (M <= 0 || N <= 0 || K <= 0 || (tile_rows != 16 && tile_rows != 32 && tile_rows != 64) || M % tile_rows ||
+        N % BN || K % BK || lda % 4 || ldw % 4 || ldc % 4 || lda < M || ldw < N || ldc < N || !cv.state || !cv.w ||
+        !cv.bias ||
         (int64_t)K * lda >= (1ll << 31) || (int64_t)K * ldw >= (1ll << 31) ||
         cv.lo < 0 || cv.lo % BN || cv.hi % BN || cv.hi <= cv.lo || cv.hi > N || cv.rows < 0 || cv.rows > M ||
         ((uintptr_t)At | (uintptr_t)Wt | (uintptr_t)C | (uintptr_t)cv.state | (uintptr_t)cv.w) % 16)
         return cudaErrorInvalidValue;
+    if (tile_rows == 16) return launch<16, EPI_CONV, false>(At, lda, Wt, ldw, C, ldc, M, N, K, s, cv);
     if (tile_rows == 32) return launch<32, EPI_CONV, false>(At, lda, Wt, ldw, C, ldc, M, N, K, s, cv);
     return launch<64, EPI_CONV, false>(At, lda, Wt, ldw, C, ldc, M, N, K, s, cv);
 }

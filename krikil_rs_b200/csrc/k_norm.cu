@@ -56,7 +56,10 @@ __global__ void __launch_bounds__(256) rmsnorm_fm_kernel(const float* __restrict
     const int tid = threadIdx.x;
     const int m0 = blockIdx.x * NORM_COLS;
     const int ncols = min(NORM_COLS, M - m0);
-    const bool full = (ncols == NORM_COLS) && ((ldx & 3) == 0) && ((((uintptr_t)x) & 15) == 0);
+    // The whole 8-column block is copied whenever it lies inside the rows (a
+    // padded batch: columns past M are read, their sums unused, and never
+    // written), so a partial block takes the copy path too.
+    const bool full = (m0 + NORM_COLS <= ldx) && ((ldx & 3) == 0) && ((((uintptr_t)x) & 15) == 0);
     // the weights travel with the block when both are 16-byte pieces
     const bool wasync = WS && (K & 3) == 0 && (((uintptr_t)w) & 15) == 0;
     if (full) {

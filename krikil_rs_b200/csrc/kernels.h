@@ -22,7 +22,7 @@ struct DeviceOnce {
 //   At: A stored feature-major, At[k*lda + m]  (M columns, K rows)
 //   Wt: W stored K-major,       Wt[k*ldw + n]
 //   out_fm=false: C[m*ldc + n];  out_fm=true: C[n*ldc + m]
-// M % 32 == 0, N % 32 == 0, K % 32 == 0; leading dims % 4 == 0; 16-B aligned.
+// M % 16 == 0, N % 32 == 0, K % 32 == 0; leading dims % 4 == 0; 16-B aligned.
 enum GemmEpilogue { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_GELU = 2, EPI_CONV = 3 };
 // EPI_CONV (batch-major output only): output columns [lo, hi) are the decode
 // conv channels; for rows m < rows whose active flag is set (or all, when
@@ -45,9 +45,9 @@ cudaError_t gemm_conv(const float* At, int lda, const float* Wt, int ldw, float*
 // out[c*ld + r] = in[r*cols + c] for r < rows, 0 for rows <= r < ld (c < cols):
 // a row-major weight [rows][cols] into the K-major layout the projections read.
 cudaError_t transpose_pad(const float* in, int rows, int cols, float* out, int ld, cudaStream_t s);
-// Rows per CTA tile (64 or 32) gemm() uses for an M x N output.
+// Rows per CTA tile (64, 32 or 16) gemm() uses for an M x N output.
 int gemm_tile_rows(int M, int N);
-// gemm() with an explicit CTA tile height (32 or 64; 0 = gemm_tile_rows).
+// gemm() with an explicit CTA tile height (16, 32 or 64; 0 = gemm_tile_rows).
 cudaError_t gemm_tiled(const float* At, int lda, const float* Wt, int ldw, float* C, int ldc, int M, int N, int K,
                        int epilogue, bool out_fm, int tile_rows, cudaStream_t s);
 

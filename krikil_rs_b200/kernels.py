@@ -51,7 +51,7 @@ def gated_rmsnorm_residual(x, z, res, w, eps: float, y=None) -> torch.Tensor:
 
 def gemm(a_t: torch.Tensor, w_t: torch.Tensor, epilogue: int = 0, out_fm: bool = False,
          c: Optional[torch.Tensor] = None, tile_rows: int = 0) -> torch.Tensor:
-    """C = A . W^T with a_t = A^T [K, M] and w_t = W^T [K, N]; tile_rows 0/32/64."""
+    """C = A . W^T with a_t = A^T [K, M] and w_t = W^T [K, N]; tile_rows 0/16/32/64."""
     _f32(a_t, w_t, c)
     k, m = a_t.shape
     k2, n = w_t.shape

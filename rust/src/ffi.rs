@@ -118,6 +118,7 @@ extern "C" {
     pub fn krk_k_gemm_tiled(at: *const c_float, lda: c_int, wt: *const c_float, ldw: c_int, c: *mut c_float,
                             ldc: c_int, m: c_int, n: c_int, k: c_int, epilogue: c_int, out_fm: c_int,
                             tile_rows: c_int, stream: *mut c_void) -> c_int;
+    pub fn krk_k_gemm_tile_rows(m: c_int, n: c_int) -> c_int;
     pub fn krk_k_embed(tok: *const u32, wte: *const c_float, vocab: c_int, k: c_int, m: c_int, out: *mut c_float,
                        ldo: c_int, stream: *mut c_void) -> c_int;
     pub fn krk_k_pointwise(op: c_int, x: *const c_float, y: *mut c_float, n: i64, stream: *mut c_void) -> c_int;

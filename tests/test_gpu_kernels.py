@@ -31,7 +31,7 @@ def np_(t):
 @pytest.mark.parametrize("m,n,k", [(64, 32, 32), (128, 2720, 608), (64, 608, 1216), (192, 608, 2432),
                                    (64, 2048, 608), (256, 1824, 608)])
 @pytest.mark.parametrize("out_fm", [False, True])
-@pytest.mark.parametrize("tile", [0, 32, 64])
+@pytest.mark.parametrize("tile", [0, 16, 32, 64])
 def test_gemm_bit_exact_vs_reference_dot(m, n, k, out_fm, tile):
     rng = np.random.default_rng(m * 7 + n + k)
     a = rng.standard_normal((m, k)).astype(np.float32)
@@ -42,7 +42,7 @@ def test_gemm_bit_exact_vs_reference_dot(m, n, k, out_fm, tile):
     np.testing.assert_array_equal(got, ref)
 
 
-@pytest.mark.parametrize("tile", [32, 64])
+@pytest.mark.parametrize("tile", [16, 32, 64])
 def test_gemm_residual_and_gelu_epilogues(tile):
     rng = np.random.default_rng(1)
     m, n, k = 128, 608, 2432
@@ -62,7 +62,7 @@ def test_gemm_residual_and_gelu_epilogues(tile):
 
 
 @pytest.mark.parametrize("m,n,k", [(1024, 2720, 608), (2048, 608, 2432)])
-@pytest.mark.parametrize("tile", [32, 64])
+@pytest.mark.parametrize("tile", [16, 32, 64])
 def test_gemm_many_waves_all_epilogues(m, n, k, tile):
     """Decode shapes with several tiles per SM (1360-5440 tiles): every output
     of every wave equals the reference dot, in both output layouts, and the
