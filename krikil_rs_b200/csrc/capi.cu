@@ -558,16 +558,31 @@ void timed(krk_state* s, const Part& p, int cls, F&& f) {
     timed_on(s, p.st, cls, p.nb, f);
 }
 
+// A single-part decode of a few sequences computes a projection of N columns
+// in the few-rows form, over the real rows only (every consumer reads only
+// those), where that form is the faster one.
+bool few_rows(const Part& p, int N) { return p.tile_rows == 0 && krk::gemm_few_rows(p.nb, N); }
+
 // Final norm + tied LM head (src/model.rs:620-621).
 void lm_head(krk_state* s, const Part& p) {
     const krk_model* m = s->m;
     const int Mp = (int)s->Mp;
+    const bool few = few_rows(p, VOC);
+    if (few) {  // lnf inside the few-rows projection
+        timed(s, p, KRK_PROF_GEMM, [&] {
+            kk(krk::gemm_few_norm(s->h_t + p.b0, Mp, m->wte_t, VOC, s->logits + (size_t)p.b0 * VOC, VOC, p.nb, VOC,
+                                  HID, krk::EPI_STORE, false, krk::GemmNorm{m->lnf, RMS_EPS}, nullptr, p.st),
+               "lnf + lm head");
+        });
+        return;
+    }
     timed(s, p, KRK_PROF_NORM, [&] {
         kk(krk::rmsnorm_fm(s->h_t + p.b0, Mp, m->lnf, RMS_EPS, HID, p.nb, s->hn_t + p.b0, Mp, p.st), "lnf");
     });
     timed(s, p, KRK_PROF_GEMM, [&] {
         kk(krk::gemm_tiled(s->hn_t + p.b0, Mp, m->wte_t, VOC, s->logits + (size_t)p.b0 * VOC, VOC, p.M, VOC, HID,
-                           krk::EPI_STORE, false, p.tile_rows, p.st), "lm head");
+                           krk::EPI_STORE, false, p.tile_rows, p.st),
+           "lm head");
     });
 }
 
@@ -584,25 +599,50 @@ void decode_embed(krk_state* s, const Part& p) {
 void decode_layer(krk_state* s, int l, const uint8_t* active, int max_keys, const Part& p) {
     const krk_model* m = s->m;
     const LayerW& L = m->L[l];
-    const int Mp = (int)s->Mp, b0 = p.b0, nb = p.nb, M = p.M, tr = p.tile_rows;
+    const int Mp = (int)s->Mp, b0 = p.b0, nb = p.nb;
+    // rows and tile height of a projection of N columns
+    auto rows = [&](int N) { return few_rows(p, N) ? nb : p.M; };
+    auto tile = [&](int N) { return few_rows(p, N) ? 1 : p.tile_rows; };
     cudaStream_t st = p.st;
     const uint8_t* act = active ? active + b0 : nullptr;
     float* h = s->h_t + b0;
     float* hn = s->hn_t + b0;
     auto gemm = [&](const float* A, const float* W, int N, int K, float* C, int ldc, int epi, bool fm, const char* w) {
-        timed(s, p, KRK_PROF_GEMM, [&] { kk(krk::gemm_tiled(A, Mp, W, N, C, ldc, M, N, K, epi, fm, tr, st), w); });
+        timed(s, p, KRK_PROF_GEMM,
+              [&] { kk(krk::gemm_tiled(A, Mp, W, N, C, ldc, rows(N), N, K, epi, fm, tile(N), st), w); });
     };
     auto norm = [&](const float* x, const float* w, float eps, int K, float* out, const char* what) {
         timed(s, p, KRK_PROF_NORM, [&] { kk(krk::rmsnorm_fm(x, Mp, w, eps, K, nb, out, Mp, st), what); });
     };
+    // rms_norm(x) into xn and the projection of xn, or both in one few-rows launch
+    auto norm_gemm = [&](const float* x, const float* nw, float eps, float* xn, const float* W, int N, int K, float* C,
+                         int ldc, int epi, bool fm, const char* what) {
+        if (few_rows(p, N)) {
+            timed(s, p, KRK_PROF_GEMM, [&] {
+                kk(krk::gemm_few_norm(x, Mp, W, N, C, ldc, nb, N, K, epi, fm, krk::GemmNorm{nw, eps}, nullptr, st), what);
+            });
+        } else {
+            norm(x, nw, eps, K, xn, what);
+            gemm(xn, W, N, K, C, ldc, epi, fm, what);
+        }
+    };
     if (is_mamba(l)) {  // src/model.rs:626-702
         float* zx = s->zx + (size_t)b0 * DIP_PAD;
-        norm(h, L.ln, RMS_EPS, HID, hn, "ln");
         // in_proj with the decode conv + SiLU of its x, B, C columns in the epilogue
         krk::GemmConv cv{s->conv[l] + (size_t)b0 * DXBC * 4, L.conv_w, L.conv_b, act, nb, OFF_X, OFF_X + DXBC};
-        timed(s, p, KRK_PROF_GEMM, [&] {
-            kk(krk::gemm_conv(hn, Mp, L.in_t, DIP_PAD, zx, DIP_PAD, M, DIP_PAD, HID, tr, cv, st), "in_proj + conv");
-        });
+        if (few_rows(p, DIP_PAD)) {  // ln inside the few-rows projection
+            timed(s, p, KRK_PROF_GEMM, [&] {
+                kk(krk::gemm_few_norm(h, Mp, L.in_t, DIP_PAD, zx, DIP_PAD, nb, DIP_PAD, HID, krk::EPI_CONV, false,
+                                      krk::GemmNorm{L.ln, RMS_EPS}, &cv, st),
+                   "ln + in_proj + conv");
+            });
+        } else {
+            norm(h, L.ln, RMS_EPS, HID, hn, "ln");
+            timed(s, p, KRK_PROF_GEMM, [&] {
+                kk(krk::gemm_conv(hn, Mp, L.in_t, DIP_PAD, zx, DIP_PAD, p.M, DIP_PAD, HID, p.tile_rows, cv, st),
+                   "in_proj + conv");
+            });
+        }
         krk::SsdStepArgs a{};
         a.x = zx + OFF_X; a.x_sb = DIP_PAD;
         a.bm = zx + OFF_B; a.cm = zx + OFF_C; a.bc_sb = DIP_PAD;
@@ -614,12 +654,11 @@ void decode_layer(krk_state* s, int l, const uint8_t* active, int max_keys, cons
         a.active = act;
         a.B = nb; a.H = MH; a.P = MP; a.N = DS;
         timed(s, p, KRK_PROF_SSD_STEP, [&] { kk(krk::ssd_step(a, false, st), "ssd step"); });
-        norm(s->y_t + b0, L.norm_w, MNORM_EPS, DI, s->yn_t + b0, "gated norm");
-        gemm(s->yn_t + b0, L.out_t, HID, DI, h, Mp, krk::EPI_RESIDUAL, true, "out_proj");
+        norm_gemm(s->y_t + b0, L.norm_w, MNORM_EPS, s->yn_t + b0, L.out_t, HID, DI, h, Mp, krk::EPI_RESIDUAL, true,
+                  "gated norm + out_proj");
     } else {  // src/model.rs:704-783
         float* qkv = s->qkv + (size_t)b0 * QKV;
-        norm(h, L.ln1, RMS_EPS, HID, hn, "ln1");
-        gemm(hn, L.qkv_t, QKV, HID, qkv, QKV, krk::EPI_STORE, false, "wqkv");
+        norm_gemm(h, L.ln1, RMS_EPS, hn, L.qkv_t, QKV, HID, qkv, QKV, krk::EPI_STORE, false, "ln1 + wqkv");
         krk::AttnDecodeArgs a{};
         a.q = qkv; a.k = qkv + HID; a.v = qkv + 2 * HID; a.in_sb = QKV; a.in_sh = HD;
         a.c_sb = (int64_t)s->ctx * HID; a.c_sh = HD; a.c_st = HID;
@@ -634,8 +673,7 @@ void decode_layer(krk_state* s, int l, const uint8_t* active, int max_keys, cons
         a.err = s->err_d;
         timed(s, p, KRK_PROF_ATTN_DECODE, [&] { kk(krk::attn_decode(a, st), "attention"); });
         gemm(s->ao_t + b0, L.wo_t, HID, HID, h, Mp, krk::EPI_RESIDUAL, true, "wo");
-        norm(h, L.ln2, RMS_EPS, HID, hn, "ln2");
-        gemm(hn, L.fc1_t, INTER, HID, s->mlp_t + b0, Mp, krk::EPI_GELU, true, "fc1");
+        norm_gemm(h, L.ln2, RMS_EPS, hn, L.fc1_t, INTER, HID, s->mlp_t + b0, Mp, krk::EPI_GELU, true, "ln2 + fc1");
         gemm(s->mlp_t + b0, L.fc2_t, HID, INTER, h, Mp, krk::EPI_RESIDUAL, true, "fc2");
     }
 }

@@ -29,6 +29,7 @@ namespace {
 constexpr int BN = 32, BK = 32, NT = 256, WSTAGE = 4;
 constexpr int WROWS = BK / 8;  // K-block rows owned by one warp
 constexpr int RLD_BM = BN + 4;  // partials red[w][m][n] for batch-major output
+constexpr int SKINNY_MAX_K = 2432;  // the widest projection input (fc2 over the MLP width)
 
 template <int BM>
 struct Tile {
@@ -244,6 +245,161 @@ __global__ void __launch_bounds__(NT, Tile<BM>::MIN_CTAS)
     }
 }
 
+// Projection of a few rows (the decode step of up to SKINNY_MAX_ROWS
+// sequences): thread (j, c) of a CTA -- warp j, lane c -- is lane j of the
+// reference dot for output column n0 + c, accumulating one FMA chain per row
+// over k = j, j + 8, ... in order; the eight lane partials are folded in the
+// reference's order through shared memory.  The same arithmetic as
+// gemm_lane8_kernel, so the results are bitwise those of any tile height, but
+// a launch reads W^T once and its longest chain is K/8 FMAs instead of a
+// 16- to 64-row tile's K loop.  Warp j streams its rows of W^T (the CTA's 32
+// columns) through a private SK_STAGES-deep cp.async ring of 4-row stages, so
+// ~32 rows are in flight per warp.  Only the M rows given are computed.
+constexpr int SKINNY_MAX_ROWS = 8;
+constexpr int SK_STAGES = 8, SK_ROWS = 4, SK_ST = SK_ROWS * BN;  // one stage of one warp: 4 rows x 32 columns
+
+// MT: M rounded up to 1, 2, 4 or 8 (the extra columns of A are read from the
+// operand's padding and their outputs never written).  A is staged permuted,
+// sa[(j * K/8 + i) * MT + m] = A(m, j + 8i), so a thread's four chain rows of a
+// stage are 4 * MT consecutive floats.
+// NORM: A is rms_norm(A) (src/math.rs:41-54) -- the staged copy is
+// normalised in place first, its scales formed as rmsnorm_fm_kernel forms
+// them (32 partials p: A(m, k)^2 for k = p, p + 32, ... in order; per group of
+// four ((p0+p1)+(p2+p3)); the eight groups in order; 1 / sqrt(sum / K + eps))
+// and each element as (x * scale) * w[k]: bitwise rmsnorm_fm and then the
+// projection, in one launch.
+template <int MT, int EPI, bool OUT_FM, bool NORM>
+__global__ void __launch_bounds__(NT) gemm_skinny_kernel(const float* __restrict__ At, int lda,
+                                                         const float* __restrict__ Wt, int ldw, float* __restrict__ C,
+                                                         int ldc, int M, int K, const GemmConv cv, const GemmNorm nm) {
+    extern __shared__ __align__(16) float smk[];  // rings [8 warps][SK_STAGES][4][32], then A [8][K/8][MT]
+    __shared__ float red[8][SKINNY_MAX_ROWS][BN + 1];
+    const int tid = threadIdx.x, j = tid >> 5, c = tid & 31;
+    const int n0 = blockIdx.x * BN;
+    const int kj = K / 8;  // rows of one dot lane
+    float* ring = smk + j * (SK_STAGES * SK_ST);
+    float* sa = smk + 8 * SK_STAGES * SK_ST;
+    const int nst = K / (8 * SK_ROWS);  // stages of this warp's rows k = j + 8i
+    // lane c copies 16 bytes of row (c >> 3) of a stage: columns n0 + 4(c & 7) ..
+    const float* wsrc = Wt + (size_t)(j + 8 * (c >> 3)) * ldw + n0 + (c & 7) * 4;
+    const size_t wstage = (size_t)8 * SK_ROWS * ldw;
+    const int wdst = (c >> 3) * BN + (c & 7) * 4;
+#pragma unroll
+    for (int st = 0; st < SK_STAGES - 1; ++st) {
+        if (st < nst) cp_async16(ring + st * SK_ST + wdst, wsrc + st * wstage);
+        cp_async_commit();
+    }
+    for (int i = tid; i < K * MT; i += NT) {
+        const int k = i / MT, m = i % MT;
+        sa[((k & 7) * kj + (k >> 3)) * MT + m] = At[(size_t)k * lda + m];
+    }
+    __syncthreads();
+    if (NORM) {
+        __shared__ float ps[32][MT];
+        __shared__ float scl[MT];
+        if (tid < 32 * MT) {
+            const int m = tid % MT, q = tid / MT;
+            float ss = 0.0f;
+            for (int k = q; k < K; k += 32) {
+                const float v = sa[((k & 7) * kj + (k >> 3)) * MT + m];
+                ss += v * v;
+            }
+            ps[q][m] = ss;
+        }
+        __syncthreads();
+        if (tid < MT) {
+            float t = 0.0f;
+#pragma unroll
+            for (int g = 0; g < 8; ++g) {
+                const float s4 = (ps[4 * g][tid] + ps[4 * g + 1][tid]) + (ps[4 * g + 2][tid] + ps[4 * g + 3][tid]);
+                t = g == 0 ? s4 : t + s4;
+            }
+            scl[tid] = 1.0f / sqrtf(t / (float)K + nm.eps);
+        }
+        __syncthreads();
+        for (int i = tid; i < K * MT; i += NT) {
+            const int pos = i / MT, m = i % MT;
+            sa[i] = sa[i] * scl[m] * __ldg(nm.w + (pos / kj) + 8 * (pos % kj));
+        }
+        __syncthreads();
+    }
+    float acc[MT];
+#pragma unroll
+    for (int m = 0; m < MT; ++m) acc[m] = 0.0f;
+    const float* aj = sa + (size_t)j * kj * MT;
+    for (int st = 0; st < nst; ++st) {
+        cp_async_wait<SK_STAGES - 2>();
+        __syncwarp();  // every lane's copy of stage st is visible; stage st - 1 is read
+        const int nx = st + SK_STAGES - 1;
+        if (nx < nst) cp_async16(ring + (nx % SK_STAGES) * SK_ST + wdst, wsrc + nx * wstage);
+        cp_async_commit();
+        const float* ws = ring + (st % SK_STAGES) * SK_ST;
+        float av[SK_ROWS * MT];  // rows 4st .. 4st+3 of this lane's chain, MT values each
+#pragma unroll
+        for (int q = 0; q < SK_ROWS * MT / 4; ++q) {
+            const float4 v = *reinterpret_cast<const float4*>(aj + (SK_ROWS * st) * MT + 4 * q);
+            av[4 * q] = v.x; av[4 * q + 1] = v.y; av[4 * q + 2] = v.z; av[4 * q + 3] = v.w;
+        }
+#pragma unroll
+        for (int r = 0; r < SK_ROWS; ++r) {  // k = j + 8(4 st + r): this lane's chain in order
+            const float w = ws[r * BN + c];
+#pragma unroll
+            for (int m = 0; m < MT; ++m) acc[m] = fmaf(av[r * MT + m], w, acc[m]);
+        }
+    }
+    cp_async_wait<0>();
+#pragma unroll
+    for (int m = 0; m < MT; ++m) red[j][m][c] = acc[m];
+    __syncthreads();
+    if (tid >= M * BN) return;
+    const int m = tid / BN, cc = tid % BN, n = n0 + cc;
+    float l[8];
+#pragma unroll
+    for (int w = 0; w < 8; ++w) l[w] = red[w][m][cc];
+    float v = ((l[0] + l[4]) + (l[2] + l[6])) + ((l[1] + l[5]) + (l[3] + l[7]));  // src/math.rs:110-117
+    float* out = OUT_FM ? C + (size_t)n * ldc + m : C + (size_t)m * ldc + n;
+    if (EPI == EPI_CONV) {  // src/model.rs:643-654 for this (row, channel)
+        if (n >= cv.lo && n < cv.hi && m < cv.rows && (!cv.active || cv.active[m])) {
+            const int ch = n - cv.lo;
+            float4* sp = reinterpret_cast<float4*>(cv.state + ((size_t)m * (cv.hi - cv.lo) + ch) * 4);
+            const float4 st = *sp, wv = reinterpret_cast<const float4*>(cv.w)[ch];
+            // after the shift the window is [st.y, st.z, st.w, x]
+            const float val = st.y * wv.x + st.z * wv.y + st.w * wv.z + v * wv.w + cv.bias[ch];
+            *sp = make_float4(st.y, st.z, st.w, v);
+            v = silu(val);
+        }
+    } else if (EPI == EPI_RESIDUAL) {
+        v = *out + v;  // x += out (src/model.rs:699-701)
+    } else if (EPI == EPI_GELU) {
+        v = gelu(v);
+    }
+    *out = v;
+}
+
+template <int MT, int EPI, bool OUT_FM, bool NORM>
+cudaError_t launch_skinny_mt(const float* At, int lda, const float* Wt, int ldw, float* C, int ldc, int M, int N, int K,
+                             cudaStream_t s, const GemmConv& cv, const GemmNorm& nm) {
+    static DeviceOnce once;
+    constexpr size_t ring_bytes = (size_t)8 * SK_STAGES * SK_ST * sizeof(float);
+    const size_t smem = ring_bytes + (size_t)K * MT * sizeof(float);
+    cudaError_t e = once.set_smem((const void*)gemm_skinny_kernel<MT, EPI, OUT_FM, NORM>,
+                                  ring_bytes + (size_t)SKINNY_MAX_K * MT * sizeof(float));
+    if (e != cudaSuccess) return e;
+    gemm_skinny_kernel<MT, EPI, OUT_FM, NORM><<<N / BN, NT, smem, s>>>(At, lda, Wt, ldw, C, ldc, M, K, cv, nm);
+    add_launches(1);
+    return cudaGetLastError();
+}
+
+// M <= 8 rows; lda >= 4 * ceil(M / 4) (lda % 4 == 0 and lda >= M guarantee it)
+template <int EPI, bool OUT_FM, bool NORM = false>
+cudaError_t launch_skinny(const float* At, int lda, const float* Wt, int ldw, float* C, int ldc, int M, int N, int K,
+                          cudaStream_t s, const GemmConv& cv = GemmConv{}, const GemmNorm& nm = GemmNorm{}) {
+    if (M == 1) return launch_skinny_mt<1, EPI, OUT_FM, NORM>(At, lda, Wt, ldw, C, ldc, M, N, K, s, cv, nm);
+    if (M == 2) return launch_skinny_mt<2, EPI, OUT_FM, NORM>(At, lda, Wt, ldw, C, ldc, M, N, K, s, cv, nm);
+    if (M <= 4) return launch_skinny_mt<4, EPI, OUT_FM, NORM>(At, lda, Wt, ldw, C, ldc, M, N, K, s, cv, nm);
+    return launch_skinny_mt<8, EPI, OUT_FM, NORM>(At, lda, Wt, ldw, C, ldc, M, N, K, s, cv, nm);
+}
+
 template <int BM, int EPI, bool OUT_FM>
 cudaError_t launch(const float* At, int lda, const float* Wt, int ldw, float* C, int ldc, int M, int N, int K,
                    cudaStream_t s, const GemmConv& cv = GemmConv{}) {
@@ -317,6 +473,34 @@ cudaError_t transpose_pad(const float* in, int rows, int cols, float* out, int l
 // occupancy) only when 64-row tiles would fill fewer than 1.5 waves of 2 CTAs
 // per SM -- e.g. the 608-column projections at batch 1024 (304 tiles on 296
 // slots).  Every choice gives bit-identical results.
+cudaError_t gemm_few_norm(const float* At, int lda, const float* Wt, int ldw, float* C, int ldc, int M, int N, int K,
+                          int epilogue, bool out_fm, const GemmNorm& nm, const GemmConv* cv, cudaStream_t s) {
+    if (M <= 0 || M > GEMM_FEW_ROWS || N <= 0 || K <= 0 || K > SKINNY_MAX_K || N % BN || K % BK || lda % 4 ||
+        ldw % 4 || ldc % 4 || lda < M || ldw < N || ldc < (out_fm ? M : N) || !nm.w ||
+        (int64_t)K * lda >= (1ll << 31) || (int64_t)K * ldw >= (1ll << 31) ||
+        ((uintptr_t)At | (uintptr_t)Wt | (uintptr_t)C) % 16)
+        return cudaErrorInvalidValue;
+    if (cv) {
+        if (epilogue != EPI_CONV || out_fm || !cv->state || !cv->w || !cv->bias || cv->lo < 0 || cv->lo % BN ||
+            cv->hi % BN || cv->hi <= cv->lo || cv->hi > N || cv->rows < 0 || cv->rows > M ||
+            ((uintptr_t)cv->state | (uintptr_t)cv->w) % 16)
+            return cudaErrorInvalidValue;
+        return launch_skinny<EPI_CONV, false, true>(At, lda, Wt, ldw, C, ldc, M, N, K, s, *cv, nm);
+    }
+    switch (epilogue * 2 + (out_fm ? 1 : 0)) {  // the forms the model uses
+        case EPI_STORE * 2 + 0: return launch_skinny<EPI_STORE, false, true>(At, lda, Wt, ldw, C, ldc, M, N, K, s, {}, nm);
+        case EPI_RESIDUAL * 2 + 1:
+            return launch_skinny<EPI_RESIDUAL, true, true>(At, lda, Wt, ldw, C, ldc, M, N, K, s, {}, nm);
+        case EPI_GELU * 2 + 1: return launch_skinny<EPI_GELU, true, true>(At, lda, Wt, ldw, C, ldc, M, N, K, s, {}, nm);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+// The few-rows form beats every tile height (CUDA graphs of the decode
+// projections) at up to 4 rows for every shape, and at 5-8 rows for the
+// projections of 1024+ columns; 16-row tiles win for the 608-column ones there.
+bool gemm_few_rows(int M, int N) { return M > 0 && M <= GEMM_FEW_ROWS && (M <= 4 || N >= 1024); }
+
 int gemm_tile_rows(int M, int N) {
     const int64_t cols = N / BN, sms = sm_count();
     for (int t = 16; t <= 64; t *= 2)
@@ -330,11 +514,24 @@ int gemm_tile_rows(int M, int N) {
 cudaError_t gemm_tiled(const float* At, int lda, const float* Wt, int ldw, float* C, int ldc, int M, int N, int K,
                        int epilogue, bool out_fm, int tile_rows, cudaStream_t s) {
     if (tile_rows == 0) tile_rows = gemm_tile_rows(M, N);
-    if (M <= 0 || N <= 0 || K <= 0 || (tile_rows != 16 && tile_rows != 32 && tile_rows != 64) || M % tile_rows ||
+    const bool skinny = tile_rows == 1;  // the few-rows form
+    if (M <= 0 || N <= 0 || K <= 0 || (tile_rows != 1 && tile_rows != 16 && tile_rows != 32 && tile_rows != 64) ||
+        M % tile_rows || (skinny && (M > SKINNY_MAX_ROWS || K > SKINNY_MAX_K)) ||
         N % BN || K % BK || lda % 4 || ldw % 4 || ldc % 4 || lda < M || ldw < N || ldc < (out_fm ? M : N) ||
         (int64_t)K * lda >= (1ll << 31) || (int64_t)K * ldw >= (1ll << 31) ||
         ((uintptr_t)At | (uintptr_t)Wt | (uintptr_t)C) % 16)
         return cudaErrorInvalidValue;
+    if (tile_rows == 1) {
+        switch (epilogue * 2 + (out_fm ? 1 : 0)) {
+            case EPI_STORE * 2 + 0: return launch_skinny<EPI_STORE, false>(At, lda, Wt, ldw, C, ldc, M, N, K, s);
+            case EPI_STORE * 2 + 1: return launch_skinny<EPI_STORE, true>(At, lda, Wt, ldw, C, ldc, M, N, K, s);
+            case EPI_RESIDUAL * 2 + 0: return launch_skinny<EPI_RESIDUAL, false>(At, lda, Wt, ldw, C, ldc, M, N, K, s);
+            case EPI_RESIDUAL * 2 + 1: return launch_skinny<EPI_RESIDUAL, true>(At, lda, Wt, ldw, C, ldc, M, N, K, s);
+            case EPI_GELU * 2 + 0: return launch_skinny<EPI_GELU, false>(At, lda, Wt, ldw, C, ldc, M, N, K, s);
+            case EPI_GELU * 2 + 1: return launch_skinny<EPI_GELU, true>(At, lda, Wt, ldw, C, ldc, M, N, K, s);
+            default: return cudaErrorInvalidValue;
+        }
+    }
     if (tile_rows == 16) return dispatch<16>(At, lda, Wt, ldw, C, ldc, M, N, K, epilogue, out_fm, s);
     if (tile_rows == 32) return dispatch<32>(At, lda, Wt, ldw, C, ldc, M, N, K, epilogue, out_fm, s);
     return dispatch<64>(At, lda, Wt, ldw, C, ldc, M, N, K, epilogue, out_fm, s);
@@ -343,13 +540,16 @@ cudaError_t gemm_tiled(const float* At, int lda, const float* Wt, int ldw, float
 cudaError_t gemm_conv(const float* At, int lda, const float* Wt, int ldw, float* C, int ldc, int M, int N, int K,
                       int tile_rows, const GemmConv& cv, cudaStream_t s) {
     if (tile_rows == 0) tile_rows = gemm_tile_rows(M, N);
-    if (M <= 0 || N <= 0 || K <= 0 || (tile_rows != 16 && tile_rows != 32 && tile_rows != 64) || M % tile_rows ||
+    const bool skinny = tile_rows == 1;  // the few-rows form
+    if (M <= 0 || N <= 0 || K <= 0 || (tile_rows != 1 && tile_rows != 16 && tile_rows != 32 && tile_rows != 64) ||
+        M % tile_rows || (skinny && (M > SKINNY_MAX_ROWS || K > SKINNY_MAX_K)) ||
         N % BN || K % BK || lda % 4 || ldw % 4 || ldc % 4 || lda < M || ldw < N || ldc < N || !cv.state || !cv.w ||
         !cv.bias ||
         (int64_t)K * lda >= (1ll << 31) || (int64_t)K * ldw >= (1ll << 31) ||
         cv.lo < 0 || cv.lo % BN || cv.hi % BN || cv.hi <= cv.lo || cv.hi > N || cv.rows < 0 || cv.rows > M ||
         ((uintptr_t)At | (uintptr_t)Wt | (uintptr_t)C | (uintptr_t)cv.state | (uintptr_t)cv.w) % 16)
         return cudaErrorInvalidValue;
+    if (skinny) return launch_skinny<EPI_CONV, false>(At, lda, Wt, ldw, C, ldc, M, N, K, s, cv);
     if (tile_rows == 16) return launch<16, EPI_CONV, false>(At, lda, Wt, ldw, C, ldc, M, N, K, s, cv);
     if (tile_rows == 32) return launch<32, EPI_CONV, false>(At, lda, Wt, ldw, C, ldc, M, N, K, s, cv);
     return launch<64, EPI_CONV, false>(At, lda, Wt, ldw, C, ldc, M, N, K, s, cv);

@@ -45,9 +45,25 @@ cudaError_t gemm_conv(const float* At, int lda, const float* Wt, int ldw, float*
 // out[c*ld + r] = in[r*cols + c] for r < rows, 0 for rows <= r < ld (c < cols):
 // a row-major weight [rows][cols] into the K-major layout the projections read.
 cudaError_t transpose_pad(const float* in, int rows, int cols, float* out, int ld, cudaStream_t s);
+// tile_rows 1 in gemm_tiled / gemm_conv: the few-rows form for M <= 8 rows
+// (K <= 2432): one thread per (output column, dot lane), bitwise the same.
+constexpr int GEMM_FEW_ROWS = 8;
+// Whether the decode step uses the few-rows form for M real rows and N columns.
+bool gemm_few_rows(int M, int N);
+// The few-rows projection of rms_norm(A) (w [K], eps): each CTA normalises
+// its staged copy of A's M rows with rmsnorm_fm's partial sums, tree and
+// expression, so the result is bitwise rmsnorm_fm and then the projection, in
+// one launch.  Forms: store (batch-major), residual / gelu (feature-major),
+// and the in_proj conv epilogue (cv non-null, batch-major).
+struct GemmNorm {
+    const float* w;
+    float eps;
+};
+cudaError_t gemm_few_norm(const float* At, int lda, const float* Wt, int ldw, float* C, int ldc, int M, int N, int K,
+                          int epilogue, bool out_fm, const GemmNorm& nm, const GemmConv* cv, cudaStream_t s);
 // Rows per CTA tile (64, 32 or 16) gemm() uses for an M x N output.
 int gemm_tile_rows(int M, int N);
-// gemm() with an explicit CTA tile height (16, 32 or 64; 0 = gemm_tile_rows).
+// gemm() with an explicit CTA tile height (16, 32 or 64; 1 = the few-rows form; 0 = gemm_tile_rows).
 cudaError_t gemm_tiled(const float* At, int lda, const float* Wt, int ldw, float* C, int ldc, int M, int N, int K,
                        int epilogue, bool out_fm, int tile_rows, cudaStream_t s);
 

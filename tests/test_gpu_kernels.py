@@ -82,6 +82,43 @@ def test_gemm_many_waves_all_epilogues(m, n, k, tile):
     np.testing.assert_allclose(g, np.vectorize(O.gelu, otypes=[np.float32])(ref), atol=1e-6, rtol=1e-5)
 
 
+@pytest.mark.parametrize("m", [1, 2, 3, 5, 8])
+@pytest.mark.parametrize("n,k", [(2720, 608), (608, 2432), (32, 32)])
+def test_gemm_few_rows_form(m, n, k):
+    """tile_rows 1, the decode form for up to 8 sequences (one thread per
+    output column and dot lane, only the m real rows of a 64-wide operand):
+    bitwise the reference dot in both layouts, with the residual epilogue, and
+    the GELU epilogue within its tolerance; no padded row is written."""
+    rng = np.random.default_rng(m * 31 + n + k)
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    w = (0.02 * rng.standard_normal((n, k))).astype(np.float32)
+    ref = O.gemm_transb(a, w)
+    at = np.zeros((k, 64), np.float32)
+    at[:, :m] = a.T
+    g_at, g_wt = cu(at), cu(w.T.copy())
+    lib, st = _lib.lib, torch.cuda.current_stream().cuda_stream
+
+    def run(epi, fm, c):
+        ldc = c.shape[1]
+        rc = lib.krk_k_gemm_tiled(g_at.data_ptr(), 64, g_wt.data_ptr(), n, c.data_ptr(), ldc, m, n, k, epi, int(fm), 1, st)
+        assert rc == _lib.OK, lib.krk_last_error()
+        return np_(c)
+
+    marker = np.float32(-7.0)
+    got = run(0, False, cu(np.full((8, n), marker, np.float32)))
+    np.testing.assert_array_equal(got[:m], ref)
+    assert (got[m:] == marker).all()
+    got = run(0, True, cu(np.full((n, 64), marker, np.float32)))
+    np.testing.assert_array_equal(got[:, :m], ref.T)
+    assert (got[:, m:] == marker).all()
+    res = rng.standard_normal((n, 64)).astype(np.float32)
+    got = run(1, True, cu(res.copy()))
+    np.testing.assert_array_equal(got[:, :m], res[:, :m] + ref.T)
+    np.testing.assert_array_equal(got[:, m:], res[:, m:])
+    got = run(2, False, cu(np.zeros((8, n), np.float32)))
+    np.testing.assert_allclose(got[:m], np.vectorize(O.gelu, otypes=[np.float32])(ref), atol=1e-6, rtol=1e-5)
+
+
 def test_gemm_rejects_bad_shapes():
     from krikil_rs_b200._lib import KrikilError
     with pytest.raises(KrikilError):

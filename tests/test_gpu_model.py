@@ -250,6 +250,33 @@ def test_large_batch_halves_match_single_sequences(models):
         assert got[b] == ref, b
 
 
+def test_few_row_batches_match_tiled_batches(models):
+    """Decode batches of up to 8 sequences compute their projections in the
+    few-rows form (one thread per output column and dot lane, real rows only);
+    their step logits and greedy tokens equal (bitwise) those of the same
+    sequences inside a 70-sequence batch (64-row tiles), and the oracle's."""
+    gpu, orc = models
+    rng = np.random.default_rng(13)
+    prompts = [rng.integers(0, 2048, int(n)).astype(np.uint32).tolist() for n in rng.integers(1, 40, 70)]
+    big = PebbleState(gpu, 96, batch=70)
+    gpu.prefill_batch(prompts, big)
+    few = PebbleState(gpu, 96, batch=6)
+    sel = [0, 9, 33, 47, 60, 69]
+    gpu.prefill_batch([prompts[b] for b in sel], few)
+    for step in range(3):
+        toks = [(17 * b + 5 * step) % 2048 for b in range(70)]
+        lg_big = gpu.step_batch(toks, big)
+        lg_few = gpu.step_batch([toks[b] for b in sel], few)
+        for i, b in enumerate(sel):
+            np.testing.assert_array_equal(lg_few[i], lg_big[b], err_msg=f"seq {b} step {step}")
+    st_few, st_big = PebbleState(gpu, 96, batch=6), PebbleState(gpu, 96, batch=70)
+    got_few = gpu.generate_greedy([prompts[b] for b in sel], st_few, 12, stop_at_eos=False)
+    got_big = gpu.generate_greedy(prompts, st_big, 12, stop_at_eos=False)
+    assert got_few == [got_big[b] for b in sel]
+    ref, _ = O.generate_greedy(orc, O.OracleState(96), prompts[sel[2]], 12, eos=None)
+    assert got_few[2] == ref
+
+
 def test_profile_modes(models):
     """krk_state_profile: mode 1 times every kernel class (event pairs read back
     when the totals are read), mode 2 only whole calls."""
