@@ -274,8 +274,10 @@ KRK_API int krk_k_gemm(const float* At, int lda, const float* Wt, int ldw, float
                        int epilogue, int out_fm, void* stream);
 
 /* krk_k_gemm with an explicit CTA tile height: 64, 32 or 16 output rows per
- * CTA (M must be a multiple of it), 0 = the automatic choice krk_k_gemm makes.
- * Every choice gives bit-identical results. */
+ * CTA (M must be a multiple of it), 0 = the automatic choice krk_k_gemm makes,
+ * 1 = the few-rows form for M <= 8 and K <= 2432 (one thread per output
+ * column and dot lane; only the M rows are read and written, so lda, ldc may
+ * be a padded batch).  Every choice gives bit-identical results. */
 KRK_API int krk_k_gemm_tiled(const float* At, int lda, const float* Wt, int ldw, float* C, int ldc, int M, int N,
                              int K, int epilogue, int out_fm, int tile_rows, void* stream);
 
