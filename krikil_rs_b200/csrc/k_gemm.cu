@@ -7,9 +7,12 @@
 // ((l0+l4)+(l2+l6)) + ((l1+l5)+(l3+l7)).  (All K here are multiples of 8, so
 // its scalar tail is empty.)  This kernel maps those eight lanes onto the eight
 // warps of a CTA: warp w owns the k = w (mod 8) slice of every K-block and keeps
-// a full 64x32 output tile of partial sums in registers (8x8 per thread); the
+// a full 64x32 (or 32x32, 16x32) output tile of partial sums in registers; the
 // eight warp tiles are folded in the reference's order through shared memory in
 // the epilogue.  The result is bit-identical to the reference gemv for any M.
+// For up to 8 rows (a small decode batch) gemm_skinny_kernel keeps the same
+// lane-per-warp order with one thread per (output column, lane), optionally
+// normalising A (the RMSNorm that feeds the projection) in the same launch.
 // The multiply-adds are issued as packed pairs (__ffma2_rn, sm_100): each
 // component is rounded exactly as fmaf, and one instruction does two, which
 // halves the issue slots the FP32 pipes need.
