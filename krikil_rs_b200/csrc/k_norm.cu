@@ -128,7 +128,7 @@ __global__ void __launch_bounds__(256) rmsnorm_fm_kernel(const float* __restrict
 // The sum of squares is per-lane sequential then a warp tree.
 // ---------------------------------------------------------------------------
 template <int VPL, bool GATED>
-__global__ void __launch_bounds__(256, VPL <= 4 ? 3 : 1) rownorm_kernel(const float* __restrict__ x, const float* __restrict__ z,
+__global__ void __launch_bounds__(256, VPL <= 4 ? 4 : 1) rownorm_kernel(const float* __restrict__ x, const float* __restrict__ z,
                                                       const float* __restrict__ res, const float* __restrict__ w,
                                                       float eps, int64_t rows, float* __restrict__ y) {
     constexpr int DIM = 128 * VPL;
@@ -142,13 +142,9 @@ __global__ void __launch_bounds__(256, VPL <= 4 ? 3 : 1) rownorm_kernel(const fl
         for (int i = 0; i < VPL; ++i) g[i] = __ldcs(xr + lane + 32 * i);
         if (GATED) {
             const float4* zr = reinterpret_cast<const float4*>(z + r * DIM);
-            const float4* rs = reinterpret_cast<const float4*>(res + r * DIM);
             float4 zz[VPL];
 #pragma unroll
-            for (int i = 0; i < VPL; ++i) {
-                zz[i] = __ldcs(zr + lane + 32 * i);
-                rr[i] = __ldcs(rs + lane + 32 * i);
-            }
+            for (int i = 0; i < VPL; ++i) zz[i] = __ldcs(zr + lane + 32 * i);
             // y *= silu(z) (src/model.rs:688-690)
 #pragma unroll
             for (int i = 0; i < VPL; ++i) {
@@ -168,6 +164,11 @@ __global__ void __launch_bounds__(256, VPL <= 4 ? 3 : 1) rownorm_kernel(const fl
         }
         ss = warp_sum(ss);
         const float scale = 1.0f / sqrtf(ss / (float)DIM + eps);
+        if (GATED) {  // the residual row, read once the squares are summed
+            const float4* rs = reinterpret_cast<const float4*>(res + r * DIM);
+#pragma unroll
+            for (int i = 0; i < VPL; ++i) rr[i] = __ldcs(rs + lane + 32 * i);
+        }
         float4* yr = reinterpret_cast<float4*>(y + r * DIM);
 #pragma unroll
         for (int i = 0; i < VPL; ++i) {
@@ -197,13 +198,15 @@ cudaError_t launch_rownorm(const float* x, const float* z, const float* res, con
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    // one wave of resident CTAs whose warps stride over the rows
-    const int64_t want = (rows + 7) / 8;
+    // At most one wave of resident CTAs whose warps stride over the rows, as
+    // few as give every warp the same number of rows (no partly idle last pass).
     auto grid_for = [&](const void* fn) {
         int per_sm = 0;
         if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, 256, 0) != cudaSuccess || per_sm < 1) per_sm = 1;
-        const int64_t cap = (int64_t)sms * per_sm;
-        return (int)(want < cap ? want : cap);
+        const int64_t cap = (int64_t)sms * per_sm;           // CTAs of 8 warps
+        const int64_t per_warp = (rows + cap * 8 - 1) / (cap * 8);
+        const int64_t ctas = (rows + per_warp * 8 - 1) / (per_warp * 8);
+        return (int)(ctas < cap ? ctas : cap);
     };
     switch (dim / 128) {
 #define KRK_CASE(V)                                                                                 \
