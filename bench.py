@@ -262,17 +262,22 @@ def kernel_table(torch, peak, scan_t=2048):
     dev = torch.device("cuda")
     res = {}
 
-    def timeit(fn, iters=10, warm=3):
+    def timeit(fn, iters=10, warm=3, reps=8):
+        """ms per launch: the median over iters of reps back-to-back launches
+        between one pair of events (so a short kernel's time does not include
+        the host's launch gaps); every operand set is larger than L2 or the
+        kernel is compute-bound."""
         for _ in range(warm):
             fn()
         torch.cuda.synchronize()
         evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
         for a, b in evs:
             a.record()
-            fn()
+            for _ in range(reps):
+                fn()
             b.record()
         torch.cuda.synchronize()
-        return statistics.median(a.elapsed_time(b) for a, b in evs)
+        return statistics.median(a.elapsed_time(b) for a, b in evs) / reps
 
     def put(name, nbytes, ms, extra=None):
         gbs = nbytes / (ms * 1e-3) / 1e9
@@ -301,11 +306,18 @@ def kernel_table(torch, peak, scan_t=2048):
                                             "fp32_frac_nominal": round(fl / (ms * 1e-3) / fp32_peak, 3)}
         del a, wt, c
 
+    # The three inputs (100.6 MB) are smaller than L2, so back-to-back launches
+    # rotate over four copies (537 MB): no launch finds its operands cached.
     x, z, r, w = (torch.from_numpy(a).to(dev) for a in synth.fused_norm_inputs())
-    y = torch.empty_like(x)
-    put("gated_rmsnorm_residual[16384,512]", 4 * x.numel() * 4 + w.numel() * 4,
-        timeit(lambda: K.gated_rmsnorm_residual(x, z, r, w, 1e-5, y)))
-    del x, z, r, y
+    sets = [(x, z, r, torch.empty_like(x))] + [(x.clone(), z.clone(), r.clone(), torch.empty_like(x)) for _ in range(3)]
+    turn = [0]
+
+    def c2():
+        xs, zs, rs, ys = sets[turn[0] % len(sets)]
+        turn[0] += 1
+        K.gated_rmsnorm_residual(xs, zs, rs, w, 1e-5, ys)
+    put("gated_rmsnorm_residual[16384,512]", 4 * x.numel() * 4 + w.numel() * 4, timeit(c2))
+    del x, z, r, sets
 
     q, k, v, pos, kc, vc = synth.attn_decode_inputs()
     q, k, v, kc, vc = (torch.from_numpy(a).to(dev) for a in (q, k, v, kc, vc))
