@@ -271,28 +271,37 @@ constexpr int SK_STAGES = 8, SK_ROWS = 4, SK_ST = SK_ROWS * BN;  // one stage of
 // four ((p0+p1)+(p2+p3)); the eight groups in order; 1 / sqrt(sum / K + eps))
 // and each element as (x * scale) * w[k]: bitwise rmsnorm_fm and then the
 // projection, in one launch.
-template <int MT, int EPI, bool OUT_FM, bool NORM>
-__global__ void __launch_bounds__(NT) gemm_skinny_kernel(const float* __restrict__ At, int lda,
-                                                         const float* __restrict__ Wt, int ldw, float* __restrict__ C,
-                                                         int ldc, int M, int K, const GemmConv cv, const GemmNorm nm) {
-    extern __shared__ __align__(16) float smk[];  // rings [8 warps][SK_STAGES][4][32], then A [8][K/8][MT]
-    __shared__ float red[8][SKINNY_MAX_ROWS][BN + 1];
-    const int tid = threadIdx.x, j = tid >> 5, c = tid & 31;
-    const int n0 = blockIdx.x * BN;
+// LPW: dot lanes per warp (1: 8 warps, 32 columns per CTA; 2: 4 warps, 16
+// columns per CTA, half-warp h taking lane w + 4h) -- twice the CTAs for
+// projections whose 32-column grid leaves most SMs idle.
+template <int MT, int EPI, bool OUT_FM, bool NORM, int LPW>
+__global__ void __launch_bounds__(256 / LPW) gemm_skinny_kernel(const float* __restrict__ At, int lda,
+                                                                const float* __restrict__ Wt, int ldw,
+                                                                float* __restrict__ C, int ldc, int M, int K,
+                                                                const GemmConv cv, const GemmNorm nm) {
+    constexpr int NWARPS = 8 / LPW, NTH = 32 * NWARPS, CW = BN / LPW;
+    extern __shared__ __align__(16) float smk[];  // rings [warps][SK_STAGES][4 * LPW][CW], then A [8][K/8][MT]
+    __shared__ float red[8][SKINNY_MAX_ROWS][CW + 1];
+    const int tid = threadIdx.x, w = tid >> 5, l = tid & 31;
+    const int h = l / CW, c = l % CW, j = w + NWARPS * h;  // this thread's dot lane and column
+    const int n0 = blockIdx.x * CW;
     const int kj = K / 8;  // rows of one dot lane
-    float* ring = smk + j * (SK_STAGES * SK_ST);
-    float* sa = smk + 8 * SK_STAGES * SK_ST;
-    const int nst = K / (8 * SK_ROWS);  // stages of this warp's rows k = j + 8i
-    // lane c copies 16 bytes of row (c >> 3) of a stage: columns n0 + 4(c & 7) ..
-    const float* wsrc = Wt + (size_t)(j + 8 * (c >> 3)) * ldw + n0 + (c & 7) * 4;
+    float* ring = smk + w * (SK_STAGES * SK_ST);
+    float* sa = smk + NWARPS * SK_STAGES * SK_ST;
+    const int nst = K / (8 * SK_ROWS);  // stages of a lane's rows k = j + 8i
+    // lane l copies 16 bytes of stage row rho = l / (CW / 4) (the warp's lane
+    // w + NWARPS * (rho / 4), chain row 4 st + rho % 4): columns n0 + 4 (l % (CW / 4)) ..
+    const int rho = l / (CW / 4), col4 = l % (CW / 4);
+    const float* wsrc =
+        Wt + (size_t)(w + NWARPS * (rho / SK_ROWS) + 8 * (rho % SK_ROWS)) * ldw + n0 + col4 * 4;
     const size_t wstage = (size_t)8 * SK_ROWS * ldw;
-    const int wdst = (c >> 3) * BN + (c & 7) * 4;
+    const int wdst = rho * CW + col4 * 4;
 #pragma unroll
     for (int st = 0; st < SK_STAGES - 1; ++st) {
         if (st < nst) cp_async16(ring + st * SK_ST + wdst, wsrc + st * wstage);
         cp_async_commit();
     }
-    for (int i = tid; i < K * MT; i += NT) {
+    for (int i = tid; i < K * MT; i += NTH) {
         const int k = i / MT, m = i % MT;
         sa[((k & 7) * kj + (k >> 3)) * MT + m] = At[(size_t)k * lda + m];
     }
@@ -300,8 +309,8 @@ __global__ void __launch_bounds__(NT) gemm_skinny_kernel(const float* __restrict
     if (NORM) {
         __shared__ float ps[32][MT];
         __shared__ float scl[MT];
-        if (tid < 32 * MT) {
-            const int m = tid % MT, q = tid / MT;
+        for (int pi = tid; pi < 32 * MT; pi += NTH) {
+            const int m = pi % MT, q = pi / MT;
             float ss = 0.0f;
             for (int k = q; k < K; k += 32) {
                 const float v = sa[((k & 7) * kj + (k >> 3)) * MT + m];
@@ -320,7 +329,7 @@ __global__ void __launch_bounds__(NT) gemm_skinny_kernel(const float* __restrict
             scl[tid] = 1.0f / sqrtf(t / (float)K + nm.eps);
         }
         __syncthreads();
-        for (int i = tid; i < K * MT; i += NT) {
+        for (int i = tid; i < K * MT; i += NTH) {
             const int pos = i / MT, m = i % MT;
             sa[i] = sa[i] * scl[m] * __ldg(nm.w + (pos / kj) + 8 * (pos % kj));
         }
@@ -336,7 +345,7 @@ __global__ void __launch_bounds__(NT) gemm_skinny_kernel(const float* __restrict
         const int nx = st + SK_STAGES - 1;
         if (nx < nst) cp_async16(ring + (nx % SK_STAGES) * SK_ST + wdst, wsrc + nx * wstage);
         cp_async_commit();
-        const float* ws = ring + (st % SK_STAGES) * SK_ST;
+        const float* ws = ring + (st % SK_STAGES) * SK_ST + h * SK_ROWS * CW;
         float av[SK_ROWS * MT];  // rows 4st .. 4st+3 of this lane's chain, MT values each
 #pragma unroll
         for (int q = 0; q < SK_ROWS * MT / 4; ++q) {
@@ -345,30 +354,30 @@ __global__ void __launch_bounds__(NT) gemm_skinny_kernel(const float* __restrict
         }
 #pragma unroll
         for (int r = 0; r < SK_ROWS; ++r) {  // k = j + 8(4 st + r): this lane's chain in order
-            const float w = ws[r * BN + c];
+            const float wv = ws[r * CW + c];
 #pragma unroll
-            for (int m = 0; m < MT; ++m) acc[m] = fmaf(av[r * MT + m], w, acc[m]);
+            for (int m = 0; m < MT; ++m) acc[m] = fmaf(av[r * MT + m], wv, acc[m]);
         }
     }
     cp_async_wait<0>();
 #pragma unroll
     for (int m = 0; m < MT; ++m) red[j][m][c] = acc[m];
     __syncthreads();
-    if (tid >= M * BN) return;
-    const int m = tid / BN, cc = tid % BN, n = n0 + cc;
-    float l[8];
+    if (tid >= M * CW) return;
+    const int m = tid / CW, cc = tid % CW, n = n0 + cc;
+    float lp[8];
 #pragma unroll
-    for (int w = 0; w < 8; ++w) l[w] = red[w][m][cc];
-    float v = ((l[0] + l[4]) + (l[2] + l[6])) + ((l[1] + l[5]) + (l[3] + l[7]));  // src/math.rs:110-117
+    for (int q = 0; q < 8; ++q) lp[q] = red[q][m][cc];
+    float v = ((lp[0] + lp[4]) + (lp[2] + lp[6])) + ((lp[1] + lp[5]) + (lp[3] + lp[7]));  // src/math.rs:110-117
     float* out = OUT_FM ? C + (size_t)n * ldc + m : C + (size_t)m * ldc + n;
     if (EPI == EPI_CONV) {  // src/model.rs:643-654 for this (row, channel)
         if (n >= cv.lo && n < cv.hi && m < cv.rows && (!cv.active || cv.active[m])) {
             const int ch = n - cv.lo;
             float4* sp = reinterpret_cast<float4*>(cv.state + ((size_t)m * (cv.hi - cv.lo) + ch) * 4);
-            const float4 st = *sp, wv = reinterpret_cast<const float4*>(cv.w)[ch];
-            // after the shift the window is [st.y, st.z, st.w, x]
-            const float val = st.y * wv.x + st.z * wv.y + st.w * wv.z + v * wv.w + cv.bias[ch];
-            *sp = make_float4(st.y, st.z, st.w, v);
+            const float4 sv = *sp, wv = reinterpret_cast<const float4*>(cv.w)[ch];
+            // after the shift the window is [sv.y, sv.z, sv.w, x]
+            const float val = sv.y * wv.x + sv.z * wv.y + sv.w * wv.z + v * wv.w + cv.bias[ch];
+            *sp = make_float4(sv.y, sv.z, sv.w, v);
             v = silu(val);
         }
     } else if (EPI == EPI_RESIDUAL) {
@@ -379,18 +388,31 @@ __global__ void __launch_bounds__(NT) gemm_skinny_kernel(const float* __restrict
     *out = v;
 }
 
-template <int MT, int EPI, bool OUT_FM, bool NORM>
+template <int MT, int EPI, bool OUT_FM, bool NORM, int LPW>
 cudaError_t launch_skinny_mt(const float* At, int lda, const float* Wt, int ldw, float* C, int ldc, int M, int N, int K,
                              cudaStream_t s, const GemmConv& cv, const GemmNorm& nm) {
     static DeviceOnce once;
-    constexpr size_t ring_bytes = (size_t)8 * SK_STAGES * SK_ST * sizeof(float);
+    constexpr size_t ring_bytes = (size_t)(8 / LPW) * SK_STAGES * SK_ST * sizeof(float);
     const size_t smem = ring_bytes + (size_t)K * MT * sizeof(float);
-    cudaError_t e = once.set_smem((const void*)gemm_skinny_kernel<MT, EPI, OUT_FM, NORM>,
+    cudaError_t e = once.set_smem((const void*)gemm_skinny_kernel<MT, EPI, OUT_FM, NORM, LPW>,
                                   ring_bytes + (size_t)SKINNY_MAX_K * MT * sizeof(float));
     if (e != cudaSuccess) return e;
-    gemm_skinny_kernel<MT, EPI, OUT_FM, NORM><<<N / BN, NT, smem, s>>>(At, lda, Wt, ldw, C, ldc, M, K, cv, nm);
+    gemm_skinny_kernel<MT, EPI, OUT_FM, NORM, LPW>
+        <<<N / (BN / LPW), 256 / LPW, smem, s>>>(At, lda, Wt, ldw, C, ldc, M, K, cv, nm);
     add_launches(1);
     return cudaGetLastError();
+}
+
+template <int MT, int EPI, bool OUT_FM, bool NORM>
+cudaError_t launch_skinny_mt(const float* At, int lda, const float* Wt, int ldw, float* C, int ldc, int M, int N, int K,
+                             cudaStream_t s, const GemmConv& cv, const GemmNorm& nm) {
+    // 16 columns per CTA where that measured faster (CUDA graphs of the decode
+    // projections): one or two rows, at most 2048 columns and no norm inside --
+    // fc2 8.7 -> 7.8 us, wo 4.0 -> 3.6 us at one row; wider projections, more
+    // rows and the norm's pass over the staged rows lose the warps it takes.
+    if (!NORM && M <= 2 && N <= 2048)
+        return launch_skinny_mt<MT, EPI, OUT_FM, NORM, 2>(At, lda, Wt, ldw, C, ldc, M, N, K, s, cv, nm);
+    return launch_skinny_mt<MT, EPI, OUT_FM, NORM, 1>(At, lda, Wt, ldw, C, ldc, M, N, K, s, cv, nm);
 }
 
 // M <= 8 rows; lda >= 4 * ceil(M / 4) (lda % 4 == 0 and lda >= M guarantee it)

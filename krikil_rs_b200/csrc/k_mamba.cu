@@ -23,8 +23,14 @@ constexpr int SSD_N = 128;  // d_state (src/model.rs:22)
 // four products followed by a warp tree.  CONV: the head's 64 x channels go
 // through the 4-tap causal conv + SiLU first, on a 3-slot state [B][H*P][3].
 // ---------------------------------------------------------------------------
-template <bool CONV>
+// RPW: state rows per warp.  16: one CTA per (sequence, head); 4 (small
+// batches, no conv): the head's 64 rows over four CTAs of four warps
+// (gridDim.z = 4), each warp's rows requested in one round trip -- the same
+// arithmetic per row, so bitwise the same state and y.
+template <bool CONV, int RPW>
 __global__ void __launch_bounds__(128) ssd_step_kernel(SsdStepArgs a) {
+    static_assert(RPW == 16 || (RPW == 4 && !CONV), "rows per warp");
+    constexpr int G0 = RPW < 8 ? RPW : 8;  // rows requested up front
     const int b = blockIdx.x, h = blockIdx.y;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     // The first 8 of this warp's 16 state rows are requested before anything
@@ -32,10 +38,10 @@ __global__ void __launch_bounds__(128) ssd_step_kernel(SsdStepArgs a) {
     // dependent round trips in front of the state stream); the other 8 after
     // the first are consumed (16 up front would cost occupancy: 122 registers).
     float* st = a.ssm + ((size_t)b * a.H + h) * (SSD_P * SSD_N) + lane * 4;
-    const int pb = warp * 16;
-    float4 s0[8], s1[8];
+    const int pb = (blockIdx.z * 4 + warp) * RPW;
+    float4 s0[G0], s1[G0];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) s0[i] = __ldcs(reinterpret_cast<const float4*>(st + (pb + i) * SSD_N));
+    for (int i = 0; i < G0; ++i) s0[i] = __ldcs(reinterpret_cast<const float4*>(st + (pb + i) * SSD_N));
     if (a.active && !a.active[b]) return;
     __shared__ float xs[SSD_P], gs[SSD_P];
     const int c0 = h * SSD_P;
@@ -67,15 +73,15 @@ __global__ void __launch_bounds__(128) ssd_step_kernel(SsdStepArgs a) {
 
     const bool gate = a.z != nullptr;
 #pragma unroll
-    for (int r0 = 0; r0 < 16; r0 += 8) {
+    for (int r0 = 0; r0 < RPW; r0 += G0) {
         const int pbase = pb + r0;
         if (r0 == 8) {
 #pragma unroll
-            for (int i = 0; i < 8; ++i) s1[i] = __ldcs(reinterpret_cast<const float4*>(st + (pb + 8 + i) * SSD_N));
+            for (int i = 0; i < G0; ++i) s1[i] = __ldcs(reinterpret_cast<const float4*>(st + (pb + 8 + i) * SSD_N));
         }
         float4* s = r0 == 0 ? s0 : s1;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
+        for (int i = 0; i < G0; ++i) {
             const int p = pbase + i;
             const float xp = xs[p];
             const float xdt = xp * dtv;
@@ -340,9 +346,13 @@ cudaError_t ssd_step(const SsdStepArgs& a, bool conv, cudaStream_t s) {
     if (a.P != SSD_P || a.N != SSD_N || a.B <= 0 || a.H <= 0 || (a.bc_sb & 3) ||
         (((uintptr_t)a.bm | (uintptr_t)a.cm | (uintptr_t)a.ssm) & 15))
         return cudaErrorInvalidValue;
-    dim3 grid(a.B, a.H);
-    if (conv) ssd_step_kernel<true><<<grid, 128, 0, s>>>(a);
-    else ssd_step_kernel<false><<<grid, 128, 0, s>>>(a);
+    if (conv) {
+        ssd_step_kernel<true, 16><<<dim3(a.B, a.H), 128, 0, s>>>(a);
+    } else if ((int64_t)a.B * a.H <= 148) {  // at most one CTA per SM: four CTAs per head, one round trip each
+        ssd_step_kernel<false, 4><<<dim3(a.B, a.H, 4), 128, 0, s>>>(a);
+    } else {
+        ssd_step_kernel<false, 16><<<dim3(a.B, a.H), 128, 0, s>>>(a);
+    }
     add_launches(1);
     return cudaGetLastError();
 }
