@@ -283,8 +283,8 @@ KRK_API int krk_k_gemm_tiled(const float* At, int lda, const float* Wt, int ldw,
 
 /* The tile height krk_k_gemm chooses for an M x N output on the current
  * device (148 SMs assumed when no device answers): the smallest of 16 / 32 /
- * 64 rows whose grid fits in one wave of one CTA per SM, else 32 when 64-row
- * tiles fill under 1.5 waves, else 64.  Host only; launches nothing. */
+ * 64 rows whose grid fits in one wave of one CTA per SM, else 32 below 256
+ * rows and 64 from there on.  Host only; launches nothing. */
 KRK_API int krk_k_gemm_tile_rows(int M, int N);
 
 /* Embedding gather (src/model.rs:330-338, :598) into feature-major

@@ -488,16 +488,18 @@ cudaError_t transpose_pad(const float* in, int rows, int cols, float* out, int l
     return cudaGetLastError();
 }
 
-// Tile choice.  When a tile height of 16, 32 or 64 rows puts the whole
-// projection in one wave (no more CTAs than SMs: the decode step of a small
-// batch, where a launch lasts one tile's K loop), the smallest such height,
-// whose warps have the shortest loop (at 64 rows: 16-row tiles for the
-// 608-column projections, 32 for wqkv and the LM head, 64 for in_proj and
-// fc1, measured as the fastest of the three each).  Otherwise 32-row tiles
-// (3 CTAs per SM, ~10% lower FMA rate than the 64-row tile at full
-// occupancy) only when 64-row tiles would fill fewer than 1.5 waves of 2 CTAs
-// per SM -- e.g. the 608-column projections at batch 1024 (304 tiles on 296
-// slots).  Every choice gives bit-identical results.
+// Tile choice (gemm_tile_rows, below).  When a tile height of 16, 32 or 64
+// rows puts the whole projection in one wave (no more CTAs than SMs: the
+// decode step of a small batch, where a launch lasts one tile's K loop), the
+// smallest such height, whose warps have the shortest loop (at 64 rows:
+// 16-row tiles for the 608-column projections, 32 for wqkv and the LM head, 64
+// for in_proj and fc1, measured as the fastest of the three each).  Otherwise
+// 32-row tiles (3 CTAs per SM) below 256 rows -- at 128 rows they beat 64-row
+// tiles by 4-27% on in_proj, out_proj, wo, fc1 and fc2 -- and 64-row tiles
+// from 256 rows on, where they match or beat 32-row ones on every projection
+// (at 320, 384 and 1024 rows, 8 back-to-back launches per timing: fc2 at 1024
+// rows 0.497 vs 0.483 of nominal FP32).  Every choice gives bit-identical
+// results.
 cudaError_t gemm_few_norm(const float* At, int lda, const float* Wt, int ldw, float* C, int ldc, int M, int N, int K,
                           int epilogue, bool out_fm, const GemmNorm& nm, const GemmConv* cv, cudaStream_t s) {
     if (M <= 0 || M > GEMM_FEW_ROWS || N <= 0 || K <= 0 || K > SKINNY_MAX_K || N % BN || K % BK || lda % 4 ||
@@ -532,8 +534,7 @@ int gemm_tile_rows(int M, int N) {
         if (M % t == 0 && (int64_t)(M / t) * cols <= sms) return t;
     if (M % 32) return 16;
     if (M % 64) return 32;
-    const int64_t t64 = (int64_t)(M / 64) * cols;
-    return 2 * t64 < 3 * sms * 2 ? 32 : 64;
+    return M < 256 ? 32 : 64;
 }
 
 cudaError_t gemm_tiled(const float* At, int lda, const float* Wt, int ldw, float* C, int ldc, int M, int N, int K,

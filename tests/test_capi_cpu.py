@@ -137,12 +137,13 @@ def test_gemm_refuses_operands_past_32bit_offsets():
 def test_gemm_tile_choice_small_batches():
     """The automatic projection tile height (host rule, B200's 148 SMs): at
     decode sizes the smallest of 16/32/64 rows whose grid fits in one wave,
-    else the 32/64 rule of larger grids.  Every height gives bitwise the same
+    else 32 rows below 256 rows and 64 from there on.  Every height gives bitwise the same
     result (the GPU projection tests run each one)."""
     m64 = {608: 16, 1824: 32, 2048: 32, 2432: 64, 2720: 64}
     m128 = {608: 32, 1824: 64, 2048: 64, 2432: 32, 2720: 32}
     for m, table in ((64, m64), (128, m128)):
         for n, t in table.items():
             assert lib.krk_k_gemm_tile_rows(m, n) == t, (m, n)
-    assert lib.krk_k_gemm_tile_rows(1024, 608) == 32 and lib.krk_k_gemm_tile_rows(1024, 2720) == 64
+    assert lib.krk_k_gemm_tile_rows(192, 608) == 32 and lib.krk_k_gemm_tile_rows(192, 2720) == 32
+    assert lib.krk_k_gemm_tile_rows(1024, 608) == 64 and lib.krk_k_gemm_tile_rows(1024, 2720) == 64
     assert lib.krk_k_gemm_tile_rows(16384, 2720) == 64 and lib.krk_k_gemm_tile_rows(0, 32) == 0
