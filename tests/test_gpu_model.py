@@ -343,20 +343,21 @@ def test_multi_group_prefill_on_streams(models):
 
 def test_small_batch_step_graphs(models):
     """Decode steps of batches of one 64-row tile replay CUDA graphs, one per
-    count of 64-key attention blocks: a 120-token generation crossing several
-    counts, and a 40-sequence batch with ragged prompts, give exactly the
-    tokens of the same calls launched kernel by kernel (per-kernel profiling
-    turns the graphs off), and the single sequence matches the oracle."""
+    count of 512-key attention splits: a 120-token generation from a
+    460-token prompt, crossing into the second split, and a 40-sequence batch
+    with ragged prompts, give exactly the tokens of the same calls launched
+    kernel by kernel (per-kernel profiling turns the graphs off), and the
+    single sequence matches the oracle."""
     gpu, orc = models
-    prompt = _prompt(100, 7)
+    prompt = _prompt(460, 7)
     runs = []
     for profiled in (False, True):
-        st = PebbleState(gpu, 512)
+        st = PebbleState(gpu, 1024)
         if profiled:
             st.profile(True)
         runs.append(gpu.generate_greedy([prompt], st, 120, repetition_penalty=1.2, stop_at_eos=False)[0])
     assert runs[0] == runs[1] and len(runs[0]) == 120
-    ref, _ = O.generate_greedy(orc, O.OracleState(512), prompt, 120, repetition_penalty=1.2, eos=None)
+    ref, _ = O.generate_greedy(orc, O.OracleState(1024), prompt, 120, repetition_penalty=1.2, eos=None)
     assert runs[0] == ref
     rng = np.random.default_rng(8)
     prompts = [rng.integers(0, 2048, int(n)).astype(np.uint32).tolist() for n in rng.integers(1, 90, 40)]
