@@ -1028,7 +1028,10 @@ cudaError_t attn_decode(const AttnDecodeArgs& args, cudaStream_t s) {
     }
     add_launches(1);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    if (max_splits > 1) {
+    // With one split in the grid (max_keys bounds every position), every
+    // sequence has one split, which the split kernel already wrote as the
+    // output, and the merge would find nothing to do: it is not launched.
+    if (max_splits > 1 && grid.z > 1) {
         // splits of the longest sequence: many take the wide merge
         const bool wide = (keys + a.split - 1) / a.split >= ACW_MIN_SPLITS;
         const size_t cs = wide ? acw_smem_bytes(max_splits, a.dh) : 0;
