@@ -716,6 +716,15 @@ void decode_forward(krk_state* s, const uint8_t* active, int max_keys) {
     const krk_model* m = s->m;
     Part parts[4];
     const int np = decode_parts(s, parts);
+    // The step of a few sequences is a chain of ~30 kernels of a few
+    // microseconds each, whose launch gaps and first memory round trips are a
+    // large share of the step: each kernel is scheduled behind the one before
+    // it and prefetches its weights meanwhile (programmatic dependent launch;
+    // step graphs: +7% tokens/s at 1 sequence, +2% at 8).  From 32 sequences
+    // on it measured slower (-9% at 32, -6% at 128), and parts on several
+    // streams fill each other's gaps anyway.  Per-kernel event timing wants
+    // the kernels apart.
+    krk::PdlScope pdl(np == 1 && s->B <= krk::GEMM_FEW_ROWS && !(s->prof.on && s->prof.per_kernel));
     cudaEvent_t joins[4] = {nullptr, s->ev_join, s->ev_join3, s->ev_join4};
     if (np >= 2) {
         kk(cudaEventRecord(s->ev_fork, m->stream), "fork");

@@ -40,6 +40,29 @@ KRK_DEV float gelu(float x) { return 0.5f * x * (1.0f + as_erf(x * 0.70710678118
 KRK_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 KRK_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
+bool pdl_enabled();  // a PdlScope(true) is alive on this thread (kernels.h)
+
+// kern<<<grid, block, smem, s>>>(args...), with programmatic stream
+// serialization while pdl_enabled().  Only for kernels that call pdl_wait()
+// in every block before they touch memory other than weights.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    if (pdl_enabled()) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    return cudaLaunchKernelEx(&cfg, kern, static_cast<Args&&>(args)...);
+}
+
 KRK_DEV float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

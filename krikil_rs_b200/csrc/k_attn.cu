@@ -84,7 +84,10 @@ __global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(AttnDecodeArgs 
     float* sc = red + AD_RED;
     float* tile = sc + a.split;
     float* scratch = tile + AD_TILE * L::KLD;
-    pdl_trigger();  // the combine kernel may be scheduled behind the last blocks
+    // behind the projection that writes q, k and v: wait for it, then let the
+    // merge (or the next projection) be scheduled behind this kernel's blocks
+    pdl_wait();
+    pdl_trigger();
 
     const int b = blockIdx.x, h = blockIdx.y, sp = blockIdx.z, tid = threadIdx.x;
     if (a.active && !a.active[b]) return;
@@ -696,6 +699,11 @@ constexpr int ACW_MIN_SPLITS = 9;  // the wide merge from this many splits per s
 // positions while that kernel drains, then waits for its partials.
 __global__ void attn_combine_kernel(AttnDecodeArgs a, int max_splits) {
     const int b = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
+    // Every block waits, also those with nothing to merge: this kernel's
+    // completion then implies the split kernel's, which the next kernel (a
+    // programmatic launch too) relies on for the outputs written unmerged.
+    pdl_wait();
+    pdl_trigger();
     if (a.active && !a.active[b]) return;
     const int pos = a.pos[b];
     if (pos < 0 || pos >= a.ctx) {
@@ -704,7 +712,6 @@ __global__ void attn_combine_kernel(AttnDecodeArgs a, int max_splits) {
     }
     const int nsplit = (pos + a.split) / a.split;
     if (nsplit <= 1 || d >= a.dh) return;
-    pdl_wait();
     // Fewer than ACW_MIN_SPLITS splits here: every partial this thread needs
     // is requested at once (one round trip), then merged in split order.
     const float* wp = a.work + ((size_t)b * a.H + h) * max_splits * (a.dh + 2);
@@ -746,6 +753,8 @@ __global__ void __launch_bounds__(ACW_THREADS) attn_combine_wide_kernel(AttnDeco
     extern __shared__ __align__(16) float cm[];
     __shared__ float mred[ACW_THREADS / 32];
     const int b = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
+    pdl_wait();  // in every block (see attn_combine_kernel)
+    pdl_trigger();
     if (a.active && !a.active[b]) return;
     const int pos = a.pos[b];
     if (pos < 0 || pos >= a.ctx) {
@@ -754,7 +763,6 @@ __global__ void __launch_bounds__(ACW_THREADS) attn_combine_wide_kernel(AttnDeco
     }
     const int nsplit = (pos + a.split) / a.split;
     if (nsplit <= 1) return;
-    pdl_wait();
     const int dh = a.dh, st = dh + 2, groups = ACW_THREADS / dh;
     float* wt = cm;               // [max_splits]: split max, then its weight
     float* ls = cm + max_splits;  // [max_splits]: split sum
@@ -1018,13 +1026,15 @@ cudaError_t attn_decode(const AttnDecodeArgs& args, cudaStream_t s) {
         const size_t smem = ad_smem_bytes<76>(a.split);
         if (smem > 227 * 1024) return cudaErrorInvalidValue;
         if ((e = once.set_smem((const void*)attn_decode_kernel<76>, 227 * 1024)) != cudaSuccess) return e;
-        attn_decode_kernel<76><<<grid, AD_THREADS, smem, s>>>(a, max_splits);
+        if ((e = launch_pdl(attn_decode_kernel<76>, grid, dim3(AD_THREADS), smem, s, a, max_splits)) != cudaSuccess)
+            return e;
     } else {
         static DeviceOnce once;
         const size_t smem = ad_smem_bytes<64>(a.split);
         if (smem > 227 * 1024) return cudaErrorInvalidValue;
         if ((e = once.set_smem((const void*)attn_decode_kernel<64>, 227 * 1024)) != cudaSuccess) return e;
-        attn_decode_kernel<64><<<grid, AD_THREADS, smem, s>>>(a, max_splits);
+        if ((e = launch_pdl(attn_decode_kernel<64>, grid, dim3(AD_THREADS), smem, s, a, max_splits)) != cudaSuccess)
+            return e;
     }
     add_launches(1);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;

@@ -88,14 +88,20 @@ __global__ void __launch_bounds__(NT, Tile<BM>::MIN_CTAS)
     unsigned a_off = (unsigned)(warp + 8 * (lane / (BM / 4))) * lda + m0 + (lane % (BM / 4)) * 4;
     unsigned w_off = (unsigned)(warp + 8 * (lane >> 3)) * ldw + n0 + (lane & 7) * 4;
     // This warp's four rows of the next K-block into the ring slot at As.
-    auto load_stage = [&](float* As) {
+    auto load_a = [&](float* As) {
 #pragma unroll
         for (int j = 0; j < T::A_F4; ++j)
             cp_async16(As + (lane / (BM / 4) + j * AR) * BM + (lane % (BM / 4)) * 4, At + a_off + j * (8 * AR) * lda);
         if (BM == 16 && lane < 16) cp_async16(As + (lane >> 2) * BM + (lane & 3) * 4, At + a_off);
-        cp_async16(As + WROWS * BM + (lane >> 3) * BN + (lane & 7) * 4, Wt + w_off);
         a_off += BK * lda;
+    };
+    auto load_w = [&](float* As) {
+        cp_async16(As + WROWS * BM + (lane >> 3) * BN + (lane & 7) * 4, Wt + w_off);
         w_off += BK * ldw;
+    };
+    auto load_stage = [&](float* As) {
+        load_a(As);
+        load_w(As);
     };
 
     // Partial sums in pairs, one __ffma2_rn per pair.  Batch-major output pairs
@@ -109,9 +115,16 @@ __global__ void __launch_bounds__(NT, Tile<BM>::MIN_CTAS)
     for (int i = 0; i < TM * 4; ++i) acc2[i] = make_float2(0.0f, 0.0f);
 
     int wr = (WSTAGE - 1) * T::WST, rd = 0;  // ring offsets of the slot filled next and the slot read next
+    // The first slots' weights are copied before A, which the kernels before
+    // this one write: they join the first slot's copy group.
+#pragma unroll
+    for (int s = 0; s < WSTAGE - 1; ++s)
+        if (s < nkb) load_w(ring + s * T::WST);
+    pdl_wait();
+    pdl_trigger();
 #pragma unroll
     for (int s = 0; s < WSTAGE - 1; ++s) {
-        if (s < nkb) load_stage(ring + s * T::WST);
+        if (s < nkb) load_a(ring + s * T::WST);
         cp_async_commit();
     }
     for (int kb = 0; kb < nkb; ++kb) {
@@ -301,6 +314,10 @@ __global__ void __launch_bounds__(256 / LPW) gemm_skinny_kernel(const float* __r
         if (st < nst) cp_async16(ring + st * SK_ST + wdst, wsrc + st * wstage);
         cp_async_commit();
     }
+    // the weights are in flight; A (and the output, the conv state) belong to
+    // the kernels before this one
+    pdl_wait();
+    pdl_trigger();
     for (int i = tid; i < K * MT; i += NTH) {
         const int k = i / MT, m = i % MT;
         sa[((k & 7) * kj + (k >> 3)) * MT + m] = At[(size_t)k * lda + m];
@@ -397,8 +414,9 @@ cudaError_t launch_skinny_mt(const float* At, int lda, const float* Wt, int ldw,
     cudaError_t e = once.set_smem((const void*)gemm_skinny_kernel<MT, EPI, OUT_FM, NORM, LPW>,
                                   ring_bytes + (size_t)SKINNY_MAX_K * MT * sizeof(float));
     if (e != cudaSuccess) return e;
-    gemm_skinny_kernel<MT, EPI, OUT_FM, NORM, LPW>
-        <<<N / (BN / LPW), 256 / LPW, smem, s>>>(At, lda, Wt, ldw, C, ldc, M, K, cv, nm);
+    e = launch_pdl(gemm_skinny_kernel<MT, EPI, OUT_FM, NORM, LPW>, dim3(N / (BN / LPW)), dim3(256 / LPW), smem, s, At,
+                   lda, Wt, ldw, C, ldc, M, K, cv, nm);
+    if (e != cudaSuccess) return e;
     add_launches(1);
     return cudaGetLastError();
 }
@@ -431,8 +449,9 @@ cudaError_t launch(const float* At, int lda, const float* Wt, int ldw, float* C,
     static DeviceOnce once;
     cudaError_t e = once.set_smem((const void*)gemm_lane8_kernel<BM, EPI, OUT_FM>, Tile<BM>::SMEM_BYTES);
     if (e != cudaSuccess) return e;
-    dim3 grid(M / BM, N / BN);
-    gemm_lane8_kernel<BM, EPI, OUT_FM><<<grid, NT, Tile<BM>::SMEM_BYTES, s>>>(At, lda, Wt, ldw, C, ldc, K, cv);
+    e = launch_pdl(gemm_lane8_kernel<BM, EPI, OUT_FM>, dim3(M / BM, N / BN), dim3(NT), Tile<BM>::SMEM_BYTES, s, At,
+                   lda, Wt, ldw, C, ldc, K, cv);
+    if (e != cudaSuccess) return e;
     add_launches(1);
     return cudaGetLastError();
 }

@@ -42,6 +42,11 @@ __global__ void __launch_bounds__(128) ssd_step_kernel(SsdStepArgs a) {
     float4 s0[G0], s1[G0];
 #pragma unroll
     for (int i = 0; i < G0; ++i) s0[i] = __ldcs(reinterpret_cast<const float4*>(st + (pb + i) * SSD_N));
+    // Launched behind the projection that writes x, B, C, dt and z: the state
+    // (last written by this layer's update a step earlier, several launches
+    // back) is already in flight.
+    pdl_wait();
+    pdl_trigger();
     if (a.active && !a.active[b]) return;
     __shared__ float xs[SSD_P], gs[SSD_P];
     const int c0 = h * SSD_P;
@@ -346,13 +351,15 @@ cudaError_t ssd_step(const SsdStepArgs& a, bool conv, cudaStream_t s) {
     if (a.P != SSD_P || a.N != SSD_N || a.B <= 0 || a.H <= 0 || (a.bc_sb & 3) ||
         (((uintptr_t)a.bm | (uintptr_t)a.cm | (uintptr_t)a.ssm) & 15))
         return cudaErrorInvalidValue;
+    cudaError_t e;
     if (conv) {
-        ssd_step_kernel<true, 16><<<dim3(a.B, a.H), 128, 0, s>>>(a);
+        e = launch_pdl(ssd_step_kernel<true, 16>, dim3(a.B, a.H), dim3(128), 0, s, a);
     } else if ((int64_t)a.B * a.H <= 148) {  // at most one CTA per SM: four CTAs per head, one round trip each
-        ssd_step_kernel<false, 4><<<dim3(a.B, a.H, 4), 128, 0, s>>>(a);
+        e = launch_pdl(ssd_step_kernel<false, 4>, dim3(a.B, a.H, 4), dim3(128), 0, s, a);
     } else {
-        ssd_step_kernel<false, 16><<<dim3(a.B, a.H), 128, 0, s>>>(a);
+        e = launch_pdl(ssd_step_kernel<false, 16>, dim3(a.B, a.H), dim3(128), 0, s, a);
     }
+    if (e != cudaSuccess) return e;
     add_launches(1);
     return cudaGetLastError();
 }

@@ -11,6 +11,11 @@ static unsigned long long g_launches = 0;
 uint64_t launch_count() { return __atomic_load_n(&g_launches, __ATOMIC_RELAXED); }
 void add_launches(uint64_t n) { __atomic_fetch_add(&g_launches, (unsigned long long)n, __ATOMIC_RELAXED); }
 
+static thread_local bool t_pdl = false;
+bool pdl_enabled() { return t_pdl; }
+PdlScope::PdlScope(bool on) : prev_(t_pdl) { t_pdl = on; }
+PdlScope::~PdlScope() { t_pdl = prev_; }
+
 cudaError_t DeviceOnce::set_smem(const void* func, size_t bytes) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -62,6 +67,13 @@ __global__ void __launch_bounds__(256) rmsnorm_fm_kernel(const float* __restrict
     const bool full = (m0 + NORM_COLS <= ldx) && ((ldx & 3) == 0) && ((((uintptr_t)x) & 15) == 0);
     // the weights travel with the block when both are 16-byte pieces
     const bool wasync = WS && (K & 3) == 0 && (((uintptr_t)w) & 15) == 0;
+    if (wasync) {  // the weights first: x comes from the kernels before this one
+        for (int i = tid; i < K / 4; i += 256) cp_async16(ws + 4 * i, w + 4 * i);
+    } else if (WS) {
+        for (int k = tid; k < K; k += 256) ws[k] = w[k];
+    }
+    pdl_wait();
+    pdl_trigger();
     if (full) {
         for (int i = tid; i < K * (NORM_COLS / 4); i += 256) {
             const int k = i / (NORM_COLS / 4), c4 = i % (NORM_COLS / 4);
@@ -72,11 +84,6 @@ __global__ void __launch_bounds__(256) rmsnorm_fm_kernel(const float* __restrict
             int k = i / NORM_COLS, c = i % NORM_COLS;
             blk[i] = c < ncols ? x[(size_t)k * ldx + m0 + c] : 0.0f;
         }
-    }
-    if (wasync) {
-        for (int i = tid; i < K / 4; i += 256) cp_async16(ws + 4 * i, w + 4 * i);
-    } else if (WS) {
-        for (int k = tid; k < K; k += 256) ws[k] = w[k];
     }
     cp_async_commit();
     cp_async_wait<0>();
@@ -232,6 +239,8 @@ __global__ void __launch_bounds__(256) embed_fm_kernel(const uint32_t* __restric
     __shared__ float tile[32][33];
     const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
     const int m0 = blockIdx.x * 32, k0 = blockIdx.y * 32;
+    pdl_wait();  // the tokens come from the kernels before this one
+    pdl_trigger();
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
         int m = m0 + ty + 8 * i, k = k0 + tx;
@@ -265,8 +274,9 @@ cudaError_t rmsnorm_fm(const float* x, int ldx, const float* w, float eps, int K
     const void* fn = ws ? (const void*)rmsnorm_fm_kernel<true> : (const void*)rmsnorm_fm_kernel<false>;
     cudaError_t e = once[ws ? 1 : 0].set_smem(fn, (size_t)NORM_MAXK * (NORM_COLS + 1) * sizeof(float));
     if (e != cudaSuccess) return e;
-    if (ws) rmsnorm_fm_kernel<true><<<(M + NORM_COLS - 1) / NORM_COLS, 256, smem, s>>>(x, ldx, w, eps, K, M, out, ldo);
-    else rmsnorm_fm_kernel<false><<<(M + NORM_COLS - 1) / NORM_COLS, 256, smem, s>>>(x, ldx, w, eps, K, M, out, ldo);
+    e = launch_pdl(ws ? rmsnorm_fm_kernel<true> : rmsnorm_fm_kernel<false>, dim3((M + NORM_COLS - 1) / NORM_COLS),
+                   dim3(256), smem, s, x, ldx, w, eps, K, M, out, ldo);
+    if (e != cudaSuccess) return e;
     add_launches(1);
     return cudaGetLastError();
 }
@@ -284,7 +294,8 @@ cudaError_t embed_fm(const uint32_t* tok, const float* wte, int vocab, int K, in
                      cudaStream_t s) {
     if (K <= 0 || M <= 0 || ldo < M) return cudaErrorInvalidValue;
     dim3 grid((M + 31) / 32, (K + 31) / 32);
-    embed_fm_kernel<<<grid, 256, 0, s>>>(tok, wte, vocab, K, M, out, ldo);
+    const cudaError_t e = launch_pdl(embed_fm_kernel, grid, dim3(256), 0, s, tok, wte, vocab, K, M, out, ldo);
+    if (e != cudaSuccess) return e;
     add_launches(1);
     return cudaGetLastError();
 }

@@ -17,6 +17,27 @@ struct DeviceOnce {
     cudaError_t set_smem(const void* func, size_t bytes);
 };
 
+// Programmatic dependent launch of a decode step's chain of kernels.  While a
+// PdlScope(true) lives on the calling thread, the launchers of the
+// projections (both forms), feature-major RMSNorm, embedding gather, SSD
+// update and decode attention launch their kernels with programmatic stream
+// serialization: a kernel is scheduled while the one before it in the stream
+// is finishing, issues only reads of weights, and waits (pdl_wait) for that
+// kernel's completion before it reads or writes any other memory -- so the
+// launch latency and the weight prefetch overlap the previous kernel.  Other
+// launchers, and these outside a scope, launch as usual.
+bool pdl_enabled();
+class PdlScope {
+  public:
+    explicit PdlScope(bool on);
+    ~PdlScope();
+    PdlScope(const PdlScope&) = delete;
+    PdlScope& operator=(const PdlScope&) = delete;
+
+  private:
+    bool prev_;
+};
+
 // ---------------------------------------------------------------- projections
 // C = A . W^T in fp32 with the reference's dot-product order (see k_gemm.cu).
 //   At: A stored feature-major, At[k*lda + m]  (M columns, K rows)

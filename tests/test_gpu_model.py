@@ -344,10 +344,12 @@ def test_multi_group_prefill_on_streams(models):
 def test_small_batch_step_graphs(models):
     """Decode steps of batches of one 64-row tile replay CUDA graphs, one per
     count of 512-key attention splits: a 120-token generation from a
-    460-token prompt, crossing into the second split, and a 40-sequence batch
-    with ragged prompts, give exactly the tokens of the same calls launched
-    kernel by kernel (per-kernel profiling turns the graphs off), and the
-    single sequence matches the oracle."""
+    460-token prompt, crossing into the second split, a 40-sequence batch
+    with ragged prompts, and a 6-sequence batch whose longer prompts reach the
+    end of the context early (inactive sequences beside active ones), give
+    exactly the tokens of the same calls launched kernel by kernel (per-kernel
+    profiling turns the graphs and the chained launches of a few sequences'
+    steps off), and the single sequence matches the oracle."""
     gpu, orc = models
     prompt = _prompt(460, 7)
     runs = []
@@ -368,6 +370,15 @@ def test_small_batch_step_graphs(models):
             st.profile(True)
         outs.append(gpu.generate_sample(prompts, st, 70, 0.8, 0.9, 20, 1.1, list(range(40)), stop_at_eos=False))
     assert outs[0] == outs[1]
+    prompts = [rng.integers(0, 2048, int(n)).astype(np.uint32).tolist() for n in (100, 5, 77, 30, 120, 64)]
+    outs = []
+    for profiled in (False, True):
+        st = PebbleState(gpu, 128, batch=6)
+        if profiled:
+            st.profile(True)
+        outs.append(gpu.generate_sample(prompts, st, 60, 0.8, 0.9, 20, 1.1, list(range(6)), stop_at_eos=False))
+    assert outs[0] == outs[1]
+    assert [len(o) for o in outs[0]] == [29, 60, 52, 60, 9, 60]  # ctx - prompt + 1 where that is below 60
 
 
 @pytest.mark.parametrize("bsz,parts", [(128, 3), (384, 3), (520, 2)])
