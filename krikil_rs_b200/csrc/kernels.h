@@ -89,8 +89,10 @@ cudaError_t gemm_tiled(const float* At, int lda, const float* Wt, int ldw, float
                        int epilogue, bool out_fm, int tile_rows, cudaStream_t s);
 
 // ---------------------------------------------------------------- norms
-// out[k*ldo+m] = x[k*ldx+m] * scale(m) * w[k], scale from the sequential sum of
-// squares over k (src/math.rs:41-54) -- feature-major activations.
+// out[k*ldo+m] = x[k*ldx+m] * scale(m) * w[k] (src/math.rs:41-54) -- feature-major
+// activations; the sum of squares over k in a fixed order of 32 partials, the
+// same for a column whatever its batch (the reference's sequential sum up to
+// rounding).
 cudaError_t rmsnorm_fm(const float* x, int ldx, const float* w, float eps, int K, int M, float* out, int ldo,
                        cudaStream_t s);
 // Row-major RMSNorm over [rows, dim].
