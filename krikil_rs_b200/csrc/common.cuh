@@ -40,11 +40,13 @@ KRK_DEV float gelu(float x) { return 0.5f * x * (1.0f + as_erf(x * 0.70710678118
 KRK_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 KRK_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
-bool pdl_enabled();  // a PdlScope(true) is alive on this thread (kernels.h)
+bool pdl_enabled();     // a PdlScope(true) is alive on this thread (kernels.h)
+int launch_priority();  // a PriorityScope's priority, or 0 (kernels.h)
 
 // kern<<<grid, block, smem, s>>>(args...), with programmatic stream
-// serialization while pdl_enabled().  Only for kernels that call pdl_wait()
-// in every block before they touch memory other than weights.
+// serialization while pdl_enabled() and the launch priority of a live
+// PriorityScope.  Only for kernels that call pdl_wait() in every block before
+// they touch memory other than weights.
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
                               Args&&... args) {
@@ -53,13 +55,20 @@ inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, siz
     cfg.blockDim = block;
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
+    unsigned na = 0;
     if (pdl_enabled()) {
-        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-        attr[0].val.programmaticStreamSerializationAllowed = 1;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
+        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[na].val.programmaticStreamSerializationAllowed = 1;
+        ++na;
     }
+    if (const int prio = launch_priority()) {
+        attr[na].id = cudaLaunchAttributePriority;
+        attr[na].val.priority = prio;
+        ++na;
+    }
+    cfg.attrs = na ? attr : nullptr;
+    cfg.numAttrs = na;
     return cudaLaunchKernelEx(&cfg, kern, static_cast<Args&&>(args)...);
 }
 

@@ -16,6 +16,11 @@ bool pdl_enabled() { return t_pdl; }
 PdlScope::PdlScope(bool on) : prev_(t_pdl) { t_pdl = on; }
 PdlScope::~PdlScope() { t_pdl = prev_; }
 
+static thread_local int t_priority = 0;
+int launch_priority() { return t_priority; }
+PriorityScope::PriorityScope(int priority) : prev_(t_priority) { t_priority = priority; }
+PriorityScope::~PriorityScope() { t_priority = prev_; }
+
 cudaError_t DeviceOnce::set_smem(const void* func, size_t bytes) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);

@@ -38,6 +38,21 @@ class PdlScope {
     bool prev_;
 };
 
+// Launch priority of the same launchers while a PriorityScope lives on the
+// calling thread (0: the stream's own; lower is more urgent, down to the
+// device's greatest priority).  Kernel nodes of a captured graph keep it.
+int launch_priority();
+class PriorityScope {
+  public:
+    explicit PriorityScope(int priority);
+    ~PriorityScope();
+    PriorityScope(const PriorityScope&) = delete;
+    PriorityScope& operator=(const PriorityScope&) = delete;
+
+  private:
+    int prev_;
+};
+
 // ---------------------------------------------------------------- projections
 // C = A . W^T in fp32 with the reference's dot-product order (see k_gemm.cu).
 //   At: A stored feature-major, At[k*lda + m]  (M columns, K rows)
