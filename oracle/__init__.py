@@ -7,6 +7,7 @@ krikil-rs; see its header for what is and is not pinned.
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes as C
 import os
 import subprocess
@@ -55,6 +56,8 @@ lib.orc_rms_norm.argtypes = [_fp, _fp, C.c_float, _fp, C.c_int]
 lib.orc_rms_norm_inplace.argtypes = [_fp, _fp, C.c_float, C.c_int]
 lib.orc_gemv.argtypes = [_fp, _fp, _fp, C.c_int, C.c_int]
 lib.orc_gemm_transb.argtypes = [_fp, _fp, _fp, C.c_int, C.c_int, C.c_int]
+lib.orc_set_prefill_gemm_order.argtypes = [C.c_int]
+lib.orc_prefill_gemm_order.restype = C.c_int
 lib.orc_softmax_inplace.argtypes = [_fp, C.c_int]
 lib.orc_apply_rope.argtypes = [_fp, _fp, C.c_int, C.c_int, C.c_int, C.c_float]
 lib.orc_precompute_a.argtypes = [_fp, _fp, C.c_int]
@@ -136,6 +139,25 @@ def gemm_transb(a, b):
     out = np.empty((a.shape[0], b.shape[0]), np.float32)
     lib.orc_gemm_transb(_p(a), _p(b), _p(out), a.shape[0], a.shape[1], b.shape[0])
     return out
+
+
+PREFILL_GEMM_ORDERS = {"dot": 0, "matrixmultiply": 1}
+
+
+@contextlib.contextmanager
+def prefill_gemm_order(order: str):
+    """Run the block with the prefill projections (gemm_transb,
+    src/math.rs:188-211) summed in ``order``: "dot" is the gemv dot order of
+    src/math.rs:70-124 (the default, and the CUDA projections' order);
+    "matrixmultiply" is the restated order of matrixmultiply 0.3.11's sgemm,
+    the crate the reference calls there (256-long K blocks, one FMA
+    accumulator per element within a block, blocks added in order)."""
+    old = lib.orc_prefill_gemm_order()
+    lib.orc_set_prefill_gemm_order(PREFILL_GEMM_ORDERS[order])
+    try:
+        yield
+    finally:
+        lib.orc_set_prefill_gemm_order(old)
 
 
 def softmax(x):

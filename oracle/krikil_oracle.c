@@ -19,9 +19,12 @@
  *   - transcendental calls go to the same glibc libm entry points Rust's f32
  *     methods lower to (expf, logf, powf, sinf, cosf), and sqrtf is IEEE;
  *   - the one third-party piece, matrixmultiply 0.3.11's sgemm used by
- *     gemm_transb (src/math.rs:188-211), is NOT restated: prefill projections use
- *     the gemv dot order instead, so prefill logits agree with the reference only
- *     within tolerance.
+ *     gemm_transb (src/math.rs:188-211), is restated from its published blocked
+ *     algorithm in a second, selectable order (orc_set_prefill_gemm_order): the
+ *     default prefill projections use the gemv dot order (the order the CUDA
+ *     projections reproduce), and the restated sgemm order measures how far the
+ *     reference's own prefill sits from it.  That restatement is unpinned
+ *     against the crate itself (no Rust toolchain to run it).
  */
 #include <math.h>
 #include <stdint.h>
@@ -122,15 +125,45 @@ EXPORT void orc_gemv(const float *w, const float *x, float *out, int rows, int c
 }
 
 /*
- * Stand-in for src/math.rs:188-211 gemm_transb (C[m,n] = A[m,:] . B[n,:]),
- * which the reference delegates to matrixmultiply::sgemm.  Each element here is
- * the gemv dot of src/math.rs:70-124, so the result matches the reference's
- * prefill only within tolerance (different summation order).
+ * src/math.rs:188-211 gemm_transb (C[m,n] = A[m,:] . B[n,:]) in the summation
+ * order of matrixmultiply 0.3.11's sgemm, restated from its published
+ * BLIS-style algorithm (the crate is a dependency the reference does not
+ * vendor; Cargo.toml:11 pins 0.3.11 with default features, so no threading):
+ * the K dimension is cut into blocks of KC = 256 (its f32 default); within a
+ * block the 8x8 AVX/FMA micro-kernel keeps one accumulator per C element,
+ * starting at zero and updated k by k with a fused multiply-add; the first
+ * block stores C = 1.0 * ab (beta 0), every later block C = 1.0 * ab + 1.0 * C
+ * (beta 1), which with alpha = beta = 1 is one rounded add whether or not the
+ * store fuses it.  Packing, the M/N blocking and the masked edge tiles move
+ * data only, so they do not change any element's order.
  */
+static float sgemm_order_dot(const float *a, const float *b, int k) {
+    enum { KC = 256 };
+    float c = 0.0f;
+    for (int k0 = 0; k0 < k; k0 += KC) {
+        int k1 = k0 + KC < k ? k0 + KC : k;
+        float ab = 0.0f;
+        for (int kk = k0; kk < k1; kk++) ab = fmaf(a[kk], b[kk], ab);
+        c = k0 == 0 ? ab : ab + c;
+    }
+    return c;
+}
+
+/* 0: each element is the gemv dot of src/math.rs:70-124 (the default, and the
+ * order the CUDA projections reproduce bit for bit); 1: the restated
+ * matrixmultiply sgemm order above.  Test infrastructure: set it only while
+ * no prefill runs. */
+static int g_prefill_gemm_order = 0;
+EXPORT void orc_set_prefill_gemm_order(int order) { g_prefill_gemm_order = order; }
+EXPORT int orc_prefill_gemm_order(void) { return g_prefill_gemm_order; }
+
 EXPORT void orc_gemm_transb(const float *a, const float *b, float *c, int m, int k, int n) {
+    const int mm = g_prefill_gemm_order == 1;
 #pragma omp parallel for schedule(static)
     for (int i = 0; i < m; i++)
-        for (int r = 0; r < n; r++) c[(size_t)i * n + r] = orc_dot(a + (size_t)i * k, b + (size_t)r * k, k);
+        for (int r = 0; r < n; r++)
+            c[(size_t)i * n + r] = mm ? sgemm_order_dot(a + (size_t)i * k, b + (size_t)r * k, k)
+                                      : orc_dot(a + (size_t)i * k, b + (size_t)r * k, k);
 }
 
 /* src/math.rs:213-232 */

@@ -135,6 +135,67 @@ def test_generate_greedy_loop_semantics(synth_weights):
     assert out == out2
 
 
+# ---- prefill projections in matrixmultiply's summation order -----------------
+def test_sgemm_order_gemm_close_to_float64():
+    """The restated matrixmultiply 0.3.11 sgemm order (src/math.rs:188-211) is a
+    correct product, and it rounds differently from the gemv dot order."""
+    rng = np.random.default_rng(3)
+    for m, k, n in ((5, 608, 37), (3, 1216, 19), (2, 2432, 11), (4, 100, 9), (3, 257, 5)):
+        a = rng.standard_normal((m, k), dtype=np.float32)
+        b = rng.standard_normal((n, k), dtype=np.float32)
+        exact = a.astype(np.float64) @ b.astype(np.float64).T
+        with O.prefill_gemm_order("matrixmultiply"):
+            mm = O.gemm_transb(a, b)
+        dot = O.gemm_transb(a, b)
+        bound = 4 * k * np.finfo(np.float32).eps * (np.abs(a).astype(np.float64) @ np.abs(b).astype(np.float64).T)
+        assert np.all(np.abs(mm - exact) <= bound)
+        assert np.all(np.abs(dot - exact) <= bound)
+        assert not np.array_equal(mm, dot)
+    assert O.lib.orc_prefill_gemm_order() == 0
+
+
+def _prefill_and_generate(w, prompt, new, order):
+    m = O.OracleModel(w)
+    with O.prefill_gemm_order(order):
+        st = O.OracleState(2048)
+        logits = O.forward_prefill(m, st, prompt)
+        ssm = {i: a.copy() for i, a in st.ssm.items()}
+        conv = {i: a.copy() for i, a in st.conv.items()}
+        kc = {i: a[:len(prompt)].copy() for i, a in st.kc.items()}
+        toks, _ = O.generate_greedy(m, O.OracleState(2048), prompt, new, eos=None)
+    return logits, ssm, conv, kc, toks
+
+
+@pytest.mark.parametrize("case", ["c1", "c5"])
+def test_prefill_in_matrixmultiply_order_within_tolerance(case, synth_weights):
+    """The reference's prefill projections go through matrixmultiply::sgemm
+    (src/math.rs:188-211, called at src/model.rs:387, 458, 484, 554, 570, 577);
+    the CUDA path and the default oracle sum them in the gemv dot order.  With
+    the sgemm order restated, the prefill logits stay within the logits
+    tolerance (max-abs 1e-4 plus rel 1e-5), the SSD, conv and K states within
+    the same tolerance, and the greedy streams that follow are identical.  c1:
+    the 32-token prompt of the batch-1 workload (seed 0) and 64 tokens; c5: two
+    of the 128-token prompts of the 1024-sequence workload (seed 1, the first
+    and the last) and 32 tokens each."""
+    from krikil_rs_b200 import synth
+    if case == "c1":
+        prompts, new = [np.random.default_rng(0).integers(0, O.VOCAB, 32).astype(np.uint32)], 64
+    else:
+        p = synth.decode_prompts()
+        prompts, new = [p[0], p[-1]], 32
+    for prompt in prompts:
+        d = _prefill_and_generate(synth_weights, prompt, new, "dot")
+        mm = _prefill_and_generate(synth_weights, prompt, new, "matrixmultiply")
+        assert not np.array_equal(d[0], mm[0])  # the orders do differ
+        np.testing.assert_allclose(mm[0], d[0], atol=1e-4, rtol=1e-5)
+        for i in d[1]:
+            np.testing.assert_allclose(mm[1][i], d[1][i], atol=1e-4, rtol=1e-5)
+            np.testing.assert_allclose(mm[2][i], d[2][i], atol=1e-4, rtol=1e-5)
+        for i in d[3]:
+            np.testing.assert_allclose(mm[3][i], d[3][i], atol=1e-4, rtol=1e-5)
+        assert mm[4] == d[4]
+
+
 # ---- golden fixtures of the reference ----------------------------------------
 def test_golden_fixtures_consistent():
     with open(os.path.join(GOLDEN, "reference_prefill_logits.json")) as f:
