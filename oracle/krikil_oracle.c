@@ -465,9 +465,11 @@ EXPORT uint32_t orc_sample_greedy(const float *logits, int vocab, const uint32_t
 /*     keystream's 32-bit words in order (block n/16, word n%16);              */
 /*   - Rng::gen::<f32>() (Standard): (next_u32 >> 8) * 2^-24, in [0, 1).       */
 /* The ChaCha block function is checked against the published ChaCha20 test   */
-/* vectors (same code with 20 rounds); the PCG expansion and the f32           */
-/* conversion have no vectors here, so the seeded stream is unpinned against   */
-/* the reference.                                                              */
+/* vectors (same code with 20 rounds), and the keyed generator (key layout,    */
+/* counter and stream words, 12 rounds, word order) against the value-         */
+/* stability known answers of rand 0.8's StdRng and rand_chacha 0.3's          */
+/* ChaCha20Rng; the PCG expansion and the f32 conversion have no vectors, so   */
+/* the seeded stream as a whole stays unpinned against the reference.          */
 /* ------------------------------------------------------------------------- */
 static uint32_t rotl32(uint32_t x, int r) { return (x << r) | (x >> (32 - r)); }
 

@@ -242,6 +242,61 @@ def test_chacha_block_published_vectors():
     assert ser[:16].hex() == "10f1e7e4d13b5915500fdd1fa32071c4"
 
 
+def _rng_from_seed_bytes(seed: bytes, rounds: int):
+    """A ChaCha generator keyed by a 32-byte seed (SeedableRng::from_seed of
+    rand_chacha 0.3): key words little-endian, block counter and stream 0.
+    With 12 rounds it is the oracle's Rng (orc_rng_next_u32); the 20-round
+    form draws keystream words from the same block function."""
+    key = [int.from_bytes(seed[4 * i:4 * i + 4], "little") for i in range(8)]
+    if rounds == 12:
+        r = O.Rng(0)
+        r.state[:8] = key
+        r.state[8:] = 0
+        return r.next_u32
+    const = [0x61707865, 0x3320646E, 0x79622D32, 0x6B206574]
+    words = iter([])
+    blk = [0]
+
+    def next_u32():
+        nonlocal words
+        w = next(words, None)
+        if w is None:
+            words = iter(O.chacha_block(const + key + [blk[0], 0, 0, 0], 20))
+            blk[0] += 1
+            w = next(words)
+        return w
+    return next_u32
+
+
+def _seed_bytes_from(next_u32) -> bytes:
+    """SeedableRng::from_rng: 32 bytes taken with fill_bytes, i.e. the next
+    eight keystream words in order."""
+    return b"".join(next_u32().to_bytes(4, "little") for _ in range(8))
+
+
+def test_stdrng_value_stability_vectors():
+    """Known answers of the generators the reference's Sampler draws from
+    (StdRng, src/sampler.rs:35-40 and :142): the value-stability vectors of
+    rand 0.8 (StdRng = rand_chacha 0.3 ChaCha12Rng) and of rand_chacha 0.3
+    (ChaCha20Rng): a generator from a 32-byte seed, its first output, then a
+    generator seeded from its next 32 bytes and that one's first output.  They
+    pin the key layout, the counter and stream words, StdRng's 12 rounds and the
+    order in which the block generator hands out words (next_u64 = two words,
+    low first).  rand_core 0.6's seed_from_u64 expansion (PCG32) has no such
+    vector and stays restated only."""
+    nxt = _rng_from_seed_bytes(bytes([1, 0, 0, 0, 23, 0, 0, 0, 200, 1, 0, 0, 210, 30, 0, 0] + [0] * 16), 12)
+    x0 = nxt() | (nxt() << 32)
+    nxt1 = _rng_from_seed_bytes(_seed_bytes_from(nxt), 12)
+    x1 = nxt1() | (nxt1() << 32)
+    assert [x0, x1] == [10719222850664546238, 14064965282130556830]
+
+    seed = bytes([0] * 8 + [1] + [0] * 7 + [2] + [0] * 7 + [3] + [0] * 7)
+    nxt = _rng_from_seed_bytes(seed, 20)
+    assert nxt() == 137206642
+    nxt1 = _rng_from_seed_bytes(_seed_bytes_from(nxt), 20)
+    assert nxt1() == 1325750369
+
+
 def test_rng_stream_deterministic_and_uniform():
     a, b = O.Rng(42), O.Rng(42)
     xs = [a.gen_f32() for _ in range(4000)]
