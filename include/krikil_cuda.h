@@ -334,6 +334,27 @@ KRK_API int krk_k_rope_kv_attn_decode(const float* q, const float* k, const floa
                                       const int32_t* pos, float* out, float* work, int B, int H, int dh, int ctx,
                                       int split, float theta, void* stream);
 
+/* Prefill RoPE (src/math.rs:234-260) + KV-cache append + causal softmax
+ * attention (src/model.rs:486-548) of packed query rows for S sequences.
+ * Sequence s owns rows cu_seqlens[s] .. cu_seqlens[s+1]-1 of qkv (q | k | v of
+ * H*dh floats each, row stride q_rs; total_rows rows in all) and its first row
+ * sits at position start[s], keys 0..start[s]-1 being in its cache already.  q
+ * is rotated in place; the rotated k and v of row r go to
+ * kc/vc[s*c_sb + h*c_sh + pos*c_st + d]; out[r*o_rs + (h*dh + d)*o_cs] gets row
+ * r's attention over keys 0..its position (dh = 64 or 76).  The rows run in
+ * blocks of rows_per_block = krk_k_attn_prefill_rows(kmax, dh) consecutive rows
+ * of one sequence: blocks holds nblocks int32 pairs (sequence, first row
+ * within it) on the device, covering every row once; kmax >= start[s] + rows of
+ * s for every s.  RoPE angles use the host-libm inverse frequencies and
+ * sincosf.  The model calls the same two kernels with its host-libm angle
+ * table. */
+KRK_API int krk_k_attn_prefill_rows(int kmax, int dh);
+KRK_API int krk_k_rope_kv_attn_prefill(float* qkv, int64_t q_rs, float* kc, float* vc, int64_t c_sb, int64_t c_sh,
+                                       int64_t c_st, const int32_t* cu_seqlens, const int32_t* start, int S,
+                                       int total_rows, int H, int dh, float theta, const int32_t* blocks,
+                                       int nblocks, int rows_per_block, int kmax, float* out, int64_t o_rs,
+                                       int64_t o_cs, void* stream);
+
 /* Allocation-free variant of krk_k_rope_kv_attn_decode (no counterpart in the
  * reference, which has no device memory).  For callers that cannot allocate or
  * pass device scratch -- a host that binds only this header and has no CUDA

@@ -1722,6 +1722,31 @@ int krk_k_rope_kv_attn_decode(const float* q, const float* k, const float* v, fl
     return cuda_status(krk::attn_decode(a, (cudaStream_t)stream), "rope_kv_attn_decode");
 }
 
+int krk_k_attn_prefill_rows(int kmax, int dh) {
+    if (kmax <= 0 || (dh != 64 && dh != 76)) return 0;
+    return krk::attn_prefill_rows(kmax, dh);
+}
+
+int krk_k_rope_kv_attn_prefill(float* qkv, int64_t q_rs, float* kc, float* vc, int64_t c_sb, int64_t c_sh,
+                               int64_t c_st, const int32_t* cu_seqlens, const int32_t* start, int S, int total_rows,
+                               int H, int dh, float theta, const int32_t* blocks, int nblocks, int rows_per_block,
+                               int kmax, float* out, int64_t o_rs, int64_t o_cs, void* stream) {
+    if (S <= 0 || total_rows <= 0 || H <= 0 || nblocks <= 0)
+        return fail(KRK_INVALID, "prefill attention needs S, total_rows, H and nblocks > 0");
+    if (q_rs < (int64_t)3 * H * dh) return fail(KRK_INVALID, "q_rs shorter than a q | k | v row");
+    if (rows_per_block != krk::attn_prefill_rows(kmax, dh))
+        return fail(KRK_INVALID, "rows_per_block must be krk_k_attn_prefill_rows(kmax, dh)");
+    const cudaStream_t s = (cudaStream_t)stream;
+    int st = cuda_status(krk::rope_kv_prefill(qkv, q_rs, kc, vc, c_sb, c_sh, c_st, cu_seqlens, start, S, H, dh,
+                                              total_rows, theta, nullptr, s),
+                         "rope_kv_prefill");
+    if (st != KRK_OK) return st;
+    return cuda_status(krk::attn_prefill(qkv, q_rs, kc, vc, c_sb, c_sh, c_st, cu_seqlens, start,
+                                         reinterpret_cast<const int2*>(blocks), nblocks, rows_per_block, H, dh, kmax,
+                                         out, o_rs, o_cs, s),
+                       "attn_prefill");
+}
+
 int krk_k_wait_probe(const float* src16, int polls, int copy, int32_t* status, void* stream) {
     return cuda_status(krk::wait_probe(src16, polls, copy != 0, status, (cudaStream_t)stream), "wait_probe");
 }

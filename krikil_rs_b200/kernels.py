@@ -5,6 +5,7 @@ of this library's sm_100a kernels (krk_k_* in include/krikil_cuda.h).
 """
 from __future__ import annotations
 
+import itertools
 from typing import Optional
 
 import torch
@@ -130,6 +131,40 @@ def rope_kv_attn_decode(q, k, v, kc, vc, pos, split: int = 0, theta: float = 100
     check(lib.krk_k_rope_kv_attn_decode(q.data_ptr(), k.data_ptr(), v.data_ptr(), kc.data_ptr(), vc.data_ptr(),
                                         pos.data_ptr(), out.data_ptr(), work.data_ptr(), b, h, dh, ctx, split, theta,
                                         _stream()))
+    return out
+
+
+def attn_prefill_rows(kmax: int, dh: int) -> int:
+    return int(lib.krk_k_attn_prefill_rows(kmax, dh))
+
+
+def rope_kv_attn_prefill(qkv, kc, vc, lens, start, H: int, dh: int, theta: float = 10000.0,
+                         cache_layout: str = "model"):
+    """Packed prefill rows of len(lens) sequences: qkv [rows, 3*H*dh] (q rotated
+    in place), sequence s starting at position start[s] of its cache.  Caches:
+    "model" [S, ctx, H*dh] (the model's layout) or "bhtd" [S, H, ctx, dh].
+    Builds the row-block table as the model does and returns out [rows, H*dh]."""
+    _f32(qkv, kc, vc)
+    lens = [int(x) for x in lens]
+    start = [int(x) for x in start]
+    S, rows = len(lens), sum(lens)
+    if cache_layout == "model":
+        ctx = kc.shape[1]
+        c_sb, c_sh, c_st = ctx * H * dh, dh, H * dh
+    else:
+        ctx = kc.shape[2]
+        c_sb, c_sh, c_st = H * ctx * dh, ctx * dh, dh
+    kmax = max(s0 + n for s0, n in zip(start, lens))
+    rpb = attn_prefill_rows(kmax, dh)
+    blocks = [(s, r0) for s in range(S) for r0 in range(0, lens[s], rpb)]
+    dev = qkv.device
+    cu = torch.tensor([0] + list(itertools.accumulate(lens)), dtype=torch.int32, device=dev)
+    st = torch.tensor(start, dtype=torch.int32, device=dev)
+    blk = torch.tensor(blocks, dtype=torch.int32, device=dev).reshape(-1)
+    out = torch.zeros((rows, H * dh), device=dev, dtype=torch.float32)
+    check(lib.krk_k_rope_kv_attn_prefill(qkv.data_ptr(), qkv.shape[1], kc.data_ptr(), vc.data_ptr(), c_sb, c_sh,
+                                         c_st, cu.data_ptr(), st.data_ptr(), S, rows, H, dh, theta, blk.data_ptr(),
+                                         len(blocks), rpb, kmax, out.data_ptr(), H * dh, 1, _stream()))
     return out
 
 

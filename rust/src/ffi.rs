@@ -138,6 +138,12 @@ extern "C" {
                                      vc: *mut c_float, pos: *const i32, out: *mut c_float, work: *mut c_float,
                                      b: c_int, h: c_int, dh: c_int, ctx: c_int, split: c_int, theta: c_float,
                                      stream: *mut c_void) -> c_int;
+    pub fn krk_k_attn_prefill_rows(kmax: c_int, dh: c_int) -> c_int;
+    pub fn krk_k_rope_kv_attn_prefill(qkv: *mut c_float, q_rs: i64, kc: *mut c_float, vc: *mut c_float, c_sb: i64,
+                                      c_sh: i64, c_st: i64, cu_seqlens: *const i32, start: *const i32, s: c_int,
+                                      total_rows: c_int, h: c_int, dh: c_int, theta: c_float, blocks: *const i32,
+                                      nblocks: c_int, rows_per_block: c_int, kmax: c_int, out: *mut c_float,
+                                      o_rs: i64, o_cs: i64, stream: *mut c_void) -> c_int;
     pub fn krk_k_rope_kv_attn_decode_noalloc(q: *const c_float, k: *const c_float, v: *const c_float,
                                              kc: *mut c_float, vc: *mut c_float, pos: *const i32,
                                              out: *mut c_float, b: c_int, h: c_int, dh: c_int, ctx: c_int,

@@ -316,6 +316,65 @@ def test_rope_kv_attn_decode_edges(dh, ctx, posv, split):
     np.testing.assert_array_equal(np_(g_vc), o_vc)
 
 
+@pytest.mark.parametrize("dh,layout,lens,start", [
+    (76, "model", [1, 17, 40], [0, 5, 100]),   # model dims: a one-row sequence, ragged blocks, nonzero starts
+    (64, "bhtd", [9, 64, 3], [0, 0, 250]),     # the synthetic cache layout, a block boundary at 64 rows
+    (76, "model", [300, 2], [0, 1500]),        # many 8-row blocks; a short sequence deep in its cache
+])
+def test_rope_kv_attn_prefill_vs_oracle(dh, layout, lens, start):
+    """Prefill RoPE + KV append + causal attention (src/model.rs:486-548) through
+    krk_k_rope_kv_attn_prefill, against the oracle run row by row: row i of a
+    sequence is the decode step at position start + i over the keys before it
+    (the reference's prefill and step attention share dot, softmax and PV
+    order).  Appended K within the RoPE tolerance, V bitwise, history untouched."""
+    rng = np.random.default_rng(sum(lens) + dh)
+    S, H = len(lens), 8
+    ctx = max(s0 + n for s0, n in zip(start, lens)) + 3
+    rows = sum(lens)
+    qkv = rng.standard_normal((rows, 3 * H * dh)).astype(np.float32)
+    kc = rng.standard_normal((S, H, ctx, dh)).astype(np.float32)
+    vc = rng.standard_normal((S, H, ctx, dh)).astype(np.float32)
+
+    o_kc, o_vc = kc.copy(), vc.copy()
+    ref = np.empty((rows, H, dh), np.float32)
+    r = 0
+    for s in range(S):
+        for i in range(lens[s]):
+            q, k, v = (a[None] for a in qkv[r].reshape(3, H, dh))
+            pos = np.array([start[s] + i], np.int32)
+            ref[r] = O.rope_kv_attn_decode(q, k, v, o_kc[s:s + 1], o_vc[s:s + 1], pos)[0]
+            r += 1
+
+    def to_dev(c):
+        return cu(c.transpose(0, 2, 1, 3).reshape(S, ctx, H * dh)) if layout == "model" else cu(c)
+
+    def from_dev(c):
+        c = np_(c)
+        return c.reshape(S, ctx, H, dh).transpose(0, 2, 1, 3) if layout == "model" else c
+
+    g_kc, g_vc = to_dev(kc), to_dev(vc)
+    out = K.rope_kv_attn_prefill(cu(qkv), g_kc, g_vc, lens, start, H, dh, cache_layout=layout)
+    np.testing.assert_allclose(np_(out).reshape(rows, H, dh), ref, atol=1e-4, rtol=1e-5)
+    gk, gv = from_dev(g_kc), from_dev(g_vc)
+    for s in range(S):
+        new = slice(start[s], start[s] + lens[s])
+        np.testing.assert_allclose(gk[s, :, new], o_kc[s, :, new], atol=1e-5, rtol=1e-5)
+        np.testing.assert_array_equal(gv[s, :, new], o_vc[s, :, new])
+        np.testing.assert_array_equal(gk[s, :, :start[s]], kc[s, :, :start[s]])  # history untouched
+        np.testing.assert_array_equal(gv[s, :, start[s] + lens[s]:], vc[s, :, start[s] + lens[s]:])
+
+
+def test_rope_kv_attn_prefill_rejects_bad_tables():
+    """Argument errors come back as KRK_INVALID before any launch."""
+    assert K.attn_prefill_rows(100, 76) == 8 and K.attn_prefill_rows(100, 80) == 0
+    qkv = torch.zeros((4, 3 * 8 * 76), device=DEV)
+    kc = torch.zeros((1, 8, 16, 76), device=DEV)
+    with pytest.raises(_lib.KrikilError):
+        _lib.check(_lib.lib.krk_k_rope_kv_attn_prefill(qkv.data_ptr(), qkv.shape[1], kc.data_ptr(), kc.data_ptr(),
+                                                       0, 0, 0, None, None, 1, 4, 8, 76, 1e4, None, 1, 1, 4,
+                                                       qkv.data_ptr(), 608, 1, None))  # rows_per_block 1, not 8
+
+
 @pytest.mark.parametrize("split,ctx", [(64, 2048), (128, 700), (256, 2048), (512, 2048), (384, 2000),
                                        (64, 64 * 65)])
 def test_rope_kv_attn_decode_split_merge(split, ctx):
