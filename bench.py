@@ -360,7 +360,7 @@ def kernel_table(torch, peak, scan_t=2048):
 
 # ----------------------------------------------------------------- our arm
 def c1_line(args, model, peak):
-    """BASELINE config 1 on the device: batch 1, a 32-token prompt (ids
+    """The single-sequence workload on the device: batch 1, a 32-token prompt (ids
     ~U[0,2048), seed 0), 64 greedy tokens, context 2048, through the same
     generate call; the oracle's batch-1 rate on this host beside it."""
     import torch
