@@ -1734,8 +1734,12 @@ int krk_k_rope_kv_attn_prefill(float* qkv, int64_t q_rs, float* kc, float* vc, i
     if (S <= 0 || total_rows <= 0 || H <= 0 || nblocks <= 0)
         return fail(KRK_INVALID, "prefill attention needs S, total_rows, H and nblocks > 0");
     if (q_rs < (int64_t)3 * H * dh) return fail(KRK_INVALID, "q_rs shorter than a q | k | v row");
-    if (rows_per_block != krk::attn_prefill_rows(kmax, dh))
+    if (kmax <= 0 || rows_per_block != krk_k_attn_prefill_rows(kmax, dh))
         return fail(KRK_INVALID, "rows_per_block must be krk_k_attn_prefill_rows(kmax, dh)");
+    if (krk::attn_prefill_check(qkv, q_rs, kc, vc, c_sb, c_sh, c_st, nblocks, rows_per_block, H, dh, kmax) !=
+        cudaSuccess)
+        return fail(KRK_INVALID, "prefill attention: dh must be 64 or 76, strides multiples of 4 floats, "
+                                 "qkv/kc/vc 16-byte aligned, and the scores of kmax keys must fit in shared memory");
     const cudaStream_t s = (cudaStream_t)stream;
     int st = cuda_status(krk::rope_kv_prefill(qkv, q_rs, kc, vc, c_sb, c_sh, c_st, cu_seqlens, start, S, H, dh,
                                               total_rows, theta, nullptr, s),

@@ -1094,10 +1094,9 @@ int attn_prefill_rows(int kmax, int dh) {
     return need <= PF_MAX_SMEM ? PF_ROWS : 1;
 }
 
-cudaError_t attn_prefill(const float* qkv, int64_t q_rs, const float* kc, const float* vc, int64_t c_sb,
-                         int64_t c_sh, int64_t c_st, const int32_t* cu_seqlens, const int32_t* start,
-                         const int2* blocks, int nblocks, int rows_per_block, int H, int dh, int kmax, float* out,
-                         int64_t o_rs, int64_t o_cs, cudaStream_t s) {
+cudaError_t attn_prefill_check(const float* qkv, int64_t q_rs, const float* kc, const float* vc, int64_t c_sb,
+                               int64_t c_sh, int64_t c_st, int nblocks, int rows_per_block, int H, int dh,
+                               int kmax) {
     if (H <= 0 || nblocks <= 0 || kmax <= 0 || (dh != 64 && dh != 76) || (q_rs & 3) || (c_st & 3) ||
         (c_sh & 3) || (c_sb & 3) || (((uintptr_t)qkv | (uintptr_t)kc | (uintptr_t)vc) & 15) ||
         (rows_per_block != PF_ROWS && rows_per_block != 1))
@@ -1105,12 +1104,22 @@ cudaError_t attn_prefill(const float* qkv, int64_t q_rs, const float* kc, const 
     const bool wide = rows_per_block == PF_ROWS;
     const size_t smem = dh == 76 ? (wide ? pf_smem_bytes<76, PF_ROWS>(kmax) : pf_smem_bytes<76, 1>(kmax))
                                  : (wide ? pf_smem_bytes<64, PF_ROWS>(kmax) : pf_smem_bytes<64, 1>(kmax));
-    if (smem > PF_MAX_SMEM) return cudaErrorInvalidValue;
+    return smem > PF_MAX_SMEM ? cudaErrorInvalidValue : cudaSuccess;
+}
+
+cudaError_t attn_prefill(const float* qkv, int64_t q_rs, const float* kc, const float* vc, int64_t c_sb,
+                         int64_t c_sh, int64_t c_st, const int32_t* cu_seqlens, const int32_t* start,
+                         const int2* blocks, int nblocks, int rows_per_block, int H, int dh, int kmax, float* out,
+                         int64_t o_rs, int64_t o_cs, cudaStream_t s) {
+    cudaError_t e = attn_prefill_check(qkv, q_rs, kc, vc, c_sb, c_sh, c_st, nblocks, rows_per_block, H, dh, kmax);
+    if (e != cudaSuccess) return e;
+    const bool wide = rows_per_block == PF_ROWS;
+    const size_t smem = dh == 76 ? (wide ? pf_smem_bytes<76, PF_ROWS>(kmax) : pf_smem_bytes<76, 1>(kmax))
+                                 : (wide ? pf_smem_bytes<64, PF_ROWS>(kmax) : pf_smem_bytes<64, 1>(kmax));
     const void* fns[4] = {(const void*)attn_prefill_kernel<64, 1>, (const void*)attn_prefill_kernel<64, PF_ROWS>,
                           (const void*)attn_prefill_kernel<76, 1>, (const void*)attn_prefill_kernel<76, PF_ROWS>};
     const int v = (dh == 76 ? 2 : 0) + (wide ? 1 : 0);
     static DeviceOnce once[4];
-    cudaError_t e;
     if ((e = once[v].set_smem(fns[v], PF_MAX_SMEM)) != cudaSuccess) return e;
     dim3 grid(nblocks, H);
     void* params[] = {(void*)&qkv, (void*)&q_rs, (void*)&kc, (void*)&vc, (void*)&c_sb, (void*)&c_sh,

@@ -207,6 +207,12 @@ cudaError_t rope_kv_prefill(float* qkv, int64_t q_rs, float* kc, float* vc, int6
 // scores of PF_ROWS rows over kmax keys do not fit in shared memory.
 constexpr int PF_ROWS = 8;
 int attn_prefill_rows(int kmax, int dh);
+// The argument checks attn_prefill makes (dh, stride and pointer alignment,
+// rows_per_block, shared memory for kmax), for a caller to make before the
+// RoPE/KV launch that precedes it.
+cudaError_t attn_prefill_check(const float* qkv, int64_t q_rs, const float* kc, const float* vc, int64_t c_sb,
+                               int64_t c_sh, int64_t c_st, int nblocks, int rows_per_block, int H, int dh,
+                               int kmax);
 cudaError_t attn_prefill(const float* qkv, int64_t q_rs, const float* kc, const float* vc, int64_t c_sb,
                          int64_t c_sh, int64_t c_st, const int32_t* cu_seqlens, const int32_t* start,
                          const int2* blocks, int nblocks, int rows_per_block, int H, int dh, int kmax, float* out,

@@ -373,6 +373,17 @@ def test_rope_kv_attn_prefill_rejects_bad_tables():
         _lib.check(_lib.lib.krk_k_rope_kv_attn_prefill(qkv.data_ptr(), qkv.shape[1], kc.data_ptr(), kc.data_ptr(),
                                                        0, 0, 0, None, None, 1, 4, 8, 76, 1e4, None, 1, 1, 4,
                                                        qkv.data_ptr(), 608, 1, None))  # rows_per_block 1, not 8
+    big = 100000  # one row's scores of this many keys exceed shared memory
+    with pytest.raises(_lib.KrikilError):
+        _lib.check(_lib.lib.krk_k_rope_kv_attn_prefill(qkv.data_ptr(), qkv.shape[1], kc.data_ptr(), kc.data_ptr(),
+                                                       0, 0, 0, None, None, 1, 4, 8, 76, 1e4, None, 1,
+                                                       K.attn_prefill_rows(big, 76), big, qkv.data_ptr(), 608, 1,
+                                                       None))
+    with pytest.raises(_lib.KrikilError):  # a cache 4 bytes off its 16-byte alignment
+        _lib.check(_lib.lib.krk_k_rope_kv_attn_prefill(qkv.data_ptr(), qkv.shape[1], kc.data_ptr() + 4,
+                                                       kc.data_ptr(), 0, 0, 0, None, None, 1, 4, 8, 76, 1e4, None,
+                                                       1, 8, 4, qkv.data_ptr(), 608, 1, None))
+    torch.cuda.synchronize()
 
 
 @pytest.mark.parametrize("split,ctx", [(64, 2048), (128, 700), (256, 2048), (512, 2048), (384, 2000),
