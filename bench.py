@@ -416,49 +416,55 @@ def run_ours(args):
     from krikil_rs_b200 import PebbleModel, PebbleState, launch_count, replicas, synth
     from krikil_rs_b200._lib import check, lib
 
-    peak, peak_kind = measured_peaks()
-    path = synth.weights_file(0)
-    model = PebbleModel.load_safetensors(path, device=local)
-    seqs, plen, new = args.seqs_per_gpu, args.prompt_len, args.new_tokens
-    prompts = replicas.shard(synth.decode_prompts(world * seqs, plen, seed=1), world, rank)
-    state = PebbleState(model, args.ctx, batch=seqs)
-    state.set_decode_streams(args.decode_streams)
-    state.set_step_graphs(not args.no_step_graphs)
+    # Two phases, each ended on every rank by one status exchange (the phase's
+    # barrier): a rank that fails reports it there and all ranks stop together.
+    group = dist if world > 1 else None
+    with replicas.Phase(group):  # set-up and warm-up
+        peak, peak_kind = measured_peaks()
+        path = synth.weights_file(0)
+        model = PebbleModel.load_safetensors(path, device=local)
+        seqs, plen, new = args.seqs_per_gpu, args.prompt_len, args.new_tokens
+        prompts = replicas.shard(synth.decode_prompts(world * seqs, plen, seed=1), world, rank)
+        state = PebbleState(model, args.ctx, batch=seqs)
+        state.set_decode_streams(args.decode_streams)
+        state.set_step_graphs(not args.no_step_graphs)
 
-    # pinned host buffers for the end-to-end calls
-    toks_h = torch.from_numpy(np.ascontiguousarray(prompts.reshape(-1).view(np.int32))).pin_memory()
-    lens_h = torch.full((seqs,), plen, dtype=torch.int32).pin_memory()
-    out_h = torch.zeros((seqs, new), dtype=torch.int32).pin_memory()
-    n_h = torch.zeros((seqs,), dtype=torch.int32).pin_memory()
+        # pinned host buffers for the end-to-end calls
+        toks_h = torch.from_numpy(np.ascontiguousarray(prompts.reshape(-1).view(np.int32))).pin_memory()
+        lens_h = torch.full((seqs,), plen, dtype=torch.int32).pin_memory()
+        out_h = torch.zeros((seqs, new), dtype=torch.int32).pin_memory()
+        n_h = torch.zeros((seqs,), dtype=torch.int32).pin_memory()
 
-    def generate():
-        check(lib.krk_generate_greedy(model._h, state._h, toks_h.data_ptr(), lens_h.data_ptr(), new, 1.0, 0,
-                                      out_h.data_ptr(), n_h.data_ptr()))
+        def generate():
+            check(lib.krk_generate_greedy(model._h, state._h, toks_h.data_ptr(), lens_h.data_ptr(), new, 1.0, 0,
+                                          out_h.data_ptr(), n_h.data_ptr()))
 
-    for _ in range(args.warmup):
-        generate()
-    stream = torch.cuda.ExternalStream(model.stream)
-    # the timed loop: whole-call device brackets only (no per-kernel events)
-    state.profile(True, per_kernel=False)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    clocks = ClockSampler(local)
-    clocks.start()
-    l0 = launch_count()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ev0.record(stream)
-    gen_tokens = 0
-    for _ in range(args.steps):
-        generate()
-        gen_tokens += int(n_h.sum())
-    ev1.record(stream)
-    torch.cuda.synchronize()
-    launches = launch_count() - l0
-    clk = clocks.stop()
-    e2e_ms = ev0.elapsed_time(ev1)
-    dev_ms = state.profile_read()["device_total"][0]
-    state.profile(False)
+        for _ in range(args.warmup):
+            generate()
+        stream = torch.cuda.ExternalStream(model.stream)
+        # the timed loop: whole-call device brackets only (no per-kernel events)
+        state.profile(True, per_kernel=False)
+        torch.cuda.synchronize()
+    with replicas.Phase(group):  # the timed loop
+        torch.cuda.synchronize()
+        clocks = ClockSampler(local)
+        clocks.start()
+        try:
+            l0 = launch_count()
+            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            ev0.record(stream)
+            gen_tokens = 0
+            for _ in range(args.steps):
+                generate()
+                gen_tokens += int(n_h.sum())
+            ev1.record(stream)
+            torch.cuda.synchronize()
+            launches = launch_count() - l0
+        finally:
+            clk = clocks.stop()
+        e2e_ms = ev0.elapsed_time(ev1)
+        dev_ms = state.profile_read()["device_total"][0]
+        state.profile(False)
     (e2e_ms, dev_ms), total_tokens = replicas.reduce_timings(dist, "cuda", [e2e_ms, dev_ms], gen_tokens)
     if world > 1:
         dist.barrier()
@@ -584,7 +590,18 @@ def main():
         peak, kind = measured_peaks()
         print(json.dumps({"kernels": kernel_table(torch, peak, args.scan_t), "peak_gbs": peak, "peak_kind": kind}))
     else:
-        run_ours(args)
+        from krikil_rs_b200.replicas import ReplicaFailure
+        try:
+            run_ours(args)
+        except ReplicaFailure as e:
+            # every rank raised it at the same exchange: rank 0 reports, all end
+            if int(os.environ.get("RANK", "0")) == 0:
+                print(json.dumps({"metric": METRIC, "error": "replica failure",
+                                  "failed_ranks": {str(r): m for r, m in sorted(e.failed.items())}}))
+            import torch.distributed as dist
+            if dist.is_available() and dist.is_initialized():
+                dist.destroy_process_group()
+            sys.exit(1)
 
 
 if __name__ == "__main__":

@@ -6,10 +6,19 @@ sequences, so the data path has no collective.  torch.distributed is used only
 around the timed region -- a barrier before it and, after it, the max over
 ranks of the device times and the sum of the generated-token counts.  Every
 rank takes the same collective steps in the same order.
+
+Failures: the driver's work runs in phases (`Phase`), each ended on every rank
+by one status exchange that also serves as the phase's barrier.  A rank whose
+phase raised still takes that exchange, so it never leaves the others waiting
+in a collective it will not reach; once any rank reports a failure, every rank
+raises `ReplicaFailure` naming the failed ranks and their errors, and skips the
+remaining collectives together.  A rank that dies outright (never reaches the
+exchange) is caught by the process group's timeout: the others' exchange ends
+with an error instead of waiting for good.
 """
 from __future__ import annotations
 
-from typing import Sequence, Tuple
+from typing import Dict, Optional, Sequence, Tuple
 
 
 def shard(items: Sequence, world: int, rank: int) -> Sequence:
@@ -34,3 +43,49 @@ def reduce_timings(dist, device, times_ms: Sequence[float], tokens: int) -> Tupl
     g = torch.tensor([int(tokens)], dtype=torch.int64, device=device)
     dist.all_reduce(g)
     return [float(x) for x in t.tolist()], int(g.item())
+
+
+class ReplicaFailure(RuntimeError):
+    """Raised on every rank when some rank's phase failed; `failed` maps each
+    failed rank to its error message."""
+
+    def __init__(self, failed: Dict[int, str]):
+        self.failed = dict(failed)
+        super().__init__("replica failure on rank(s) " +
+                         "; ".join(f"{r}: {m}" for r, m in sorted(self.failed.items())))
+
+
+def exchange_status(dist, error: Optional[str]) -> None:
+    """Every rank reports its phase's outcome (None = fine); all ranks raise
+    ReplicaFailure together if any rank failed.  Without an initialised
+    multi-rank process group the local outcome alone decides."""
+    if not (dist is not None and dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        if error is not None:
+            raise ReplicaFailure({0: error})
+        return
+    msgs = [None] * dist.get_world_size()
+    dist.all_gather_object(msgs, error)
+    failed = {r: m for r, m in enumerate(msgs) if m is not None}
+    if failed:
+        raise ReplicaFailure(failed)
+
+
+class Phase:
+    """A phase of the replicated driver: `with Phase(dist): ...` runs the body
+    on this rank, then exchanges the outcome with the other ranks (the
+    exchange is the phase's barrier).  An exception from the body is reported,
+    not propagated alone: every rank then raises ReplicaFailure together.
+    Exceptions that are not Exceptions (KeyboardInterrupt, SystemExit) pass
+    through untouched."""
+
+    def __init__(self, dist):
+        self.dist = dist
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, et, ev, tb):
+        if et is not None and not issubclass(et, Exception):
+            return False
+        exchange_status(self.dist, None if ev is None else f"{et.__name__}: {ev}")
+        return False
