@@ -251,7 +251,8 @@ def workload_config(args):
             "seqs_total": args.seqs_per_gpu * args.world, "seqs_per_gpu": args.seqs_per_gpu,
             "prompt_len": args.prompt_len, "new_tokens": args.new_tokens,
             "ctx": args.ctx, "eos": "ignored", "prompts": "U[0,2048) numpy seed 1",
-            "l2": "inputs larger than L2 (SSD state + KV cache per GPU: 3.8 GB at 1024 sequences)",
+            "l2": "inputs larger than L2 (SSD state per GPU: %.2f GB, plus the KV caches)"
+                  % (args.seqs_per_gpu * 6 * 19 * 64 * 128 * 4 / 1e9),
             "decode_parts": args.decode_streams, "step_graphs": not args.no_step_graphs,
             "parallelism": f"replicas x{args.world} (no collectives)"}
 
