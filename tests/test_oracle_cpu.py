@@ -88,6 +88,24 @@ def test_oracle_model_matches_float64(perturb, synth_weights, synth_weights_pert
     np.testing.assert_allclose(st.kc[7][:9], ref.k[7][:9], atol=1e-5, rtol=1e-4)
 
 
+def test_oracle_model_matches_float64_c1_prompt(synth_weights_perturbed):
+    """The batch-1 workload's 32-token prompt (seed 0) and eight decode steps
+    on the perturbed weights (norm weights, D and conv bias away from their
+    constants), against the float64 model: longer contexts for the SSD and the
+    attention cache than the short-prompt test."""
+    w = synth_weights_perturbed
+    m = O.OracleModel(w)
+    st = O.OracleState(64)
+    ref = NpPebble(w, 64)
+    toks = np.random.default_rng(0).integers(0, O.VOCAB, 32).tolist()
+    np.testing.assert_allclose(O.forward_prefill(m, st, toks), ref.prefill(toks), atol=2e-5, rtol=1e-4)
+    for t in (199, 490, 0, 2047, 5, 5, 1024, 77):
+        np.testing.assert_allclose(O.forward_step(m, st, t), ref.step(t), atol=2e-5, rtol=1e-4)
+    np.testing.assert_allclose(st.ssm[5], ref.ssm[5], atol=1e-5, rtol=1e-4)
+    np.testing.assert_allclose(st.conv[1], ref.conv[1], atol=1e-6, rtol=1e-5)
+    np.testing.assert_allclose(st.kc[3][:40], ref.k[3][:40], atol=1e-5, rtol=1e-4)
+
+
 def test_prefill_then_prefill_equals_one_prefill(synth_weights):
     """Prefill at a nonzero start (src/model.rs:495, :506) continues the sequence."""
     m = O.OracleModel(synth_weights)
