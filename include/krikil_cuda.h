@@ -281,6 +281,18 @@ KRK_API int krk_k_gemm(const float* At, int lda, const float* Wt, int ldw, float
 KRK_API int krk_k_gemm_tiled(const float* At, int lda, const float* Wt, int ldw, float* C, int ldc, int M, int N,
                              int K, int epilogue, int out_fm, int tile_rows, void* stream);
 
+/* C = A . W^T with the operand layouts of krk_k_gemm (batch-major C, store
+ * only), every element summed in the order of matrixmultiply 0.3.11's sgemm,
+ * which the reference's gemm_transb (src/math.rs:188-211) calls for its prefill
+ * projections (src/model.rs:387, 458, 484, 554, 570, 577): a fused
+ * multiply-add chain over k from zero within each 256-long block of K, the
+ * blocks' sums added to the output in order.  That order is restated from the
+ * crate's published algorithm (the crate is not part of the reference tree);
+ * the model's prefill keeps krk_k_gemm's gemv dot order.  M % 64 == 0,
+ * N % 32 == 0, K % 32 == 0, leading dims % 4 == 0, pointers 16-byte aligned. */
+KRK_API int krk_k_gemm_sgemm_order(const float* At, int lda, const float* Wt, int ldw, float* C, int ldc, int M,
+                                   int N, int K, void* stream);
+
 /* The tile height krk_k_gemm chooses for an M x N output on the current
  * device (148 SMs assumed when no device answers): the smallest of 16 / 32 /
  * 64 rows whose grid fits in one wave of one CTA per SM, else 32 below 256

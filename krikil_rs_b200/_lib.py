@@ -69,6 +69,7 @@ _SIGS = {
     "krk_attn_work_floats": (C.c_size_t, [_i32, _i32, _i32, _i32, _i32]),
     "krk_k_rope_kv_attn_decode": (_i32, [_fp] * 8 + [_i32] * 5 + [_f32, _vp]),
     "krk_k_greedy": (_i32, [_fp, _i64, _i32, _i32, _vp, _f32, _vp, _vp]),
+    "krk_k_gemm_sgemm_order": (_i32, [_fp, _i32, _fp, _i32, _fp, _i32, _i32, _i32, _i32, _vp]),
     "krk_k_attn_prefill_rows": (_i32, [_i32, _i32]),
     "krk_k_rope_kv_attn_prefill": (_i32, [_fp, _i64, _fp, _fp, _i64, _i64, _i64, _vp, _vp] + [_i32] * 4
                                    + [_f32, _vp] + [_i32] * 3 + [_fp, _i64, _i64, _vp]),

@@ -1722,6 +1722,12 @@ int krk_k_rope_kv_attn_decode(const float* q, const float* k, const float* v, fl
     return cuda_status(krk::attn_decode(a, (cudaStream_t)stream), "rope_kv_attn_decode");
 }
 
+int krk_k_gemm_sgemm_order(const float* At, int lda, const float* Wt, int ldw, float* C, int ldc, int M, int N,
+                           int K, void* stream) {
+    return cuda_status(krk::gemm_sgemm_order(At, lda, Wt, ldw, C, ldc, M, N, K, (cudaStream_t)stream),
+                       "gemm_sgemm_order");
+}
+
 int krk_k_attn_prefill_rows(int kmax, int dh) {
     if (kmax <= 0 || (dh != 64 && dh != 76)) return 0;
     return krk::attn_prefill_rows(kmax, dh);

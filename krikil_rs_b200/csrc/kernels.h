@@ -97,6 +97,10 @@ struct GemmNorm {
 };
 cudaError_t gemm_few_norm(const float* At, int lda, const float* Wt, int ldw, float* C, int ldc, int M, int N, int K,
                           int epilogue, bool out_fm, const GemmNorm& nm, const GemmConv* cv, cudaStream_t s);
+// C = A . W^T (batch-major C[M][ldc]) summed in matrixmultiply 0.3.11 sgemm's
+// order (k_gemm_sgemm.cu).  M % 64 == 0, N % 32 == 0, K % 32 == 0.
+cudaError_t gemm_sgemm_order(const float* At, int lda, const float* Wt, int ldw, float* C, int ldc, int M, int N,
+                             int K, cudaStream_t s);
 // Rows per CTA tile (64, 32 or 16) gemm() uses for an M x N output.
 int gemm_tile_rows(int M, int N);
 // gemm() with an explicit CTA tile height (16, 32 or 64; 1 = the few-rows form; 0 = gemm_tile_rows).

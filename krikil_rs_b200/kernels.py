@@ -134,6 +134,18 @@ def rope_kv_attn_decode(q, k, v, kc, vc, pos, split: int = 0, theta: float = 100
     return out
 
 
+def gemm_sgemm_order(a_t: torch.Tensor, w_t: torch.Tensor) -> torch.Tensor:
+    """C = A . W^T (a_t = A^T [K, M], w_t = W^T [K, N]) summed in the order of
+    matrixmultiply's sgemm (the reference's prefill GEMM)."""
+    _f32(a_t, w_t)
+    k, m = a_t.shape
+    k2, n = w_t.shape
+    assert k == k2
+    c = torch.empty((m, n), device=a_t.device, dtype=torch.float32)
+    check(lib.krk_k_gemm_sgemm_order(a_t.data_ptr(), m, w_t.data_ptr(), n, c.data_ptr(), n, m, n, k, _stream()))
+    return c
+
+
 def attn_prefill_rows(kmax: int, dh: int) -> int:
     return int(lib.krk_k_attn_prefill_rows(kmax, dh))
 

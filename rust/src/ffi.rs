@@ -138,6 +138,8 @@ extern "C" {
                                      vc: *mut c_float, pos: *const i32, out: *mut c_float, work: *mut c_float,
                                      b: c_int, h: c_int, dh: c_int, ctx: c_int, split: c_int, theta: c_float,
                                      stream: *mut c_void) -> c_int;
+    pub fn krk_k_gemm_sgemm_order(at: *const c_float, lda: c_int, wt: *const c_float, ldw: c_int, c: *mut c_float,
+                                  ldc: c_int, m: c_int, n: c_int, k: c_int, stream: *mut c_void) -> c_int;
     pub fn krk_k_attn_prefill_rows(kmax: c_int, dh: c_int) -> c_int;
     pub fn krk_k_rope_kv_attn_prefill(qkv: *mut c_float, q_rs: i64, kc: *mut c_float, vc: *mut c_float, c_sb: i64,
                                       c_sh: i64, c_st: i64, cu_seqlens: *const i32, start: *const i32, s: c_int,

@@ -125,6 +125,32 @@ def test_gemm_rejects_bad_shapes():
         K.gemm(torch.zeros(32, 60, device=DEV), torch.zeros(32, 32, device=DEV))
 
 
+@pytest.mark.parametrize("m,n,k", [(64, 32, 32), (64, 64, 288), (128, 2720, 608), (64, 608, 1216),
+                                   (192, 608, 2432), (64, 1824, 608), (128, 2432, 608)])
+def test_gemm_sgemm_order_bit_exact(m, n, k):
+    """krk_k_gemm_sgemm_order against the oracle's restatement of
+    matrixmultiply 0.3.11's sgemm order (the reference's prefill GEMM,
+    src/math.rs:188-211), bitwise, at the prefill projection shapes and at K
+    one K-block past a 256-long block; the dot-order kernel rounds differently."""
+    rng = np.random.default_rng(m * 5 + n + k)
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    w = (0.02 * rng.standard_normal((n, k))).astype(np.float32)
+    with O.prefill_gemm_order("matrixmultiply"):
+        ref = O.gemm_transb(a, w)
+    a_t, w_t = cu(a.T.copy()), cu(w.T.copy())
+    np.testing.assert_array_equal(np_(K.gemm_sgemm_order(a_t, w_t)), ref)
+    if k >= 64:
+        assert not np.array_equal(np_(K.gemm(a_t, w_t)), ref)
+
+
+def test_gemm_sgemm_order_rejects_bad_shapes():
+    from krikil_rs_b200._lib import KrikilError
+    with pytest.raises(KrikilError):  # M not a multiple of 64
+        K.gemm_sgemm_order(torch.zeros(32, 96, device=DEV), torch.zeros(32, 32, device=DEV))
+    with pytest.raises(KrikilError):  # K not a multiple of 32
+        K.gemm_sgemm_order(torch.zeros(40, 64, device=DEV), torch.zeros(40, 32, device=DEV))
+
+
 # ------------------------------------------------------------- norms
 @pytest.mark.parametrize("kdim,m,ld", [(608, 64, 64), (1216, 37, 64), (608, 1, 64), (608, 1024, 1024),
                                        (100, 13, 16)])
