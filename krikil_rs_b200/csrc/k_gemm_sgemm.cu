@@ -7,8 +7,8 @@
 // reach the output in order: the first is stored, each later one added to it
 // (alpha = beta = 1: one rounded add).
 //
-// A plain register-tiled GEMM computes exactly that: a thread owns a 4x4 block
-// of outputs and walks k in increasing order, so no dot-lane partials need
+// A plain register-tiled GEMM computes exactly that: a thread owns a block of
+// outputs and walks k in increasing order, so no dot-lane partials need
 // folding (unlike gemm_lane8_kernel, which reproduces the gemv dot order of
 // the decode projections).  Operands as in k_gemm.cu: A feature-major
 // (At[k][m]) and W K-major (Wt[k][n]), staged through a two-slot cp.async
@@ -97,6 +97,97 @@ __global__ void __launch_bounds__(SG_NT) gemm_sgemm_order_kernel(const float* __
             make_float4(tot[r][0].x, tot[r][0].y, tot[r][1].x, tot[r][1].y);
 }
 
+// The wide form for M % 256 == 0: 256x32 CTA tiles, an 8x8 output block per
+// thread (four 16-byte shared loads per 32 packed FMAs).  To keep the 64
+// chains in registers, a finished 256-long block's sums go to C directly --
+// stored by the first block, added to C by each later one -- and only the
+// thread that owns an element ever reads or writes it.
+constexpr int SW_BM = 256, SW_BN = 32, SW_BK = 32, SW_NT = 128;
+constexpr size_t SW_SMEM = 2 * (size_t)SW_BK * (SW_BM + SW_BN) * sizeof(float);
+
+__global__ void __launch_bounds__(SW_NT) gemm_sgemm_order_wide_kernel(const float* __restrict__ At, int lda,
+                                                                      const float* __restrict__ Wt, int ldw,
+                                                                      float* __restrict__ C, int ldc, int K) {
+    extern __shared__ __align__(16) float sw[];
+    float* As = sw;                          // [2][SW_BK][SW_BM]
+    float* Ws = sw + 2 * SW_BK * SW_BM;      // [2][SW_BK][SW_BN]
+    const int tid = threadIdx.x, tm = tid >> 2, tn = tid & 3;  // rows tm*8.., columns tn*8..
+    const int m0 = blockIdx.x * SW_BM, n0 = blockIdx.y * SW_BN;
+    const int nkb = K / SW_BK;
+
+    auto load = [&](int slot, int kb) {
+        const size_t k0 = (size_t)kb * SW_BK;
+        float* as = As + slot * SW_BK * SW_BM;
+        float* ws = Ws + slot * SW_BK * SW_BN;
+#pragma unroll
+        for (int i = 0; i < SW_BK * SW_BM / 4 / SW_NT; ++i) {
+            const int idx = tid + i * SW_NT, kk = idx / (SW_BM / 4), c4 = idx % (SW_BM / 4);
+            cp_async16(as + kk * SW_BM + c4 * 4, At + (k0 + kk) * lda + m0 + c4 * 4);
+        }
+#pragma unroll
+        for (int i = 0; i < SW_BK * SW_BN / 4 / SW_NT; ++i) {
+            const int idx = tid + i * SW_NT, kk = idx / (SW_BN / 4), c4 = idx % (SW_BN / 4);
+            cp_async16(ws + kk * SW_BN + c4 * 4, Wt + (k0 + kk) * ldw + n0 + c4 * 4);
+        }
+        cp_async_commit();
+    };
+
+    float2 acc[8][4];  // rows r, column pairs (2j, 2j+1)
+#pragma unroll
+    for (int r = 0; r < 8; ++r)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[r][j] = make_float2(0.0f, 0.0f);
+
+    load(0, 0);
+    for (int kb = 0; kb < nkb; ++kb) {
+        if (kb + 1 < nkb) {
+            load((kb + 1) & 1, kb + 1);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        __syncthreads();
+        const float* as = As + (kb & 1) * SW_BK * SW_BM;
+        const float* ws = Ws + (kb & 1) * SW_BK * SW_BN;
+#pragma unroll 4
+        for (int kk = 0; kk < SW_BK; ++kk) {  // k in increasing order
+            const float4 a0 = *reinterpret_cast<const float4*>(as + kk * SW_BM + tm * 8);
+            const float4 a1 = *reinterpret_cast<const float4*>(as + kk * SW_BM + tm * 8 + 4);
+            const float4 w0 = *reinterpret_cast<const float4*>(ws + kk * SW_BN + tn * 8);
+            const float4 w1 = *reinterpret_cast<const float4*>(ws + kk * SW_BN + tn * 8 + 4);
+            const float ar[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+            const float2 wp[4] = {make_float2(w0.x, w0.y), make_float2(w0.z, w0.w), make_float2(w1.x, w1.y),
+                                  make_float2(w1.z, w1.w)};
+#pragma unroll
+            for (int r = 0; r < 8; ++r) {
+                const float2 aa = make_float2(ar[r], ar[r]);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[r][j] = __ffma2_rn(aa, wp[j], acc[r][j]);
+            }
+        }
+        __syncthreads();
+        const int k_end = (kb + 1) * SW_BK;
+        if (k_end % SG_KC == 0 || kb + 1 == nkb) {  // a 256-long block of K (or the last, shorter one) ends
+            const bool first = k_end <= SG_KC;
+#pragma unroll
+            for (int r = 0; r < 8; ++r) {
+                float4* c = reinterpret_cast<float4*>(C + (size_t)(m0 + tm * 8 + r) * ldc + n0 + tn * 8);
+                float4 lo = make_float4(acc[r][0].x, acc[r][0].y, acc[r][1].x, acc[r][1].y);
+                float4 hi = make_float4(acc[r][2].x, acc[r][2].y, acc[r][3].x, acc[r][3].y);
+                if (!first) {
+                    const float4 p0 = c[0], p1 = c[1];
+                    lo = make_float4(lo.x + p0.x, lo.y + p0.y, lo.z + p0.z, lo.w + p0.w);
+                    hi = make_float4(hi.x + p1.x, hi.y + p1.y, hi.z + p1.z, hi.w + p1.w);
+                }
+                c[0] = lo;
+                c[1] = hi;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[r][j] = make_float2(0.0f, 0.0f);
+            }
+        }
+    }
+}
+
 }  // namespace
 
 cudaError_t gemm_sgemm_order(const float* At, int lda, const float* Wt, int ldw, float* C, int ldc, int M, int N,
@@ -104,7 +195,14 @@ cudaError_t gemm_sgemm_order(const float* At, int lda, const float* Wt, int ldw,
     if (M <= 0 || N <= 0 || K <= 0 || M % SG_BM || N % SG_BN || K % SG_BK || N / SG_BN > 65535 || lda % 4 ||
         ldw % 4 || ldc % 4 || lda < M || ldw < N || ldc < N || ((uintptr_t)At | (uintptr_t)Wt | (uintptr_t)C) % 16)
         return cudaErrorInvalidValue;
-    gemm_sgemm_order_kernel<<<dim3(M / SG_BM, N / SG_BN), SG_NT, 0, s>>>(At, lda, Wt, ldw, C, ldc, K);
+    if (M % SW_BM == 0) {
+        static DeviceOnce once;
+        cudaError_t e;
+        if ((e = once.set_smem((const void*)gemm_sgemm_order_wide_kernel, (int)SW_SMEM)) != cudaSuccess) return e;
+        gemm_sgemm_order_wide_kernel<<<dim3(M / SW_BM, N / SW_BN), SW_NT, SW_SMEM, s>>>(At, lda, Wt, ldw, C, ldc, K);
+    } else {
+        gemm_sgemm_order_kernel<<<dim3(M / SG_BM, N / SG_BN), SG_NT, 0, s>>>(At, lda, Wt, ldw, C, ldc, K);
+    }
     add_launches(1);
     return cudaGetLastError();
 }

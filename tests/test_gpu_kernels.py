@@ -126,7 +126,10 @@ def test_gemm_rejects_bad_shapes():
 
 
 @pytest.mark.parametrize("m,n,k", [(64, 32, 32), (64, 64, 288), (128, 2720, 608), (64, 608, 1216),
-                                   (192, 608, 2432), (64, 1824, 608), (128, 2432, 608)])
+                                   (192, 608, 2432), (64, 1824, 608), (128, 2432, 608),
+                                   # the wide form (M % 256 == 0): block sums added in C
+                                   (256, 32, 32), (256, 64, 288), (256, 2720, 608), (512, 608, 2432),
+                                   (256, 1824, 608), (768, 608, 1216)])
 def test_gemm_sgemm_order_bit_exact(m, n, k):
     """krk_k_gemm_sgemm_order against the oracle's restatement of
     matrixmultiply 0.3.11's sgemm order (the reference's prefill GEMM,
