@@ -158,7 +158,8 @@ def test_sgemm_order_gemm_close_to_float64():
     """The restated matrixmultiply 0.3.11 sgemm order (src/math.rs:188-211) is a
     correct product, and it rounds differently from the gemv dot order."""
     rng = np.random.default_rng(3)
-    for m, k, n in ((5, 608, 37), (3, 1216, 19), (2, 2432, 11), (4, 100, 9), (3, 257, 5)):
+    for m, k, n in ((5, 608, 37), (3, 1216, 19), (2, 2432, 11), (4, 100, 9), (3, 257, 5), (3, 256, 7),
+                    (2, 512, 6)):
         a = rng.standard_normal((m, k), dtype=np.float32)
         b = rng.standard_normal((n, k), dtype=np.float32)
         exact = a.astype(np.float64) @ b.astype(np.float64).T
@@ -169,6 +170,16 @@ def test_sgemm_order_gemm_close_to_float64():
         assert np.all(np.abs(mm - exact) <= bound)
         assert np.all(np.abs(dot - exact) <= bound)
         assert not np.array_equal(mm, dot)
+    # one block of K is a single FMA chain from zero; two blocks add their chains
+    # (the two 2^-24 terms are absorbed one at a time by the running 1.0: the
+    # exact sum 2^-23 comes out as 0; split over two blocks they survive)
+    a = np.array([[1.0, 2.0 ** -24, 2.0 ** -24, -1.0]], np.float32)
+    b = np.ones((1, 4), np.float32)
+    with O.prefill_gemm_order("matrixmultiply"):
+        assert O.gemm_transb(a, b)[0, 0] == 0.0
+        a2 = np.zeros((1, 512), np.float32)
+        a2[0, 0], a2[0, 256], a2[0, 257], a2[0, 1] = 1.0, 2.0 ** -24, 2.0 ** -24, -1.0
+        assert O.gemm_transb(a2, np.ones((1, 512), np.float32))[0, 0] == np.float32(2.0 ** -23)
     assert O.lib.orc_prefill_gemm_order() == 0
 
 
