@@ -146,6 +146,18 @@ def test_gemm_sgemm_order_bit_exact(m, n, k):
         assert not np.array_equal(np_(K.gemm(a_t, w_t)), ref)
 
 
+@pytest.mark.parametrize("m", [64, 256])
+def test_gemm_sgemm_order_known_answer(m):
+    """One float32 FMA chain per 256-long block of K: 1 + 2^-24 + 2^-24 - 1 in
+    one block gives 0 (each 2^-24 absorbed), split over two blocks 2^-23."""
+    a = np.zeros((m, 512), np.float32)
+    a[0, [0, 1, 2, 3]] = [1.0, 2.0 ** -24, 2.0 ** -24, -1.0]
+    a[1, [0, 1, 256, 257]] = [1.0, -1.0, 2.0 ** -24, 2.0 ** -24]
+    w = np.ones((32, 512), np.float32)
+    c = np_(K.gemm_sgemm_order(cu(a.T.copy()), cu(w.T.copy())))
+    assert (c[0] == 0.0).all() and (c[1] == np.float32(2.0 ** -23)).all() and not c[2:].any()
+
+
 def test_gemm_sgemm_order_rejects_bad_shapes():
     from krikil_rs_b200._lib import KrikilError
     with pytest.raises(KrikilError):  # M not a multiple of 64
